@@ -1,0 +1,172 @@
+"""Training/validation batch sources built from a :class:`TrainConfig`.
+
+``make_batch_source(cfg, split, rank, world)`` returns an object with ``next(batch, seq)`` giving
+host int32 ``(inputs, targets)`` arrays and an ``epoch`` attribute. Each rank draws from its own
+seeded stream (seed, split and rank mixed), so data-parallel ranks see disjoint data, like separate
+browser tabs in the reference. The validation split uses a different seed, i.e. a held-out stream.
+
+``PinnedPrefetcher`` produces the next batch on a host thread into page-locked buffers and copies
+it to the device on a side stream, so the host->device transfer overlaps the previous step.
+"""
+from __future__ import annotations
+
+import threading
+from queue import Queue
+
+import numpy as np
+import torch
+
+from ..config import TrainConfig
+from .loader import BestFitDocumentBatcher, TokenDataLoader, load_tokens_bin
+from .synthetic import UniformBOSStream, ZipfDocumentSource, bos_id
+
+
+def _native():
+    try:
+        from .. import _native_data  # type: ignore
+        return _native_data
+    except Exception:
+        return None
+
+
+def _seed(cfg: TrainConfig, split: str, rank: int) -> int:
+    return (cfg.seed * 1_000_003 + (0 if split == "train" else 7_777_777) + rank * 9176) & 0x7FFFFFFF
+
+
+class _ZipfNative:
+    def __init__(self, cfg: TrainConfig, seed: int):
+        mod = _native()
+        self.mod = mod
+        self.p = mod.zipf_packer(cfg.model.vocab_size, cfg.zipf_s, float(cfg.doc_mean_len), seed,
+                                 cfg.document_buffer_size, 0)
+
+    @property
+    def epoch(self):
+        return self.p.epoch
+
+    def next(self, batch: int, seq: int):
+        rows = np.empty((batch, seq + 1), np.int32)
+        self.mod.pack_rows(self.p, rows, batch, seq)
+        return rows[:, :seq], rows[:, 1:]
+
+    def next_into(self, inputs: torch.Tensor, targets: torch.Tensor, batch: int, seq: int):
+        self.mod.pack_split(self.p, inputs.data_ptr(), targets.data_ptr(), batch, seq)
+
+
+class _ZipfPython:
+    def __init__(self, cfg: TrainConfig, seed: int):
+        src = ZipfDocumentSource(cfg.model.vocab_size, cfg.zipf_s, cfg.doc_mean_len, seed)
+        self.b = BestFitDocumentBatcher(src.documents, bos_id(cfg.model.vocab_size), cfg.document_buffer_size)
+
+    @property
+    def epoch(self):
+        return self.b.epoch
+
+    def next(self, batch: int, seq: int):
+        x, y, _ = self.b.next_batch(batch, seq)
+        return x, y
+
+
+class _Uniform:
+    def __init__(self, cfg: TrainConfig, seed: int):
+        self.s = UniformBOSStream(cfg.model.vocab_size, cfg.bos_every, seed)
+        self.epoch = 0
+
+    def next(self, batch: int, seq: int):
+        rows = self.s.take(batch * (seq + 1)).reshape(batch, seq + 1)
+        return rows[:, :seq].copy(), rows[:, 1:].copy()
+
+
+class _Tokens:
+    def __init__(self, tokens: np.ndarray):
+        self.l = TokenDataLoader(tokens)
+
+    @property
+    def epoch(self):
+        return self.l.epochs
+
+    def next(self, batch: int, seq: int):
+        return self.l.next_batch(batch, seq)
+
+
+def make_batch_source(cfg: TrainConfig, split: str = "train", rank: int = 0, world: int = 1, native: bool = True):
+    seed = _seed(cfg, split, rank)
+    if cfg.data == "zipf":
+        if native and _native() is not None:
+            return _ZipfNative(cfg, seed)
+        return _ZipfPython(cfg, seed)
+    if cfg.data == "uniform":
+        return _Uniform(cfg, seed)
+    if cfg.data == "tokens":
+        toks = load_tokens_bin(cfg.data_path)
+        split_at = int(len(toks) * (1 - cfg.val_fraction))
+        part = toks[:split_at] if split == "train" else toks[split_at:]
+        if split == "train" and world > 1:  # contiguous per-rank shards of the training stream
+            n = len(part) // world
+            part = part[rank * n:(rank + 1) * n]
+        return _Tokens(part)
+    raise ValueError(f"unknown data source {cfg.data!r}")
+
+
+class PinnedPrefetcher:
+    """Host thread packs batches into pinned buffers; ``get()`` returns device tensors.
+
+    The H2D copy of batch k+1 is issued on a side stream while step k runs; ``get`` makes the
+    compute stream wait on that copy's event.
+    """
+
+    def __init__(self, source, batch: int, seq: int, device: torch.device, depth: int = 2):
+        self.source, self.batch, self.seq, self.device = source, batch, seq, device
+        self.depth = depth
+        self.host = [(torch.empty((batch, seq), dtype=torch.int32, pin_memory=True),
+                      torch.empty((batch, seq), dtype=torch.int32, pin_memory=True)) for _ in range(depth + 1)]
+        self.dev = [(torch.empty((batch, seq), dtype=torch.int32, device=device),
+                     torch.empty((batch, seq), dtype=torch.int32, device=device)) for _ in range(depth + 1)]
+        self.copy_stream = torch.cuda.Stream(device=device)
+        self.events = [torch.cuda.Event() for _ in range(depth + 1)]
+        self.free: Queue = Queue()
+        self.ready: Queue = Queue()
+        for i in range(depth + 1):
+            self.free.put(i)
+        self.h2d_bytes = 2 * batch * seq * 4
+        self._stop = False
+        self.thread = threading.Thread(target=self._fill, daemon=True)
+        self.thread.start()
+        self._inflight: list[int] = []
+
+    def _fill(self):
+        while not self._stop:
+            i = self.free.get()
+            if i is None:
+                return
+            hx, hy = self.host[i]
+            if hasattr(self.source, "next_into"):
+                self.source.next_into(hx, hy, self.batch, self.seq)
+            else:
+                x, y = self.source.next(self.batch, self.seq)
+                hx.numpy()[...] = x
+                hy.numpy()[...] = y
+            self.ready.put(i)
+
+    def get(self):
+        i = self.ready.get()
+        hx, hy = self.host[i]
+        dx, dy = self.dev[i]
+        cur = torch.cuda.current_stream(self.device)
+        # the device slot may still be read by an earlier step
+        self.copy_stream.wait_stream(cur)
+        with torch.cuda.stream(self.copy_stream):
+            dx.copy_(hx, non_blocking=True)
+            dy.copy_(hy, non_blocking=True)
+            self.events[i].record(self.copy_stream)
+        cur.wait_event(self.events[i])
+        self._inflight.append(i)
+        if len(self._inflight) > 1:  # the host slot of the previous batch is free once its copy completed
+            j = self._inflight.pop(0)
+            self.events[j].synchronize()
+            self.free.put(j)
+        return dx, dy
+
+    def close(self):
+        self._stop = True
+        self.free.put(None)

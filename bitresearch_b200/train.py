@@ -1,0 +1,453 @@
+"""Data-parallel trainer: the fixed-time-budget loop of the reference's ``DistributedTrainer``.
+
+One process per GPU (``torchrun``) or per CPU rank (gloo). Per step (src/distributed/trainer.ts:723-888):
+
+1. next batch (host packer -> pinned buffer -> device);
+2. forward + backward: the sm_100a engine (``impl='cuda'``) writes every gradient straight into one
+   flat buffer in the reference's variable order; the eager path (``impl='torch'``) uses autograd with
+   ``.grad`` views into the same buffer;
+3. non-finite check -> skip the update (the reference's overflow/NaN skip, trainer.ts:751-791); with
+   ``dtype='fp16'`` the reference's dynamic loss scale is kept (start 1024, halve + skip on
+   overflow, double after 2000 good steps);
+4. optional top-k + error feedback, then the gradient mean over ranks: in-kernel NVLink
+   reduce-scatter (``comm='p2p'``), NCCL all-reduce (``'nccl'``), or the reference's ring over the
+   process group (``'ring'``, the CPU/gloo path); an aborted collective skips the update
+   (trainer.ts:821-830);
+5. schedules (lr multiplier, Muon momentum and weight decay, trainer.ts:577-602) and the optimizer
+   (sharded over ranks on the p2p path, followed by the parameter all-gather);
+6. metrics: loss, EMA smooth loss (0.9), tokens/s over all ranks, MFU against the measured B200 peak.
+
+``start_training`` stops when ``total_training_time`` (which excludes the first 10 steps,
+trainer.ts:986, 1005) reaches ``time_budget`` or at ``max_steps``, then runs ``evaluate_bpb`` on the
+held-out split and prints the summary block (trainer.ts:1040-1068) and a ``results.tsv`` row.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import time
+from collections import OrderedDict
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import checkpoint as ckpt
+from .config import TrainConfig, apply_overrides, estimate_params, preset
+from .data.pipeline import PinnedPrefetcher, make_batch_source
+from .data.synthetic import make_token_bytes
+from .data.loader import load_token_bytes
+from .eval import evaluate_bpb
+from .models.gpt import GPT
+from .optim.muon_adamw import MuonAdamW, lr_multiplier, muon_momentum, weight_decay_at
+from .parallel.ring import RingAllReduce
+from .parallel.sparsify import GradientSparsifier
+from .utils.logging import MetricsLog, ResultsLogger, TrainerMetrics, summary_block
+
+B200_BF16_PEAK_FLOPS = 1630e12  # measured cuBLAS bf16 burst on this hardware (H100: 989.5e12, trainer.ts:102)
+
+
+class LossScaler:
+    """Dynamic loss scale of trainer.ts:159-160, 741-791 (used for fp16 compute)."""
+
+    def __init__(self, enabled: bool, init: float = 1024.0, growth_interval: int = 2000):
+        self.enabled = enabled
+        self.scale = init if enabled else 1.0
+        self.good = 0
+        self.growth_interval = growth_interval
+
+    def update(self, overflow: bool) -> None:
+        if not self.enabled:
+            return
+        if overflow:
+            self.scale /= 2
+            self.good = 0
+            return
+        self.good += 1
+        if self.good >= self.growth_interval:
+            self.scale *= 2
+            self.good = 0
+
+
+def init_distributed(backend: str | None = None, timeout_s: float = 120.0):
+    """Initialise the default process group from torchrun's env; returns (rank, world, local_rank)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        import datetime
+        if backend is None:
+            backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s),
+                                **({"device_id": torch.device("cuda", local)} if backend == "nccl" else {}))
+    return rank, world, local
+
+
+class Trainer:
+    def __init__(self, cfg: TrainConfig, device: str | torch.device | None = None, log=None):
+        self.cfg = cfg
+        self.rank = dist.get_rank() if dist.is_initialized() else 0
+        self.world = dist.get_world_size() if dist.is_initialized() else 1
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
+        self.device = torch.device(device)
+        self.is_cuda = self.device.type == "cuda"
+        self._log = log or (lambda m: print(m, flush=True) if self.rank == 0 else None)
+        self.metrics = TrainerMetrics()
+        self.total_training_time = 0.0
+        self.start_time = 0.0
+        self.running = False
+        self.scaler = LossScaler(cfg.dtype == "fp16")
+        self.skipped = 0
+        self.model: GPT | None = None
+        self.engine = None
+        self.optimizer: MuonAdamW | None = None
+        self.comm = None
+        self.sparsifier: GradientSparsifier | None = None
+        self.prefetch = None
+
+    def log(self, msg: str) -> None:
+        self._log(msg)
+
+    # ------------------------------------------------------------------ setup
+    def initialize(self) -> None:
+        cfg = self.cfg
+        torch.manual_seed(cfg.seed)
+        self.model = GPT(cfg.model, init="karpathy", seed=42, device=self.device)
+        self.specs = self.model.specs
+        self.metrics.num_params_m = self.model.num_params() / 1e6
+        self.flops_per_token = self.model.estimate_flops_per_token()
+        if self.rank == 0:
+            self.log(f"model: {self.metrics.num_params_m:.1f}M params (estimate {estimate_params(cfg.model) / 1e6:.2f}M), "
+                     f"{self.flops_per_token / 1e6:.1f} MFLOP/token, world={self.world}, impl={cfg.impl}")
+        T = cfg.model.sequence_len
+        per_rank_tokens = cfg.total_batch_tokens // self.world
+        if per_rank_tokens % T:
+            raise ValueError("total_batch_tokens / world must be a multiple of sequence_len")
+        rows = per_rank_tokens // T
+        self.device_batch = min(cfg.device_batch, rows)
+        if rows % self.device_batch:
+            raise ValueError(f"per-rank rows {rows} not divisible by device_batch {self.device_batch}")
+        self.grad_accum = rows // self.device_batch
+        # flat gradient buffer in the reference's order with per-parameter views
+        sizes = [int(np.prod(s)) for _, s, _ in self.specs]
+        self.offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+        self.flat_grad = torch.zeros(int(self.offsets[-1]), dtype=torch.float32, device=self.device)
+        self.grad_views: "OrderedDict[str, torch.Tensor]" = OrderedDict()
+        for (name, shape, _), a in zip(self.specs, self.offsets[:-1]):
+            self.grad_views[name] = self.flat_grad[a:a + int(np.prod(shape))].view(shape)
+        owned = None
+        if cfg.impl == "cuda":
+            from .models.engine import FusedGPTEngine
+            self.engine = FusedGPTEngine(self.model, self.grad_views, self.device_batch, T)
+            if self.world > 1 and cfg.comm == "p2p":
+                from .parallel.comm import P2PGradSync
+                self.comm = P2PGradSync(self, cfg)
+                owned = self.comm.owned_names
+        else:
+            for name, p in self.model.named().items():
+                p.grad = self.grad_views[name]
+        if self.world > 1 and cfg.comm == "ring":
+            self.comm = RingAllReduce(wire_dtype=cfg.wire_dtype, timeout_s=cfg.comm_timeout_s, log=self.log)
+        fused_comm = cfg.impl == "cuda" and cfg.comm == "p2p" and self.world > 1
+        if cfg.sparsify.enabled and not fused_comm:
+            self.sparsifier = GradientSparsifier(cfg.sparsify.top_k_ratio, cfg.sparsify.warmup_steps,
+                                                 cfg.sparsify.sample_size, cfg.sparsify.momentum_factor,
+                                                 seed=cfg.seed + self.rank)
+        self.optimizer = MuonAdamW(
+            self.model.named(), self.model.param_groups(), model_dim=cfg.model.n_embd,
+            unembedding_lr=cfg.unembedding_lr, embedding_lr=cfg.embedding_lr, matrix_lr=cfg.matrix_lr,
+            scalar_lr=cfg.scalar_lr, weight_decay=cfg.weight_decay, adam_betas=cfg.adam_betas, ns_steps=cfg.ns_steps,
+            beta2=cfg.muon_beta2, ns_dtype=cfg.ns_dtype if self.is_cuda else "fp32", owned=owned,
+            impl="cuda" if cfg.impl == "cuda" else "torch",
+            shadows=self.engine.shadows if self.engine is not None else None)
+        if self.engine is not None:
+            self.engine.attach_optimizer(self.optimizer)
+        # data
+        self.train_source = make_batch_source(cfg, "train", self.rank, self.world)
+        if cfg.data == "tokens" and cfg.token_bytes_path:
+            self.token_bytes = load_token_bytes(cfg.token_bytes_path, cfg.model.vocab_size)
+        else:
+            self.token_bytes = make_token_bytes(cfg.model.vocab_size, cfg.token_bytes_max)
+        if self.is_cuda:
+            self.prefetch = PinnedPrefetcher(self.train_source, self.device_batch, T, self.device)
+
+    # ------------------------------------------------------------------ batches
+    def next_batch(self):
+        if self.prefetch is not None:
+            return self.prefetch.get()
+        x, y = self.train_source.next(self.device_batch, self.cfg.model.sequence_len)
+        return (torch.as_tensor(np.ascontiguousarray(x), device=self.device),
+                torch.as_tensor(np.ascontiguousarray(y), device=self.device))
+
+    # ------------------------------------------------------------------ step
+    def _forward_backward(self, x, y, scale: float):
+        if self.engine is not None:
+            return self.engine.forward_backward(x, y, loss_scale=scale / self.grad_accum,
+                                                accumulate=self._micro > 0)
+        cd = torch.bfloat16 if self.is_cuda and self.cfg.dtype == "bf16" else (
+            torch.float16 if self.is_cuda and self.cfg.dtype == "fp16" else None)
+        loss = self.model.forward_torch(x, y, compute_dtype=cd, exact_ce=not self.is_cuda)
+        (loss * (scale / self.grad_accum)).backward()
+        return loss.detach()
+
+    def train_step(self, batch=None) -> float:
+        """One optimizer step over ``grad_accum`` micro-batches; returns the (host) loss."""
+        cfg = self.cfg
+        t0 = time.perf_counter()
+        progress = min(self.total_training_time / cfg.time_budget, 1.0)
+        if self.engine is None:
+            self.flat_grad.zero_()
+        losses = []
+        scale = self.scaler.scale
+        for self._micro in range(self.grad_accum):
+            x, y = batch if batch is not None else self.next_batch()
+            losses.append(self._forward_backward(x, y, scale))
+        loss_t = torch.stack(losses).float().mean()
+        t_compute = time.perf_counter()
+        ok = self._sync_and_update(progress, scale)
+        loss = float(loss_t)  # device -> host read of the step result
+        if not math.isfinite(loss):
+            self.log(f"non-finite loss at step {self.metrics.step}")
+        self._update_metrics(loss, t0, t_compute, ok)
+        return loss
+
+    def _sync_and_update(self, progress: float, scale: float) -> bool:
+        cfg = self.cfg
+        if self.comm is not None and hasattr(self.comm, "step"):  # in-kernel p2p path
+            ok = self.comm.step(self.metrics.step, scale, self._set_schedules(progress))
+            return ok
+        g = self.flat_grad
+        finite = torch.isfinite(g).all()
+        if scale != 1.0:
+            g.div_(scale)
+        overflow = not bool(finite)
+        if self.scaler.enabled and not overflow:
+            overflow = float(g.abs().max()) * scale > 65000
+        if self.world > 1:
+            flag = torch.tensor([1.0 if overflow else 0.0], device=self.device)
+            if isinstance(self.comm, RingAllReduce):
+                flag = flag.cpu()
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+            overflow = bool(flag.item() > 0)
+        self.scaler.update(overflow)
+        if overflow:
+            self.skipped += 1
+            return False
+        if self.sparsifier is not None:
+            sp = self.sparsifier.sparsify(g)
+            if self.metrics.step % 50 == 0:
+                self.log(f"sparsification: {sp.indices.numel()}/{sp.length} kept "
+                         f"({100 * GradientSparsifier.compression_ratio(sp):.1f}% of dense)")
+        t_ar = time.perf_counter()
+        if self.world > 1:
+            if isinstance(self.comm, RingAllReduce):
+                red = self.comm.all_reduce(g, self.metrics.step)
+                if red is None:
+                    self.log(f"all-reduce aborted at step {self.metrics.step}, skipping optimizer update")
+                    self.skipped += 1
+                    return False
+                g.copy_(red)
+            else:
+                dist.all_reduce(g, op=dist.ReduceOp.AVG if self.is_cuda else dist.ReduceOp.SUM)
+                if not self.is_cuda:
+                    g.div_(self.world)
+        if self.is_cuda:
+            torch.cuda.synchronize(self.device) if cfg.log_every and self.metrics.step % cfg.log_every == 0 else None
+        self.metrics.all_reduce_time_ms = (time.perf_counter() - t_ar) * 1e3
+        self._set_schedules(progress)
+        self.optimizer.step(self.grad_views)
+        return True
+
+    def _set_schedules(self, progress: float):
+        cfg = self.cfg
+        o = self.optimizer
+        o.lr_multiplier = lr_multiplier(progress, cfg.warmup_ratio, cfg.warmdown_ratio, cfg.final_lr_frac)
+        o.muon_momentum = muon_momentum(self.metrics.step)
+        o.muon_weight_decay = weight_decay_at(progress, cfg.weight_decay)
+        return o
+
+    def _update_metrics(self, loss: float, t0: float, t_compute: float, ok: bool):
+        m = self.metrics
+        tokens = self.device_batch * self.grad_accum * self.cfg.model.sequence_len * self.world
+        m.step += 1
+        m.loss = loss
+        m.smooth_loss = loss if m.smooth_loss == 0 else 0.9 * m.smooth_loss + 0.1 * loss
+        m.total_tokens += tokens
+        m.compute_time_ms = (t_compute - t0) * 1e3
+        m.step_time_ms = (time.perf_counter() - t0) * 1e3
+        m.tokens_per_sec = tokens / max(m.step_time_ms / 1e3, 1e-9)
+        m.elapsed_seconds = time.perf_counter() - self.start_time if self.start_time else 0.0
+        m.peers_connected = self.world
+        m.skipped_steps = self.skipped
+        steady = max(1, m.step - self.cfg.warmup_steps_excluded)
+        if self.total_training_time > 0:
+            m.mfu_percent = 100 * self.flops_per_token * tokens * steady / self.total_training_time / (
+                B200_BF16_PEAK_FLOPS * self.world)
+
+    # ------------------------------------------------------------------ eval
+    def per_token_nats(self, x, y):
+        if self.engine is not None:
+            return self.engine.per_token_nats(x, y)
+        cd = torch.bfloat16 if self.is_cuda else None
+        with torch.no_grad():
+            return self.model.forward_torch(x, y, reduction="none", compute_dtype=cd, exact_ce=True)
+
+    def evaluate_bpb(self, batch: int | None = None) -> float:
+        cfg = self.cfg
+        B = batch or self.device_batch
+        val = make_batch_source(cfg, "val", 0, 1)
+        # ranks split the eval batches; sums are reduced over the group
+        tokens = max(cfg.eval_tokens // self.world, B * cfg.model.sequence_len)
+        bpb, nats, nbytes = evaluate_bpb(self.per_token_nats, _Skip(val, self.rank, self.world, B, cfg.model.sequence_len),
+                                         self.token_bytes, B, cfg.model.sequence_len, tokens, self.device)
+        if self.world > 1:
+            t = torch.tensor([nats, nbytes], dtype=torch.float64, device=self.device if self.is_cuda else "cpu")
+            dist.all_reduce(t)
+            nats, nbytes = float(t[0]), float(t[1])
+            bpb = nats / (math.log(2) * nbytes) if nbytes > 0 else 0.0
+        self.metrics.val_bpb = bpb
+        return bpb
+
+    # ------------------------------------------------------------------ loop
+    def start_training(self) -> TrainerMetrics:
+        cfg = self.cfg
+        if self.model is None:
+            self.initialize()
+        self.running = True
+        self.start_time = time.perf_counter()
+        jl = MetricsLog(cfg.metrics_jsonl if self.rank == 0 else "")
+        while self.running and self.metrics.step < cfg.max_steps:
+            if self.metrics.step > cfg.warmup_steps_excluded and self.total_training_time >= cfg.time_budget:
+                self.log("time budget exhausted")
+                break
+            t0 = time.perf_counter()
+            loss = self.train_step()
+            dt = time.perf_counter() - t0
+            if self.metrics.step > cfg.warmup_steps_excluded:
+                self.total_training_time += dt
+            m = self.metrics
+            if cfg.log_every and m.step % cfg.log_every == 0:
+                lrm = lr_multiplier(min(self.total_training_time / cfg.time_budget, 1), cfg.warmup_ratio,
+                                    cfg.warmdown_ratio, cfg.final_lr_frac)
+                self.log(f"Step {m.step} | loss={loss:.6f} | smooth={m.smooth_loss:.6f} | grad={m.grad_norm:.4f} | "
+                         f"lrm={lrm:.2f} | {m.tokens_per_sec:.0f} tok/s | peers={m.peers_connected} | "
+                         f"{m.elapsed_seconds:.0f}s")
+            jl.write({"step": m.step, "loss": loss, "smooth_loss": m.smooth_loss, "tokens_per_sec": m.tokens_per_sec,
+                      "step_ms": m.step_time_ms, "all_reduce_ms": m.all_reduce_time_ms, "mfu": m.mfu_percent})
+            if cfg.checkpoint_interval > 0 and m.step % cfg.checkpoint_interval == 0:
+                self.save_checkpoint()
+        self.log("running final BPB evaluation")
+        self.evaluate_bpb()
+        total = time.perf_counter() - self.start_time
+        peak = torch.cuda.max_memory_allocated(self.device) / 2 ** 20 if self.is_cuda else 0.0
+        if self.rank == 0:
+            print(summary_block(self.metrics, self.total_training_time, total, peak, cfg.model.n_layer), flush=True)
+            if cfg.results_tsv:
+                ResultsLogger(cfg.results_tsv).log(
+                    self.metrics.val_bpb, peak, "keep" if self.metrics.val_bpb > 0 else "crash",
+                    f"step {self.metrics.step} | {self.metrics.num_params_m:.1f}M params | depth={cfg.model.n_layer}")
+        return self.metrics
+
+    def stop(self) -> None:
+        self.running = False
+
+    def destroy(self) -> None:
+        self.stop()
+        if self.prefetch is not None:
+            self.prefetch.close()
+        if self.comm is not None and hasattr(self.comm, "close"):
+            self.comm.close()
+
+    # ------------------------------------------------------------------ checkpoints
+    def checkpoint_state(self):
+        if self.engine is not None:
+            self.engine.sync_params_to_model()
+        return ckpt.build_state(
+            self.model, self.optimizer, step=self.metrics.step, loss_scale=self.scaler.scale,
+            total_tokens=self.metrics.total_tokens,
+            extra_meta={"totalTrainingTime": self.total_training_time, "smoothLoss": self.metrics.smooth_loss,
+                        "trainConfig": self.cfg.to_json()})
+
+    def save_checkpoint(self, path: str | None = None) -> str:
+        tensors, meta = self.checkpoint_state()
+        if self.world > 1:
+            # each rank holds the optimizer state of its own shard; weights are replicated
+            own = set(self.optimizer.state)
+            t_local = OrderedDict((k, v) for k, v in tensors.items()
+                                  if not (k.startswith("adam_") or k.startswith("muon_")) or
+                                  k.split("_", 2)[-1] in own)
+            d = path or os.path.join(self.cfg.checkpoint_dir, f"step{self.metrics.step:06d}")
+            ckpt.save_sharded(d, self.rank, self.world, t_local if self.rank == 0 else
+                              OrderedDict((k, v) for k, v in t_local.items() if k.startswith(("adam_", "muon_"))), meta)
+            dist.barrier()
+            if self.rank == 0:
+                out = d + ".safetensors"
+                ckpt.merge_shards(d, out, order=[n for n, _, _ in self.specs])
+                return out
+            return d
+        path = path or os.path.join(self.cfg.checkpoint_dir, ckpt.checkpoint_filename(self.metrics.step))
+        ckpt.save(path, tensors, meta)
+        self.log(f"checkpoint saved: {path}")
+        return path
+
+    def load_checkpoint(self, path: str) -> dict:
+        if self.model is None:
+            raise RuntimeError("Cannot load checkpoint: model not initialized. Call initialize() first.")
+        tensors, meta = ckpt.load(path)
+        info = ckpt.restore(self.model, tensors, meta, self.optimizer, log=self.log)
+        self.metrics.step = int(info.get("step", 0) or 0)
+        self.scaler.scale = float(info.get("lossScale", 1.0) or 1.0)
+        self.metrics.total_tokens = int(info.get("totalTokens", 0) or 0)
+        self.total_training_time = float(info.get("totalTrainingTime", 0.0) or 0.0)
+        self.metrics.smooth_loss = float(info.get("smoothLoss", 0.0) or 0.0)
+        if self.engine is not None:
+            self.engine.refresh_shadows()
+        self.log(f"resumed from step {self.metrics.step} ({info['restored']} weights)")
+        return info
+
+
+class _Skip:
+    """Round-robin view of a batch source: rank r takes batches r, r+W, r+2W, ..."""
+
+    def __init__(self, src, rank, world, B, T):
+        self.src, self.rank, self.world, self.B, self.T = src, rank, world, B, T
+        self.first = True
+
+    def next(self, B, T):
+        skip = self.rank if self.first else self.world - 1
+        self.first = False
+        for _ in range(skip):
+            self.src.next(B, T)
+        return self.src.next(B, T)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description="bitresearch-b200 data-parallel GPT trainer")
+    ap.add_argument("--preset", default="d512")
+    ap.add_argument("--resume", default="")
+    ap.add_argument("overrides", nargs="*", help="key=value config overrides (e.g. max_steps=100 model.n_layer=4)")
+    args = ap.parse_args(argv)
+    cfg = apply_overrides(preset(args.preset), args.overrides)
+    rank, world, local = init_distributed("nccl" if torch.cuda.is_available() and cfg.impl != "cpu" else "gloo")
+    if not torch.cuda.is_available():
+        cfg.impl = "torch"
+    tr = Trainer(cfg)
+    tr.initialize()
+    if args.resume:
+        tr.load_checkpoint(args.resume)
+    try:
+        tr.start_training()
+    finally:
+        tr.destroy()
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

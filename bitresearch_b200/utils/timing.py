@@ -1,0 +1,120 @@
+"""Device timing helpers: CUDA-event phase timers, NVTX ranges and a clock sampler.
+
+* ``PhaseTimer`` records CUDA events around named phases (forward, backward, reduce-scatter,
+  optimizer, all-gather) on the launching stream and reports milliseconds once synchronised.
+* ``nvtx`` is a no-op context manager when CUDA is absent.
+* ``ClockSampler`` polls ``nvidia-smi`` in a background process during a timed region and
+  summarises the SM clock and the throttle reasons it saw (read-only: it changes no setting).
+"""
+from __future__ import annotations
+
+import contextlib
+import os
+import signal
+import statistics
+import subprocess
+import tempfile
+
+import torch
+
+
+class PhaseTimer:
+    def __init__(self, enabled: bool = True):
+        self.enabled = enabled and torch.cuda.is_available()
+        self.events: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+
+    @contextlib.contextmanager
+    def phase(self, name: str):
+        if not self.enabled:
+            yield
+            return
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        try:
+            yield
+        finally:
+            b.record()
+            self.events.append((name, a, b))
+
+    def collect(self) -> dict[str, float]:
+        out: dict[str, float] = {}
+        for name, a, b in self.events:
+            b.synchronize()
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        self.events.clear()
+        return out
+
+
+@contextlib.contextmanager
+def nvtx(name: str):
+    if torch.cuda.is_available():
+        torch.cuda.nvtx.range_push(name)
+        try:
+            yield
+        finally:
+            torch.cuda.nvtx.range_pop()
+    else:
+        yield
+
+
+_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+class ClockSampler:
+    """Samples ``nvidia-smi`` every ``period_ms`` between ``start()`` and ``stop()``."""
+
+    def __init__(self, gpu_index: int | None = None, period_ms: int = 200):
+        self.gpu_index = gpu_index
+        self.period_ms = period_ms
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        cmd = ["nvidia-smi", f"--query-gpu={_QUERY}", "--format=csv,noheader,nounits", f"-lms={self.period_ms}"]
+        if self.gpu_index is not None:
+            cmd.insert(1, f"--id={self.gpu_index}")
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"), stderr=subprocess.DEVNULL,
+                                         start_new_session=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        try:
+            os.killpg(self.proc.pid, signal.SIGTERM)
+        except Exception:
+            pass
+        self.proc.wait(timeout=10)
+        return summarise_clock_csv(self.path)
+
+
+def summarise_clock_csv(path: str) -> dict:
+    sm, smax, reasons = [], [], set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    with open(path) as f:
+        for line in f:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+    if not sm:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+    # median over samples taken under load (clock above idle)
+    loaded = [s for s in sm if s > 0.3 * max(sm)] or sm
+    return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+            "samples": len(sm)}

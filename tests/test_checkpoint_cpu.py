@@ -1,0 +1,66 @@
+import json
+import struct
+
+import torch
+
+from bitresearch_b200 import checkpoint as ckpt
+from bitresearch_b200.config import GPTConfig
+from bitresearch_b200.models.gpt import GPT
+from bitresearch_b200.optim.muon_adamw import MuonAdamW
+
+
+def _cfg():
+    return GPTConfig(sequence_len=16, vocab_size=64, n_layer=2, n_head=2, n_kv_head=2, n_embd=32, window_pattern="L")
+
+
+def test_roundtrip_weights_optimizer_metadata(tmp_path):
+    m = GPT(_cfg(), seed=1)
+    opt = MuonAdamW(m.named(), m.param_groups(), model_dim=32)
+    opt.step({n: torch.randn_like(p) for n, p in m.named().items()})
+    t, meta = ckpt.build_state(m, opt, step=7, loss_scale=512.0, total_tokens=1234,
+                               extra_meta={"smoothLoss": 3.5})
+    path = ckpt.save(str(tmp_path / ckpt.checkpoint_filename(7)), t, meta)
+    assert "checkpoint_step000007_" in path
+    m2 = GPT(_cfg(), seed=2)
+    opt2 = MuonAdamW(m2.named(), m2.param_groups(), model_dim=32)
+    t2, meta2 = ckpt.load(path)
+    assert all(isinstance(v, str) for v in meta2.values())  # safetensors spec: string metadata
+    info = ckpt.restore(m2, t2, meta2, opt2)
+    assert info["step"] == 7 and info["lossScale"] == 512.0 and info["totalTokens"] == 1234
+    assert info["smoothLoss"] == 3.5 and json.loads(meta2["config"])["nEmbd"] == 32
+    for n, p in m.named().items():
+        assert torch.equal(p, m2.named()[n]), n
+    for k, v in opt.state_tensors().items():
+        assert torch.equal(v, opt2.state_tensors()[k])
+    assert opt2.state_steps() == opt.state_steps()
+
+
+def test_reads_reference_written_file_with_numeric_metadata_and_exporter_alias(tmp_path):
+    # header layout of trainer.ts:1139-1153: numbers in __metadata__ and F32 tensors in order
+    cfg = _cfg()
+    m = GPT(cfg, seed=3)
+    tensors = {n: p.detach().numpy() for n, p in m.named().items()}
+    tensors["layer1_value_embed"] = tensors.pop("ve_1")  # exporter alias
+    header, off, blobs = {}, 0, []
+    for n, a in tensors.items():
+        b = a.astype("<f4").tobytes()
+        header[n] = {"dtype": "F32", "shape": list(a.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    header["__metadata__"] = {"step": 42, "lossScale": 1024, "totalTokens": 99, "config": json.dumps(cfg.to_reference_dict())}
+    hb = json.dumps(header).encode()
+    (tmp_path / "ref.safetensors").write_bytes(struct.pack("<Q", len(hb)) + hb + b"".join(blobs))
+    m2 = GPT(cfg, seed=9)
+    t, meta = ckpt.load(str(tmp_path / "ref.safetensors"))
+    info = ckpt.restore(m2, t, meta)
+    assert info["step"] == 42 and info["restored"] == len(m.named())
+    assert torch.equal(m2.named()["ve_1"], m.named()["ve_1"])
+
+
+def test_safetensors_library_reads_our_files(tmp_path):
+    st = __import__("pytest").importorskip("safetensors.torch")
+    m = GPT(_cfg())
+    t, meta = ckpt.build_state(m, None, step=1)
+    ckpt.save(str(tmp_path / "a.safetensors"), t, meta)
+    loaded = st.load_file(str(tmp_path / "a.safetensors"))
+    assert torch.equal(loaded["wte"], m.named()["wte"])

@@ -1,0 +1,80 @@
+import numpy as np
+import pytest
+
+from bitresearch_b200.config import preset
+from bitresearch_b200.data.loader import BestFitDocumentBatcher, TokenDataLoader
+from bitresearch_b200.data.pipeline import make_batch_source
+from bitresearch_b200.data.synthetic import UniformBOSStream, ZipfDocumentSource, bos_id, make_token_bytes
+
+
+def test_token_loader_wraps_and_targets_shift():
+    tl = TokenDataLoader(np.arange(10, dtype=np.int32))
+    x, y = tl.next_batch(2, 3)
+    assert x.tolist() == [[0, 1, 2], [3, 4, 5]] and y.tolist() == [[1, 2, 3], [4, 5, 6]]
+    x, y = tl.next_batch(2, 3)
+    assert x.tolist() == [[6, 7, 8], [9, 0, 1]] and y.tolist() == [[7, 8, 9], [0, 1, 2]]
+    assert tl.epochs == 1
+    val = TokenDataLoader(np.arange(100, dtype=np.int32)).val_split(0.1)
+    assert val.tolist() == list(range(90, 100))
+    x, y = TokenDataLoader.batch_from_array(np.arange(5, dtype=np.int32), 1, 4, 3)
+    assert x.tolist() == [[3, 4, 0, 1]] and y.tolist() == [[4, 0, 1, 2]]
+
+
+def test_best_fit_packing_reference_semantics():
+    docs = [[1] * 5, [2] * 3, [3] * 9, [4] * 2, [5] * 4]
+    b = BestFitDocumentBatcher(docs, bos_id=0, buffer_size=3)
+    rows = b.pack_rows(2, 7)  # capacity 8
+    # buffer [6,4,10] -> 6 fits (largest <=8) -> rem 2 -> refill [4,10,3] nothing fits -> crop shortest (3 -> [0,4])
+    assert rows[0].tolist() == [0, 1, 1, 1, 1, 1, 0, 4]
+    assert rows[1, 0] == 0  # every row starts at a BOS
+
+
+@pytest.mark.parametrize("buffer_size", [1, 4, 50])
+def test_native_packer_matches_python(buffer_size):
+    nd = pytest.importorskip("bitresearch_b200._native_data")
+    rng = np.random.default_rng(0)
+    docs = [rng.integers(0, 50, size=int(rng.integers(1, 40)), dtype=np.int32) for _ in range(300)]
+    offs = np.zeros(len(docs) + 1, np.int64)
+    np.cumsum([len(d) for d in docs], out=offs[1:])
+    toks = np.concatenate(docs)
+    p = nd.corpus_packer(63, buffer_size, toks, offs, False)
+    py = BestFitDocumentBatcher(docs, bos_id=63, buffer_size=buffer_size)
+    for _ in range(5):
+        rows = np.empty((4, 33), np.int32)
+        ep = nd.pack_rows(p, rows, 4, 32)
+        assert np.array_equal(rows, py.pack_rows(4, 32))
+        assert ep == py.epoch
+
+
+def test_zipf_sources_are_seeded_and_bos_packed():
+    nd = pytest.importorskip("bitresearch_b200._native_data")
+    V = 512
+    a = nd.zipf_packer(V, 1.1, 64.0, 7, 100, 0)
+    b = nd.zipf_packer(V, 1.1, 64.0, 7, 100, 0)
+    ra, rb = np.empty((8, 129), np.int32), np.empty((8, 129), np.int32)
+    nd.pack_rows(a, ra, 8, 128)
+    nd.pack_rows(b, rb, 8, 128)
+    assert np.array_equal(ra, rb)
+    assert (ra[:, 0] == V - 1).all() and ra.max() < V and ra.min() >= 0
+    frac_bos = (ra == V - 1).mean()
+    assert 0.005 < frac_bos < 0.1  # about 1/(mean_len+1) BOS density
+    counts = np.bincount(ra[ra != V - 1].ravel(), minlength=V)
+    assert counts.max() > 20 * np.median(counts[counts > 0])  # heavy head of a Zipf law
+    py = ZipfDocumentSource(V, 1.1, 64, seed=1).documents(2000)
+    assert 50 < np.mean([len(d) for d in py]) < 80
+
+
+def test_uniform_stream_and_token_bytes():
+    s = UniformBOSStream(512, 64, seed=0)
+    t = s.take(256)
+    assert (t[::64] == bos_id(512)).all() and t.max() < 512
+    tb = make_token_bytes(512, 4)
+    assert tb[bos_id(512)] == 0 and tb.min() == 0 and tb.max() == 4 and (tb[:-1] >= 1).all()
+
+
+def test_pipeline_ranks_get_distinct_streams():
+    cfg = preset("tiny-cpu")
+    a = make_batch_source(cfg, "train", 0, 2).next(2, 16)[0]
+    b = make_batch_source(cfg, "train", 1, 2).next(2, 16)[0]
+    v = make_batch_source(cfg, "val", 0, 2).next(2, 16)[0]
+    assert not np.array_equal(a, b) and not np.array_equal(a, v)
