@@ -1,0 +1,190 @@
+"""Training-throughput benchmark: the d512 depth-8 autoresearch GPT, data-parallel, 2^19 tokens/step.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|ddp|reference]
+  (N > 1: torchrun --nproc-per-node N bench.py --gpus N ...; one rank per GPU over NCCL)
+
+Arms:
+  ours       the sm_100a engine (tcgen05 GEMMs, fused kernels, flash attention, fused optimizer)
+  ddp        plain PyTorch DistributedDataParallel + cuBLAS + SDPA of the same model and optimizer
+  reference  the upstream project (a TypeScript/TF.js browser trainer; it has no Python package)
+
+Measurement: W untimed warm-up steps, then K timed full training steps (forward, backward, gradient
+synchronisation, optimizer) bracketed by a barrier and ``torch.cuda.synchronize()`` on both sides,
+timed with CUDA events on the launching stream; the per-step time is the max over ranks. ``value``
+uses device-resident synthetic batches; ``e2e`` repeats the measurement through the public
+``Trainer.train_step()`` API, which packs each batch on the host, copies it from pinned memory and
+reads the loss back every step. SM clocks and throttle reasons are sampled with ``nvidia-smi``
+during the timed region. Every step touches tens of GB of activations (far larger than the 126 MB
+L2), so no explicit L2 flush is done between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "tokens/s (device-timed, max over ranks)"
+MODEL = "autoresearch GPT d512 depth-8 (4x128 heads, vocab 8192, SSSL windows 1024/2048, VE, ReLU^2, QK-norm)"
+REF_UNAVAILABLE = ("the reference (gauravsaini/bitresearch) is a TypeScript/TensorFlow.js browser trainer with no "
+                   "setup.py/pyproject (pip: 'Directory is not installable'); its GPU path is WebGPU and no Node "
+                   "runtime is present")
+
+
+def _rank_world():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def _max_over_ranks(x: float) -> float:
+    if dist.is_initialized():
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    return x
+
+
+def _barrier_sync():
+    torch.cuda.synchronize()
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def _time_steps(step_fn, K: int) -> float:
+    """ms per step on this rank (CUDA events around K steps)."""
+    _barrier_sync()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(K):
+        step_fn()
+    b.record()
+    _barrier_sync()
+    return a.elapsed_time(b) / K
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "ddp", "reference"])
+    ap.add_argument("--preset", default="d512")
+    ap.add_argument("--device-batch", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("overrides", nargs="*")
+    args = ap.parse_args()
+    rank, world, local = _rank_world()
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": REF_UNAVAILABLE}), flush=True)
+        return 0
+
+    from bitresearch_b200.config import apply_overrides, preset
+    from bitresearch_b200.ops._ext import launch_counts, reset_launch_counts
+    from bitresearch_b200.train import Trainer, init_distributed
+    from bitresearch_b200.utils.timing import ClockSampler
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        init_distributed("nccl", timeout_s=300)
+    cfg = apply_overrides(preset(args.preset), list(args.overrides))
+    if args.device_batch:
+        cfg.device_batch = args.device_batch
+    cfg.log_every = 0
+    cfg.results_tsv = ""
+    device = torch.device("cuda", local)
+    T = cfg.model.sequence_len
+    global_tokens = cfg.total_batch_tokens
+    K, W = args.steps, args.warmup
+
+    if args.impl == "ours":
+        cfg.impl = "cuda"
+        if cfg.comm == "p2p" and world > 1:
+            cfg.comm = "nccl"  # in-kernel NVLink path is selected with comm=p2p explicitly
+        tr = Trainer(cfg, device=device, log=lambda m: None)
+        tr.initialize()
+        accum = tr.grad_accum
+        B = tr.device_batch
+        gen = torch.Generator(device="cpu").manual_seed(1234 + rank)
+        batches = [[(torch.randint(0, cfg.model.vocab_size, (B, T), generator=gen, dtype=torch.int32).to(device),
+                     torch.randint(0, cfg.model.vocab_size, (B, T), generator=gen, dtype=torch.int32).to(device))
+                    for _ in range(accum)] for _ in range(2)]
+        it = [0]
+
+        def step():
+            tr.train_step(batches[it[0] % 2], sync=False)
+            it[0] += 1
+
+        def e2e_step():
+            tr.train_step()
+    else:
+        from baseline.ddp_baseline import DDPBaseline
+        cfg.impl = "torch"
+        tr = DDPBaseline(cfg, device)
+        accum, B = tr.grad_accum, tr.device_batch
+        gen = torch.Generator(device="cpu").manual_seed(1234 + rank)
+        batches = [[(torch.randint(0, cfg.model.vocab_size, (B, T), generator=gen).to(device),
+                     torch.randint(0, cfg.model.vocab_size, (B, T), generator=gen).to(device))
+                    for _ in range(accum)] for _ in range(2)]
+        it = [0]
+
+        def step():
+            tr.train_step(batches[it[0] % 2])
+            it[0] += 1
+        host = [[(x.cpu().pin_memory(), y.cpu().pin_memory()) for x, y in bb] for bb in batches]
+
+        def e2e_step():
+            bs = [(x.to(device, non_blocking=True), y.to(device, non_blocking=True)) for x, y in host[it[0] % 2]]
+            float(tr.train_step(bs))
+            it[0] += 1
+
+    for _ in range(W):
+        step()
+    clocks = ClockSampler(gpu_index=None).start()
+    reset_launch_counts()
+    ms = _time_steps(step, K)
+    launches = sum(launch_counts().values())
+    clk = clocks.stop()
+    ms = _max_over_ranks(ms)
+    value = global_tokens / (ms / 1e3)
+
+    e2e = None
+    if not args.no_e2e:
+        for _ in range(1):
+            e2e_step()
+        ms_e2e = _max_over_ranks(_time_steps(e2e_step, K))
+        e2e = {"value": global_tokens / (ms_e2e / 1e3), "unit": "tokens/s", "ms_per_step": ms_e2e,
+               "h2d_bytes_per_step": 2 * 4 * B * T * accum, "d2h_bytes_per_step": 4,
+               "api": "Trainer.train_step()" if args.impl == "ours" else "DDPBaseline.train_step() + loss.item()"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic: seeded random token ids; random-init weights",
+            "config": {"model": MODEL, "global_batch": global_tokens, "global_batch_unit": "tokens",
+                       "seq_len": T, "device_batch": B, "grad_accum": accum, "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (activations tens of GB per step); no flush"},
+            "impl": args.impl, "clocks": clk, "e2e": e2e,
+            "gpu_launches": launches if args.impl == "ours" else 0,
+            "launches_by_kernel": launch_counts() if args.impl == "ours" else {},
+        }
+        print(json.dumps(line), flush=True)
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -59,6 +59,7 @@ class GPT(nn.Module):
         for name, shape, _ in self.specs:
             self.params[name] = nn.Parameter(torch.empty(shape, dtype=torch.float32, device=device))
         self.init_weights(init, seed)
+        self.compute_dtype: torch.dtype | None = None  # matmul operand dtype of the eager path
         cos, sin = _rope(cfg.sequence_len, cfg.head_dim, device)
         self.register_buffer("rope_cos", cos, persistent=False)
         self.register_buffer("rope_sin", sin, persistent=False)
@@ -110,7 +111,8 @@ class GPT(nn.Module):
 
     # ------------------------------------------------------------------ eager forward
     def forward(self, idx, targets=None, reduction: str = "mean", exact_ce: bool = True):
-        return self.forward_torch(idx, targets, reduction=reduction, exact_ce=exact_ce)
+        return self.forward_torch(idx, targets, reduction=reduction, exact_ce=exact_ce,
+                                  compute_dtype=self.compute_dtype)
 
     def forward_torch(self, idx: torch.Tensor, targets: torch.Tensor | None = None, reduction: str = "mean",
                       exact_ce: bool = True, compute_dtype: torch.dtype | None = None):

@@ -144,7 +144,7 @@ class Trainer:
         owned = None
         if cfg.impl == "cuda":
             from .models.engine import FusedGPTEngine
-            self.engine = FusedGPTEngine(self.model, self.grad_views, self.device_batch, T)
+            self.engine = FusedGPTEngine(self.model, self.grad_views, self.device_batch, T, flat_grad=self.flat_grad)
             if self.world > 1 and cfg.comm == "p2p":
                 from .parallel.comm import P2PGradSync
                 self.comm = P2PGradSync(self, cfg)
@@ -196,8 +196,13 @@ class Trainer:
         (loss * (scale / self.grad_accum)).backward()
         return loss.detach()
 
-    def train_step(self, batch=None) -> float:
-        """One optimizer step over ``grad_accum`` micro-batches; returns the (host) loss."""
+    def train_step(self, batch=None, sync: bool = True):
+        """One optimizer step over ``grad_accum`` micro-batches.
+
+        ``batch``: None (draw from the data pipeline), one ``(inputs, targets)`` pair used for every
+        micro-batch, or a list with one pair per micro-batch. Returns the host loss, or the device
+        loss tensor with ``sync=False`` (no device->host read).
+        """
         cfg = self.cfg
         t0 = time.perf_counter()
         progress = min(self.total_training_time / cfg.time_budget, 1.0)
@@ -206,11 +211,19 @@ class Trainer:
         losses = []
         scale = self.scaler.scale
         for self._micro in range(self.grad_accum):
-            x, y = batch if batch is not None else self.next_batch()
+            if batch is None:
+                x, y = self.next_batch()
+            elif isinstance(batch, list):
+                x, y = batch[self._micro]
+            else:
+                x, y = batch
             losses.append(self._forward_backward(x, y, scale))
-        loss_t = torch.stack(losses).float().mean()
+        loss_t = losses[0].float() if len(losses) == 1 else torch.stack(losses).float().mean()
         t_compute = time.perf_counter()
         ok = self._sync_and_update(progress, scale)
+        if not sync:
+            self.metrics.step += 1
+            return loss_t
         loss = float(loss_t)  # device -> host read of the step result
         if not math.isfinite(loss):
             self.log(f"non-finite loss at step {self.metrics.step}")

@@ -1,0 +1,75 @@
+// Python bindings of the sm_100a kernels (module bitresearch_b200._C).
+#include <torch/extension.h>
+
+namespace br {
+int64_t read_status(int64_t device);
+void reset_status(int64_t device);
+void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, const torch::Tensor& b, bool b_mn,
+                 int64_t ldb, int64_t bsb, torch::Tensor& c, int64_t ldc, int64_t bsc, int64_t M, int64_t N,
+                 int64_t K, int64_t batch, int64_t epi, c10::optional<torch::Tensor> aux, int64_t ld_aux,
+                 int64_t bs_aux, double alpha, double beta, int64_t k_splits, int64_t block_n);
+void embed_rms_fwd(const torch::Tensor& idx, const torch::Tensor& wte, torch::Tensor& x0, torch::Tensor& rstd);
+void ladder_rms_fwd(const torch::Tensor& x, const torch::Tensor& x0, const torch::Tensor& lam_r,
+                    const torch::Tensor& lam_0, int64_t layer, torch::Tensor& cur, torch::Tensor& xn,
+                    torch::Tensor& rstd);
+void rms_fwd(const torch::Tensor& x, torch::Tensor& xn, c10::optional<torch::Tensor> rstd);
+void rms_bwd(const torch::Tensor& x, const torch::Tensor& rstd, const torch::Tensor& dy,
+             c10::optional<torch::Tensor> dres, c10::optional<torch::Tensor> dx, c10::optional<torch::Tensor> dxb);
+void ladder_bwd(const torch::Tensor& x, const torch::Tensor& x0, const torch::Tensor& lam_r,
+                const torch::Tensor& lam_0, int64_t layer, const torch::Tensor& rstd, const torch::Tensor& dxn,
+                const torch::Tensor& dres, c10::optional<torch::Tensor> dgate_in, torch::Tensor& dx,
+                torch::Tensor& dx0_acc, torch::Tensor& dlam_r, torch::Tensor& dlam_0, bool first_layer);
+void embed_bwd(const torch::Tensor& idx, const torch::Tensor& wte, const torch::Tensor& rstd, const torch::Tensor& dx0,
+               torch::Tensor& dwte);
+void cast_bf16(const torch::Tensor& x, torch::Tensor& y);
+void rope_fwd(torch::Tensor& qkv, int64_t T, int64_t H, int64_t KV, int64_t hd, const torch::Tensor& cosT,
+              const torch::Tensor& sinT, torch::Tensor& rq, torch::Tensor& rk, const torch::Tensor& idx,
+              c10::optional<torch::Tensor> ve, c10::optional<torch::Tensor> cur, c10::optional<torch::Tensor> wg,
+              c10::optional<torch::Tensor> gate);
+void rope_bwd(torch::Tensor& dqkv, const torch::Tensor& qkv, int64_t T, int64_t H, int64_t KV, int64_t hd,
+              const torch::Tensor& cosT, const torch::Tensor& sinT, const torch::Tensor& rq, const torch::Tensor& rk,
+              const torch::Tensor& idx, c10::optional<torch::Tensor> ve, c10::optional<torch::Tensor> gate,
+              c10::optional<torch::Tensor> dve, c10::optional<torch::Tensor> dz);
+void ve_gate_bwd(const torch::Tensor& cur, const torch::Tensor& dz, const torch::Tensor& wg, torch::Tensor& dwg,
+                 torch::Tensor& dgate_in);
+void softcap_ce(torch::Tensor& logits, const torch::Tensor& targets, double cap, double scale,
+                c10::optional<torch::Tensor> nats, c10::optional<torch::Tensor> loss_sum, bool grad);
+void adamw_multi(const std::vector<torch::Tensor>& params, const std::vector<torch::Tensor>& grads,
+                 const std::vector<torch::Tensor>& ms, const std::vector<torch::Tensor>& vs,
+                 const std::vector<torch::Tensor>& shadows, const std::vector<double>& hyper);
+void muon_prepare(const std::vector<torch::Tensor>& grads, const std::vector<torch::Tensor>& moms, double mu,
+                  torch::Tensor& X, torch::Tensor& ss);
+void muon_finish(const torch::Tensor& X, const std::vector<torch::Tensor>& grads,
+                 const std::vector<torch::Tensor>& params, const std::vector<torch::Tensor>& secs,
+                 const std::vector<torch::Tensor>& shadows, int64_t r, int64_t c, double beta2, double lr, double wd,
+                 torch::Tensor& work);
+void attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
+              torch::Tensor& lse, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd, int64_t window);
+void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& o,
+              const torch::Tensor& dout, const torch::Tensor& lse, torch::Tensor& dq, torch::Tensor& dk,
+              torch::Tensor& dv, torch::Tensor& delta, torch::Tensor& dq_acc, int64_t B, int64_t T, int64_t H,
+              int64_t KV, int64_t hd, int64_t window);
+}  // namespace br
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "bitresearch-b200 sm_100a kernels";
+  m.def("read_status", &br::read_status);
+  m.def("reset_status", &br::reset_status);
+  m.def("gemm", &br::gemm_launch);
+  m.def("embed_rms_fwd", &br::embed_rms_fwd);
+  m.def("ladder_rms_fwd", &br::ladder_rms_fwd);
+  m.def("rms_fwd", &br::rms_fwd);
+  m.def("rms_bwd", &br::rms_bwd);
+  m.def("ladder_bwd", &br::ladder_bwd);
+  m.def("embed_bwd", &br::embed_bwd);
+  m.def("cast_bf16", &br::cast_bf16);
+  m.def("rope_fwd", &br::rope_fwd);
+  m.def("rope_bwd", &br::rope_bwd);
+  m.def("ve_gate_bwd", &br::ve_gate_bwd);
+  m.def("softcap_ce", &br::softcap_ce);
+  m.def("adamw_multi", &br::adamw_multi);
+  m.def("muon_prepare", &br::muon_prepare);
+  m.def("muon_finish", &br::muon_finish);
+  m.def("attn_fwd", &br::attn_fwd);
+  m.def("attn_bwd", &br::attn_bwd);
+}

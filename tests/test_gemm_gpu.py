@@ -1,0 +1,83 @@
+"""tcgen05 GEMM vs an fp32 PyTorch matmul of the same bf16 operands."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from bitresearch_b200.ops import gemm
+    from bitresearch_b200.ops._ext import check_status
+    return gemm, check_status
+
+
+def _close(out, ref, K):
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err <= 2e-2 * scale, (err, scale)
+
+
+def _rand(*shape, dev):
+    return (torch.randn(*shape, device=dev) * 0.5).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 512), (300, 520, 200), (1000, 1536, 512), (64, 128, 96)])
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm_majors_and_tails(cuda, M, N, K, a_t, b_t):
+    gemm, check_status = _ops()
+    torch.manual_seed(0)
+    a = _rand(K, M, dev=cuda).t() if a_t else _rand(M, K, dev=cuda)       # logical [M, K]
+    b = _rand(N, K, dev=cuda).t() if b_t else _rand(K, N, dev=cuda)       # logical [K, N]
+    if (a_t and M % 8) or (b_t and K % 8) or (not b_t and N % 8) or (not a_t and K % 8):
+        pytest.skip("TMA row strides must be multiples of 16 bytes")
+    out = gemm.matmul(a, b)
+    torch.cuda.synchronize()
+    assert check_status() == 0
+    _close(out, a.float() @ b.float(), K)
+
+
+def test_gemm_epilogues(cuda):
+    gemm, check_status = _ops()
+    torch.manual_seed(1)
+    M, N, K = 384, 512, 256
+    a, b = _rand(M, K, dev=cuda), _rand(K, N, dev=cuda)
+    ref = a.float() @ b.float()
+    aux = _rand(M, N, dev=cuda)
+    _close(gemm.matmul(a, b, epi=gemm.BF16, aux=aux, alpha=0.5, beta=2.0), 0.5 * ref + 2 * aux.float(), K)
+    r = torch.randn(M, N, device=cuda)
+    out = r.clone()
+    gemm.matmul(a, b, out=out, epi=gemm.F32, aux=out, beta=1.0)
+    _close(out, ref + r, K)
+    _close(gemm.matmul(a, b, epi=gemm.RELU2), torch.relu(ref) ** 2, K)
+    h = (torch.relu(torch.randn(M, N, device=cuda)) ** 2).to(torch.bfloat16)
+    _close(gemm.matmul(a, b, epi=gemm.RELU2_BWD, aux=h), ref * 2 * h.float().sqrt(), K)
+    _close(gemm.matmul(a, b, epi=gemm.SOFTCAP, alpha=1 / 15, beta=15.0), 15 * torch.tanh(ref / 15), K)
+    torch.cuda.synchronize()
+    assert check_status() == 0
+
+
+@pytest.mark.parametrize("splits", [1, 4, 0])
+def test_gemm_split_k_weight_grad(cuda, splits):
+    gemm, check_status = _ops()
+    torch.manual_seed(2)
+    T, Din, Dout = 8192, 512, 1536
+    x, dy = _rand(T, Din, dev=cuda), _rand(T, Dout, dev=cuda)
+    acc = torch.randn(Din, Dout, device=cuda)
+    ref = acc + x.float().t() @ dy.float()
+    gemm.matmul(x.t(), dy, out=acc, epi=gemm.ATOMIC, k_splits=splits)
+    torch.cuda.synchronize()
+    assert check_status() == 0
+    _close(acc, ref, T)
+
+
+def test_gemm_batched(cuda):
+    gemm, check_status = _ops()
+    torch.manual_seed(3)
+    S, r, c = 6, 512, 256
+    X = _rand(S, r, c, dev=cuda)
+    A = gemm.matmul(X.mT, X)  # X^T X per matrix (MN-major A and B)
+    _close(A, X.float().mT @ X.float(), r)
+    Bm = gemm.matmul(A, A, epi=gemm.BF16, aux=A, alpha=0.5, beta=-1.0)
+    _close(Bm, 0.5 * (A.float() @ A.float()) - A.float(), c)
+    torch.cuda.synchronize()
+    assert check_status() == 0
