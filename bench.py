@@ -153,7 +153,8 @@ def main():
     clocks = ClockSampler(gpu_index=None).start()
     reset_launch_counts()
     ms = _time_steps(step, K)
-    launches = sum(launch_counts().values())
+    by_kernel = launch_counts()
+    launches = sum(by_kernel.values())
     clk = clocks.stop()
     ms = _max_over_ranks(ms)
     value = global_tokens / (ms / 1e3)
@@ -177,7 +178,7 @@ def main():
                        "l2": "inputs larger than L2 (activations tens of GB per step); no flush"},
             "impl": args.impl, "clocks": clk, "e2e": e2e,
             "gpu_launches": launches if args.impl == "ours" else 0,
-            "launches_by_kernel": launch_counts() if args.impl == "ours" else {},
+            "launches_by_kernel": by_kernel if args.impl == "ours" else {},
         }
         print(json.dumps(line), flush=True)
     if dist.is_initialized():

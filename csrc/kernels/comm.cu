@@ -1,0 +1,296 @@
+// In-kernel data-parallel collectives over NVLink / NVSwitch peer memory.
+//
+// Symmetric buffers: each rank cudaMallocs a region, exports a CUDA IPC handle, and opens its peers'
+// handles (peer access is enabled lazily by the driver); kernels then read peers' memory with plain
+// loads. No multicast, no TMA on peer memory.
+//
+// Step protocol (epoch = training step, monotonic):
+//   pack      local fp32 gradients of a bucket -> this rank's symmetric send buffer in the wire
+//             dtype (fp32 / bf16 / fp16), fused with a non-finite check;
+//   signal    flags[slot] = epoch with a system-scope release store (separate 1-thread launch after
+//             the pack kernel on the same stream, so all of the bucket is written first);
+//   reduce    for every element of the segments this rank owns inside the bucket: wait (acquire,
+//             bounded) until every peer's flags[slot] >= epoch, then out = scale * sum_p send_p;
+//   gather    after the owners' optimizer steps, each rank pulls the parameters it does not own from
+//             the owners' symmetric parameter buffers (again after an acquire on the owner's flag),
+//             writing the fp32 master and, for GEMM weights, the bf16 shadow.
+// A wait that exceeds its budget records kErrTimeoutPeer in the device status word and the block
+// skips its work; the host treats the step as aborted (the reference's abort-and-skip), so nothing
+// spins forever and nothing traps.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "status.h"
+
+namespace br {
+namespace {
+
+enum Wire : int { W_F32 = 0, W_BF16 = 1, W_F16 = 2 };
+
+__device__ __forceinline__ int64_t ld_acquire_sys(const int64_t* p) {
+  int64_t v;
+  asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(int64_t* p, int64_t v) {
+  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Waits (thread 0 of the block) until flags_p[slot] >= epoch for every peer; returns false on timeout.
+__device__ bool wait_peers(const int64_t* const* flags, int npeers, int slot, int64_t epoch, uint64_t budget_ns,
+                           int* status) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (int p = 0; p < npeers && ok; ++p) {
+      const int64_t* f = flags[p] + slot;
+      uint32_t it = 0;
+      while (ld_acquire_sys(f) < epoch) {
+        if ((++it & 63u) == 0 && globaltimer_ns() - t0 > budget_ns) {
+          ok = 0;
+          if (status) atomicCAS(status, 0, kErrTimeoutPeer);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+struct Chunk {
+  int64_t off;
+  int64_t len;
+};
+
+template <int WIRE>
+__device__ __forceinline__ void load8(const void* base, int64_t i, float (&v)[8]) {
+  if constexpr (WIRE == W_F32) {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if constexpr (WIRE == W_BF16) {
+        const float2 f = unpack_bf16(w[k]);
+        v[2 * k] = f.x;
+        v[2 * k + 1] = f.y;
+      } else {
+        const __half2 h = *reinterpret_cast<const __half2*>(&w[k]);
+        const float2 f = __half22float2(h);
+        v[2 * k] = f.x;
+        v[2 * k + 1] = f.y;
+      }
+    }
+  }
+}
+
+template <int WIRE>
+__device__ __forceinline__ float load1(const void* base, int64_t i) {
+  if constexpr (WIRE == W_F32) return reinterpret_cast<const float*>(base)[i];
+  if constexpr (WIRE == W_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[i]);
+  return __half2float(reinterpret_cast<const __half*>(base)[i]);
+}
+
+template <int WIRE>
+__device__ __forceinline__ void store_wire(void* base, int64_t i, float x) {
+  if constexpr (WIRE == W_F32) reinterpret_cast<float*>(base)[i] = x;
+  else if constexpr (WIRE == W_BF16) reinterpret_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16(x);
+  else reinterpret_cast<__half*>(base)[i] = __float2half(x);
+}
+
+// grid-stride over [lo, hi): send[i] = wire(src[i] * scale); *bad |= any non-finite
+template <int WIRE>
+__global__ void pack_kernel(const float* __restrict__ src, void* __restrict__ send, int64_t lo, int64_t hi, float scale,
+                            int* __restrict__ bad) {
+  int nonfinite = 0;
+  for (int64_t i = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < hi; i += (int64_t)gridDim.x * blockDim.x) {
+    const float x = src[i] * scale;
+    nonfinite |= !isfinite(x);
+    store_wire<WIRE>(send, i, x);
+  }
+  if (__syncthreads_or(nonfinite) && threadIdx.x == 0) atomicOr(bad, 1);
+}
+
+__global__ void signal_kernel(int64_t* flag, int64_t value) {
+  __threadfence_system();
+  st_release_sys(flag, value);
+}
+
+// One block per chunk (grid-stride over chunks). out[i] = scale * sum_p send_p[i].
+template <int WIRE>
+__global__ void __launch_bounds__(256) reduce_kernel(const void* const* __restrict__ peers, const int64_t* const* flags,
+                                                     int npeers, int slot, int64_t epoch, const Chunk* __restrict__ chunks,
+                                                     int nchunks, float* __restrict__ out, float scale,
+                                                     uint64_t budget_ns, int* status) {
+  if (!wait_peers(flags, npeers, slot, epoch, budget_ns, status)) return;
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    const Chunk ch = chunks[c];
+    const int64_t n8 = ch.len & ~int64_t(7);
+    for (int64_t j = threadIdx.x * 8; j < n8; j += blockDim.x * 8) {
+      const int64_t i = ch.off + j;
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int p = 0; p < npeers; ++p) {
+        float v[8];
+        load8<WIRE>(peers[p], i, v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] += v[k];
+      }
+      float4* o = reinterpret_cast<float4*>(out + i);
+      o[0] = make_float4(acc[0] * scale, acc[1] * scale, acc[2] * scale, acc[3] * scale);
+      o[1] = make_float4(acc[4] * scale, acc[5] * scale, acc[6] * scale, acc[7] * scale);
+    }
+    for (int64_t j = n8 + threadIdx.x; j < ch.len; j += blockDim.x) {
+      float acc = 0.f;
+      for (int p = 0; p < npeers; ++p) acc += load1<WIRE>(peers[p], ch.off + j);
+      out[ch.off + j] = acc * scale;
+    }
+  }
+}
+
+struct GatherSeg {
+  int64_t off;        // element offset in the flat parameter buffer
+  int64_t len;
+  int64_t owner;
+  int64_t cols;       // shadow row length (elements); 0 when no shadow
+  int64_t shadow_ld;
+  int64_t shadow;     // bf16 shadow base pointer of the parameter, 0 if none
+  int64_t start;      // element offset of this chunk inside its parameter (for shadow row/col)
+};
+
+__global__ void __launch_bounds__(256) gather_kernel(const float* const* __restrict__ peers, const int64_t* const* flags,
+                                                     int npeers, int slot, int64_t epoch,
+                                                     const GatherSeg* __restrict__ segs, int nsegs,
+                                                     float* __restrict__ local, uint64_t budget_ns, int* status) {
+  if (!wait_peers(flags, npeers, slot, epoch, budget_ns, status)) return;
+  for (int s = blockIdx.x; s < nsegs; s += gridDim.x) {
+    const GatherSeg g = segs[s];
+    const float* src = peers[g.owner];
+    for (int64_t j = threadIdx.x; j < g.len; j += blockDim.x) {
+      const float x = src[g.off + j];
+      local[g.off + j] = x;
+      if (g.shadow) {
+        const int64_t e = g.start + j;
+        reinterpret_cast<__nv_bfloat16*>(g.shadow)[(e / g.cols) * g.shadow_ld + (e % g.cols)] = __float2bfloat16(x);
+      }
+    }
+  }
+}
+
+int sm_count() {
+  int dev, n;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------- symmetric memory
+// Allocates `bytes` of device memory (zeroed) and returns (pointer, 64-byte IPC handle).
+std::tuple<int64_t, torch::Tensor> sym_alloc(int64_t bytes) {
+  void* p = nullptr;
+  C10_CUDA_CHECK(cudaMalloc(&p, (size_t)bytes));
+  C10_CUDA_CHECK(cudaMemset(p, 0, (size_t)bytes));
+  cudaIpcMemHandle_t h;
+  C10_CUDA_CHECK(cudaIpcGetMemHandle(&h, p));
+  auto t = torch::empty({(int64_t)sizeof(h)}, torch::dtype(torch::kUInt8));
+  std::memcpy(t.data_ptr(), &h, sizeof(h));
+  return {reinterpret_cast<int64_t>(p), t};
+}
+
+int64_t sym_open(const torch::Tensor& handle) {
+  TORCH_CHECK(handle.numel() == (int64_t)sizeof(cudaIpcMemHandle_t), "bad IPC handle");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.data_ptr(), sizeof(h));
+  void* p = nullptr;
+  C10_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void sym_close(int64_t ptr) { C10_CUDA_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr))); }
+void sym_free(int64_t ptr) { C10_CUDA_CHECK(cudaFree(reinterpret_cast<void*>(ptr))); }
+
+// Wraps raw device memory as a tensor view (no ownership).
+torch::Tensor sym_view(int64_t ptr, int64_t numel, int64_t dtype_code, int64_t device) {
+  const at::ScalarType st = dtype_code == 0 ? at::kFloat : dtype_code == 1 ? at::kBFloat16 : dtype_code == 2 ? at::kHalf
+                                                                                                         : at::kLong;
+  return torch::from_blob(reinterpret_cast<void*>(ptr), {numel},
+                          torch::TensorOptions().dtype(st).device(torch::kCUDA, (c10::DeviceIndex)device));
+}
+
+// ------------------------------------------------------------------------------------- kernels
+void comm_pack(const torch::Tensor& src, int64_t send_ptr, int64_t wire, int64_t lo, int64_t hi, double scale,
+               torch::Tensor& bad) {
+  c10::cuda::CUDAGuard g(src.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int64_t n = hi - lo;
+  if (n <= 0) return;
+  const int grid = (int)std::min<int64_t>((n + 1023) / 1024, 2 * sm_count());
+  void* send = reinterpret_cast<void*>(send_ptr);
+  if (wire == W_F32)
+    pack_kernel<W_F32><<<grid, 256, 0, st>>>(src.data_ptr<float>(), send, lo, hi, (float)scale, bad.data_ptr<int>());
+  else if (wire == W_BF16)
+    pack_kernel<W_BF16><<<grid, 256, 0, st>>>(src.data_ptr<float>(), send, lo, hi, (float)scale, bad.data_ptr<int>());
+  else
+    pack_kernel<W_F16><<<grid, 256, 0, st>>>(src.data_ptr<float>(), send, lo, hi, (float)scale, bad.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void comm_signal(int64_t flag_ptr, int64_t value) {
+  signal_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<int64_t*>(flag_ptr), value);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// peers: int64 device tensor [N] of send-buffer pointers; flags: int64 device tensor [N] of flag-array pointers;
+// chunks: int64 device tensor [nchunks, 2] (offset, length) in elements (offsets multiples of 8).
+void comm_reduce(const torch::Tensor& peers, const torch::Tensor& flags, int64_t slot, int64_t epoch,
+                 const torch::Tensor& chunks, torch::Tensor& out, int64_t wire, double scale, int64_t max_blocks,
+                 double budget_s) {
+  c10::cuda::CUDAGuard g(out.device());
+  const int nch = (int)chunks.size(0);
+  if (nch == 0) return;
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int grid = (int)std::min<int64_t>(nch, max_blocks > 0 ? max_blocks : sm_count());
+  const uint64_t budget = (uint64_t)(budget_s * 1e9);
+  int* status = status_ptr(out.device().index());
+  auto P = reinterpret_cast<const void* const*>(peers.data_ptr<int64_t>());
+  auto F = reinterpret_cast<const int64_t* const*>(flags.data_ptr<int64_t>());
+  auto C = reinterpret_cast<const Chunk*>(chunks.data_ptr<int64_t>());
+  const int np = (int)peers.numel();
+  if (wire == W_F32)
+    reduce_kernel<W_F32><<<grid, 256, 0, st>>>(P, F, np, (int)slot, epoch, C, nch, out.data_ptr<float>(), (float)scale, budget, status);
+  else if (wire == W_BF16)
+    reduce_kernel<W_BF16><<<grid, 256, 0, st>>>(P, F, np, (int)slot, epoch, C, nch, out.data_ptr<float>(), (float)scale, budget, status);
+  else
+    reduce_kernel<W_F16><<<grid, 256, 0, st>>>(P, F, np, (int)slot, epoch, C, nch, out.data_ptr<float>(), (float)scale, budget, status);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// segs: int64 device tensor [nsegs, 7] = (off, len, owner, cols, shadow_ld, shadow_ptr, start)
+void comm_gather(const torch::Tensor& peers, const torch::Tensor& flags, int64_t slot, int64_t epoch,
+                 const torch::Tensor& segs, torch::Tensor& local, int64_t max_blocks, double budget_s) {
+  static_assert(sizeof(GatherSeg) == 7 * 8, "GatherSeg layout");
+  c10::cuda::CUDAGuard g(local.device());
+  const int ns = (int)segs.size(0);
+  if (ns == 0) return;
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int grid = (int)std::min<int64_t>(ns, max_blocks > 0 ? max_blocks : sm_count());
+  gather_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const float* const*>(peers.data_ptr<int64_t>()),
+                                      reinterpret_cast<const int64_t* const*>(flags.data_ptr<int64_t>()),
+                                      (int)peers.numel(), (int)slot, epoch,
+                                      reinterpret_cast<const GatherSeg*>(segs.data_ptr<int64_t>()), ns,
+                                      local.data_ptr<float>(), (uint64_t)(budget_s * 1e9),
+                                      status_ptr(local.device().index()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace br

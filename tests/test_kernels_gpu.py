@@ -216,27 +216,36 @@ def test_attention_fwd_bwd(cuda, B, T, H, KV, window):
 
 
 def test_adamw_and_muon_kernels_match_torch_optimizer(cuda):
+    """The fused step (bf16 Newton-Schulz on tcgen05) must be as close to an fp32 Newton-Schulz step as
+    the eager bf16 step is; AdamW parameters must match the eager step to fp32 rounding."""
     from bitresearch_b200.config import GPTConfig
     from bitresearch_b200.models.gpt import GPT
     from bitresearch_b200.optim.muon_adamw import MuonAdamW
     torch.manual_seed(4)
     cfg = GPTConfig(sequence_len=64, vocab_size=512, n_layer=2, n_head=2, n_kv_head=2, n_embd=256)
-    m1 = GPT(cfg, device=cuda)
-    m2 = GPT(cfg, device=cuda)
-    m2.load_state_dict(m1.state_dict())
-    o1 = MuonAdamW(m1.named(), m1.param_groups(), model_dim=256, ns_dtype="bf16", impl="torch")
-    shadows = {n: torch.empty_like(p, dtype=torch.bfloat16) for n, p in m2.named().items() if p.dim() == 2}
-    o2 = MuonAdamW(m2.named(), m2.param_groups(), model_dim=256, ns_dtype="bf16", impl="cuda", shadows=shadows)
-    for o in (o1, o2):
+    models = [GPT(cfg, device=cuda) for _ in range(3)]
+    for m in models[1:]:
+        m.load_state_dict(models[0].state_dict())
+    ref32 = MuonAdamW(models[0].named(), models[0].param_groups(), model_dim=256, ns_dtype="fp32", impl="torch")
+    eager = MuonAdamW(models[1].named(), models[1].param_groups(), model_dim=256, ns_dtype="bf16", impl="torch")
+    shadows = {n: torch.empty_like(p, dtype=torch.bfloat16) for n, p in models[2].named().items() if p.dim() == 2}
+    fused = MuonAdamW(models[2].named(), models[2].param_groups(), model_dim=256, ns_dtype="bf16", impl="cuda",
+                      shadows=shadows)
+    init = {n: p.detach().clone() for n, p in models[0].named().items()}
+    for o in (ref32, eager, fused):
         o.lr_multiplier, o.muon_momentum, o.muon_weight_decay = 0.9, 0.9, 0.1
     for _ in range(3):
-        grads = {n: torch.randn_like(p) * 0.01 for n, p in m1.named().items()}
-        o1.step(grads)
-        o2.step(grads)
-    for n, p in m1.named().items():
-        q = m2.named()[n]
-        delta = (p - q).abs().max().item()
-        moved = (p - GPT(cfg, device=cuda).named()[n]).abs().max().item() + 1e-8
-        assert delta <= 0.05 * moved, (n, delta, moved)
+        grads = {n: torch.randn_like(p) * 0.01 for n, p in models[0].named().items()}
+        for o in (ref32, eager, fused):
+            o.step(grads)
+    for n, p32 in models[0].named().items():
+        pe, pf = models[1].named()[n], models[2].named()[n]
+        moved = (p32 - init[n]).abs().max().item() + 1e-8
+        err_eager = (pe - p32).abs().max().item()
+        err_fused = (pf - p32).abs().max().item()
+        if p32.dim() == 2 and n.startswith("layer") and not n.endswith("ve_gate"):
+            assert err_fused <= 1.5 * err_eager + 0.02 * moved, (n, err_fused, err_eager, moved)
+        else:
+            assert err_fused <= 1e-4 * moved + 1e-6, (n, err_fused, moved)
     for n, s in shadows.items():
-        _assert(s, m2.named()[n], 1e-2)
+        _assert(s, models[2].named()[n], 1e-2)
