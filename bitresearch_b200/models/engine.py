@@ -53,6 +53,13 @@ class FusedGPTEngine:
         self.refresh_shadows()
         self.bufs: dict[int, dict] = {}
         self.optimizer = None
+        # bucket_hook(b, grad_scale) is called on the compute stream when bucket b's gradients are
+        # final (b = 0: lm_head, 1..L: layers L-1..0, L+1: embeddings and scalars)
+        self.bucket_hook = None
+        # tcgen05 attention needs whole 128-row tiles; other lengths use the register-tiled kernels
+        self.tc_attention = seq % 128 == 0
+        self._hook_on = False
+        self._grad_scale = 1.0
 
     # ------------------------------------------------------------------ weights
     def _alloc_shadows(self):
@@ -138,8 +145,11 @@ class FusedGPTEngine:
             else:
                 E.rope_fwd(qkv, T, H, KV, hd, self.cos, self.sin, b["rq"][i], b["rk"][i], idx, None, None, None, None)
             o = b["o"][i]
-            E.attn_fwd(qkv[:, :Dq], qkv[:, Dq:Dq + Dkv], qkv[:, Dq + Dkv:], o, b["lse"][i], B, T, H, KV, hd,
-                       self.windows[i])
+            if self.tc_attention:
+                E.attn_fwd_tc(qkv, o, b["lse"][i], B, T, H, KV, hd, self.windows[i])
+            else:
+                E.attn_fwd(qkv[:, :Dq], qkv[:, Dq:Dq + Dkv], qkv[:, Dq + Dkv:], o, b["lse"][i], B, T, H, KV, hd,
+                           self.windows[i])
             mid = b["mid"][i]
             gemm.matmul(o, self.shadows[f"layer{i}_proj"], out=mid, epi=gemm.F32, aux=cur, beta=1.0)
             E.rms_fwd(mid, b["xn2"][i], b["rstd2"][i])
@@ -160,6 +170,7 @@ class FusedGPTEngine:
         # head: dlmHead += dz^T xf ; dxf = dz @ lmHead
         gemm.matmul(b["logits"].t(), b["xf"], out=G["lmHead"], epi=A, k_splits=0)
         gemm.matmul(b["logits"], self.shadows["lmHead"], out=b["dxn"])
+        self._ready(0)
         E.rms_bwd(b["xs"][-1], b["rstdf"], b["dxn"], None, b["dx"], b["dx_b"])
         b["dx0"].zero_()
         for i in reversed(range(self.L)):
@@ -193,15 +204,26 @@ class FusedGPTEngine:
             x_in = b["xs"][i - 1] if i > 0 else b["x0"]
             E.ladder_bwd(x_in, b["x0"], P["residLambdas"], P["x0Lambdas"], i, b["rstd1"][i], b["dxn"], b["dmid"],
                          b["dgate_in"] if ve else None, b["dx"], b["dx0"], G["residLambdas"], G["x0Lambdas"], i == 0)
+            self._ready(self.L - i)
             if i > 0:
                 E.cast_bf16(b["dx"], b["dx_b"])
         E.embed_bwd(idx, P["wte"], b["rstd0"], b["dx0"], G["wte"])
+        self._ready(self.L + 1)
+
+    def _ready(self, bucket: int):
+        if self._hook_on:
+            self.bucket_hook(bucket, self._grad_scale)
 
     # ------------------------------------------------------------------ API
     def forward_backward(self, idx: torch.Tensor, targets: torch.Tensor, loss_scale: float = 1.0,
-                         accumulate: bool = False) -> torch.Tensor:
-        """Accumulates gradients of ``loss_scale * mean CE`` into the flat buffer; returns the mean CE."""
+                         accumulate: bool = False, last_micro: bool = True, grad_scale: float = 1.0) -> torch.Tensor:
+        """Accumulates gradients of ``loss_scale * mean CE`` into the flat buffer; returns the mean CE.
+
+        On the last micro-batch of a step the bucket hook fires as each bucket's gradients become
+        final (``grad_scale`` is the loss scale to divide out when packing them)."""
         B = idx.shape[0]
+        self._hook_on = last_micro and self.bucket_hook is not None
+        self._grad_scale = grad_scale
         assert idx.shape[1] == self.T
         b = self._buffers(B)
         if not accumulate:

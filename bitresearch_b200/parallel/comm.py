@@ -1,0 +1,248 @@
+"""Data-parallel gradient synchronisation with in-kernel NVLink collectives (one process per GPU).
+
+Replaces the reference's WebRTC ring all-reduce (src/distributed/ring-allreduce.ts:85-215) on an
+NVSwitch node with a direct algorithm:
+
+* **Layout.** The trainer's flat fp32 gradient buffer is ordered by backward completion (lm_head,
+  then layers L-1 .. 0, then embeddings/scalars), so each *bucket* (one layer's parameters) is one
+  contiguous range. Parameters live in a symmetric (CUDA-IPC exported) fp32 buffer with the same
+  offsets; gradients are packed into a symmetric send buffer in the wire dtype.
+* **Ownership (sharded optimizer).** Every parameter tensor has one owner rank (greedy balance by
+  size, Newton-Schulz work counted for matrices). Only the owner keeps optimizer state and updates it.
+* **Per bucket, overlapped with backward** (comm stream, after an event recorded when the engine
+  finishes the bucket): ``pack`` (fp32 -> wire dtype, 1/loss-scale, non-finite check) ->
+  ``signal`` (flags[bucket] = step, release) -> ``reduce`` (every owner reads its owned elements from
+  all peers' send buffers, sums in fp32, scales by 1/N). The 1/N scale is the mean, fixing the
+  reference's ring, which returns the sum (ring-allreduce.ts:161-165).
+* **After backward:** the sharded MuonAdamW step on owned parameters, ``signal`` (flags[params]),
+  then ``gather``: each rank pulls the parameters it does not own from their owners, refreshing the
+  bf16 GEMM shadows in the same pass.
+* **Failure handling:** every device-side wait is bounded (``comm_timeout_s``); a timeout sets the
+  device status word, the host sees it and reports the step as aborted (the reference's
+  ``allReduce() -> null``). Non-finite gradients on any rank skip the update on all ranks.
+"""
+from __future__ import annotations
+
+import math
+from collections import OrderedDict
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from ..ops._ext import check_status, ext
+
+WIRE_CODE = {"fp32": 0, "f32": 0, "bf16": 1, "fp16": 2, "f16": 2}
+WIRE_BYTES = {0: 4, 1: 2, 2: 2}
+ALIGN = 16  # elements; keeps every parameter 64-byte aligned in the flat buffers
+CHUNK = 1 << 16
+
+
+def bucket_order(specs, n_layer: int) -> list[list[str]]:
+    """Parameter names grouped by the point in backward where their gradients are final."""
+    names = [n for n, _, _ in specs]
+    buckets = [["lmHead"]]
+    for i in reversed(range(n_layer)):
+        b = [n for n in names if n.startswith(f"layer{i}_")]
+        if f"ve_{i}" in names:
+            b.append(f"ve_{i}")
+        buckets.append(b)
+    buckets.append(["wte", "residLambdas", "x0Lambdas"])
+    return buckets
+
+
+def flat_layout(specs, n_layer: int):
+    """(OrderedDict name -> (offset, numel, shape), bucket ranges [(lo, hi)], bucket names, total)."""
+    shapes = {n: s for n, s, _ in specs}
+    layout: "OrderedDict[str, tuple[int, int, tuple]]" = OrderedDict()
+    ranges, groups = [], bucket_order(specs, n_layer)
+    off = 0
+    for grp in groups:
+        lo = off
+        for n in grp:
+            numel = int(np.prod(shapes[n]))
+            layout[n] = (off, numel, tuple(shapes[n]))
+            off += -(-numel // ALIGN) * ALIGN
+        ranges.append((lo, off))
+    return layout, ranges, groups, off
+
+
+def assign_owners(specs, world: int) -> dict[str, int]:
+    """Greedy longest-processing-time assignment of whole parameters to ranks.
+
+    Cost = elements (optimizer memory traffic) plus, for matrices, the Newton-Schulz FLOPs expressed
+    in element-equivalents, so the Muon work is spread too. Deterministic on every rank.
+    """
+    costs = []
+    for n, shape, group in specs:
+        numel = int(np.prod(shape))
+        c = float(numel)
+        if group == "matrices" and len(shape) == 2:
+            r, cc = shape
+            small, big = min(r, cc), max(r, cc)
+            c += 15 * 2 * small * small * big / 2000.0  # 5 NS iterations x 3 GEMMs, scaled to elements
+        costs.append((c, n))
+    costs.sort(key=lambda t: (-t[0], t[1]))
+    load = [0.0] * world
+    owner = {}
+    for c, n in costs:
+        r = min(range(world), key=lambda i: (load[i], i))
+        owner[n] = r
+        load[r] += c
+    return owner
+
+
+def chunk_ranges(off: int, numel: int, start_in_param: int = 0, size: int = CHUNK):
+    out = []
+    s = 0
+    while s < numel:
+        ln = min(size, numel - s)
+        out.append((off + s, ln, start_in_param + s))
+        s += ln
+    return out
+
+
+class SymmetricBuffer:
+    """A device buffer exported over CUDA IPC and opened by every rank of the group."""
+
+    def __init__(self, nbytes: int, group=None):
+        self.E = ext()
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.nbytes = nbytes
+        self.ptr, handle = self.E.sym_alloc(nbytes)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.numpy().tobytes(), group=group)
+        self.peer_ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.peer_ptrs.append(self.ptr)
+            else:
+                self.peer_ptrs.append(self.E.sym_open(torch.frombuffer(bytearray(h), dtype=torch.uint8)))
+        self.device = torch.cuda.current_device()
+        self.peers_dev = torch.tensor(self.peer_ptrs, dtype=torch.int64, device="cuda")
+
+    def view(self, numel: int, dtype_code: int, offset_bytes: int = 0) -> torch.Tensor:
+        return self.E.sym_view(self.ptr + offset_bytes, numel, dtype_code, self.device)
+
+    def close(self):
+        for r, p in enumerate(self.peer_ptrs):
+            if r != self.rank:
+                try:
+                    self.E.sym_close(p)
+                except Exception:
+                    pass
+        self.E.sym_free(self.ptr)
+
+
+class P2PGradSync:
+    """Bucketed, backward-overlapped reduce-scatter + sharded optimizer + parameter gather."""
+
+    def __init__(self, trainer, cfg):
+        self.tr = trainer
+        self.cfg = cfg
+        self.E = ext()
+        self.rank, self.world = trainer.rank, trainer.world
+        self.wire = WIRE_CODE[cfg.wire_dtype]
+        self.budget = float(cfg.comm_timeout_s)
+        specs = trainer.model.specs
+        self.layout = trainer.layout
+        self.ranges = trainer.bucket_ranges
+        self.groups = trainer.bucket_groups
+        total = trainer.flat_grad.numel()
+        self.owner = assign_owners(specs, self.world)
+        self.owned_names = {n for n, r in self.owner.items() if r == self.rank}
+        dev = trainer.device
+        # symmetric buffers: send (wire dtype), params (fp32), flags (int64)
+        self.send = SymmetricBuffer(total * WIRE_BYTES[self.wire])
+        self.param_buf = SymmetricBuffer(total * 4)
+        self.nflags = len(self.ranges) + 2
+        self.flags = SymmetricBuffer(self.nflags * 8)
+        self.flag_view = self.flags.view(self.nflags, 3)
+        self.params_flat = self.param_buf.view(total, 0)
+        self.red = torch.zeros(total, dtype=torch.float32, device=dev)
+        self.bad = torch.zeros(1, dtype=torch.int32, device=dev)
+        # re-point the model parameters into the symmetric parameter buffer
+        with torch.no_grad():
+            for n, p in trainer.model.named().items():
+                off, numel, shape = self.layout[n]
+                v = self.params_flat[off:off + numel].view(shape)
+                v.copy_(p.data)
+                p.data = v
+        # the reduced gradients the sharded optimizer consumes (views of ``red``)
+        self.red_views = OrderedDict((n, self.red[o:o + k].view(s)) for n, (o, k, s) in self.layout.items())
+        # per-bucket owned chunks (offset, len) for the reduce kernel
+        self.reduce_chunks = []
+        for grp in self.groups:
+            ch = []
+            for n in grp:
+                if self.owner[n] == self.rank:
+                    off, numel, _ = self.layout[n]
+                    ch += [(o, ln) for o, ln, _ in chunk_ranges(off, numel)]
+            self.reduce_chunks.append(torch.tensor(ch, dtype=torch.int64, device=dev).view(-1, 2))
+        self.flag_ptrs = torch.tensor([p for p in self.flags.peer_ptrs], dtype=torch.int64, device=dev)
+        self._build_gather_table(trainer)
+        self.comm_stream = torch.cuda.Stream(device=dev)
+        self.events = [torch.cuda.Event() for _ in self.ranges]
+        self.done = torch.cuda.Event()
+        self.epoch = 0
+        dist.barrier()
+
+    def _build_gather_table(self, trainer):
+        shadows = trainer.engine.shadows if trainer.engine is not None else {}
+        rows = []
+        for n, (off, numel, shape) in self.layout.items():
+            o = self.owner[n]
+            if o == self.rank:
+                continue
+            sh = shadows.get(n)
+            cols = int(shape[-1]) if sh is not None else 0
+            ld = int(sh.stride(0)) if sh is not None else 0
+            ptr = int(sh.data_ptr()) if sh is not None else 0
+            for c_off, ln, start in chunk_ranges(off, numel):
+                rows.append((c_off, ln, o, cols, ld, ptr, start))
+        self.gather_segs = torch.tensor(rows, dtype=torch.int64, device=trainer.device).view(-1, 7)
+
+    # ------------------------------------------------------------------ hooks from the engine
+    def bucket_ready(self, b: int, loss_scale: float) -> None:
+        """Called on the compute stream when bucket ``b``'s gradients are final for this step."""
+        ev = self.events[b]
+        ev.record()
+        s = self.comm_stream
+        s.wait_event(ev)
+        lo, hi = self.ranges[b]
+        with torch.cuda.stream(s):
+            self.E.comm_pack(self.tr.flat_grad, self.send.ptr, self.wire, lo, hi, 1.0 / loss_scale, self.bad)
+            self.E.comm_signal(self.flags.ptr + 8 * b, self.epoch + 1)
+            self.E.comm_reduce(self.send.peers_dev, self.flag_ptrs, b, self.epoch + 1, self.reduce_chunks[b],
+                               self.red, self.wire, 1.0 / self.world, 32, self.budget)
+
+    def begin_step(self) -> None:
+        self.bad.zero_()
+
+    # ------------------------------------------------------------------ step
+    def step(self, step_idx: int, scale: float, opt) -> bool:
+        cur = torch.cuda.current_stream()
+        cur.wait_stream(self.comm_stream)
+        epoch = self.epoch + 1
+        # agree on skipping: any non-finite gradient on any rank skips the update everywhere
+        flag = self.bad.clone().float()
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        status = check_status()
+        ok = status == 0 and float(flag.item()) == 0.0
+        if ok:
+            opt.step({n: self.red_views[n] for n in self.owned_names})
+        # publish (possibly unchanged) parameters and pull the ones owned elsewhere
+        self.E.comm_signal(self.flags.ptr + 8 * (self.nflags - 1), epoch)
+        self.E.comm_gather(self.param_buf.peers_dev, self.flag_ptrs, self.nflags - 1, epoch, self.gather_segs,
+                           self.params_flat, 64, self.budget)
+        self.epoch = epoch
+        if status:
+            self.tr.log(f"p2p collective timed out (status {status}); step {step_idx} skipped")
+        return ok
+
+    def close(self):
+        torch.cuda.synchronize()
+        dist.barrier()
+        for b in (self.send, self.param_buf, self.flags):
+            b.close()

@@ -43,6 +43,7 @@ from .data.loader import load_token_bytes
 from .eval import evaluate_bpb
 from .models.gpt import GPT
 from .optim.muon_adamw import MuonAdamW, lr_multiplier, muon_momentum, weight_decay_at
+from .parallel.comm import flat_layout
 from .parallel.ring import RingAllReduce
 from .parallel.sparsify import GradientSparsifier
 from .utils.logging import MetricsLog, ResultsLogger, TrainerMetrics, summary_block
@@ -134,13 +135,14 @@ class Trainer:
         if rows % self.device_batch:
             raise ValueError(f"per-rank rows {rows} not divisible by device_batch {self.device_batch}")
         self.grad_accum = rows // self.device_batch
-        # flat gradient buffer in the reference's order with per-parameter views
-        sizes = [int(np.prod(s)) for _, s, _ in self.specs]
-        self.offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
-        self.flat_grad = torch.zeros(int(self.offsets[-1]), dtype=torch.float32, device=self.device)
+        # one flat fp32 gradient buffer ordered by backward completion (one contiguous range per
+        # communication bucket), with a view per parameter
+        self.layout, self.bucket_ranges, self.bucket_groups, total = flat_layout(self.specs, cfg.model.n_layer)
+        self.flat_grad = torch.zeros(total, dtype=torch.float32, device=self.device)
         self.grad_views: "OrderedDict[str, torch.Tensor]" = OrderedDict()
-        for (name, shape, _), a in zip(self.specs, self.offsets[:-1]):
-            self.grad_views[name] = self.flat_grad[a:a + int(np.prod(shape))].view(shape)
+        for name, _, _ in self.specs:
+            off, numel, shape = self.layout[name]
+            self.grad_views[name] = self.flat_grad[off:off + numel].view(shape)
         owned = None
         if cfg.impl == "cuda":
             from .models.engine import FusedGPTEngine
@@ -149,6 +151,7 @@ class Trainer:
                 from .parallel.comm import P2PGradSync
                 self.comm = P2PGradSync(self, cfg)
                 owned = self.comm.owned_names
+                self.engine.bucket_hook = self.comm.bucket_ready
         else:
             for name, p in self.model.named().items():
                 p.grad = self.grad_views[name]
@@ -189,7 +192,8 @@ class Trainer:
     def _forward_backward(self, x, y, scale: float):
         if self.engine is not None:
             return self.engine.forward_backward(x, y, loss_scale=scale / self.grad_accum,
-                                                accumulate=self._micro > 0)
+                                                accumulate=self._micro > 0,
+                                                last_micro=self._micro == self.grad_accum - 1, grad_scale=scale)
         cd = torch.bfloat16 if self.is_cuda and self.cfg.dtype == "bf16" else (
             torch.float16 if self.is_cuda and self.cfg.dtype == "fp16" else None)
         loss = self.model.forward_torch(x, y, compute_dtype=cd, exact_ce=not self.is_cuda)
@@ -210,6 +214,8 @@ class Trainer:
             self.flat_grad.zero_()
         losses = []
         scale = self.scaler.scale
+        if self.comm is not None and hasattr(self.comm, "begin_step"):
+            self.comm.begin_step()
         for self._micro in range(self.grad_accum):
             if batch is None:
                 x, y = self.next_batch()

@@ -1,0 +1,335 @@
+// tcgen05/TMEM flash attention forward for sm_100a (head_dim 128, causal + sliding window).
+//
+// One CTA per (128-query tile, head, batch); 192 threads:
+//   warp 0      TMA: the Q tile once, then 128-key K and V tiles into a 2-stage ring (128-byte
+//               swizzle, 3-D tensor maps over the fused [B, T, Dq+2Dkv] projection buffer, zero fill
+//               past T; no multicast);
+//   warp 1      TMEM allocation and the single MMA-issuing lane:
+//                 S_j = Q K_j^T  -> TMEM columns [128*(j%2), +128)  (two ping-pong buffers)
+//                 O  += P_j V_j  -> TMEM columns [256, 384)
+//               S_{j+1} is issued before waiting for P_j, so the next scores overlap this softmax;
+//   warps 2-5   softmax, one query row per thread (TMEM lane = row): masked row max, conditional
+//               rescale of O in TMEM (only when the running max grows by more than 2^8, so P stays
+//               below 256), P = exp2(S*scale - m) written as bf16 to shared memory in the K-major
+//               128-byte-swizzled layout the PV MMA reads; finally O / l and the log-sum-exp.
+// Key tiles entirely outside [q - w + 1, q] are never loaded. All mbarrier waits are bounded; on
+// timeout the CTA records a status code, drains its MMAs, frees TMEM and exits.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "status.h"
+#include "tma_host.h"
+
+namespace br {
+namespace {
+
+constexpr int HD = 128;
+constexpr int BQ = 128;
+constexpr int BKV = 128;
+constexpr int TILE_BYTES = 128 * 128 * 2;  // one 128 x 128 bf16 tile (two 64-column swizzle atoms)
+constexpr int ATOM_BYTES = 128 * 128;      // 128 rows x 128 bytes
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint64_t kBudgetNs = 2000000000ull;
+
+struct FwdParams {
+  int T, H, KV, Dq, Dkv, window;
+  float scale_log2;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  float* lse;
+  int* status;
+};
+
+// smem layout (offsets from a 1024-aligned base)
+constexpr int SM_Q = 0;
+constexpr int SM_K = SM_Q + TILE_BYTES;
+constexpr int SM_V = SM_K + 2 * TILE_BYTES;
+constexpr int SM_P = SM_V + 2 * TILE_BYTES;
+constexpr int SM_BAR = SM_P + TILE_BYTES;
+constexpr int FWD_SMEM = SM_BAR + 256 + 1024;
+
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* v_full = bars + 3;    // [2]
+  uint64_t* kv_empty = bars + 5;  // [2]
+  uint64_t* s_full = bars + 7;    // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (p.H / p.KV);
+  const int q0 = qb * BQ;
+  const int w = p.window;
+  const int kb_lo = max(0, q0 - w + 1) / BKV;
+  const int kb_hi = min(q0 + BQ - 1, p.T - 1) / BKV;
+  const int nkv = kb_hi - kb_lo + 1;
+  const int warp = warp_id();
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&](int code) {
+    *abort_flag = 1;
+    if (p.status) atomicCAS(p.status, 0, code);
+  };
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tm);
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_3d(&tm, q_full, smem + SM_Q, h * HD, q0, b);
+      tma_load_3d(&tm, q_full, smem + SM_Q + ATOM_BYTES, h * HD + 64, q0, b);
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, kBudgetNs, abort_flag)) {
+          fail(kErrTimeoutProducer);
+          break;
+        }
+        const int k0 = (kb_lo + j) * BKV;
+        uint8_t* ks = smem + SM_K + st * TILE_BYTES;
+        uint8_t* vs = smem + SM_V + st * TILE_BYTES;
+        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+        tma_load_3d(&tm, &k_full[st], ks, p.Dq + kvh * HD, k0, b);
+        tma_load_3d(&tm, &k_full[st], ks + ATOM_BYTES, p.Dq + kvh * HD + 64, k0, b);
+        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+        tma_load_3d(&tm, &v_full[st], vs, p.Dq + p.Dkv + kvh * HD, k0, b);
+        tma_load_3d(&tm, &v_full[st], vs + ATOM_BYTES, p.Dq + p.Dkv + kvh * HD + 64, k0, b);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t idesc_o = umma_idesc_bf16(128, 128, false, true);
+      const uint32_t q_addr = smem_u32(smem + SM_Q);
+      const uint32_t p_addr = smem_u32(smem + SM_P);
+      bool ok = mbar_wait(q_full, 0, kBudgetNs, abort_flag);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1, kBudgetNs, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + SM_K + st * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
+          umma_bf16_ss(tmem + st * 128, umma_desc_sw128(q_addr + off, 16, 1024),
+                       umma_desc_sw128(k_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[st]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < nkv && ok; ++j) {
+        if (j + 1 < nkv && !issue_s(j + 1)) {
+          ok = false;
+          break;
+        }
+        const int st = j & 1;
+        if (!mbar_wait(p_full, j & 1, kBudgetNs, abort_flag) ||
+            !mbar_wait(&v_full[st], (j >> 1) & 1, kBudgetNs, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + SM_V + st * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * ATOM_BYTES + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = umma_desc_sw128(v_addr + kk * 2048, ATOM_BYTES, 1024);
+          umma_bf16_ss(tmem + 256, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(o_done);
+        umma_commit(&kv_empty[st]);
+      }
+      if (!ok) fail(kErrTimeoutMma);
+      umma_commit(drain);
+      mbar_wait(drain, 0, 100000000ull, nullptr);
+    }
+  } else {
+    // softmax warps: row r of the tile
+    const int wq = warp & 3;
+    const int lane = lane_id();
+    const int r = wq * 32 + lane;
+    const int qi = q0 + r;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+    uint8_t* prow = smem + SM_P + r * 128;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait(&s_full[st], (j >> 1) & 1, kBudgetNs, abort_flag)) {
+        fail(kErrTimeoutEpilogue);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int k0 = (kb_lo + j) * BKV;
+      const uint32_t s_addr = lane_base + st * 128;
+      // pass 1: masked row max (log2 domain)
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(s_addr + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int kj = k0 + c * 32 + i;
+          const bool vis = kj <= qi && kj > qi - w && kj < p.T;
+          mx = fmaxf(mx, vis ? __uint_as_float(v[i]) * p.scale_log2 : -INFINITY);
+        }
+      }
+      // PV_{j-1} must be complete before P is overwritten or O is rescaled
+      if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, kBudgetNs, abort_flag)) {
+        fail(kErrTimeoutEpilogue);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (j == 0) {
+        m_ref = mx;
+      } else if (mx > m_ref + 8.f) {
+        const float alpha = m_ref == -INFINITY ? 0.f : exp2f(m_ref - mx);
+        l *= alpha;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + 256 + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+          tmem_st32(lane_base + 256 + c * 32, v);
+        }
+        tmem_st_wait();
+        m_ref = mx;
+      }
+      // pass 2: P = exp2(s - m_ref) -> bf16 into the swizzled K-major P tile
+      const bool live = m_ref != -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(s_addr + c * 32, v);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int kj = k0 + c * 32 + i;
+          const bool v0 = live && kj <= qi && kj > qi - w && kj < p.T;
+          const bool v1 = live && kj + 1 <= qi && kj + 1 > qi - w && kj + 1 < p.T;
+          const float p0 = v0 ? exp2f(__uint_as_float(v[i]) * p.scale_log2 - m_ref) : 0.f;
+          const float p1 = v1 ? exp2f(__uint_as_float(v[i + 1]) * p.scale_log2 - m_ref) : 0.f;
+          l += p0 + p1;
+          pk[i / 2] = pack_bf16(p0, p1);
+        }
+        // columns c*32 .. c*32+31: atom c/2, 16-byte chunks (c%2)*4 .. +3, XOR-swizzled by row
+        uint8_t* atom = prow + (c >> 1) * ATOM_BYTES;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = (c & 1) * 4 + q;
+          *reinterpret_cast<uint4*>(atom + ((chunk ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(o_done, (nkv - 1) & 1, kBudgetNs, abort_flag)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.out + ((int64_t)b * p.T + qi) * p.ldo + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(lane_base + 256 + c * 32, v);
+        tmem_ld_wait();
+        if (qi < p.T) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 o;
+            o.x = pack_bf16(__uint_as_float(v[8 * q + 0]) * inv, __uint_as_float(v[8 * q + 1]) * inv);
+            o.y = pack_bf16(__uint_as_float(v[8 * q + 2]) * inv, __uint_as_float(v[8 * q + 3]) * inv);
+            o.z = pack_bf16(__uint_as_float(v[8 * q + 4]) * inv, __uint_as_float(v[8 * q + 5]) * inv);
+            o.w = pack_bf16(__uint_as_float(v[8 * q + 6]) * inv, __uint_as_float(v[8 * q + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + q * 8) = o;
+          }
+        }
+      }
+      if (qi < p.T) p.lse[((int64_t)b * p.H + h) * p.T + qi] = (m_ref + __log2f(l)) / kLog2e;
+    } else if (ok) {
+      fail(kErrTimeoutEpilogue);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+// qkv: [B*T, Dq + 2*Dkv] bf16 (q | k | v columns, contiguous rows); o: [B*T, *] bf16 (head h at h*128).
+void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int64_t B, int64_t T, int64_t H,
+                 int64_t KV, int64_t hd, int64_t window) {
+  TORCH_CHECK(hd == HD, "attn_fwd_tc: head_dim 128");
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.stride(1) == 1, "attn_fwd_tc: bf16 rows");
+  TORCH_CHECK(o.stride(1) == 1 && o.stride(0) % 8 == 0, "attn_fwd_tc: output rows");
+  const int64_t W = qkv.size(1);
+  TORCH_CHECK(W == (H + 2 * KV) * hd && H % KV == 0, "attn_fwd_tc: qkv width");
+  c10::cuda::CUDAGuard g(qkv.device());
+  CUtensorMap tm = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.data_ptr(), W, T, B, qkv.stride(0),
+                              qkv.stride(0) * T, 64, 128);
+  FwdParams p;
+  p.T = (int)T;
+  p.H = (int)H;
+  p.KV = (int)KV;
+  p.Dq = (int)(H * hd);
+  p.Dkv = (int)(KV * hd);
+  p.window = (int)std::min<int64_t>(window <= 0 ? T : window, T);
+  p.scale_log2 = kLog2e / sqrtf((float)hd);
+  p.out = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.ldo = o.stride(0);
+  p.lse = lse.data_ptr<float>();
+  p.status = status_ptr(qkv.device().index());
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
+    attr = true;
+  }
+  dim3 grid((unsigned)((T + BQ - 1) / BQ), (unsigned)H, (unsigned)B);
+  attn_fwd_tc_kernel<<<grid, 192, FWD_SMEM, at::cuda::getCurrentCUDAStream()>>>(tm, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace br

@@ -49,6 +49,21 @@ void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
               const torch::Tensor& dout, const torch::Tensor& lse, torch::Tensor& dq, torch::Tensor& dk,
               torch::Tensor& dv, torch::Tensor& delta, torch::Tensor& dq_acc, int64_t B, int64_t T, int64_t H,
               int64_t KV, int64_t hd, int64_t window);
+void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int64_t B, int64_t T, int64_t H,
+                 int64_t KV, int64_t hd, int64_t window);
+std::tuple<int64_t, torch::Tensor> sym_alloc(int64_t bytes);
+int64_t sym_open(const torch::Tensor& handle);
+void sym_close(int64_t ptr);
+void sym_free(int64_t ptr);
+torch::Tensor sym_view(int64_t ptr, int64_t numel, int64_t dtype_code, int64_t device);
+void comm_pack(const torch::Tensor& src, int64_t send_ptr, int64_t wire, int64_t lo, int64_t hi, double scale,
+               torch::Tensor& bad);
+void comm_signal(int64_t flag_ptr, int64_t value);
+void comm_reduce(const torch::Tensor& peers, const torch::Tensor& flags, int64_t slot, int64_t epoch,
+                 const torch::Tensor& chunks, torch::Tensor& out, int64_t wire, double scale, int64_t max_blocks,
+                 double budget_s);
+void comm_gather(const torch::Tensor& peers, const torch::Tensor& flags, int64_t slot, int64_t epoch,
+                 const torch::Tensor& segs, torch::Tensor& local, int64_t max_blocks, double budget_s);
 }  // namespace br
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -72,4 +87,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("muon_finish", &br::muon_finish);
   m.def("attn_fwd", &br::attn_fwd);
   m.def("attn_bwd", &br::attn_bwd);
+  m.def("attn_fwd_tc", &br::attn_fwd_tc);
+  m.def("sym_alloc", &br::sym_alloc);
+  m.def("sym_open", &br::sym_open);
+  m.def("sym_close", &br::sym_close);
+  m.def("sym_free", &br::sym_free);
+  m.def("sym_view", &br::sym_view);
+  m.def("comm_pack", &br::comm_pack);
+  m.def("comm_signal", &br::comm_signal);
+  m.def("comm_reduce", &br::comm_reduce);
+  m.def("comm_gather", &br::comm_gather);
 }

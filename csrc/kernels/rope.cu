@@ -1,4 +1,4 @@
-// Attention-input transforms, one warp per (token, head slot) over the fused QKV projection output
+// Attention-input transforms, one warp per token over the fused QKV projection output
 // qkv[M, H*hd + 2*KV*hd] (bf16, columns q | k | v):
 //
 //   q, k : half-split RoPE (y1 = x1 c + x2 s, y2 = -x1 s + x2 c, base 10000, gpt.ts:159-177) then
@@ -28,51 +28,55 @@ struct RopeArgs {
   int ld;  // row stride of qkv (elements)
 };
 
+// One warp per token; lane l owns head elements {2l, 2l+1} and {h2+2l, h2+2l+1} (hd = 128), so every
+// load/store of the warp is a contiguous 128-byte bf16x2 access.
+__device__ __forceinline__ float2 ldb2(const __nv_bfloat16* p) {
+  return unpack_bf16(*reinterpret_cast<const uint32_t*>(p));
+}
+__device__ __forceinline__ void stb2(__nv_bfloat16* p, float a, float b) {
+  *reinterpret_cast<uint32_t*>(p) = pack_bf16(a, b);
+}
+
 __global__ void rope_fwd_kernel(__nv_bfloat16* __restrict__ qkv, RopeArgs a, const float* __restrict__ cosT,
                                 const float* __restrict__ sinT, float* __restrict__ rq, float* __restrict__ rk,
                                 const int* __restrict__ idx, const float* __restrict__ ve,
                                 const float* __restrict__ cur, const float* __restrict__ wg, float* __restrict__ gate,
                                 int D) {
   const int lane = threadIdx.x & 31;
-  const int slots = a.H + 2 * a.KV;
-  const int h2 = a.hd / 2;
-  const int64_t total = (int64_t)a.M * slots;
-  for (int64_t task = blockIdx.x * (int64_t)kWarps + (threadIdx.x >> 5); task < total;
-       task += (int64_t)gridDim.x * kWarps) {
-    const int m = (int)(task / slots);
-    const int s = (int)(task % slots);
+  const int h2 = a.hd / 2;  // 64
+  for (int m = blockIdx.x * kWarps + (threadIdx.x >> 5); m < a.M; m += gridDim.x * kWarps) {
     __nv_bfloat16* row = qkv + (int64_t)m * a.ld;
-    if (s < a.H + a.KV) {
-      const bool isq = s < a.H;
-      const int head = isq ? s : s - a.H;
-      __nv_bfloat16* p = row + (isq ? head * a.hd : a.H * a.hd + head * a.hd);
-      const int t = m % a.T;
-      float y1[4], y2[4];
-      float ss = 0.f;
-      int n = 0;
-      for (int j = lane; j < h2; j += 32, ++n) {
-        const float c = cosT[t * h2 + j], sn = sinT[t * h2 + j];
-        const float x1 = __bfloat162float(p[j]), x2 = __bfloat162float(p[j + h2]);
-        y1[n] = x1 * c + x2 * sn;
-        y2[n] = -x1 * sn + x2 * c;
-        ss += y1[n] * y1[n] + y2[n] * y2[n];
+    const int t = m % a.T;
+    const float2 c = *reinterpret_cast<const float2*>(cosT + t * h2 + 2 * lane);
+    const float2 sn = *reinterpret_cast<const float2*>(sinT + t * h2 + 2 * lane);
+    const int nqk = a.H + a.KV;
+#pragma unroll 2
+    for (int s = 0; s < nqk; ++s) {
+      __nv_bfloat16* p = row + s * a.hd;
+      const float2 x1 = ldb2(p + 2 * lane), x2 = ldb2(p + h2 + 2 * lane);
+      const float y1a = x1.x * c.x + x2.x * sn.x, y1b = x1.y * c.y + x2.y * sn.y;
+      const float y2a = -x1.x * sn.x + x2.x * c.x, y2b = -x1.y * sn.y + x2.y * c.y;
+      const float r = rsqrtf(warp_sum(y1a * y1a + y1b * y1b + y2a * y2a + y2b * y2b) / a.hd + kEps);
+      stb2(p + 2 * lane, y1a * r, y1b * r);
+      stb2(p + h2 + 2 * lane, y2a * r, y2b * r);
+      if (lane == 0) (s < a.H ? rq[(int64_t)m * a.H + s] : rk[(int64_t)m * a.KV + (s - a.H)]) = r;
+    }
+    if (ve != nullptr) {
+      const float cz = cur[(int64_t)m * D + lane];
+      const float* e = ve + (int64_t)idx[m] * (a.KV * a.hd);
+      for (int h = 0; h < a.KV; ++h) {
+        const float z = warp_sum(cz * wg[lane * a.KV + h]);
+        const float g = 2.f / (1.f + __expf(-z));
+        __nv_bfloat16* p = row + (nqk + h) * a.hd;
+        const float4 ev = *reinterpret_cast<const float4*>(e + h * a.hd + 4 * lane);
+        const uint2 u = *reinterpret_cast<const uint2*>(p + 4 * lane);
+        const float2 v01 = unpack_bf16(u.x), v23 = unpack_bf16(u.y);
+        uint2 o;
+        o.x = pack_bf16(v01.x + ev.x * g, v01.y + ev.y * g);
+        o.y = pack_bf16(v23.x + ev.z * g, v23.y + ev.w * g);
+        *reinterpret_cast<uint2*>(p + 4 * lane) = o;
+        if (lane == 0) gate[(int64_t)m * a.KV + h] = g;
       }
-      const float r = rsqrtf(warp_sum(ss) / a.hd + kEps);
-      n = 0;
-      for (int j = lane; j < h2; j += 32, ++n) {
-        p[j] = __float2bfloat16(y1[n] * r);
-        p[j + h2] = __float2bfloat16(y2[n] * r);
-      }
-      if (lane == 0) (isq ? rq[(int64_t)m * a.H + head] : rk[(int64_t)m * a.KV + head]) = r;
-    } else if (ve != nullptr) {
-      const int head = s - a.H - a.KV;
-      float z = lane < kGateCh ? cur[(int64_t)m * D + lane] * wg[lane * a.KV + head] : 0.f;
-      z = warp_sum(z);
-      const float g = 2.f / (1.f + __expf(-z));
-      __nv_bfloat16* p = row + a.H * a.hd + a.KV * a.hd + head * a.hd;
-      const float* e = ve + (int64_t)idx[m] * (a.KV * a.hd) + head * a.hd;
-      for (int j = lane; j < a.hd; j += 32) p[j] = __float2bfloat16(__bfloat162float(p[j]) + e[j] * g);
-      if (lane == 0) gate[(int64_t)m * a.KV + head] = g;
     }
   }
 }
@@ -84,52 +88,37 @@ __global__ void rope_bwd_kernel(__nv_bfloat16* __restrict__ dqkv, const __nv_bfl
                                 const int* __restrict__ idx, const float* __restrict__ ve,
                                 const float* __restrict__ gate, float* __restrict__ dve, float* __restrict__ dz) {
   const int lane = threadIdx.x & 31;
-  const int slots = a.H + 2 * a.KV;
   const int h2 = a.hd / 2;
-  const int64_t total = (int64_t)a.M * slots;
-  for (int64_t task = blockIdx.x * (int64_t)kWarps + (threadIdx.x >> 5); task < total;
-       task += (int64_t)gridDim.x * kWarps) {
-    const int m = (int)(task / slots);
-    const int s = (int)(task % slots);
-    if (s < a.H + a.KV) {
-      const bool isq = s < a.H;
-      const int head = isq ? s : s - a.H;
-      const int64_t off = (int64_t)m * a.ld + (isq ? head * a.hd : a.H * a.hd + head * a.hd);
-      const float r = isq ? rq[(int64_t)m * a.H + head] : rk[(int64_t)m * a.KV + head];
-      float g1[4], g2[4], u1[4], u2[4];
-      float dot = 0.f;
-      int n = 0;
-      for (int j = lane; j < h2; j += 32, ++n) {
-        g1[n] = __bfloat162float(dqkv[off + j]);
-        g2[n] = __bfloat162float(dqkv[off + j + h2]);
-        u1[n] = __bfloat162float(qkv[off + j]);  // normalised outputs y
-        u2[n] = __bfloat162float(qkv[off + j + h2]);
-        dot += g1[n] * u1[n] + g2[n] * u2[n];
-      }
-      const float mean = warp_sum(dot) / a.hd;
-      const int t = m % a.T;
-      n = 0;
-      for (int j = lane; j < h2; j += 32, ++n) {
-        const float d1 = r * (g1[n] - u1[n] * mean), d2 = r * (g2[n] - u2[n] * mean);
-        const float c = cosT[t * h2 + j], sn = sinT[t * h2 + j];
-        dqkv[off + j] = __float2bfloat16(d1 * c - d2 * sn);
-        dqkv[off + j + h2] = __float2bfloat16(d1 * sn + d2 * c);
-      }
-    } else if (ve != nullptr) {
-      const int head = s - a.H - a.KV;
-      const int64_t off = (int64_t)m * a.ld + a.H * a.hd + a.KV * a.hd + head * a.hd;
-      const int64_t eoff = (int64_t)idx[m] * (a.KV * a.hd) + head * a.hd;
-      const float g = gate[(int64_t)m * a.KV + head];
-      float dg = 0.f;
-      for (int j = lane * 4; j < a.hd; j += 128) {
-        const float4 e = *reinterpret_cast<const float4*>(ve + eoff + j);
-        const uint2 u = *reinterpret_cast<const uint2*>(dqkv + off + j);
+  for (int m = blockIdx.x * kWarps + (threadIdx.x >> 5); m < a.M; m += gridDim.x * kWarps) {
+    const int64_t base = (int64_t)m * a.ld;
+    const int t = m % a.T;
+    const float2 c = *reinterpret_cast<const float2*>(cosT + t * h2 + 2 * lane);
+    const float2 sn = *reinterpret_cast<const float2*>(sinT + t * h2 + 2 * lane);
+    const int nqk = a.H + a.KV;
+#pragma unroll 2
+    for (int s = 0; s < nqk; ++s) {
+      const int64_t off = base + s * a.hd;
+      const float r = s < a.H ? rq[(int64_t)m * a.H + s] : rk[(int64_t)m * a.KV + (s - a.H)];
+      const float2 g1 = ldb2(dqkv + off + 2 * lane), g2 = ldb2(dqkv + off + h2 + 2 * lane);
+      const float2 u1 = ldb2(qkv + off + 2 * lane), u2 = ldb2(qkv + off + h2 + 2 * lane);
+      const float mean = warp_sum(g1.x * u1.x + g1.y * u1.y + g2.x * u2.x + g2.y * u2.y) / a.hd;
+      const float d1a = r * (g1.x - u1.x * mean), d1b = r * (g1.y - u1.y * mean);
+      const float d2a = r * (g2.x - u2.x * mean), d2b = r * (g2.y - u2.y * mean);
+      stb2(dqkv + off + 2 * lane, d1a * c.x - d2a * sn.x, d1b * c.y - d2b * sn.y);
+      stb2(dqkv + off + h2 + 2 * lane, d1a * sn.x + d2a * c.x, d1b * sn.y + d2b * c.y);
+    }
+    if (ve != nullptr) {
+      const int64_t erow = (int64_t)idx[m] * (a.KV * a.hd);
+      for (int h = 0; h < a.KV; ++h) {
+        const int64_t off = base + (nqk + h) * a.hd + 4 * lane;
+        const float g = gate[(int64_t)m * a.KV + h];
+        const float4 e = *reinterpret_cast<const float4*>(ve + erow + h * a.hd + 4 * lane);
+        const uint2 u = *reinterpret_cast<const uint2*>(dqkv + off);
         const float2 d01 = unpack_bf16(u.x), d23 = unpack_bf16(u.y);
-        dg += d01.x * e.x + d01.y * e.y + d23.x * e.z + d23.y * e.w;
-        red_add_v4_f32(dve + eoff + j, d01.x * g, d01.y * g, d23.x * g, d23.y * g);
+        const float dg = warp_sum(d01.x * e.x + d01.y * e.y + d23.x * e.z + d23.y * e.w);
+        red_add_v4_f32(dve + erow + h * a.hd + 4 * lane, d01.x * g, d01.y * g, d23.x * g, d23.y * g);
+        if (lane == 0) dz[(int64_t)m * a.KV + h] = dg * g * (1.f - 0.5f * g);
       }
-      dg = warp_sum(dg);
-      if (lane == 0) dz[(int64_t)m * a.KV + head] = dg * g * (1.f - 0.5f * g);
     }
   }
 }
@@ -186,13 +175,13 @@ void rope_fwd(torch::Tensor& qkv, int64_t T, int64_t H, int64_t KV, int64_t hd, 
               const torch::Tensor& sinT, torch::Tensor& rq, torch::Tensor& rk, const torch::Tensor& idx,
               c10::optional<torch::Tensor> ve, c10::optional<torch::Tensor> cur, c10::optional<torch::Tensor> wg,
               c10::optional<torch::Tensor> gate) {
-  TORCH_CHECK(hd % 2 == 0 && hd <= 256 && hd % 4 == 0, "rope_fwd: head_dim must be a multiple of 4, <= 256");
+  TORCH_CHECK(hd == 128, "rope_fwd: head_dim 128");
+  TORCH_CHECK(qkv.stride(0) % 8 == 0, "rope_fwd: row stride must be a multiple of 8");
   const int64_t M = qkv.size(0);
   RopeArgs a{(int)M, (int)T, (int)H, (int)KV, (int)hd, (int)qkv.stride(0)};
   const bool has_ve = ve.has_value() && ve->defined();
   c10::cuda::CUDAGuard g(qkv.device());
-  const int64_t slots = H + (has_ve ? 2 : 1) * KV;
-  rope_fwd_kernel<<<grid_for(M * slots), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
+  rope_fwd_kernel<<<grid_for(M), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), a, cosT.data_ptr<float>(), sinT.data_ptr<float>(),
       rq.data_ptr<float>(), rk.data_ptr<float>(), idx.data_ptr<int>(), has_ve ? ve->data_ptr<float>() : nullptr,
       has_ve ? cur->data_ptr<float>() : nullptr, has_ve ? wg->data_ptr<float>() : nullptr,
@@ -209,8 +198,7 @@ void rope_bwd(torch::Tensor& dqkv, const torch::Tensor& qkv, int64_t T, int64_t 
   RopeArgs a{(int)M, (int)T, (int)H, (int)KV, (int)hd, (int)qkv.stride(0)};
   const bool has_ve = ve.has_value() && ve->defined();
   c10::cuda::CUDAGuard g(qkv.device());
-  const int64_t slots = H + (has_ve ? 2 : 1) * KV;
-  rope_bwd_kernel<<<grid_for(M * slots), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
+  rope_bwd_kernel<<<grid_for(M), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), a,
       cosT.data_ptr<float>(), sinT.data_ptr<float>(), rq.data_ptr<float>(), rk.data_ptr<float>(), idx.data_ptr<int>(),
       has_ve ? ve->data_ptr<float>() : nullptr, has_ve ? gate->data_ptr<float>() : nullptr,

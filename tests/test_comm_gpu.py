@@ -1,0 +1,192 @@
+"""NVLink collective kernels.
+
+* 1 GPU: a reduce whose peer flag is never set gives up after its budget, records the timeout in the
+  device status word and leaves the context usable.
+* 2 GPUs (one process each, NCCL only for rendezvous): packed bf16/fp32 gradients reduced by their
+  owners equal the mean of the ranks' inputs; the parameter gather returns the owners' values and
+  refreshes bf16 shadows; the trainer's p2p path tracks the NCCL path step for step.
+"""
+import datetime
+import os
+import socket
+import time
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def test_bounded_wait_times_out_and_context_survives(cuda):
+    from bitresearch_b200.ops._ext import check_status, ext
+    E = ext()
+    check_status()
+    ptr, _ = E.sym_alloc(1 << 20)
+    try:
+        flags = torch.tensor([ptr], dtype=torch.int64, device=cuda)
+        peers = torch.tensor([ptr], dtype=torch.int64, device=cuda)
+        chunks = torch.tensor([[0, 1024]], dtype=torch.int64, device=cuda)
+        out = torch.zeros(1024, device=cuda)
+        t0 = time.time()
+        E.comm_reduce(peers, flags, 0, 1, chunks, out, 0, 1.0, 4, 0.2)  # flag stays 0 < epoch 1
+        torch.cuda.synchronize()
+        dt = time.time() - t0
+        assert check_status() == 4  # kErrTimeoutPeer
+        assert 0.15 < dt < 5.0
+        x = torch.randn(1000, device=cuda)  # context still healthy
+        assert torch.isfinite((x @ x).reshape(1)).all()
+    finally:
+        E.sym_free(ptr)
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, fn, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    try:
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        q.put((rank, "ok", fn(rank, world)))
+    except BaseException:
+        import traceback
+        q.put((rank, "err", traceback.format_exc()))
+    finally:
+        try:
+            torch.cuda.synchronize()
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _run(fn, world=2, timeout=300):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker, args=(r, world, port, fn, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = {}
+    try:
+        for _ in range(world):
+            r, st, v = q.get(timeout=timeout)
+            assert st == "ok", f"rank {r}:\n{v}"
+            res[r] = v
+    finally:
+        for p in ps:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    return [res[r] for r in range(world)]
+
+
+def _reduce_gather(rank, world):
+    from bitresearch_b200.ops._ext import check_status, ext
+    from bitresearch_b200.parallel.comm import SymmetricBuffer
+    E = ext()
+    n = 40000
+    out = {}
+    for wire, code, nbytes in (("fp32", 0, 4), ("bf16", 1, 2)):
+        send = SymmetricBuffer(n * nbytes)
+        flags = SymmetricBuffer(64)
+        g = torch.Generator(device="cpu").manual_seed(rank)
+        src = torch.randn(n, generator=g).cuda()
+        bad = torch.zeros(1, dtype=torch.int32, device="cuda")
+        E.comm_pack(src, send.ptr, code, 0, n, 0.5, bad)
+        E.comm_signal(flags.ptr, 7)
+        # rank r owns [r*n/2, (r+1)*n/2)
+        half = n // 2
+        chunks = torch.tensor([[rank * half, half]], dtype=torch.int64, device="cuda")
+        red = torch.zeros(n, device="cuda")
+        fp = torch.tensor(flags.peer_ptrs, dtype=torch.int64, device="cuda")
+        E.comm_reduce(send.peers_dev, fp, 0, 7, chunks, red, code, 1.0 / world, 16, 10.0)
+        torch.cuda.synchronize()
+        out[wire] = (red[rank * half:(rank + 1) * half].cpu(), int(bad.item()), check_status())
+        torch.distributed.barrier()
+        send.close()
+        flags.close()
+    # gather: every rank pulls the other rank's half of a symmetric parameter buffer
+    pbuf = SymmetricBuffer(n * 4)
+    flags = SymmetricBuffer(64)
+    local = E.sym_view(pbuf.ptr, n, 0, rank)
+    local.copy_(torch.full((n,), float(rank + 1), device="cuda"))
+    torch.cuda.synchronize()
+    E.comm_signal(flags.ptr + 8, 3)
+    other = 1 - rank
+    shadow = torch.zeros(100, 200, dtype=torch.bfloat16, device="cuda")
+    # the other half is a [100, 200] matrix with a bf16 shadow of row stride 200
+    seg = torch.tensor([[other * (n // 2), n // 2, other, 200, 200, shadow.data_ptr(), 0]], dtype=torch.int64,
+                       device="cuda")
+    fp = torch.tensor(flags.peer_ptrs, dtype=torch.int64, device="cuda")
+    E.comm_gather(pbuf.peers_dev, fp, 1, 3, seg, local, 8, 10.0)
+    torch.cuda.synchronize()
+    out["gather"] = (local.cpu(), shadow.float().cpu(), check_status())
+    torch.distributed.barrier()
+    pbuf.close()
+    flags.close()
+    return out
+
+
+def test_p2p_reduce_and_gather_2gpu():
+    res = _run(_reduce_gather)
+    n, half = 40000, 20000
+    srcs = [torch.randn(n, generator=torch.Generator().manual_seed(r)) for r in range(2)]
+    mean = (srcs[0] + srcs[1]) * 0.5 * 0.5
+    for r in range(2):
+        red32, bad, st = res[r]["fp32"]
+        assert st == 0 and bad == 0
+        torch.testing.assert_close(red32, mean[r * half:(r + 1) * half], rtol=1e-6, atol=1e-6)
+        red16, _, _ = res[r]["bf16"]
+        torch.testing.assert_close(red16, mean[r * half:(r + 1) * half], rtol=1e-2, atol=1e-2)
+        local, shadow, st = res[r]["gather"]
+        assert st == 0
+        other = 1 - r
+        assert torch.all(local[other * half:(other + 1) * half] == other + 1)
+        assert torch.all(local[r * half:(r + 1) * half] == r + 1)
+        assert torch.all(shadow == other + 1)
+
+
+def _train(rank, world):
+    from bitresearch_b200.config import apply_overrides, preset
+    from bitresearch_b200.train import Trainer
+    out = {}
+    for comm in ("nccl", "p2p"):
+        cfg = apply_overrides(preset("d512"), ["model.n_layer=2", "model.sequence_len=256", "model.vocab_size=1024",
+                                               "device_batch=4", f"total_batch_tokens={4 * 256 * world}",
+                                               "log_every=0", "results_tsv=", f"comm={comm}", "wire_dtype=fp32"])
+        tr = Trainer(cfg, device=torch.device("cuda", rank), log=lambda m: None)
+        tr.initialize()
+        g = torch.Generator(device="cpu").manual_seed(100 + rank)
+        losses = []
+        for _ in range(3):
+            x = torch.randint(0, 1024, (4, 256), generator=g, dtype=torch.int32).cuda()
+            y = torch.randint(0, 1024, (4, 256), generator=g, dtype=torch.int32).cuda()
+            losses.append(float(tr.train_step((x, y))))
+        out[comm] = (losses, {n: p.detach().float().cpu() for n, p in tr.model.named().items()})
+        tr.destroy()
+    return out
+
+
+def test_p2p_trainer_matches_nccl_2gpu():
+    res = _run(_train)
+    for r in range(2):
+        ln, pn = res[r]["nccl"]
+        lp, pp = res[r]["p2p"]
+        for a, b in zip(ln, lp):
+            assert abs(a - b) < 2e-3 * abs(a)
+        for n in pn:
+            d = (pn[n] - pp[n]).abs().max().item()
+            assert d < 5e-3 * (pn[n].abs().max().item() + 1e-6), n
+    for n in res[0]["p2p"][1]:
+        assert torch.equal(res[0]["p2p"][1][n], res[1]["p2p"][1][n]), n  # ranks hold identical replicas

@@ -186,7 +186,7 @@ def _attn_ref(q, k, v, window):
 
 
 @pytest.mark.parametrize("B,T,H,KV,window", [(2, 256, 4, 4, 256), (1, 300, 4, 2, 100), (2, 512, 2, 2, 128),
-                                             (1, 193, 2, 1, 1000)])
+                                             (1, 193, 2, 1, 1000), (2, 1024, 2, 1, 300), (1, 2048, 2, 2, 1024)])
 def test_attention_fwd_bwd(cuda, B, T, H, KV, window):
     E = _ext()
     torch.manual_seed(3)
@@ -198,12 +198,22 @@ def test_attention_fwd_bwd(cuda, B, T, H, KV, window):
     o = torch.empty(M, D, device=cuda, dtype=torch.bfloat16)
     lse = torch.empty(B, H, T, device=cuda)
     E.attn_fwd(q, k, v, o, lse, B, T, H, KV, hd, window)
+    if T % 128 == 0:
+        o_tc = torch.empty_like(o)
+        lse_tc = torch.empty_like(lse)
+        E.attn_fwd_tc(qkv, o_tc, lse_tc, B, T, H, KV, hd, window)
+        torch.cuda.synchronize()
+        from bitresearch_b200.ops._ext import check_status
+        assert check_status() == 0
     qr = q.float().view(B, T, H, hd).requires_grad_()
     kr = k.float().view(B, T, KV, hd).requires_grad_()
     vr = v.float().view(B, T, KV, hd).requires_grad_()
     ref, lse_ref = _attn_ref(qr, kr, vr, min(window, T))
     _assert(o, ref.reshape(M, D), 2e-2)
     _assert(lse, lse_ref, 1e-3)
+    if T % 128 == 0:
+        _assert(o_tc, ref.reshape(M, D), 2e-2)
+        _assert(lse_tc, lse_ref, 1e-3)
     do = torch.randn(M, D, device=cuda).to(torch.bfloat16)
     (ref.reshape(M, D) * do.float()).sum().backward()
     dqkv = torch.empty_like(qkv)
