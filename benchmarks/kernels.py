@@ -151,6 +151,11 @@ def main():
             ms = timeit(lambda: E.attn_bwd(q, k, v, o, do, lse, dqkv[:, :D], dqkv[:, D:2 * D], dqkv[:, 2 * D:], delta,
                                            delta, B, T, H, H, 128, window), reps=5)
             report(f"attn_bwd w={window} (2.5x fwd FLOPs)", ms, flops=2.5 * f_fwd)
+            o2 = torch.empty(M, D, **bf)
+            ms = timeit(lambda: E.attn_fwd_tc(qkv, o2, lse, B, T, H, H, 128, window), reps=5)
+            report(f"attn_fwd_tc w={window}", ms, flops=f_fwd, lib=lib)
+            ms = timeit(lambda: E.attn_bwd_tc(qkv, o2, do, lse, dqkv, delta, B, T, H, H, 128, window), reps=5)
+            report(f"attn_bwd_tc w={window} (2.5x fwd FLOPs)", ms, flops=2.5 * f_fwd)
 
     # ------------------------------------------------------------------ row kernels
     if want("rows"):

@@ -185,9 +185,12 @@ class FusedGPTEngine:
             gemm.matmul(b["o"][i].t(), b["dmid_b"], out=G[f"layer{i}_proj"], epi=A, k_splits=0)
             gemm.matmul(b["dmid_b"], self.shadows[f"layer{i}_proj"].t(), out=b["do"])
             qkv, dqkv = b["qkv"][i], b["dqkv"]
-            E.attn_bwd(qkv[:, :Dq], qkv[:, Dq:Dq + Dkv], qkv[:, Dq + Dkv:], b["o"][i], b["do"], b["lse"][i],
-                       dqkv[:, :Dq], dqkv[:, Dq:Dq + Dkv], dqkv[:, Dq + Dkv:], b["delta"], b["delta"], B, T, H, KV, hd,
-                       self.windows[i])
+            if self.tc_attention:
+                E.attn_bwd_tc(qkv, b["o"][i], b["do"], b["lse"][i], dqkv, b["delta"], B, T, H, KV, hd, self.windows[i])
+            else:
+                E.attn_bwd(qkv[:, :Dq], qkv[:, Dq:Dq + Dkv], qkv[:, Dq + Dkv:], b["o"][i], b["do"], b["lse"][i],
+                           dqkv[:, :Dq], dqkv[:, Dq:Dq + Dkv], dqkv[:, Dq + Dkv:], b["delta"], b["delta"], B, T, H, KV,
+                           hd, self.windows[i])
             ve = i in b["gate"]
             if ve:
                 E.rope_bwd(dqkv, qkv, T, H, KV, hd, self.cos, self.sin, b["rq"][i], b["rk"][i], idx, P[f"ve_{i}"],

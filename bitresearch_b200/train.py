@@ -231,6 +231,10 @@ class Trainer:
             self.metrics.step += 1
             return loss_t
         loss = float(loss_t)  # device -> host read of the step result
+        if self.engine is not None:
+            st = self.engine.status()
+            if st:
+                raise RuntimeError(f"a kernel gave up a bounded wait (status {st}) at step {self.metrics.step}")
         if not math.isfinite(loss):
             self.log(f"non-finite loss at step {self.metrics.step}")
         self._update_metrics(loss, t0, t_compute, ok)

@@ -518,6 +518,17 @@ void attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void attn_delta(const torch::Tensor& o, const torch::Tensor& dout, torch::Tensor& delta, int64_t B, int64_t T,
+                int64_t H) {
+  const int64_t tasks = B * T * H;
+  attn_delta_kernel<<<(unsigned)std::min<int64_t>((tasks + 7) / 8, 148 * 16), 256, 0,
+                      at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), o.stride(0),
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0), delta.data_ptr<float>(), (int)B, (int)T,
+      (int)H);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // dq, dk, dv: column slices like q, k, v (may live in one fused [B*T, 3D] buffer).
 void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& o,
               const torch::Tensor& dout, const torch::Tensor& lse, torch::Tensor& dq, torch::Tensor& dk,

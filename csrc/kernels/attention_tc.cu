@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(192, 1)
   const int kb_hi = min(q0 + BQ - 1, p.T - 1) / BKV;
   const int nkv = kb_hi - kb_lo + 1;
   const int warp = warp_id();
+  if (device_failed(p.status)) return;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -111,7 +112,7 @@ __global__ void __launch_bounds__(192, 1)
       tma_load_3d(&tm, q_full, smem + SM_Q + ATOM_BYTES, h * HD + 64, q0, b);
       for (int j = 0; j < nkv; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, kBudgetNs, abort_flag)) {
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
           fail(kErrTimeoutProducer);
           break;
         }
@@ -132,10 +133,10 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t idesc_o = umma_idesc_bf16(128, 128, false, true);
       const uint32_t q_addr = smem_u32(smem + SM_Q);
       const uint32_t p_addr = smem_u32(smem + SM_P);
-      bool ok = mbar_wait(q_full, 0, kBudgetNs, abort_flag);
+      bool ok = mbar_wait(q_full, 0, kBudgetNs, abort_flag, p.status);
       auto issue_s = [&](int j) -> bool {
         const int st = j & 1;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1, kBudgetNs, abort_flag)) return false;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) return false;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + SM_K + st * TILE_BYTES);
 #pragma unroll
@@ -154,8 +155,8 @@ __global__ void __launch_bounds__(192, 1)
           break;
         }
         const int st = j & 1;
-        if (!mbar_wait(p_full, j & 1, kBudgetNs, abort_flag) ||
-            !mbar_wait(&v_full[st], (j >> 1) & 1, kBudgetNs, abort_flag)) {
+        if (!mbar_wait(p_full, j & 1, kBudgetNs, abort_flag, p.status) ||
+            !mbar_wait(&v_full[st], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
           ok = false;
           break;
         }
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__(192, 1)
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int st = j & 1;
-      if (!mbar_wait(&s_full[st], (j >> 1) & 1, kBudgetNs, abort_flag)) {
+      if (!mbar_wait_warp(&s_full[st], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
         break;
@@ -209,17 +210,25 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       // PV_{j-1} must be complete before P is overwritten or O is rescaled
-      if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, kBudgetNs, abort_flag)) {
+      if (j > 0 && !mbar_wait_warp(o_done, (j - 1) & 1, kBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
         break;
       }
       tc_fence_after();
+      // The rescale decision is per row, but tcgen05.ld/st are warp-collective: the warp rescales
+      // together whenever any of its rows needs it, rows that do not use alpha = 1.
+      float alpha = 1.f;
+      bool mine = false;
       if (j == 0) {
         m_ref = mx;
       } else if (mx > m_ref + 8.f) {
-        const float alpha = m_ref == -INFINITY ? 0.f : exp2f(m_ref - mx);
+        mine = true;
+        alpha = m_ref == -INFINITY ? 0.f : exp2f(m_ref - mx);
         l *= alpha;
+        m_ref = mx;
+      }
+      if (__any_sync(0xffffffffu, mine)) {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t v[32];
@@ -230,7 +239,6 @@ __global__ void __launch_bounds__(192, 1)
           tmem_st32(lane_base + 256 + c * 32, v);
         }
         tmem_st_wait();
-        m_ref = mx;
       }
       // pass 2: P = exp2(s - m_ref) -> bf16 into the swizzled K-major P tile
       const bool live = m_ref != -INFINITY;
@@ -263,7 +271,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    if (ok && mbar_wait(o_done, (nkv - 1) & 1, kBudgetNs, abort_flag)) {
+    if (ok && mbar_wait_warp(o_done, (nkv - 1) & 1, kBudgetNs, abort_flag, p.status)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = p.out + ((int64_t)b * p.T + qi) * p.ldo + h * HD;
@@ -285,6 +293,448 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       if (qi < p.T) p.lse[((int64_t)b * p.H + h) * p.T + qi] = (m_ref + __log2f(l)) / kLog2e;
+    } else if (ok) {
+      fail(kErrTimeoutEpilogue);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+
+// ------------------------------------------------------------------------------------------- backward
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+struct BwdParams {
+  int T, H, KV, Dq, Dkv, window;
+  float scale_log2, scale;
+  const float* lse;
+  const float* delta;
+  __nv_bfloat16* dq;
+  int64_t lddq;
+  __nv_bfloat16* dk;
+  int64_t lddk;
+  __nv_bfloat16* dv;
+  int64_t lddv;
+  int* status;
+};
+
+// ---- dQ: one CTA per (128 queries, head, batch); S, dP, dQ in TMEM columns [0,128), [128,256), [256,384)
+constexpr int DQ_Q = 0;
+constexpr int DQ_DO = DQ_Q + TILE_BYTES;
+constexpr int DQ_K = DQ_DO + TILE_BYTES;
+constexpr int DQ_V = DQ_K + 2 * TILE_BYTES;
+constexpr int DQ_DS = DQ_V + 2 * TILE_BYTES;
+constexpr int DQ_BAR = DQ_DS + TILE_BYTES;
+constexpr int DQ_SMEM = DQ_BAR + 256 + 1024;
+
+__global__ void __launch_bounds__(192, 1)
+    attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                      BwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DQ_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (p.H / p.KV);
+  const int q0 = qb * BQ;
+  const int w = p.window;
+  const int kb_lo = max(0, q0 - w + 1) / BKV;
+  const int kb_hi = min(q0 + BQ - 1, p.T - 1) / BKV;
+  const int nkv = kb_hi - kb_lo + 1;
+  const int warp = warp_id();
+  if (device_failed(p.status)) return;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&](int code) {
+    *abort_flag = 1;
+    if (p.status) atomicCAS(p.status, 0, code);
+  };
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+      tma_load_3d(&tm_qkv, q_full, smem + DQ_Q, h * HD, q0, b);
+      tma_load_3d(&tm_qkv, q_full, smem + DQ_Q + ATOM_BYTES, h * HD + 64, q0, b);
+      tma_load_3d(&tm_do, q_full, smem + DQ_DO, h * HD, q0, b);
+      tma_load_3d(&tm_do, q_full, smem + DQ_DO + ATOM_BYTES, h * HD + 64, q0, b);
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
+          fail(kErrTimeoutProducer);
+          break;
+        }
+        const int k0 = (kb_lo + j) * BKV;
+        uint8_t* ks = smem + DQ_K + st * TILE_BYTES;
+        uint8_t* vs = smem + DQ_V + st * TILE_BYTES;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        tma_load_3d(&tm_qkv, &kv_full[st], ks, p.Dq + kvh * HD, k0, b);
+        tma_load_3d(&tm_qkv, &kv_full[st], ks + ATOM_BYTES, p.Dq + kvh * HD + 64, k0, b);
+        tma_load_3d(&tm_qkv, &kv_full[st], vs, p.Dq + p.Dkv + kvh * HD, k0, b);
+        tma_load_3d(&tm_qkv, &kv_full[st], vs + ATOM_BYTES, p.Dq + p.Dkv + kvh * HD + 64, k0, b);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_kk = umma_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t idesc_kmn = umma_idesc_bf16(128, 128, false, true);
+      const uint32_t q_addr = smem_u32(smem + DQ_Q), do_addr = smem_u32(smem + DQ_DO);
+      const uint32_t ds_addr = smem_u32(smem + DQ_DS);
+      bool ok = mbar_wait(q_full, 0, kBudgetNs, abort_flag, p.status);
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + DQ_K + st * TILE_BYTES);
+        const uint32_t v_addr = smem_u32(smem + DQ_V + st * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
+          umma_bf16_ss(tmem, umma_desc_sw128(q_addr + off, 16, 1024), umma_desc_sw128(k_addr + off, 16, 1024),
+                       idesc_kk, kk > 0 ? 1u : 0u);
+          umma_bf16_ss(tmem + 128, umma_desc_sw128(do_addr + off, 16, 1024), umma_desc_sw128(v_addr + off, 16, 1024),
+                       idesc_kk, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, j & 1, kBudgetNs, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(ds_addr + (kk >> 2) * ATOM_BYTES + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = umma_desc_sw128(k_addr + kk * 2048, ATOM_BYTES, 1024);
+          umma_bf16_ss(tmem + 256, ad, bd, idesc_kmn, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&kv_empty[st]);
+      }
+      if (!ok) fail(kErrTimeoutMma);
+      umma_commit(done);
+      mbar_wait(done, 0, kBudgetNs, nullptr);
+    }
+  } else {
+    const int wq = warp & 3, lane = lane_id();
+    const int r = wq * 32 + lane;
+    const int qi = q0 + r;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+    uint8_t* drow = smem + DQ_DS + r * 128;
+    const int qc = min(qi, p.T - 1);
+    const float lse2 = p.lse[((int64_t)b * p.H + h) * p.T + qc] * kLog2e;
+    const float dl = p.delta[((int64_t)b * p.H + h) * p.T + qc];
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      if (!mbar_wait_warp(s_full, j & 1, kBudgetNs, abort_flag, p.status)) {
+        fail(kErrTimeoutEpilogue);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int k0 = (kb_lo + j) * BKV;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(lane_base + c * 32, sv);
+        tmem_ld32(lane_base + 128 + c * 32, dv);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int kj = k0 + c * 32 + i;
+          const bool v0 = kj <= qi && kj > qi - w && kj < p.T;
+          const bool v1 = kj + 1 <= qi && kj + 1 > qi - w && kj + 1 < p.T;
+          const float p0 = v0 ? exp2f(__uint_as_float(sv[i]) * p.scale_log2 - lse2) : 0.f;
+          const float p1 = v1 ? exp2f(__uint_as_float(sv[i + 1]) * p.scale_log2 - lse2) : 0.f;
+          pk[i / 2] = pack_bf16(p0 * (__uint_as_float(dv[i]) - dl), p1 * (__uint_as_float(dv[i + 1]) - dl));
+        }
+        uint8_t* atom = drow + (c >> 1) * ATOM_BYTES;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = (c & 1) * 4 + q;
+          *reinterpret_cast<uint4*>(atom + ((chunk ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait_warp(done, 0, kBudgetNs, abort_flag, p.status)) {
+      tc_fence_after();
+      __nv_bfloat16* row = p.dq + ((int64_t)b * p.T + qi) * p.lddq + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(lane_base + 256 + c * 32, v);
+        tmem_ld_wait();
+        if (qi < p.T) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 o;
+            o.x = pack_bf16(__uint_as_float(v[8 * q + 0]) * p.scale, __uint_as_float(v[8 * q + 1]) * p.scale);
+            o.y = pack_bf16(__uint_as_float(v[8 * q + 2]) * p.scale, __uint_as_float(v[8 * q + 3]) * p.scale);
+            o.z = pack_bf16(__uint_as_float(v[8 * q + 4]) * p.scale, __uint_as_float(v[8 * q + 5]) * p.scale);
+            o.w = pack_bf16(__uint_as_float(v[8 * q + 6]) * p.scale, __uint_as_float(v[8 * q + 7]) * p.scale);
+            *reinterpret_cast<uint4*>(row + c * 32 + q * 8) = o;
+          }
+        }
+      }
+    } else if (ok) {
+      fail(kErrTimeoutEpilogue);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---- dK, dV: one CTA per (128 keys, kv head, batch), 64-query blocks;
+// TMEM: S^T [0,64), dP^T [64,128), dV [128,256), dK [256,384)
+constexpr int KB_Q = 64;
+constexpr int HALF_TILE = 64 * 128 * 2;   // 64 rows x 128 hd, two 8 KB swizzle atoms
+constexpr int HALF_ATOM = 64 * 128;
+constexpr int DK_K = 0;
+constexpr int DK_V = DK_K + TILE_BYTES;
+constexpr int DK_Q = DK_V + TILE_BYTES;            // [2] x HALF_TILE
+constexpr int DK_DO = DK_Q + 2 * HALF_TILE;        // [2] x HALF_TILE
+constexpr int DK_PT = DK_DO + 2 * HALF_TILE;       // 128 keys x 64 q bf16 (one 16 KB atom)
+constexpr int DK_DST = DK_PT + 128 * 128;
+constexpr int DK_STAT = DK_DST + 128 * 128;        // [2] x (lse[64], delta[64]) floats
+constexpr int DK_BAR = DK_STAT + 2 * 512;
+constexpr int DK_SMEM = DK_BAR + 256 + 1024;
+
+__global__ void __launch_bounds__(192, 1)
+    attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                        BwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DK_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qd_full = bars + 1;   // [2]
+  uint64_t* qd_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* stat = reinterpret_cast<float*>(smem + DK_STAT);
+
+  const int kb = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int group = p.H / p.KV;
+  const int k0 = kb * BKV;
+  const int w = p.window;
+  const int qb_lo = k0 / KB_Q;
+  const int qb_hi = min(p.T - 1, k0 + BKV - 1 + w - 1) / KB_Q;
+  const int nq = qb_hi - qb_lo + 1;
+  const int iters = nq * group;
+  const int warp = warp_id();
+  if (device_failed(p.status)) return;
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&](int code) {
+    *abort_flag = 1;
+    if (p.status) atomicCAS(p.status, 0, code);
+  };
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+      tma_load_3d(&tm_qkv, kv_full, smem + DK_K, p.Dq + kvh * HD, k0, b);
+      tma_load_3d(&tm_qkv, kv_full, smem + DK_K + ATOM_BYTES, p.Dq + kvh * HD + 64, k0, b);
+      tma_load_3d(&tm_qkv, kv_full, smem + DK_V, p.Dq + p.Dkv + kvh * HD, k0, b);
+      tma_load_3d(&tm_qkv, kv_full, smem + DK_V + ATOM_BYTES, p.Dq + p.Dkv + kvh * HD + 64, k0, b);
+      for (int it = 0; it < iters; ++it) {
+        const int st = it & 1;
+        if (!mbar_wait(&qd_empty[st], ((it >> 1) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
+          fail(kErrTimeoutProducer);
+          break;
+        }
+        const int h = kvh * group + it / nq;
+        const int q0 = (qb_lo + it % nq) * KB_Q;
+        uint8_t* qs = smem + DK_Q + st * HALF_TILE;
+        uint8_t* ds = smem + DK_DO + st * HALF_TILE;
+        float* ls = stat + st * 128;
+        const int64_t srow = ((int64_t)b * p.H + h) * p.T + q0;
+        mbar_arrive_expect_tx(&qd_full[st], 2 * HALF_TILE + 512);
+        tma_load_3d(&tm_qkv, &qd_full[st], qs, h * HD, q0, b);
+        tma_load_3d(&tm_qkv, &qd_full[st], qs + HALF_ATOM, h * HD + 64, q0, b);
+        tma_load_3d(&tm_do, &qd_full[st], ds, h * HD, q0, b);
+        tma_load_3d(&tm_do, &qd_full[st], ds + HALF_ATOM, h * HD + 64, q0, b);
+        bulk_load(ls, p.lse + srow, 256, &qd_full[st]);
+        bulk_load(ls + 64, p.delta + srow, 256, &qd_full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(128, 64, false, false);
+      constexpr uint32_t idesc_g = umma_idesc_bf16(128, 128, false, true);
+      const uint32_t k_addr = smem_u32(smem + DK_K), v_addr = smem_u32(smem + DK_V);
+      const uint32_t pt_addr = smem_u32(smem + DK_PT), dst_addr = smem_u32(smem + DK_DST);
+      bool ok = mbar_wait(kv_full, 0, kBudgetNs, abort_flag, p.status);
+      for (int it = 0; it < iters && ok; ++it) {
+        const int st = it & 1;
+        if (!mbar_wait(&qd_full[st], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(smem + DK_Q + st * HALF_TILE);
+        const uint32_t do_addr = smem_u32(smem + DK_DO + st * HALF_TILE);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t offa = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
+          const uint32_t offb = (kk >> 2) * HALF_ATOM + (kk & 3) * 32;
+          umma_bf16_ss(tmem, umma_desc_sw128(k_addr + offa, 16, 1024), umma_desc_sw128(q_addr + offb, 16, 1024),
+                       idesc_s, kk > 0 ? 1u : 0u);
+          umma_bf16_ss(tmem + 64, umma_desc_sw128(v_addr + offa, 16, 1024), umma_desc_sw128(do_addr + offb, 16, 1024),
+                       idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, it & 1, kBudgetNs, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < KB_Q / 16; ++kk) {
+          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+          umma_bf16_ss(tmem + 128, umma_desc_sw128(pt_addr + kk * 32, 16, 1024),
+                       umma_desc_sw128(do_addr + kk * 2048, HALF_ATOM, 1024), idesc_g, acc);
+          umma_bf16_ss(tmem + 256, umma_desc_sw128(dst_addr + kk * 32, 16, 1024),
+                       umma_desc_sw128(q_addr + kk * 2048, HALF_ATOM, 1024), idesc_g, acc);
+        }
+        umma_commit(&qd_empty[st]);
+      }
+      if (!ok) fail(kErrTimeoutMma);
+      umma_commit(done);
+      mbar_wait(done, 0, kBudgetNs, nullptr);
+    }
+  } else {
+    const int wq = warp & 3, lane = lane_id();
+    const int r = wq * 32 + lane;
+    const int kj = k0 + r;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+    uint8_t* prow = smem + DK_PT + r * 128;
+    uint8_t* srow = smem + DK_DST + r * 128;
+    bool ok = true;
+    for (int it = 0; it < iters; ++it) {
+      const int st = it & 1;
+      if (!mbar_wait_warp(s_full, it & 1, kBudgetNs, abort_flag, p.status)) {
+        fail(kErrTimeoutEpilogue);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int q0 = (qb_lo + it % nq) * KB_Q;
+      const float* ls = stat + st * 128;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(lane_base + c * 32, sv);
+        tmem_ld32(lane_base + 64 + c * 32, dv);
+        tmem_ld_wait();
+        uint32_t pp[16], ss[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int qa = q0 + c * 32 + i;
+          const bool v0 = kj <= qa && kj > qa - w && qa < p.T && kj < p.T;
+          const bool v1 = kj <= qa + 1 && kj > qa + 1 - w && qa + 1 < p.T && kj < p.T;
+          const float p0 = v0 ? exp2f(__uint_as_float(sv[i]) * p.scale_log2 - ls[c * 32 + i] * kLog2e) : 0.f;
+          const float p1 = v1 ? exp2f(__uint_as_float(sv[i + 1]) * p.scale_log2 - ls[c * 32 + i + 1] * kLog2e) : 0.f;
+          pp[i / 2] = pack_bf16(p0, p1);
+          ss[i / 2] = pack_bf16(p0 * (__uint_as_float(dv[i]) - ls[64 + c * 32 + i]),
+                                p1 * (__uint_as_float(dv[i + 1]) - ls[64 + c * 32 + i + 1]));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = c * 4 + q;
+          const int phys = (chunk ^ (r & 7)) << 4;
+          *reinterpret_cast<uint4*>(prow + phys) = make_uint4(pp[4 * q], pp[4 * q + 1], pp[4 * q + 2], pp[4 * q + 3]);
+          *reinterpret_cast<uint4*>(srow + phys) = make_uint4(ss[4 * q], ss[4 * q + 1], ss[4 * q + 2], ss[4 * q + 3]);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait_warp(done, 0, kBudgetNs, abort_flag, p.status)) {
+      tc_fence_after();
+      __nv_bfloat16* vrow = p.dv + ((int64_t)b * p.T + kj) * p.lddv + kvh * HD;
+      __nv_bfloat16* krow = p.dk + ((int64_t)b * p.T + kj) * p.lddk + kvh * HD;
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        uint32_t v[32];
+        const bool isk = c >= 4;
+        const int cc = c & 3;
+        tmem_ld32(lane_base + (isk ? 256 : 128) + cc * 32, v);
+        tmem_ld_wait();
+        const float sc = isk ? p.scale : 1.f;
+        __nv_bfloat16* row = isk ? krow : vrow;
+        if (kj < p.T) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 o;
+            o.x = pack_bf16(__uint_as_float(v[8 * q + 0]) * sc, __uint_as_float(v[8 * q + 1]) * sc);
+            o.y = pack_bf16(__uint_as_float(v[8 * q + 2]) * sc, __uint_as_float(v[8 * q + 3]) * sc);
+            o.z = pack_bf16(__uint_as_float(v[8 * q + 4]) * sc, __uint_as_float(v[8 * q + 5]) * sc);
+            o.w = pack_bf16(__uint_as_float(v[8 * q + 6]) * sc, __uint_as_float(v[8 * q + 7]) * sc);
+            *reinterpret_cast<uint4*>(row + cc * 32 + q * 8) = o;
+          }
+        }
+      }
     } else if (ok) {
       fail(kErrTimeoutEpilogue);
     }
@@ -332,4 +782,60 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+}  // namespace br
+
+namespace br {
+void attn_delta(const torch::Tensor& o, const torch::Tensor& dout, torch::Tensor& delta, int64_t B, int64_t T,
+                int64_t H);
+
+// dqkv: [B*T, Dq + 2*Dkv] bf16 output (dq | dk | dv); dout: [B*T, H*hd] bf16; lse, delta: fp32 [B, H, T].
+void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::Tensor& dout, const torch::Tensor& lse,
+                 torch::Tensor& dqkv, torch::Tensor& delta, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd,
+                 int64_t window) {
+  TORCH_CHECK(hd == HD && T % 128 == 0, "attn_bwd_tc: head_dim 128 and T % 128 == 0");
+  const int64_t W = qkv.size(1);
+  TORCH_CHECK(W == (H + 2 * KV) * hd && dqkv.size(1) == W, "attn_bwd_tc: widths");
+  TORCH_CHECK(dout.stride(1) == 1 && dout.size(1) == H * hd, "attn_bwd_tc: dout");
+  c10::cuda::CUDAGuard g(qkv.device());
+  attn_delta(o, dout, delta, B, T, H);
+  CUtensorMap tq = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.data_ptr(), W, T, B, qkv.stride(0),
+                              qkv.stride(0) * T, 64, 128);
+  CUtensorMap td = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dout.data_ptr(), H * hd, T, B, dout.stride(0),
+                              dout.stride(0) * T, 64, 128);
+  // the dK/dV kernel loads 64-query tiles of Q and dO
+  CUtensorMap tq64 = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.data_ptr(), W, T, B, qkv.stride(0),
+                                qkv.stride(0) * T, 64, 64);
+  CUtensorMap td64 = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dout.data_ptr(), H * hd, T, B, dout.stride(0),
+                                dout.stride(0) * T, 64, 64);
+  BwdParams p;
+  p.T = (int)T;
+  p.H = (int)H;
+  p.KV = (int)KV;
+  p.Dq = (int)(H * hd);
+  p.Dkv = (int)(KV * hd);
+  p.window = (int)std::min<int64_t>(window <= 0 ? T : window, T);
+  p.scale = 1.f / sqrtf((float)hd);
+  p.scale_log2 = kLog2e * p.scale;
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  auto* base = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  p.dq = base;
+  p.lddq = dqkv.stride(0);
+  p.dk = base + H * hd;
+  p.lddk = dqkv.stride(0);
+  p.dv = base + (H + KV) * hd;
+  p.lddv = dqkv.stride(0);
+  p.status = status_ptr(qkv.device().index());
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DK_SMEM));
+    attr = true;
+  }
+  auto st = at::cuda::getCurrentCUDAStream();
+  attn_dq_tc_kernel<<<dim3((unsigned)(T / BQ), (unsigned)H, (unsigned)B), 192, DQ_SMEM, st>>>(tq, td, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  attn_dkdv_tc_kernel<<<dim3((unsigned)(T / BKV), (unsigned)KV, (unsigned)B), 192, DK_SMEM, st>>>(tq64, td64, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 }  // namespace br

@@ -51,6 +51,9 @@ void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
               int64_t KV, int64_t hd, int64_t window);
 void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int64_t B, int64_t T, int64_t H,
                  int64_t KV, int64_t hd, int64_t window);
+void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::Tensor& dout, const torch::Tensor& lse,
+                 torch::Tensor& dqkv, torch::Tensor& delta, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd,
+                 int64_t window);
 std::tuple<int64_t, torch::Tensor> sym_alloc(int64_t bytes);
 int64_t sym_open(const torch::Tensor& handle);
 void sym_close(int64_t ptr);
@@ -88,6 +91,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &br::attn_fwd);
   m.def("attn_bwd", &br::attn_bwd);
   m.def("attn_fwd_tc", &br::attn_fwd_tc);
+  m.def("attn_bwd_tc", &br::attn_bwd_tc);
   m.def("sym_alloc", &br::sym_alloc);
   m.def("sym_open", &br::sym_open);
   m.def("sym_close", &br::sym_close);

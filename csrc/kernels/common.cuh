@@ -72,17 +72,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait on a phase parity. Returns false once `budget_ns` has elapsed (or when another role
 // of the CTA already flagged an error through `abort_flag`).
+// `gstatus` is the device-wide status word: once any CTA has recorded a failure, every other wait
+// gives up at its next check instead of spending its own budget.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t budget_ns,
-                                          volatile int* abort_flag) {
+                                          volatile int* abort_flag, const volatile int* gstatus = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (abort_flag && *abort_flag) return false;
+      if (gstatus && *gstatus) return false;
       if (globaltimer_ns() - t0 > budget_ns) return false;
     }
   }
+}
+
+// Warp-uniform bounded wait for code paths that issue warp-collective tcgen05.ld/st afterwards: every
+// lane waits, and the result is true only if all lanes succeeded, so a timeout never splits the warp.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, uint64_t budget_ns,
+                                               volatile int* abort_flag, const volatile int* gstatus = nullptr) {
+  const bool ok = mbar_wait(bar, parity, budget_ns, abort_flag, gstatus);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// True when an earlier kernel already recorded a failure: the caller returns before allocating anything.
+__device__ __forceinline__ bool device_failed(const int* status) {
+  return status != nullptr && *reinterpret_cast<const volatile int*>(status) != 0;
 }
 
 // ----------------------------------------------------------------------------------- TMA
@@ -208,6 +224,13 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
   __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
   return __bfloat1622float2(v);
+}
+
+// hardware tanh (max relative error about 2^-11; outputs here are rounded to bf16)
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -9,21 +9,27 @@
 //           STAGES-deep ring of shared-memory stages guarded by full/empty mbarriers;
 //   warp 1  allocates TMEM (two BN-column fp32 accumulators) and one elected lane issues
 //           tcgen05.mma (M=128, N=BN, K=16) and tcgen05.commit;
-//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM lanes 32*(w%4)..),
-//           applies the fused epilogue and stores; the accumulator is released to the MMA warp
-//           through tmem_empty so the next tile's main loop overlaps this epilogue.
+//   warps 2-5  epilogue. Warp w owns TMEM lanes / tile rows 32*(w%4) .. +31. Per chunk of 128 bytes
+//           of output row (64 bf16 or 32 fp32 columns) it reads the accumulator with tcgen05.ld,
+//           applies the fused epilogue, writes the 32 x 128 B chunk into a double-buffered, 128-byte
+//           swizzled staging tile in shared memory and issues one TMA store (or TMA reduce-add for
+//           split-K) for it. Auxiliary inputs (residual, saved activation) arrive by TMA load into
+//           the same staging tile. TMA bounds-checks the M/N edges. The accumulator is released to
+//           the MMA warp after the last tcgen05.ld of a tile, so the next tile's main loop overlaps
+//           the remaining stores.
 // Work units are (k-split, n-tile, m-tile, batch) with n fastest so CTAs running at the same time
-// share A rows through L2. With k_splits > 1 each unit accumulates its fp32 partial into C with
-// vector reductions (used for weight gradients, whose reduction dimension is the token count).
+// share A rows through L2. With k_splits > 1 each unit reduce-adds its fp32 partial into C (weight
+// gradients, whose reduction dimension is the token count).
 //
 // All mbarrier waits are bounded (2 s); on timeout the kernel records a status code, drains its
-// in-flight TMA loads and MMAs, frees TMEM and returns.
+// in-flight TMA loads, MMAs and stores, frees TMEM and returns.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
 #include "status.h"
+#include "tma_host.h"
 
 namespace br {
 
@@ -32,7 +38,7 @@ enum GemmEpi : int {
   EPI_F32 = 1,         // C(f32)  = alpha*acc + beta*aux(f32, optional; may alias C)
   EPI_RELU2 = 2,       // C(bf16) = relu(alpha*acc)^2
   EPI_RELU2_BWD = 3,   // C(bf16) = alpha*acc * 2*sqrt(aux(bf16))   (d/du of relu(u)^2 given h = relu(u)^2)
-  EPI_ATOMIC_F32 = 4,  // C(f32) += alpha*acc
+  EPI_ATOMIC_F32 = 4,  // C(f32) += alpha*acc                       (TMA reduce-add)
   EPI_SOFTCAP = 5,     // C(bf16) = beta*tanh(alpha*acc)             (alpha = 1/cap, beta = cap)
 };
 
@@ -40,16 +46,14 @@ struct GemmParams {
   int M, N, K, batch;
   int k_splits, kb_per_split;
   int m_tiles, n_tiles, k_blocks;
-  void* C;
-  int64_t ldc, bsc;
-  const void* aux;
-  int64_t ld_aux, bs_aux;
+  int has_aux;
   float alpha, beta;
   int* status;
 };
 
 constexpr int BM = 128;
 constexpr int BK = 64;
+constexpr int CHUNK_BYTES = 32 * 128;  // one epilogue warp's 32 rows x 128 bytes
 constexpr uint64_t kWaitBudgetNs = 2000000000ull;
 
 template <int BN>
@@ -59,8 +63,12 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int EPI_BYTES = 4 * 2 * CHUNK_BYTES;  // 4 warps x 2 buffers
+  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 256 /*barriers*/ + 1024 /*align*/;
 };
+
+constexpr bool epi_f32(int e) { return e == EPI_F32 || e == EPI_ATOMIC_F32; }
+constexpr bool epi_reads_aux(int e) { return e == EPI_BF16 || e == EPI_F32 || e == EPI_RELU2_BWD; }
 
 __device__ __forceinline__ void decode_unit(const GemmParams& p, int u, int& m, int& n, int& b, int& kb0, int& kb1) {
   int s = u % p.k_splits;
@@ -73,129 +81,68 @@ __device__ __forceinline__ void decode_unit(const GemmParams& p, int u, int& m, 
   kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
 }
 
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* m, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled staging tile.
+__device__ __forceinline__ int swz_off(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+// Epilogue math on 8 values (one 16-byte bf16 chunk or two fp32 chunks), aux values already unpacked.
 template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int b, int row, int col0, uint32_t (&r)[32]) {
-  if (row >= p.M) return;
-  const bool full = col0 + 32 <= p.N;
-  float v[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
-  if constexpr (EPI == EPI_BF16 || EPI == EPI_RELU2 || EPI == EPI_RELU2_BWD || EPI == EPI_SOFTCAP) {
-    __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C) + (int64_t)b * p.bsc + (int64_t)row * p.ldc + col0;
-    const __nv_bfloat16* X = p.aux ? reinterpret_cast<const __nv_bfloat16*>(p.aux) + (int64_t)b * p.bs_aux +
-                                         (int64_t)row * p.ld_aux + col0
-                                   : nullptr;
-    if (full) {
-      if constexpr (EPI == EPI_BF16 || EPI == EPI_RELU2_BWD) {
-        if (X) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 xv = *reinterpret_cast<const uint4*>(X + q * 8);
-            uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float2 f = unpack_bf16(xs[j]);
-              if constexpr (EPI == EPI_BF16) {
-                v[q * 8 + 2 * j] += p.beta * f.x;
-                v[q * 8 + 2 * j + 1] += p.beta * f.y;
-              } else {
-                v[q * 8 + 2 * j] *= 2.f * sqrtf(fmaxf(f.x, 0.f));
-                v[q * 8 + 2 * j + 1] *= 2.f * sqrtf(fmaxf(f.y, 0.f));
-              }
-            }
-          }
-        }
-      }
-      if constexpr (EPI == EPI_RELU2) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float t = fmaxf(v[i], 0.f);
-          v[i] = t * t;
-        }
-      }
-      if constexpr (EPI == EPI_SOFTCAP) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = p.beta * tanhf(v[i]);
-      }
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 o;
-        o.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
-        o.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
-        o.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
-        o.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
-        *reinterpret_cast<uint4*>(C + q * 8) = o;
-      }
-    } else {
-      for (int i = 0; i < 32 && col0 + i < p.N; ++i) {
-        float x = v[i];
-        if constexpr (EPI == EPI_BF16) {
-          if (X) x += p.beta * __bfloat162float(X[i]);
-        } else if constexpr (EPI == EPI_RELU2_BWD) {
-          x *= 2.f * sqrtf(fmaxf(__bfloat162float(X[i]), 0.f));
-        } else if constexpr (EPI == EPI_RELU2) {
-          x = fmaxf(x, 0.f);
-          x = x * x;
-        } else {
-          x = p.beta * tanhf(x);
-        }
-        C[i] = __float2bfloat16(x);
-      }
-    }
-  } else {  // fp32 outputs
-    float* C = reinterpret_cast<float*>(p.C) + (int64_t)b * p.bsc + (int64_t)row * p.ldc + col0;
-    if constexpr (EPI == EPI_ATOMIC_F32) {
-      if (full) {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) red_add_v4_f32(C + q * 4, v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
-      } else {
-        for (int i = 0; i < 32 && col0 + i < p.N; ++i) atomicAdd(C + i, v[i]);
-      }
-    } else {
-      const float* X = p.aux ? reinterpret_cast<const float*>(p.aux) + (int64_t)b * p.bs_aux +
-                                   (int64_t)row * p.ld_aux + col0
-                             : nullptr;
-      if (full) {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 o = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
-          if (X) {
-            float4 x = *reinterpret_cast<const float4*>(X + q * 4);
-            o.x += p.beta * x.x;
-            o.y += p.beta * x.y;
-            o.z += p.beta * x.z;
-            o.w += p.beta * x.w;
-          }
-          *reinterpret_cast<float4*>(C + q * 4) = o;
-        }
-      } else {
-        for (int i = 0; i < 32 && col0 + i < p.N; ++i) C[i] = v[i] + (X ? p.beta * X[i] : 0.f);
-      }
-    }
+__device__ __forceinline__ float epi_op(float acc, float aux, const GemmParams& p) {
+  float v = acc * p.alpha;
+  if constexpr (EPI == EPI_BF16 || EPI == EPI_F32) {
+    v += p.beta * aux;
+  } else if constexpr (EPI == EPI_RELU2) {
+    v = fmaxf(v, 0.f);
+    v = v * v;
+  } else if constexpr (EPI == EPI_RELU2_BWD) {
+    v *= 2.f * sqrtf(fmaxf(aux, 0.f));
+  } else if constexpr (EPI == EPI_SOFTCAP) {
+    v = p.beta * tanh_approx(v);
   }
+  return v;
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(192, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, GemmParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint8_t* sE = smem + STAGES * Cfg::STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sE + Cfg::EPI_BYTES);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + STAGES;
   uint64_t* tfull_bar = bars + 2 * STAGES;
   uint64_t* tempty_bar = bars + 2 * STAGES + 2;
   uint64_t* drain_bar = bars + 2 * STAGES + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint64_t* aux_bar = bars + 2 * STAGES + 5;  // [4], one per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
   const int total = p.m_tiles * p.n_tiles * p.batch * p.k_splits;
 
+  if (device_failed(p.status)) return;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -206,6 +153,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&tempty_bar[a], 128);
     }
     mbar_init(drain_bar, 1);
+    for (int w = 0; w < 4; ++w) mbar_init(&aux_bar[w], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -232,7 +180,7 @@ __global__ void __launch_bounds__(192, 1)
         int m, n, b, kb0, kb1;
         decode_unit(p, u, m, n, b, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1, kWaitBudgetNs, abort_flag)) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, kWaitBudgetNs, abort_flag, p.status)) {
             fail(kErrTimeoutProducer);
             ok = false;
             break;
@@ -261,7 +209,6 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       if (!ok || *abort_flag) {
-        // wait (bounded) for the loads still in flight before the CTA's shared memory goes away
         int n_inflight = issued < STAGES ? issued : STAGES;
         int s = stage;
         uint32_t ph = phase;
@@ -286,14 +233,14 @@ __global__ void __launch_bounds__(192, 1)
         decode_unit(p, u, m, n, b, kb0, kb1);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, kWaitBudgetNs, abort_flag)) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, kWaitBudgetNs, abort_flag, p.status)) {
           fail(kErrTimeoutMma);
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, kWaitBudgetNs, abort_flag)) {
+          if (!mbar_wait(&full_bar[stage], phase, kWaitBudgetNs, abort_flag, p.status)) {
             fail(kErrTimeoutMma);
             ok = false;
             break;
@@ -317,37 +264,106 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (ok) umma_commit(&tfull_bar[acc]);
       }
-      // all MMAs issued by this thread have completed once drain_bar flips
       umma_commit(drain_bar);
       mbar_wait(drain_bar, 0, 100000000ull, nullptr);
     }
   } else {
-    // epilogue warps 2..5
+    // ---------------------------------------------------------------- epilogue warps 2..5
     const int wq = warp & 3;
     const int lane = lane_id();
+    const bool leader = lane == 0;
+    uint8_t* ebuf = sE + wq * 2 * CHUNK_BYTES;
+    uint64_t* xbar = &aux_bar[wq];
+    uint32_t xphase = 0;
+    int nchunk = 0;
+    constexpr int COLS = epi_f32(EPI) ? 32 : 64;  // columns per 128-byte chunk
     int local = 0;
+    if (leader) {
+      tma_prefetch_desc(&tmC);
+      if (p.has_aux) tma_prefetch_desc(&tmX);
+    }
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++local) {
       int m, n, b, kb0, kb1;
       decode_unit(p, u, m, n, b, kb0, kb1);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull_bar[acc], acc_phase, kWaitBudgetNs, abort_flag)) {
+      if (!mbar_wait_warp(&tfull_bar[acc], acc_phase, kWaitBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         break;
       }
       tc_fence_after();
-      const int row = m * BM + wq * 32 + lane;
+      const int row0 = m * BM + wq * 32;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * BN;
+      bool ok = true;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c * 32, r);
+      for (int c = 0; c < BN / COLS; ++c, ++nchunk) {
+        uint8_t* buf = ebuf + (nchunk & 1) * CHUNK_BYTES;
+        const int col0 = n * BN + c * COLS;
+        if (leader) bulk_wait_read1();  // the store that last used this buffer has read it
+        __syncwarp();
+        const bool use_aux = epi_reads_aux(EPI) && p.has_aux;
+        if (use_aux) {
+          if (leader) {
+            mbar_arrive_expect_tx(xbar, CHUNK_BYTES);
+            tma_load_3d(&tmX, xbar, buf, col0, row0, b);
+          }
+        }
+        uint32_t r[COLS];
+        tmem_ld32(taddr + c * COLS, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        if constexpr (COLS == 64) tmem_ld32(taddr + c * COLS + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tmem_ld_wait();
-        epilogue_chunk<EPI>(p, b, row, n * BN + c * 32, r);
+        if (use_aux) {
+          if (!mbar_wait_warp(xbar, xphase, kWaitBudgetNs, abort_flag, p.status)) {
+            fail(kErrTimeoutEpilogue);
+            ok = false;
+          }
+          xphase ^= 1;
+        }
+        uint8_t* myrow = buf;  // row `lane` of this warp's 32-row chunk
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {  // eight 16-byte chunks per 128-byte row
+          uint4* slot = reinterpret_cast<uint4*>(myrow + swz_off(lane, q));
+          if constexpr (epi_f32(EPI)) {
+            float4 x = use_aux ? *reinterpret_cast<const float4*>(slot) : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 o;
+            o.x = epi_op<EPI == EPI_ATOMIC_F32 ? EPI_BF16 : EPI>(__uint_as_float(r[4 * q + 0]), x.x, p);
+            o.y = epi_op<EPI == EPI_ATOMIC_F32 ? EPI_BF16 : EPI>(__uint_as_float(r[4 * q + 1]), x.y, p);
+            o.z = epi_op<EPI == EPI_ATOMIC_F32 ? EPI_BF16 : EPI>(__uint_as_float(r[4 * q + 2]), x.z, p);
+            o.w = epi_op<EPI == EPI_ATOMIC_F32 ? EPI_BF16 : EPI>(__uint_as_float(r[4 * q + 3]), x.w, p);
+            *reinterpret_cast<float4*>(slot) = o;
+          } else {
+            uint4 xv = use_aux ? *slot : make_uint4(0, 0, 0, 0);
+            const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+            uint32_t os[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = unpack_bf16(xs[j]);
+              os[j] = pack_bf16(epi_op<EPI>(__uint_as_float(r[8 * q + 2 * j]), f.x, p),
+                                epi_op<EPI>(__uint_as_float(r[8 * q + 2 * j + 1]), f.y, p));
+            }
+            *slot = make_uint4(os[0], os[1], os[2], os[3]);
+          }
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (c == BN / COLS - 1) {
+          // accumulator fully read: hand it back to the MMA warp
+          tc_fence_before();
+          mbar_arrive(&tempty_bar[acc]);
+        }
+        if (leader && ok) {
+          if constexpr (EPI == EPI_ATOMIC_F32)
+            tma_reduce_add_3d(&tmC, buf, col0, row0, b);
+          else
+            tma_store_3d(&tmC, buf, col0, row0, b);
+          bulk_commit();
+        }
+        if (!ok) break;
       }
-      tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
+      if (!ok) break;
     }
+    if (leader) bulk_wait_all();
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -360,40 +376,6 @@ __global__ void __launch_bounds__(192, 1)
 // ----------------------------------------------------------------------------------- host
 namespace {
 
-using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeFn get_encode() {
-  static EncodeFn fn = nullptr;
-  if (!fn) {
-    cudaDriverEntryPointQueryResult q;
-    void* ptr = nullptr;
-    C10_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
-    TORCH_CHECK(q == cudaDriverEntryPointSuccess && ptr, "cuTensorMapEncodeTiled unavailable");
-    fn = reinterpret_cast<EncodeFn>(ptr);
-  }
-  return fn;
-}
-
-// 3-D bf16 map over storage [batch][outer][inner] with a 128-byte-swizzled box {64, box_outer, 1}.
-CUtensorMap make_map(const void* base, int64_t inner, int64_t outer, int64_t batch, int64_t ld_elems,
-                     int64_t bs_elems, int box_outer) {
-  CUtensorMap m;
-  if (batch == 1 || bs_elems == 0) bs_elems = ld_elems * outer;  // unused for one batch, but must be a valid stride
-  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)(ld_elems * 2), (cuuint64_t)(bs_elems * 2)};
-  cuuint32_t box[3] = {64, (cuuint32_t)box_outer, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
-  TORCH_CHECK((ld_elems * 2) % 16 == 0 && (bs_elems * 2) % 16 == 0, "TMA strides must be multiples of 16 bytes");
-  CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
-                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
-  return m;
-}
-
 int num_sms() {
   static int n = 0;
   if (!n) {
@@ -404,31 +386,35 @@ int num_sms() {
   return n;
 }
 
+struct Maps {
+  CUtensorMap a, b, c, x;
+};
+
 template <int BN, bool AMN, bool BMN, int EPI>
-void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid, cudaStream_t st) {
+void launch_t(const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
   auto k = gemm_kernel<BN, AMN, BMN, EPI>;
   static bool attr = false;
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM));
     attr = true;
   }
-  k<<<grid, 192, GemmCfg<BN>::SMEM, st>>>(ta, tb, p);
+  k<<<grid, 192, GemmCfg<BN>::SMEM, st>>>(mp.a, mp.b, mp.c, mp.x, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 template <int BN, bool AMN, bool BMN>
-void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid, cudaStream_t st) {
+void dispatch_epi(int epi, const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
   switch (epi) {
-    case EPI_BF16: return launch_t<BN, AMN, BMN, EPI_BF16>(ta, tb, p, grid, st);
-    case EPI_F32: return launch_t<BN, AMN, BMN, EPI_F32>(ta, tb, p, grid, st);
-    case EPI_ATOMIC_F32: return launch_t<BN, AMN, BMN, EPI_ATOMIC_F32>(ta, tb, p, grid, st);
+    case EPI_BF16: return launch_t<BN, AMN, BMN, EPI_BF16>(mp, p, grid, st);
+    case EPI_F32: return launch_t<BN, AMN, BMN, EPI_F32>(mp, p, grid, st);
+    case EPI_ATOMIC_F32: return launch_t<BN, AMN, BMN, EPI_ATOMIC_F32>(mp, p, grid, st);
     default: break;
   }
   if constexpr (BN == 256) {
     switch (epi) {
-      case EPI_RELU2: return launch_t<BN, AMN, BMN, EPI_RELU2>(ta, tb, p, grid, st);
-      case EPI_RELU2_BWD: return launch_t<BN, AMN, BMN, EPI_RELU2_BWD>(ta, tb, p, grid, st);
-      case EPI_SOFTCAP: return launch_t<BN, AMN, BMN, EPI_SOFTCAP>(ta, tb, p, grid, st);
+      case EPI_RELU2: return launch_t<BN, AMN, BMN, EPI_RELU2>(mp, p, grid, st);
+      case EPI_RELU2_BWD: return launch_t<BN, AMN, BMN, EPI_RELU2_BWD>(mp, p, grid, st);
+      case EPI_SOFTCAP: return launch_t<BN, AMN, BMN, EPI_SOFTCAP>(mp, p, grid, st);
       default: break;
     }
   }
@@ -436,12 +422,22 @@ void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const G
 }
 
 template <int BN>
-void dispatch_major(bool amn, bool bmn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-                    int grid, cudaStream_t st) {
-  if (!amn && !bmn) return dispatch_epi<BN, false, false>(epi, ta, tb, p, grid, st);
-  if (!amn && bmn) return dispatch_epi<BN, false, true>(epi, ta, tb, p, grid, st);
-  if (amn && !bmn) return dispatch_epi<BN, true, false>(epi, ta, tb, p, grid, st);
-  return dispatch_epi<BN, true, true>(epi, ta, tb, p, grid, st);
+void dispatch_major(bool amn, bool bmn, int epi, const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
+  if (!amn && !bmn) return dispatch_epi<BN, false, false>(epi, mp, p, grid, st);
+  if (!amn && bmn) return dispatch_epi<BN, false, true>(epi, mp, p, grid, st);
+  if (amn && !bmn) return dispatch_epi<BN, true, false>(epi, mp, p, grid, st);
+  return dispatch_epi<BN, true, true>(epi, mp, p, grid, st);
+}
+
+CUtensorMap bf16_map(const void* base, int64_t inner, int64_t outer, int64_t batch, int64_t ld, int64_t bs, int box_outer) {
+  return tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, inner, outer, batch, ld, bs, 64, box_outer);
+}
+
+// map for the epilogue's 32-row x 128-byte chunks of an [batch][M][N] tensor
+CUtensorMap out_map(const torch::Tensor& t, int64_t M, int64_t N, int64_t batch, int64_t ld, int64_t bs) {
+  if (t.scalar_type() == at::kFloat)
+    return tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, t.data_ptr(), N, M, batch, ld, bs, 32, 32);
+  return tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, t.data_ptr(), N, M, batch, ld, bs, 64, 32);
 }
 
 }  // namespace
@@ -459,12 +455,13 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
   const bool f32_out = epi == EPI_F32 || epi == EPI_ATOMIC_F32;
   TORCH_CHECK(c.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm: output dtype mismatch");
   TORCH_CHECK(M > 0 && N > 0 && K > 0 && batch > 0, "gemm: empty problem");
-  TORCH_CHECK(ldc % 8 == 0, "gemm: ldc must be a multiple of 8");
   c10::cuda::CUDAGuard guard(a.device());
   const int BN = block_n > 0 ? (int)block_n : (N <= 128 ? 128 : 256);
   TORCH_CHECK(BN == 128 || BN == 256, "block_n must be 128 or 256");
-  CUtensorMap ta = a_mn ? make_map(a.data_ptr(), M, K, batch, lda, bsa, 64) : make_map(a.data_ptr(), K, M, batch, lda, bsa, BM);
-  CUtensorMap tb = b_mn ? make_map(b.data_ptr(), N, K, batch, ldb, bsb, 64) : make_map(b.data_ptr(), K, N, batch, ldb, bsb, BN);
+  Maps mp;
+  mp.a = a_mn ? bf16_map(a.data_ptr(), M, K, batch, lda, bsa, 64) : bf16_map(a.data_ptr(), K, M, batch, lda, bsa, BM);
+  mp.b = b_mn ? bf16_map(b.data_ptr(), N, K, batch, ldb, bsb, 64) : bf16_map(b.data_ptr(), K, N, batch, ldb, bsb, BN);
+  mp.c = out_map(c, M, N, batch, ldc, bsc);
   GemmParams p{};
   p.M = (int)M;
   p.N = (int)N;
@@ -482,13 +479,14 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
   TORCH_CHECK(splits == 1 || epi == EPI_ATOMIC_F32, "k_splits > 1 needs the accumulating epilogue");
   p.kb_per_split = (p.k_blocks + splits - 1) / splits;
   p.k_splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
-  p.C = c.data_ptr();
-  p.ldc = ldc;
-  p.bsc = bsc;
   if (aux.has_value() && aux->defined()) {
-    p.aux = aux->data_ptr();
-    p.ld_aux = ld_aux;
-    p.bs_aux = bs_aux;
+    TORCH_CHECK(aux->scalar_type() == c.scalar_type(), "gemm: aux dtype must match the output");
+    mp.x = out_map(*aux, M, N, batch, ld_aux, bs_aux);
+    p.has_aux = 1;
+  } else {
+    TORCH_CHECK(epi != EPI_RELU2_BWD, "gemm: the ReLU^2 backward epilogue needs aux");
+    mp.x = mp.c;
+    p.has_aux = 0;
   }
   p.alpha = (float)alpha;
   p.beta = (float)beta;
@@ -497,9 +495,9 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
   const int grid = std::min(total, num_sms());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (BN == 256)
-    dispatch_major<256>(a_mn, b_mn, (int)epi, ta, tb, p, grid, st);
+    dispatch_major<256>(a_mn, b_mn, (int)epi, mp, p, grid, st);
   else
-    dispatch_major<128>(a_mn, b_mn, (int)epi, ta, tb, p, grid, st);
+    dispatch_major<128>(a_mn, b_mn, (int)epi, mp, p, grid, st);
 }
 
 }  // namespace br

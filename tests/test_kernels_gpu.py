@@ -223,6 +223,16 @@ def test_attention_fwd_bwd(cuda, B, T, H, KV, window):
     _assert(dqkv[:, :D], qr.grad.reshape(M, D), 3e-2)
     _assert(dqkv[:, D:D + Dkv], kr.grad.reshape(M, Dkv), 3e-2)
     _assert(dqkv[:, D + Dkv:], vr.grad.reshape(M, Dkv), 3e-2)
+    if T % 128 == 0:
+        dqkv_tc = torch.empty_like(qkv)
+        delta_tc = torch.empty(B, H, T, device=cuda)
+        E.attn_bwd_tc(qkv, o_tc, do, lse_tc, dqkv_tc, delta_tc, B, T, H, KV, hd, window)
+        torch.cuda.synchronize()
+        from bitresearch_b200.ops._ext import check_status
+        assert check_status() == 0
+        _assert(dqkv_tc[:, :D], qr.grad.reshape(M, D), 3e-2)
+        _assert(dqkv_tc[:, D:D + Dkv], kr.grad.reshape(M, Dkv), 3e-2)
+        _assert(dqkv_tc[:, D + Dkv:], vr.grad.reshape(M, Dkv), 3e-2)
 
 
 def test_adamw_and_muon_kernels_match_torch_optimizer(cuda):
