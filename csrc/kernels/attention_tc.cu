@@ -542,8 +542,9 @@ constexpr int DK_BAR = DK_STAT + 2 * 512;
 constexpr int DK_SMEM = DK_BAR + 256 + 1024;
 
 __global__ void __launch_bounds__(192, 1)
-    attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                        BwdParams p) {
+    attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_qkv,
+                        const __grid_constant__ CUtensorMap tm_do, BwdParams p) {
+  // tm_kv: 128-row boxes (the CTA's K and V tiles); tm_qkv / tm_do: 64-row boxes (query blocks)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DK_BAR);
@@ -592,10 +593,10 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     if (elect_one()) {
       mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
-      tma_load_3d(&tm_qkv, kv_full, smem + DK_K, p.Dq + kvh * HD, k0, b);
-      tma_load_3d(&tm_qkv, kv_full, smem + DK_K + ATOM_BYTES, p.Dq + kvh * HD + 64, k0, b);
-      tma_load_3d(&tm_qkv, kv_full, smem + DK_V, p.Dq + p.Dkv + kvh * HD, k0, b);
-      tma_load_3d(&tm_qkv, kv_full, smem + DK_V + ATOM_BYTES, p.Dq + p.Dkv + kvh * HD + 64, k0, b);
+      tma_load_3d(&tm_kv, kv_full, smem + DK_K, p.Dq + kvh * HD, k0, b);
+      tma_load_3d(&tm_kv, kv_full, smem + DK_K + ATOM_BYTES, p.Dq + kvh * HD + 64, k0, b);
+      tma_load_3d(&tm_kv, kv_full, smem + DK_V, p.Dq + p.Dkv + kvh * HD, k0, b);
+      tma_load_3d(&tm_kv, kv_full, smem + DK_V + ATOM_BYTES, p.Dq + p.Dkv + kvh * HD + 64, k0, b);
       for (int it = 0; it < iters; ++it) {
         const int st = it & 1;
         if (!mbar_wait(&qd_empty[st], ((it >> 1) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
@@ -835,7 +836,7 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::
   auto st = at::cuda::getCurrentCUDAStream();
   attn_dq_tc_kernel<<<dim3((unsigned)(T / BQ), (unsigned)H, (unsigned)B), 192, DQ_SMEM, st>>>(tq, td, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  attn_dkdv_tc_kernel<<<dim3((unsigned)(T / BKV), (unsigned)KV, (unsigned)B), 192, DK_SMEM, st>>>(tq64, td64, p);
+  attn_dkdv_tc_kernel<<<dim3((unsigned)(T / BKV), (unsigned)KV, (unsigned)B), 192, DK_SMEM, st>>>(tq, tq64, td64, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 }  // namespace br
