@@ -80,6 +80,8 @@ def main():
     ap.add_argument("--preset", default="d512")
     ap.add_argument("--device-batch", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"],
+                    help="gradient/parameter exchange for N > 1: in-kernel NVLink (p2p) or NCCL")
     ap.add_argument("overrides", nargs="*")
     args = ap.parse_args()
     rank, world, local = _rank_world()
@@ -109,8 +111,7 @@ def main():
 
     if args.impl == "ours":
         cfg.impl = "cuda"
-        if cfg.comm == "p2p" and world > 1:
-            cfg.comm = "nccl"  # in-kernel NVLink path is selected with comm=p2p explicitly
+        cfg.comm = args.comm
         tr = Trainer(cfg, device=device, log=lambda m: None)
         tr.initialize()
         accum = tr.grad_accum
@@ -175,12 +176,15 @@ def main():
             "dtype": "bf16", "data": "synthetic: seeded random token ids; random-init weights",
             "config": {"model": MODEL, "global_batch": global_tokens, "global_batch_unit": "tokens",
                        "seq_len": T, "device_batch": B, "grad_accum": accum, "parallelism": f"dp{world}",
+                       "comm": (args.comm if args.impl == "ours" else "nccl-ddp") if world > 1 else "none",
                        "l2": "inputs larger than L2 (activations tens of GB per step); no flush"},
             "impl": args.impl, "clocks": clk, "e2e": e2e,
             "gpu_launches": launches if args.impl == "ours" else 0,
             "launches_by_kernel": by_kernel if args.impl == "ours" else {},
         }
         print(json.dumps(line), flush=True)
+    if args.impl == "ours":
+        tr.destroy()
     if dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()
