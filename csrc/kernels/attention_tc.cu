@@ -195,18 +195,28 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int k0 = (kb_lo + j) * BKV;
       const uint32_t s_addr = lane_base + st * 128;
-      // pass 1: masked row max (log2 domain)
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(s_addr + c * 32, v);
-        tmem_ld_wait();
+      // interior tiles (every key visible to every row of the tile) skip the per-element mask
+      const bool interior = (k0 + BKV - 1 <= q0) && (k0 > q0 + BQ - 1 - w) && (k0 + BKV <= p.T);
+      // S row -> registers once (log2 domain), masked row max
+      uint32_t sr[4][32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int kj = k0 + c * 32 + i;
+      for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, sr[c]);
+      tmem_ld_wait();
+      float sv[BKV];
+      float mx = -INFINITY;
+      if (interior) {
+#pragma unroll
+        for (int i = 0; i < BKV; ++i) {
+          sv[i] = __uint_as_float(sr[i >> 5][i & 31]) * p.scale_log2;
+          mx = fmaxf(mx, sv[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < BKV; ++i) {
+          const int kj = k0 + i;
           const bool vis = kj <= qi && kj > qi - w && kj < p.T;
-          mx = fmaxf(mx, vis ? __uint_as_float(v[i]) * p.scale_log2 : -INFINITY);
+          sv[i] = vis ? __uint_as_float(sr[i >> 5][i & 31]) * p.scale_log2 : -INFINITY;
+          mx = fmaxf(mx, sv[i]);
         }
       }
       // PV_{j-1} must be complete before P is overwritten or O is rescaled
@@ -240,21 +250,15 @@ __global__ void __launch_bounds__(192, 1)
         }
         tmem_st_wait();
       }
-      // pass 2: P = exp2(s - m_ref) -> bf16 into the swizzled K-major P tile
-      const bool live = m_ref != -INFINITY;
-#pragma unroll 1
+      // P = exp2(s - m_ref) -> bf16 into the swizzled K-major P tile (masked entries are -inf -> 0)
+      const float mref = m_ref == -INFINITY ? 0.f : m_ref;
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(s_addr + c * 32, v);
-        tmem_ld_wait();
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const int kj = k0 + c * 32 + i;
-          const bool v0 = live && kj <= qi && kj > qi - w && kj < p.T;
-          const bool v1 = live && kj + 1 <= qi && kj + 1 > qi - w && kj + 1 < p.T;
-          const float p0 = v0 ? exp2f(__uint_as_float(v[i]) * p.scale_log2 - m_ref) : 0.f;
-          const float p1 = v1 ? exp2f(__uint_as_float(v[i + 1]) * p.scale_log2 - m_ref) : 0.f;
+          const float p0 = exp2f(sv[c * 32 + i] - mref);
+          const float p1 = exp2f(sv[c * 32 + i + 1] - mref);
           l += p0 + p1;
           pk[i / 2] = pack_bf16(p0, p1);
         }

@@ -168,25 +168,39 @@ def _train(rank, world):
         tr = Trainer(cfg, device=torch.device("cuda", rank), log=lambda m: None)
         tr.initialize()
         g = torch.Generator(device="cpu").manual_seed(100 + rank)
-        losses = []
-        for _ in range(3):
+        losses, grads = [], None
+        for step in range(3):
             x = torch.randint(0, 1024, (4, 256), generator=g, dtype=torch.int32).cuda()
             y = torch.randint(0, 1024, (4, 256), generator=g, dtype=torch.int32).cuda()
             losses.append(float(tr.train_step((x, y))))
-        out[comm] = (losses, {n: p.detach().float().cpu() for n, p in tr.model.named().items()})
+            if step == 0:  # the mean gradient the optimizer consumed on the first step
+                if comm == "nccl":
+                    grads = {n: v.detach().float().cpu().clone() for n, v in tr.grad_views.items()}
+                else:
+                    grads = {n: tr.comm.red_views[n].detach().float().cpu().clone() for n in tr.comm.owned_names}
+        out[comm] = (losses, {n: p.detach().float().cpu() for n, p in tr.model.named().items()}, grads)
         tr.destroy()
     return out
 
 
 def test_p2p_trainer_matches_nccl_2gpu():
+    """Same batches through the NCCL all-reduce path and the in-kernel NVLink path: the mean gradients
+    agree to fp32 accumulation-order noise, losses track, replicas stay identical across ranks, and
+    parameters agree except where AdamW (eps 1e-10) amplifies a near-zero gradient's rounding."""
     res = _run(_train)
     for r in range(2):
-        ln, pn = res[r]["nccl"]
-        lp, pp = res[r]["p2p"]
+        ln, pn, gn = res[r]["nccl"]
+        lp, pp, gp = res[r]["p2p"]
         for a, b in zip(ln, lp):
             assert abs(a - b) < 2e-3 * abs(a)
+        for n, g in gp.items():  # owned parameters of this rank
+            ref = gn[n]
+            err = (g - ref).abs().max().item()
+            assert err <= 1e-4 * (ref.abs().max().item() + 1e-12), (n, err)
         for n in pn:
-            d = (pn[n] - pp[n]).abs().max().item()
-            assert d < 5e-3 * (pn[n].abs().max().item() + 1e-6), n
+            d = (pn[n] - pp[n]).abs()
+            scale = pn[n].abs().max().item() + 1e-6
+            frac_bad = (d > 5e-3 * scale).float().mean().item()
+            assert frac_bad < 1e-3, (n, frac_bad)
     for n in res[0]["p2p"][1]:
         assert torch.equal(res[0]["p2p"][1][n], res[1]["p2p"][1][n]), n  # ranks hold identical replicas
