@@ -182,6 +182,9 @@ class P2PGradSync:
             self.reduce_chunks.append(torch.tensor(ch, dtype=torch.int64, device=dev).view(-1, 2))
         self.flag_ptrs = torch.tensor([p for p in self.flags.peer_ptrs], dtype=torch.int64, device=dev)
         self._build_gather_table(trainer)
+        self.sparse = cfg.sparsify.enabled
+        if self.sparse:
+            self._init_sparse(trainer, cfg)
         self.comm_stream = torch.cuda.Stream(device=dev)
         self.events = [torch.cuda.Event() for _ in self.ranges]
         self.done = torch.cuda.Event()
@@ -203,6 +206,59 @@ class P2PGradSync:
                 rows.append((c_off, ln, o, cols, ld, ptr, start))
         self.gather_segs = torch.tensor(rows, dtype=torch.int64, device=trainer.device).view(-1, 7)
 
+    # ------------------------------------------------------------------ top-k + error feedback
+    def _init_sparse(self, trainer, cfg):
+        """Per (bucket, owner) index/value lists in symmetric memory, sized for the worst case (every
+        element kept), so a list can never overflow; error-feedback and velocity buffers are local."""
+        sp = cfg.sparsify
+        dev = trainer.device
+        total = trainer.flat_grad.numel()
+        W = self.world
+        self.sp_cfg = sp
+        self.err = torch.zeros(total, dtype=torch.float32, device=dev)
+        self.vel = torch.zeros(total, dtype=torch.float32, device=dev) if sp.momentum_factor > 0 else None
+        self.thr = torch.zeros(len(self.ranges), dtype=torch.float32, device=dev)
+        # list regions: bucket-major, then owner
+        cap = {}
+        for b, grp in enumerate(self.groups):
+            for o in range(W):
+                cap[(b, o)] = sum(self.layout[n][1] for n in grp if self.owner[n] == o)
+        base, off = {}, 0
+        for b in range(len(self.groups)):
+            for o in range(W):
+                base[(b, o)] = off
+                off += -(-cap[(b, o)] // 8) * 8
+        self.list_base = base
+        self.sp_idx = SymmetricBuffer(max(off, 8) * 4)
+        self.sp_val = SymmetricBuffer(max(off, 8) * 2)
+        self.sp_cnt = SymmetricBuffer(len(self.groups) * W * 4 + 16)
+        self.sp_cnt_view = self.sp_cnt.view(len(self.groups) * W, 0)  # int32 counters, zeroed per step as fp32 words
+        self.sp_peers = torch.tensor([[self.sp_idx.peer_ptrs[r], self.sp_val.peer_ptrs[r], self.sp_cnt.peer_ptrs[r]]
+                                      for r in range(W)], dtype=torch.int64, device=dev)
+        self.sel_chunks = []
+        for b, grp in enumerate(self.groups):
+            rows = []
+            for n in grp:
+                o = self.owner[n]
+                noff, numel, _ = self.layout[n]
+                for c_off, ln, _ in chunk_ranges(noff, numel, size=1 << 14):
+                    rows.append((c_off, ln, base[(b, o)], b * W + o))
+            self.sel_chunks.append(torch.tensor(rows, dtype=torch.int64, device=dev).view(-1, 4))
+        self.sp_step = 0
+
+    def _sparse_bucket(self, b: int, loss_scale: float) -> None:
+        sp = self.sp_cfg
+        lo, hi = self.ranges[b]
+        mu = sp.momentum_factor
+        seed = (self.epoch * 1000003 + b * 7919 + self.rank * 104729) & 0x7FFFFFFF
+        self.E.topk_threshold(self.tr.flat_grad, self.err, self.vel, lo, hi, 1.0 / loss_scale, mu, sp.sample_size,
+                              sp.top_k_ratio, seed, self.thr[b:b + 1])
+        self.E.topk_select(self.tr.flat_grad, self.err, self.vel, self.sel_chunks[b], 1.0 / loss_scale, mu,
+                           self.thr[b:b + 1], self.sp_idx.ptr, self.sp_val.ptr, self.sp_cnt.ptr)
+        self.E.comm_signal(self.flags.ptr + 8 * b, self.epoch + 1)
+        self.E.topk_reduce(self.sp_peers, self.flag_ptrs, b, self.epoch + 1, self.list_base[(b, self.rank)],
+                           b * self.world + self.rank, self.red, 1.0 / self.world, 32, self.budget)
+
     # ------------------------------------------------------------------ hooks from the engine
     def bucket_ready(self, b: int, loss_scale: float) -> None:
         """Called on the compute stream when bucket ``b``'s gradients are final for this step."""
@@ -212,6 +268,9 @@ class P2PGradSync:
         s.wait_event(ev)
         lo, hi = self.ranges[b]
         with torch.cuda.stream(s):
+            if self.sparse and self.sp_step >= self.sp_cfg.warmup_steps:
+                self._sparse_bucket(b, loss_scale)
+                return
             self.E.comm_pack(self.tr.flat_grad, self.send.ptr, self.wire, lo, hi, 1.0 / loss_scale, self.bad)
             self.E.comm_signal(self.flags.ptr + 8 * b, self.epoch + 1)
             self.E.comm_reduce(self.send.peers_dev, self.flag_ptrs, b, self.epoch + 1, self.reduce_chunks[b],
@@ -219,6 +278,12 @@ class P2PGradSync:
 
     def begin_step(self) -> None:
         self.bad.zero_()
+        if self.sparse:
+            # the reference counts the step before checking the dense warm-up (gradient-sparsifier.ts:87-91)
+            self.sp_step += 1
+            if self.sp_step >= self.sp_cfg.warmup_steps:
+                self.sp_cnt_view.zero_()
+                self.red.zero_()
 
     # ------------------------------------------------------------------ step
     def step(self, step_idx: int, scale: float, opt) -> bool:
@@ -244,5 +309,8 @@ class P2PGradSync:
     def close(self):
         torch.cuda.synchronize()
         dist.barrier()
-        for b in (self.send, self.param_buf, self.flags):
+        bufs = [self.send, self.param_buf, self.flags]
+        if self.sparse:
+            bufs += [self.sp_idx, self.sp_val, self.sp_cnt]
+        for b in bufs:
             b.close()

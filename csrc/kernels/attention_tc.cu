@@ -332,46 +332,54 @@ struct BwdParams {
   int* status;
 };
 
-// ---- dQ: one CTA per (128 queries, head, batch); S, dP, dQ in TMEM columns [0,128), [128,256), [256,384)
+// ---- dQ: one CTA per (128 queries, head, batch), 64-key blocks in a 4-stage K/V ring.
+// TMEM: two S/dP sets (set s: S at [128s, +64), dP at [128s+64, +64)) so block j+1's scores are
+// computed while the softmax warps turn block j into dS; dQ accumulates at [256, 384).
+constexpr int BK64 = 64;
+constexpr int KV64 = 64 * 128 * 2;        // 64 keys x 128 hd: two 8 KB swizzle atoms
+constexpr int KV64_ATOM = 64 * 128;
+constexpr int DQ_STAGES = 4;
 constexpr int DQ_Q = 0;
 constexpr int DQ_DO = DQ_Q + TILE_BYTES;
-constexpr int DQ_K = DQ_DO + TILE_BYTES;
-constexpr int DQ_V = DQ_K + 2 * TILE_BYTES;
-constexpr int DQ_DS = DQ_V + 2 * TILE_BYTES;
-constexpr int DQ_BAR = DQ_DS + TILE_BYTES;
+constexpr int DQ_K = DQ_DO + TILE_BYTES;            // [4] x 16 KB
+constexpr int DQ_V = DQ_K + DQ_STAGES * KV64;       // [4] x 16 KB
+constexpr int DQ_DS = DQ_V + DQ_STAGES * KV64;      // [2] x (128 q x 64 keys bf16 = one 16 KB atom)
+constexpr int DQ_BAR = DQ_DS + 2 * 16384;
 constexpr int DQ_SMEM = DQ_BAR + 256 + 1024;
 
 __global__ void __launch_bounds__(192, 1)
-    attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                      BwdParams p) {
+    attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                      const __grid_constant__ CUtensorMap tm_kv, BwdParams p) {
+  // tm_q / tm_do: 128-row boxes; tm_kv: 64-row boxes
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DQ_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* done = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* kv_full = bars + 1;   // [4]
+  uint64_t* kv_empty = bars + 5;  // [4]
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* p_full = bars + 11;
+  uint64_t* done = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (p.H / p.KV);
   const int q0 = qb * BQ;
   const int w = p.window;
-  const int kb_lo = max(0, q0 - w + 1) / BKV;
-  const int kb_hi = min(q0 + BQ - 1, p.T - 1) / BKV;
+  const int kb_lo = max(0, q0 - w + 1) / BK64;
+  const int kb_hi = min(q0 + BQ - 1, p.T - 1) / BK64;
   const int nkv = kb_hi - kb_lo + 1;
   const int warp = warp_id();
   if (device_failed(p.status)) return;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < DQ_STAGES; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(s_full, 1);
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
     mbar_init(p_full, 128);
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -390,62 +398,67 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     if (elect_one()) {
       mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
-      tma_load_3d(&tm_qkv, q_full, smem + DQ_Q, h * HD, q0, b);
-      tma_load_3d(&tm_qkv, q_full, smem + DQ_Q + ATOM_BYTES, h * HD + 64, q0, b);
+      tma_load_3d(&tm_q, q_full, smem + DQ_Q, h * HD, q0, b);
+      tma_load_3d(&tm_q, q_full, smem + DQ_Q + ATOM_BYTES, h * HD + 64, q0, b);
       tma_load_3d(&tm_do, q_full, smem + DQ_DO, h * HD, q0, b);
       tma_load_3d(&tm_do, q_full, smem + DQ_DO + ATOM_BYTES, h * HD + 64, q0, b);
       for (int j = 0; j < nkv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
+        const int st = j % DQ_STAGES;
+        if (!mbar_wait(&kv_empty[st], ((j / DQ_STAGES) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
           fail(kErrTimeoutProducer);
           break;
         }
-        const int k0 = (kb_lo + j) * BKV;
-        uint8_t* ks = smem + DQ_K + st * TILE_BYTES;
-        uint8_t* vs = smem + DQ_V + st * TILE_BYTES;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
-        tma_load_3d(&tm_qkv, &kv_full[st], ks, p.Dq + kvh * HD, k0, b);
-        tma_load_3d(&tm_qkv, &kv_full[st], ks + ATOM_BYTES, p.Dq + kvh * HD + 64, k0, b);
-        tma_load_3d(&tm_qkv, &kv_full[st], vs, p.Dq + p.Dkv + kvh * HD, k0, b);
-        tma_load_3d(&tm_qkv, &kv_full[st], vs + ATOM_BYTES, p.Dq + p.Dkv + kvh * HD + 64, k0, b);
+        const int k0 = (kb_lo + j) * BK64;
+        uint8_t* ks = smem + DQ_K + st * KV64;
+        uint8_t* vs = smem + DQ_V + st * KV64;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * KV64);
+        tma_load_3d(&tm_kv, &kv_full[st], ks, p.Dq + kvh * HD, k0, b);
+        tma_load_3d(&tm_kv, &kv_full[st], ks + KV64_ATOM, p.Dq + kvh * HD + 64, k0, b);
+        tma_load_3d(&tm_kv, &kv_full[st], vs, p.Dq + p.Dkv + kvh * HD, k0, b);
+        tma_load_3d(&tm_kv, &kv_full[st], vs + KV64_ATOM, p.Dq + p.Dkv + kvh * HD + 64, k0, b);
       }
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idesc_kk = umma_idesc_bf16(128, 128, false, false);
-      constexpr uint32_t idesc_kmn = umma_idesc_bf16(128, 128, false, true);
+      constexpr uint32_t idesc_s = umma_idesc_bf16(128, 64, false, false);
+      constexpr uint32_t idesc_q = umma_idesc_bf16(128, 128, false, true);
       const uint32_t q_addr = smem_u32(smem + DQ_Q), do_addr = smem_u32(smem + DQ_DO);
-      const uint32_t ds_addr = smem_u32(smem + DQ_DS);
       bool ok = mbar_wait(q_full, 0, kBudgetNs, abort_flag, p.status);
+      auto issue_sdp = [&](int j) -> bool {
+        const int st = j % DQ_STAGES, set = j & 1;
+        if (!mbar_wait(&kv_full[st], (j / DQ_STAGES) & 1, kBudgetNs, abort_flag, p.status)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + DQ_K + st * KV64), v_addr = smem_u32(smem + DQ_V + st * KV64);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t offa = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
+          const uint32_t offb = (kk >> 2) * KV64_ATOM + (kk & 3) * 32;
+          umma_bf16_ss(tmem + set * 128, umma_desc_sw128(q_addr + offa, 16, 1024),
+                       umma_desc_sw128(k_addr + offb, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          umma_bf16_ss(tmem + set * 128 + 64, umma_desc_sw128(do_addr + offa, 16, 1024),
+                       umma_desc_sw128(v_addr + offb, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[set]);
+        return true;
+      };
+      if (ok) ok = issue_sdp(0);
       for (int j = 0; j < nkv && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+        if (j + 1 < nkv && !issue_sdp(j + 1)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + DQ_K + st * TILE_BYTES);
-        const uint32_t v_addr = smem_u32(smem + DQ_V + st * TILE_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
-          umma_bf16_ss(tmem, umma_desc_sw128(q_addr + off, 16, 1024), umma_desc_sw128(k_addr + off, 16, 1024),
-                       idesc_kk, kk > 0 ? 1u : 0u);
-          umma_bf16_ss(tmem + 128, umma_desc_sw128(do_addr + off, 16, 1024), umma_desc_sw128(v_addr + off, 16, 1024),
-                       idesc_kk, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(s_full);
         if (!mbar_wait(p_full, j & 1, kBudgetNs, abort_flag, p.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        const int st = j % DQ_STAGES;
+        const uint32_t k_addr = smem_u32(smem + DQ_K + st * KV64);
+        const uint32_t ds_addr = smem_u32(smem + DQ_DS + (j & 1) * 16384);
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint64_t ad = umma_desc_sw128(ds_addr + (kk >> 2) * ATOM_BYTES + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = umma_desc_sw128(k_addr + kk * 2048, ATOM_BYTES, 1024);
-          umma_bf16_ss(tmem + 256, ad, bd, idesc_kmn, (j > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < BK64 / 16; ++kk)
+          umma_bf16_ss(tmem + 256, umma_desc_sw128(ds_addr + kk * 32, 16, 1024),
+                       umma_desc_sw128(k_addr + kk * 2048, KV64_ATOM, 1024), idesc_q, (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&kv_empty[st]);
       }
       if (!ok) fail(kErrTimeoutMma);
@@ -457,40 +470,43 @@ __global__ void __launch_bounds__(192, 1)
     const int r = wq * 32 + lane;
     const int qi = q0 + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
-    uint8_t* drow = smem + DQ_DS + r * 128;
     const int qc = min(qi, p.T - 1);
     const float lse2 = p.lse[((int64_t)b * p.H + h) * p.T + qc] * kLog2e;
     const float dl = p.delta[((int64_t)b * p.H + h) * p.T + qc];
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      if (!mbar_wait_warp(s_full, j & 1, kBudgetNs, abort_flag, p.status)) {
+      const int set = j & 1;
+      if (!mbar_wait_warp(&s_full[set], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
         break;
       }
       tc_fence_after();
-      const int k0 = (kb_lo + j) * BKV;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dv[32];
-        tmem_ld32(lane_base + c * 32, sv);
-        tmem_ld32(lane_base + 128 + c * 32, dv);
-        tmem_ld_wait();
+      const int k0 = (kb_lo + j) * BK64;
+      const bool interior = (k0 + BK64 - 1 <= q0) && (k0 > q0 + BQ - 1 - w) && (k0 + BK64 <= p.T);
+      uint32_t sv[2][32], dv[2][32];
+      tmem_ld32(lane_base + set * 128, sv[0]);
+      tmem_ld32(lane_base + set * 128 + 32, sv[1]);
+      tmem_ld32(lane_base + set * 128 + 64, dv[0]);
+      tmem_ld32(lane_base + set * 128 + 96, dv[1]);
+      tmem_ld_wait();
+      uint8_t* drow = smem + DQ_DS + set * 16384 + r * 128;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const int kj = k0 + c * 32 + i;
-          const bool v0 = kj <= qi && kj > qi - w && kj < p.T;
-          const bool v1 = kj + 1 <= qi && kj + 1 > qi - w && kj + 1 < p.T;
-          const float p0 = v0 ? exp2f(__uint_as_float(sv[i]) * p.scale_log2 - lse2) : 0.f;
-          const float p1 = v1 ? exp2f(__uint_as_float(sv[i + 1]) * p.scale_log2 - lse2) : 0.f;
-          pk[i / 2] = pack_bf16(p0 * (__uint_as_float(dv[i]) - dl), p1 * (__uint_as_float(dv[i + 1]) - dl));
+          const bool v0 = interior || (kj <= qi && kj > qi - w && kj < p.T);
+          const bool v1 = interior || (kj + 1 <= qi && kj + 1 > qi - w && kj + 1 < p.T);
+          const float p0 = v0 ? exp2f(__uint_as_float(sv[c][i]) * p.scale_log2 - lse2) : 0.f;
+          const float p1 = v1 ? exp2f(__uint_as_float(sv[c][i + 1]) * p.scale_log2 - lse2) : 0.f;
+          pk[i / 2] = pack_bf16(p0 * (__uint_as_float(dv[c][i]) - dl), p1 * (__uint_as_float(dv[c][i + 1]) - dl));
         }
-        uint8_t* atom = drow + (c >> 1) * ATOM_BYTES;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const int chunk = (c & 1) * 4 + q;
-          *reinterpret_cast<uint4*>(atom + ((chunk ^ (r & 7)) << 4)) =
+          const int chunk = c * 4 + q;
+          *reinterpret_cast<uint4*>(drow + ((chunk ^ (r & 7)) << 4)) =
               make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
@@ -530,8 +546,8 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// ---- dK, dV: one CTA per (128 keys, kv head, batch), 64-query blocks;
-// TMEM: S^T [0,64), dP^T [64,128), dV [128,256), dK [256,384)
+// ---- dK, dV: one CTA per (128 keys, kv head, batch), 64-query blocks in a 2-stage Q/dO ring.
+// TMEM: two S^T/dP^T sets (set s: S^T at [128s, +64), dP^T at [128s+64, +64)), dV [256,384), dK [384,512).
 constexpr int KB_Q = 64;
 constexpr int HALF_TILE = 64 * 128 * 2;   // 64 rows x 128 hd, two 8 KB swizzle atoms
 constexpr int HALF_ATOM = 64 * 128;
@@ -539,9 +555,9 @@ constexpr int DK_K = 0;
 constexpr int DK_V = DK_K + TILE_BYTES;
 constexpr int DK_Q = DK_V + TILE_BYTES;            // [2] x HALF_TILE
 constexpr int DK_DO = DK_Q + 2 * HALF_TILE;        // [2] x HALF_TILE
-constexpr int DK_PT = DK_DO + 2 * HALF_TILE;       // 128 keys x 64 q bf16 (one 16 KB atom)
-constexpr int DK_DST = DK_PT + 128 * 128;
-constexpr int DK_STAT = DK_DST + 128 * 128;        // [2] x (lse[64], delta[64]) floats
+constexpr int DK_PT = DK_DO + 2 * HALF_TILE;       // [2] x (128 keys x 64 q bf16 = one 16 KB atom)
+constexpr int DK_DST = DK_PT + 2 * 16384;          // [2] x 16 KB
+constexpr int DK_STAT = DK_DST + 2 * 16384;        // [2] x (lse[64], delta[64]) floats
 constexpr int DK_BAR = DK_STAT + 2 * 512;
 constexpr int DK_SMEM = DK_BAR + 256 + 1024;
 
@@ -555,10 +571,10 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* kv_full = bars + 0;
   uint64_t* qd_full = bars + 1;   // [2]
   uint64_t* qd_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* done = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* p_full = bars + 7;
+  uint64_t* done = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* stat = reinterpret_cast<float*>(smem + DK_STAT);
 
@@ -577,8 +593,8 @@ __global__ void __launch_bounds__(192, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
+      mbar_init(&s_full[i], 1);
     }
-    mbar_init(s_full, 1);
     mbar_init(p_full, 128);
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -627,14 +643,10 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, 64, false, false);
       constexpr uint32_t idesc_g = umma_idesc_bf16(128, 128, false, true);
       const uint32_t k_addr = smem_u32(smem + DK_K), v_addr = smem_u32(smem + DK_V);
-      const uint32_t pt_addr = smem_u32(smem + DK_PT), dst_addr = smem_u32(smem + DK_DST);
       bool ok = mbar_wait(kv_full, 0, kBudgetNs, abort_flag, p.status);
-      for (int it = 0; it < iters && ok; ++it) {
+      auto issue_s = [&](int it) -> bool {
         const int st = it & 1;
-        if (!mbar_wait(&qd_full[st], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait(&qd_full[st], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) return false;
         tc_fence_after();
         const uint32_t q_addr = smem_u32(smem + DK_Q + st * HALF_TILE);
         const uint32_t do_addr = smem_u32(smem + DK_DO + st * HALF_TILE);
@@ -642,23 +654,36 @@ __global__ void __launch_bounds__(192, 1)
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t offa = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
           const uint32_t offb = (kk >> 2) * HALF_ATOM + (kk & 3) * 32;
-          umma_bf16_ss(tmem, umma_desc_sw128(k_addr + offa, 16, 1024), umma_desc_sw128(q_addr + offb, 16, 1024),
-                       idesc_s, kk > 0 ? 1u : 0u);
-          umma_bf16_ss(tmem + 64, umma_desc_sw128(v_addr + offa, 16, 1024), umma_desc_sw128(do_addr + offb, 16, 1024),
-                       idesc_s, kk > 0 ? 1u : 0u);
+          umma_bf16_ss(tmem + st * 128, umma_desc_sw128(k_addr + offa, 16, 1024),
+                       umma_desc_sw128(q_addr + offb, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          umma_bf16_ss(tmem + st * 128 + 64, umma_desc_sw128(v_addr + offa, 16, 1024),
+                       umma_desc_sw128(do_addr + offb, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(s_full);
+        umma_commit(&s_full[st]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int it = 0; it < iters && ok; ++it) {
+        if (it + 1 < iters && !issue_s(it + 1)) {
+          ok = false;
+          break;
+        }
         if (!mbar_wait(p_full, it & 1, kBudgetNs, abort_flag, p.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        const int st = it & 1;
+        const uint32_t q_addr = smem_u32(smem + DK_Q + st * HALF_TILE);
+        const uint32_t do_addr = smem_u32(smem + DK_DO + st * HALF_TILE);
+        const uint32_t pt_addr = smem_u32(smem + DK_PT + st * 16384);
+        const uint32_t dst_addr = smem_u32(smem + DK_DST + st * 16384);
 #pragma unroll
         for (int kk = 0; kk < KB_Q / 16; ++kk) {
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          umma_bf16_ss(tmem + 128, umma_desc_sw128(pt_addr + kk * 32, 16, 1024),
+          umma_bf16_ss(tmem + 256, umma_desc_sw128(pt_addr + kk * 32, 16, 1024),
                        umma_desc_sw128(do_addr + kk * 2048, HALF_ATOM, 1024), idesc_g, acc);
-          umma_bf16_ss(tmem + 256, umma_desc_sw128(dst_addr + kk * 32, 16, 1024),
+          umma_bf16_ss(tmem + 384, umma_desc_sw128(dst_addr + kk * 32, 16, 1024),
                        umma_desc_sw128(q_addr + kk * 2048, HALF_ATOM, 1024), idesc_g, acc);
         }
         umma_commit(&qd_empty[st]);
@@ -672,12 +697,10 @@ __global__ void __launch_bounds__(192, 1)
     const int r = wq * 32 + lane;
     const int kj = k0 + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
-    uint8_t* prow = smem + DK_PT + r * 128;
-    uint8_t* srow = smem + DK_DST + r * 128;
     bool ok = true;
     for (int it = 0; it < iters; ++it) {
       const int st = it & 1;
-      if (!mbar_wait_warp(s_full, it & 1, kBudgetNs, abort_flag, p.status)) {
+      if (!mbar_wait_warp(&s_full[st], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
         break;
@@ -685,23 +708,29 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int q0 = (qb_lo + it % nq) * KB_Q;
       const float* ls = stat + st * 128;
-#pragma unroll 1
+      // every (query, key) pair of this block visible: keys of the tile <= first query and within the window
+      const bool interior = (k0 + BKV - 1 <= q0) && (k0 > q0 + KB_Q - 1 - w) && (q0 + KB_Q <= p.T) && (k0 + BKV <= p.T);
+      uint32_t sv[2][32], dv[2][32];
+      tmem_ld32(lane_base + st * 128, sv[0]);
+      tmem_ld32(lane_base + st * 128 + 32, sv[1]);
+      tmem_ld32(lane_base + st * 128 + 64, dv[0]);
+      tmem_ld32(lane_base + st * 128 + 96, dv[1]);
+      tmem_ld_wait();
+      uint8_t* prow = smem + DK_PT + st * 16384 + r * 128;
+      uint8_t* srow = smem + DK_DST + st * 16384 + r * 128;
+#pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t sv[32], dv[32];
-        tmem_ld32(lane_base + c * 32, sv);
-        tmem_ld32(lane_base + 64 + c * 32, dv);
-        tmem_ld_wait();
         uint32_t pp[16], ss[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const int qa = q0 + c * 32 + i;
-          const bool v0 = kj <= qa && kj > qa - w && qa < p.T && kj < p.T;
-          const bool v1 = kj <= qa + 1 && kj > qa + 1 - w && qa + 1 < p.T && kj < p.T;
-          const float p0 = v0 ? exp2f(__uint_as_float(sv[i]) * p.scale_log2 - ls[c * 32 + i] * kLog2e) : 0.f;
-          const float p1 = v1 ? exp2f(__uint_as_float(sv[i + 1]) * p.scale_log2 - ls[c * 32 + i + 1] * kLog2e) : 0.f;
+          const bool v0 = interior || (kj <= qa && kj > qa - w && qa < p.T && kj < p.T);
+          const bool v1 = interior || (kj <= qa + 1 && kj > qa + 1 - w && qa + 1 < p.T && kj < p.T);
+          const float p0 = v0 ? exp2f(__uint_as_float(sv[c][i]) * p.scale_log2 - ls[c * 32 + i] * kLog2e) : 0.f;
+          const float p1 = v1 ? exp2f(__uint_as_float(sv[c][i + 1]) * p.scale_log2 - ls[c * 32 + i + 1] * kLog2e) : 0.f;
           pp[i / 2] = pack_bf16(p0, p1);
-          ss[i / 2] = pack_bf16(p0 * (__uint_as_float(dv[i]) - ls[64 + c * 32 + i]),
-                                p1 * (__uint_as_float(dv[i + 1]) - ls[64 + c * 32 + i + 1]));
+          ss[i / 2] = pack_bf16(p0 * (__uint_as_float(dv[c][i]) - ls[64 + c * 32 + i]),
+                                p1 * (__uint_as_float(dv[c][i + 1]) - ls[64 + c * 32 + i + 1]));
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -724,7 +753,7 @@ __global__ void __launch_bounds__(192, 1)
         uint32_t v[32];
         const bool isk = c >= 4;
         const int cc = c & 3;
-        tmem_ld32(lane_base + (isk ? 256 : 128) + cc * 32, v);
+        tmem_ld32(lane_base + (isk ? 384 : 256) + cc * 32, v);
         tmem_ld_wait();
         const float sc = isk ? p.scale : 1.f;
         __nv_bfloat16* row = isk ? krow : vrow;
@@ -838,7 +867,7 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::
     attr = true;
   }
   auto st = at::cuda::getCurrentCUDAStream();
-  attn_dq_tc_kernel<<<dim3((unsigned)(T / BQ), (unsigned)H, (unsigned)B), 192, DQ_SMEM, st>>>(tq, td, p);
+  attn_dq_tc_kernel<<<dim3((unsigned)(T / BQ), (unsigned)H, (unsigned)B), 192, DQ_SMEM, st>>>(tq, td, tq64, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   attn_dkdv_tc_kernel<<<dim3((unsigned)(T / BKV), (unsigned)KV, (unsigned)B), 192, DK_SMEM, st>>>(tq, tq64, td64, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

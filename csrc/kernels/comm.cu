@@ -185,6 +185,123 @@ __global__ void __launch_bounds__(256) gather_kernel(const float* const* __restr
   }
 }
 
+// ------------------------------------------------------------------------------ top-k + error feedback
+// Deep Gradient Compression as in the reference sparsifier (gradient-sparsifier.ts:82-144), per bucket:
+//   g = grad * scale + e (+ momentum correction v = mu*v + g, g = v); thr = the floor(S*(1-k))-th
+//   smallest of S sampled |g|; keep |g| >= thr (e = 0) else e = g. Kept entries go on the wire as
+//   (u32 index, f16 value) pairs, appended to the list of the element's owner.
+
+__device__ __forceinline__ uint32_t hash_u32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352dU;
+  x ^= x >> 15;
+  x *= 0x846ca68bU;
+  x ^= x >> 16;
+  return x;
+}
+
+// One block: sample, sort (bitonic in shared memory) and pick the threshold for bucket [lo, hi).
+__global__ void __launch_bounds__(1024) topk_threshold_kernel(const float* __restrict__ grad, const float* __restrict__ err,
+                                                              const float* __restrict__ vel, int64_t lo, int64_t hi,
+                                                              float scale, float mu, int S, float keep_ratio,
+                                                              uint32_t seed, float* __restrict__ thr_out) {
+  extern __shared__ float smp[];  // S (power of two)
+  const int64_t n = hi - lo;
+  for (int i = threadIdx.x; i < S; i += blockDim.x) {
+    const int64_t j = lo + (int64_t)(hash_u32(seed ^ (uint32_t)(i * 2654435761u)) % (uint64_t)n);
+    float g = grad[j] * scale + err[j];
+    if (vel) g = mu * vel[j] + g;
+    smp[i] = fabsf(g);
+  }
+  __syncthreads();
+  for (int k = 2; k <= S; k <<= 1) {
+    for (int jj = k >> 1; jj > 0; jj >>= 1) {
+      for (int i = threadIdx.x; i < S; i += blockDim.x) {
+        const int ix = i ^ jj;
+        if (ix > i) {
+          const float a = smp[i], b = smp[ix];
+          const bool up = (i & k) == 0;
+          if ((a > b) == up) {
+            smp[i] = b;
+            smp[ix] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  if (threadIdx.x == 0) {
+    int cut = (int)floorf((float)S * (1.f - keep_ratio));
+    if (cut > S - 1) cut = S - 1;
+    *thr_out = smp[cut];
+  }
+}
+
+struct SelChunk {
+  int64_t off;    // element offset (flat layout)
+  int64_t len;
+  int64_t list;   // slot offset of the owner's list for this bucket (in pairs)
+  int64_t cnt;    // counter index of (bucket, owner)
+};
+
+// counts: this rank's per-(bucket, owner) counters (symmetric memory); idx/val: this rank's lists.
+__global__ void __launch_bounds__(256) topk_select_kernel(const float* __restrict__ grad, float* __restrict__ err,
+                                                          float* __restrict__ vel, const SelChunk* __restrict__ chunks,
+                                                          int nchunks, float scale, float mu,
+                                                          const float* __restrict__ thr_p, uint32_t* __restrict__ idx,
+                                                          __half* __restrict__ val, int* __restrict__ counts) {
+  const float thr = *thr_p;
+  const int lane = threadIdx.x & 31;
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    const SelChunk ch = chunks[c];
+    for (int64_t j0 = 0; j0 < ch.len; j0 += blockDim.x) {
+      const int64_t j = j0 + threadIdx.x;
+      bool keep = false;
+      float g = 0.f;
+      const int64_t i = ch.off + j;
+      if (j < ch.len) {
+        g = grad[i] * scale + err[i];
+        if (vel) {
+          g = mu * vel[i] + g;
+          vel[i] = g;
+        }
+        keep = fabsf(g) >= thr;
+        err[i] = keep ? 0.f : g;
+      }
+      const unsigned m = __ballot_sync(0xffffffffu, keep);
+      int base = 0;
+      if (lane == 0 && m) base = atomicAdd(counts + ch.cnt, __popc(m));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      if (keep) {
+        const int64_t slot = ch.list + base + __popc(m & ((1u << lane) - 1));
+        idx[slot] = (uint32_t)i;
+        val[slot] = __float2half(g);
+      }
+    }
+  }
+}
+
+struct PeerList {
+  int64_t idx;    // pointer to the peer's index array
+  int64_t val;    // pointer to the peer's value array
+  int64_t cnt;    // pointer to the peer's counters
+};
+
+// Owner side: red[idx] += val / N for every pair in every peer's list for (bucket, me).
+__global__ void __launch_bounds__(256) topk_reduce_kernel(const PeerList* __restrict__ peers, int npeers,
+                                                          const int64_t* const* flags, int slot, int64_t epoch,
+                                                          int64_t list_off, int cnt_index, float* __restrict__ red,
+                                                          float scale, uint64_t budget_ns, int* status) {
+  if (!wait_peers(flags, npeers, slot, epoch, budget_ns, status)) return;
+  for (int p = 0; p < npeers; ++p) {
+    const uint32_t* ix = reinterpret_cast<const uint32_t*>(peers[p].idx) + list_off;
+    const __half* vx = reinterpret_cast<const __half*>(peers[p].val) + list_off;
+    const int n = reinterpret_cast<const volatile int*>(peers[p].cnt)[cnt_index];
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
+      atomicAdd(red + ix[j], __half2float(vx[j]) * scale);
+  }
+}
+
 int sm_count() {
   int dev, n;
   cudaGetDevice(&dev);
@@ -293,4 +410,49 @@ void comm_gather(const torch::Tensor& peers, const torch::Tensor& flags, int64_t
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+}  // namespace br
+
+namespace br {
+void topk_threshold(const torch::Tensor& grad, const torch::Tensor& err, c10::optional<torch::Tensor> vel, int64_t lo,
+                    int64_t hi, double scale, double mu, int64_t sample, double keep_ratio, int64_t seed,
+                    torch::Tensor& thr_out) {
+  int S = 1;
+  while (S < std::min<int64_t>(sample, hi - lo)) S <<= 1;
+  TORCH_CHECK(S <= 16384, "topk_threshold: sample size must be <= 16384");
+  c10::cuda::CUDAGuard g(grad.device());
+  const size_t sm = (size_t)S * sizeof(float);
+  if (sm > 48 * 1024)
+    C10_CUDA_CHECK(cudaFuncSetAttribute(topk_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  topk_threshold_kernel<<<1, 1024, sm, at::cuda::getCurrentCUDAStream()>>>(
+      grad.data_ptr<float>(), err.data_ptr<float>(), vel.has_value() ? vel->data_ptr<float>() : nullptr, lo, hi,
+      (float)scale, (float)mu, S, (float)keep_ratio, (uint32_t)seed, thr_out.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// chunks: int64 [n, 4] = (off, len, list_slot, counter_index)
+void topk_select(const torch::Tensor& grad, torch::Tensor& err, c10::optional<torch::Tensor> vel,
+                 const torch::Tensor& chunks, double scale, double mu, const torch::Tensor& thr, int64_t idx_ptr,
+                 int64_t val_ptr, int64_t cnt_ptr) {
+  static_assert(sizeof(SelChunk) == 32, "SelChunk layout");
+  c10::cuda::CUDAGuard g(grad.device());
+  const int n = (int)chunks.size(0);
+  if (n == 0) return;
+  topk_select_kernel<<<std::min(n, 4 * sm_count()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      grad.data_ptr<float>(), err.data_ptr<float>(), vel.has_value() ? vel->data_ptr<float>() : nullptr,
+      reinterpret_cast<const SelChunk*>(chunks.data_ptr<int64_t>()), n, (float)scale, (float)mu, thr.data_ptr<float>(),
+      reinterpret_cast<uint32_t*>(idx_ptr), reinterpret_cast<__half*>(val_ptr), reinterpret_cast<int*>(cnt_ptr));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// peers: int64 [N, 3] = (idx ptr, val ptr, counters ptr) of every rank
+void topk_reduce(const torch::Tensor& peers, const torch::Tensor& flags, int64_t slot, int64_t epoch, int64_t list_off,
+                 int64_t cnt_index, torch::Tensor& red, double scale, int64_t max_blocks, double budget_s) {
+  static_assert(sizeof(PeerList) == 24, "PeerList layout");
+  c10::cuda::CUDAGuard g(red.device());
+  topk_reduce_kernel<<<(int)std::max<int64_t>(1, max_blocks), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const PeerList*>(peers.data_ptr<int64_t>()), (int)peers.size(0),
+      reinterpret_cast<const int64_t* const*>(flags.data_ptr<int64_t>()), (int)slot, epoch, list_off, (int)cnt_index,
+      red.data_ptr<float>(), (float)scale, (uint64_t)(budget_s * 1e9), status_ptr(red.device().index()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 }  // namespace br
