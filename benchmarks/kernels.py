@@ -156,6 +156,10 @@ def main():
             report(f"attn_fwd_tc w={window}", ms, flops=f_fwd, lib=lib)
             ms = timeit(lambda: E.attn_bwd_tc(qkv, o2, do, lse, dqkv, delta, B, T, H, H, 128, window), reps=5)
             report(f"attn_bwd_tc w={window} (2.5x fwd FLOPs)", ms, flops=2.5 * f_fwd)
+            ms = timeit(lambda: E.attn_bwd_tc(qkv, o2, do, lse, dqkv, delta, B, T, H, H, 128, window, 1), reps=5)
+            report(f"  attn_bwd_tc dq only (1.5x fwd)", ms, flops=1.5 * f_fwd)
+            ms = timeit(lambda: E.attn_bwd_tc(qkv, o2, do, lse, dqkv, delta, B, T, H, H, 128, window, 2), reps=5)
+            report(f"  attn_bwd_tc dkdv only (2x fwd)", ms, flops=2.0 * f_fwd)
 
     # ------------------------------------------------------------------ row kernels
     if want("rows"):

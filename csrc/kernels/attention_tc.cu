@@ -551,14 +551,15 @@ __global__ void __launch_bounds__(192, 1)
 constexpr int KB_Q = 64;
 constexpr int HALF_TILE = 64 * 128 * 2;   // 64 rows x 128 hd, two 8 KB swizzle atoms
 constexpr int HALF_ATOM = 64 * 128;
+constexpr int DK_STAGES = 3;                        // Q/dO ring: block i+1 is issued ahead while i-1 drains
 constexpr int DK_K = 0;
 constexpr int DK_V = DK_K + TILE_BYTES;
-constexpr int DK_Q = DK_V + TILE_BYTES;            // [2] x HALF_TILE
-constexpr int DK_DO = DK_Q + 2 * HALF_TILE;        // [2] x HALF_TILE
-constexpr int DK_PT = DK_DO + 2 * HALF_TILE;       // [2] x (128 keys x 64 q bf16 = one 16 KB atom)
+constexpr int DK_Q = DK_V + TILE_BYTES;            // [3] x HALF_TILE
+constexpr int DK_DO = DK_Q + DK_STAGES * HALF_TILE;  // [3] x HALF_TILE
+constexpr int DK_PT = DK_DO + DK_STAGES * HALF_TILE; // [2] x (128 keys x 64 q bf16 = one 16 KB atom)
 constexpr int DK_DST = DK_PT + 2 * 16384;          // [2] x 16 KB
-constexpr int DK_STAT = DK_DST + 2 * 16384;        // [2] x (lse[64], delta[64]) floats
-constexpr int DK_BAR = DK_STAT + 2 * 512;
+constexpr int DK_STAT = DK_DST + 2 * 16384;        // [3] x (lse[64], delta[64]) floats
+constexpr int DK_BAR = DK_STAT + DK_STAGES * 512;
 constexpr int DK_SMEM = DK_BAR + 256 + 1024;
 
 __global__ void __launch_bounds__(192, 1)
@@ -569,12 +570,12 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DK_BAR);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;   // [2]
-  uint64_t* qd_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* p_full = bars + 7;
-  uint64_t* done = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t* qd_full = bars + 1;   // [3]
+  uint64_t* qd_empty = bars + 4;  // [3]
+  uint64_t* s_full = bars + 7;    // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* done = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* stat = reinterpret_cast<float*>(smem + DK_STAT);
 
@@ -590,11 +591,12 @@ __global__ void __launch_bounds__(192, 1)
   if (device_failed(p.status)) return;
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < DK_STAGES; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
-      mbar_init(&s_full[i], 1);
     }
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
     mbar_init(p_full, 128);
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -618,8 +620,8 @@ __global__ void __launch_bounds__(192, 1)
       tma_load_3d(&tm_kv, kv_full, smem + DK_V, p.Dq + p.Dkv + kvh * HD, k0, b);
       tma_load_3d(&tm_kv, kv_full, smem + DK_V + ATOM_BYTES, p.Dq + p.Dkv + kvh * HD + 64, k0, b);
       for (int it = 0; it < iters; ++it) {
-        const int st = it & 1;
-        if (!mbar_wait(&qd_empty[st], ((it >> 1) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
+        const int st = it % DK_STAGES;
+        if (!mbar_wait(&qd_empty[st], ((it / DK_STAGES) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
           fail(kErrTimeoutProducer);
           break;
         }
@@ -645,8 +647,8 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t k_addr = smem_u32(smem + DK_K), v_addr = smem_u32(smem + DK_V);
       bool ok = mbar_wait(kv_full, 0, kBudgetNs, abort_flag, p.status);
       auto issue_s = [&](int it) -> bool {
-        const int st = it & 1;
-        if (!mbar_wait(&qd_full[st], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) return false;
+        const int st = it % DK_STAGES, set = it & 1;
+        if (!mbar_wait(&qd_full[st], (it / DK_STAGES) & 1, kBudgetNs, abort_flag, p.status)) return false;
         tc_fence_after();
         const uint32_t q_addr = smem_u32(smem + DK_Q + st * HALF_TILE);
         const uint32_t do_addr = smem_u32(smem + DK_DO + st * HALF_TILE);
@@ -654,12 +656,12 @@ __global__ void __launch_bounds__(192, 1)
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t offa = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
           const uint32_t offb = (kk >> 2) * HALF_ATOM + (kk & 3) * 32;
-          umma_bf16_ss(tmem + st * 128, umma_desc_sw128(k_addr + offa, 16, 1024),
+          umma_bf16_ss(tmem + set * 128, umma_desc_sw128(k_addr + offa, 16, 1024),
                        umma_desc_sw128(q_addr + offb, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-          umma_bf16_ss(tmem + st * 128 + 64, umma_desc_sw128(v_addr + offa, 16, 1024),
+          umma_bf16_ss(tmem + set * 128 + 64, umma_desc_sw128(v_addr + offa, 16, 1024),
                        umma_desc_sw128(do_addr + offb, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[st]);
+        umma_commit(&s_full[set]);
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -673,11 +675,11 @@ __global__ void __launch_bounds__(192, 1)
           break;
         }
         tc_fence_after();
-        const int st = it & 1;
+        const int st = it % DK_STAGES, set = it & 1;
         const uint32_t q_addr = smem_u32(smem + DK_Q + st * HALF_TILE);
         const uint32_t do_addr = smem_u32(smem + DK_DO + st * HALF_TILE);
-        const uint32_t pt_addr = smem_u32(smem + DK_PT + st * 16384);
-        const uint32_t dst_addr = smem_u32(smem + DK_DST + st * 16384);
+        const uint32_t pt_addr = smem_u32(smem + DK_PT + set * 16384);
+        const uint32_t dst_addr = smem_u32(smem + DK_DST + set * 16384);
 #pragma unroll
         for (int kk = 0; kk < KB_Q / 16; ++kk) {
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
@@ -699,8 +701,8 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
     bool ok = true;
     for (int it = 0; it < iters; ++it) {
-      const int st = it & 1;
-      if (!mbar_wait_warp(&s_full[st], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+      const int set = it & 1, st = it % DK_STAGES;
+      if (!mbar_wait_warp(&s_full[set], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
         break;
@@ -711,13 +713,13 @@ __global__ void __launch_bounds__(192, 1)
       // every (query, key) pair of this block visible: keys of the tile <= first query and within the window
       const bool interior = (k0 + BKV - 1 <= q0) && (k0 > q0 + KB_Q - 1 - w) && (q0 + KB_Q <= p.T) && (k0 + BKV <= p.T);
       uint32_t sv[2][32], dv[2][32];
-      tmem_ld32(lane_base + st * 128, sv[0]);
-      tmem_ld32(lane_base + st * 128 + 32, sv[1]);
-      tmem_ld32(lane_base + st * 128 + 64, dv[0]);
-      tmem_ld32(lane_base + st * 128 + 96, dv[1]);
+      tmem_ld32(lane_base + set * 128, sv[0]);
+      tmem_ld32(lane_base + set * 128 + 32, sv[1]);
+      tmem_ld32(lane_base + set * 128 + 64, dv[0]);
+      tmem_ld32(lane_base + set * 128 + 96, dv[1]);
       tmem_ld_wait();
-      uint8_t* prow = smem + DK_PT + st * 16384 + r * 128;
-      uint8_t* srow = smem + DK_DST + st * 16384 + r * 128;
+      uint8_t* prow = smem + DK_PT + set * 16384 + r * 128;
+      uint8_t* srow = smem + DK_DST + set * 16384 + r * 128;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t pp[16], ss[16];
@@ -825,13 +827,14 @@ void attn_delta(const torch::Tensor& o, const torch::Tensor& dout, torch::Tensor
 // dqkv: [B*T, Dq + 2*Dkv] bf16 output (dq | dk | dv); dout: [B*T, H*hd] bf16; lse, delta: fp32 [B, H, T].
 void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::Tensor& dout, const torch::Tensor& lse,
                  torch::Tensor& dqkv, torch::Tensor& delta, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd,
-                 int64_t window) {
+                 int64_t window, int64_t which) {
+  // which: 0 = delta, dQ and dK/dV; 1 = delta and dQ only; 2 = dK/dV only (delta already computed)
   TORCH_CHECK(hd == HD && T % 128 == 0, "attn_bwd_tc: head_dim 128 and T % 128 == 0");
   const int64_t W = qkv.size(1);
   TORCH_CHECK(W == (H + 2 * KV) * hd && dqkv.size(1) == W, "attn_bwd_tc: widths");
   TORCH_CHECK(dout.stride(1) == 1 && dout.size(1) == H * hd, "attn_bwd_tc: dout");
   c10::cuda::CUDAGuard g(qkv.device());
-  attn_delta(o, dout, delta, B, T, H);
+  if (which != 2) attn_delta(o, dout, delta, B, T, H);
   CUtensorMap tq = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.data_ptr(), W, T, B, qkv.stride(0),
                               qkv.stride(0) * T, 64, 128);
   CUtensorMap td = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dout.data_ptr(), H * hd, T, B, dout.stride(0),
@@ -867,9 +870,13 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::
     attr = true;
   }
   auto st = at::cuda::getCurrentCUDAStream();
-  attn_dq_tc_kernel<<<dim3((unsigned)(T / BQ), (unsigned)H, (unsigned)B), 192, DQ_SMEM, st>>>(tq, td, tq64, p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-  attn_dkdv_tc_kernel<<<dim3((unsigned)(T / BKV), (unsigned)KV, (unsigned)B), 192, DK_SMEM, st>>>(tq, tq64, td64, p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (which != 2) {
+    attn_dq_tc_kernel<<<dim3((unsigned)(T / BQ), (unsigned)H, (unsigned)B), 192, DQ_SMEM, st>>>(tq, td, tq64, p);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  if (which != 1) {
+    attn_dkdv_tc_kernel<<<dim3((unsigned)(T / BKV), (unsigned)KV, (unsigned)B), 192, DK_SMEM, st>>>(tq, tq64, td64, p);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
 }
 }  // namespace br

@@ -53,7 +53,7 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse,
                  int64_t KV, int64_t hd, int64_t window);
 void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::Tensor& dout, const torch::Tensor& lse,
                  torch::Tensor& dqkv, torch::Tensor& delta, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd,
-                 int64_t window);
+                 int64_t window, int64_t which);
 std::tuple<int64_t, torch::Tensor> sym_alloc(int64_t bytes);
 int64_t sym_open(const torch::Tensor& handle);
 void sym_close(int64_t ptr);
@@ -99,7 +99,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &br::attn_fwd);
   m.def("attn_bwd", &br::attn_bwd);
   m.def("attn_fwd_tc", &br::attn_fwd_tc);
-  m.def("attn_bwd_tc", &br::attn_bwd_tc);
+  m.def("attn_bwd_tc", &br::attn_bwd_tc, pybind11::arg("qkv"), pybind11::arg("o"), pybind11::arg("dout"),
+        pybind11::arg("lse"), pybind11::arg("dqkv"), pybind11::arg("delta"), pybind11::arg("B"), pybind11::arg("T"),
+        pybind11::arg("H"), pybind11::arg("KV"), pybind11::arg("hd"), pybind11::arg("window"),
+        pybind11::arg("which") = 0);
   m.def("sym_alloc", &br::sym_alloc);
   m.def("sym_open", &br::sym_open);
   m.def("sym_close", &br::sym_close);
