@@ -347,7 +347,7 @@ constexpr int DQ_DS = DQ_V + DQ_STAGES * KV64;      // [2] x (128 q x 64 keys bf
 constexpr int DQ_BAR = DQ_DS + 2 * 16384;
 constexpr int DQ_SMEM = DQ_BAR + 256 + 1024;
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                       const __grid_constant__ CUtensorMap tm_kv, BwdParams p) {
   // tm_q / tm_do: 128-row boxes; tm_kv: 64-row boxes
@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -466,7 +466,9 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(done, 0, kBudgetNs, nullptr);
     }
   } else {
+    // 8 softmax warps: warps w and w+4 share TMEM lane group w%4 (rows) and split each block's columns
     const int wq = warp & 3, lane = lane_id();
+    const int half = (warp - 2) >> 2;
     const int r = wq * 32 + lane;
     const int qi = q0 + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
@@ -482,33 +484,28 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      const int k0 = (kb_lo + j) * BK64;
-      const bool interior = (k0 + BK64 - 1 <= q0) && (k0 > q0 + BQ - 1 - w) && (k0 + BK64 <= p.T);
-      uint32_t sv[2][32], dv[2][32];
-      tmem_ld32(lane_base + set * 128, sv[0]);
-      tmem_ld32(lane_base + set * 128 + 32, sv[1]);
-      tmem_ld32(lane_base + set * 128 + 64, dv[0]);
-      tmem_ld32(lane_base + set * 128 + 96, dv[1]);
+      const int k0 = (kb_lo + j) * BK64 + half * 32;
+      const bool interior = (k0 + 31 <= q0) && (k0 > q0 + BQ - 1 - w) && (k0 + 32 <= p.T);
+      uint32_t sv[32], dv[32];
+      tmem_ld32(lane_base + set * 128 + half * 32, sv);
+      tmem_ld32(lane_base + set * 128 + 64 + half * 32, dv);
       tmem_ld_wait();
       uint8_t* drow = smem + DQ_DS + set * 16384 + r * 128;
+      uint32_t pk[16];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[16];
+      for (int i = 0; i < 32; i += 2) {
+        const int kj = k0 + i;
+        const bool v0 = interior || (kj <= qi && kj > qi - w && kj < p.T);
+        const bool v1 = interior || (kj + 1 <= qi && kj + 1 > qi - w && kj + 1 < p.T);
+        const float p0 = v0 ? exp2f(__uint_as_float(sv[i]) * p.scale_log2 - lse2) : 0.f;
+        const float p1 = v1 ? exp2f(__uint_as_float(sv[i + 1]) * p.scale_log2 - lse2) : 0.f;
+        pk[i / 2] = pack_bf16(p0 * (__uint_as_float(dv[i]) - dl), p1 * (__uint_as_float(dv[i + 1]) - dl));
+      }
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int kj = k0 + c * 32 + i;
-          const bool v0 = interior || (kj <= qi && kj > qi - w && kj < p.T);
-          const bool v1 = interior || (kj + 1 <= qi && kj + 1 > qi - w && kj + 1 < p.T);
-          const float p0 = v0 ? exp2f(__uint_as_float(sv[c][i]) * p.scale_log2 - lse2) : 0.f;
-          const float p1 = v1 ? exp2f(__uint_as_float(sv[c][i + 1]) * p.scale_log2 - lse2) : 0.f;
-          pk[i / 2] = pack_bf16(p0 * (__uint_as_float(dv[c][i]) - dl), p1 * (__uint_as_float(dv[c][i + 1]) - dl));
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = c * 4 + q;
-          *reinterpret_cast<uint4*>(drow + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-        }
+      for (int q = 0; q < 4; ++q) {
+        const int chunk = half * 4 + q;
+        *reinterpret_cast<uint4*>(drow + ((chunk ^ (r & 7)) << 4)) =
+            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
       }
       fence_async_smem();
       tc_fence_before();
@@ -518,7 +515,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       __nv_bfloat16* row = p.dq + ((int64_t)b * p.T + qi) * p.lddq + h * HD;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = half * 2; c < half * 2 + 2; ++c) {
         uint32_t v[32];
         tmem_ld32(lane_base + 256 + c * 32, v);
         tmem_ld_wait();
@@ -562,7 +559,7 @@ constexpr int DK_STAT = DK_DST + 2 * 16384;        // [3] x (lse[64], delta[64])
 constexpr int DK_BAR = DK_STAT + DK_STAGES * 512;
 constexpr int DK_SMEM = DK_BAR + 256 + 1024;
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_qkv,
                         const __grid_constant__ CUtensorMap tm_do, BwdParams p) {
   // tm_kv: 128-row boxes (the CTA's K and V tiles); tm_qkv / tm_do: 64-row boxes (query blocks)
@@ -597,7 +594,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -695,7 +692,9 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(done, 0, kBudgetNs, nullptr);
     }
   } else {
+    // 8 softmax warps: warps w and w+4 share TMEM lane group w%4 (keys) and split each block's queries
     const int wq = warp & 3, lane = lane_id();
+    const int half = (warp - 2) >> 2;
     const int r = wq * 32 + lane;
     const int kj = k0 + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
@@ -708,39 +707,33 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      const int q0 = (qb_lo + it % nq) * KB_Q;
-      const float* ls = stat + st * 128;
-      // every (query, key) pair of this block visible: keys of the tile <= first query and within the window
-      const bool interior = (k0 + BKV - 1 <= q0) && (k0 > q0 + KB_Q - 1 - w) && (q0 + KB_Q <= p.T) && (k0 + BKV <= p.T);
-      uint32_t sv[2][32], dv[2][32];
-      tmem_ld32(lane_base + set * 128, sv[0]);
-      tmem_ld32(lane_base + set * 128 + 32, sv[1]);
-      tmem_ld32(lane_base + set * 128 + 64, dv[0]);
-      tmem_ld32(lane_base + set * 128 + 96, dv[1]);
+      const int q0 = (qb_lo + it % nq) * KB_Q + half * 32;
+      const float* ls = stat + st * 128 + half * 32;
+      // every (query, key) pair of these 32 queries visible to every key row of the tile
+      const bool interior = (k0 + BKV - 1 <= q0) && (k0 > q0 + 31 - w) && (q0 + 32 <= p.T) && (k0 + BKV <= p.T);
+      uint32_t sv[32], dv[32];
+      tmem_ld32(lane_base + set * 128 + half * 32, sv);
+      tmem_ld32(lane_base + set * 128 + 64 + half * 32, dv);
       tmem_ld_wait();
       uint8_t* prow = smem + DK_PT + set * 16384 + r * 128;
       uint8_t* srow = smem + DK_DST + set * 16384 + r * 128;
+      uint32_t pp[16], ss[16];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pp[16], ss[16];
+      for (int i = 0; i < 32; i += 2) {
+        const int qa = q0 + i;
+        const bool v0 = interior || (kj <= qa && kj > qa - w && qa < p.T && kj < p.T);
+        const bool v1 = interior || (kj <= qa + 1 && kj > qa + 1 - w && qa + 1 < p.T && kj < p.T);
+        const float p0 = v0 ? exp2f(__uint_as_float(sv[i]) * p.scale_log2 - ls[i] * kLog2e) : 0.f;
+        const float p1 = v1 ? exp2f(__uint_as_float(sv[i + 1]) * p.scale_log2 - ls[i + 1] * kLog2e) : 0.f;
+        pp[i / 2] = pack_bf16(p0, p1);
+        ss[i / 2] = pack_bf16(p0 * (__uint_as_float(dv[i]) - ls[64 + i]), p1 * (__uint_as_float(dv[i + 1]) - ls[64 + i + 1]));
+      }
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int qa = q0 + c * 32 + i;
-          const bool v0 = interior || (kj <= qa && kj > qa - w && qa < p.T && kj < p.T);
-          const bool v1 = interior || (kj <= qa + 1 && kj > qa + 1 - w && qa + 1 < p.T && kj < p.T);
-          const float p0 = v0 ? exp2f(__uint_as_float(sv[c][i]) * p.scale_log2 - ls[c * 32 + i] * kLog2e) : 0.f;
-          const float p1 = v1 ? exp2f(__uint_as_float(sv[c][i + 1]) * p.scale_log2 - ls[c * 32 + i + 1] * kLog2e) : 0.f;
-          pp[i / 2] = pack_bf16(p0, p1);
-          ss[i / 2] = pack_bf16(p0 * (__uint_as_float(dv[c][i]) - ls[64 + c * 32 + i]),
-                                p1 * (__uint_as_float(dv[c][i + 1]) - ls[64 + c * 32 + i + 1]));
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = c * 4 + q;
-          const int phys = (chunk ^ (r & 7)) << 4;
-          *reinterpret_cast<uint4*>(prow + phys) = make_uint4(pp[4 * q], pp[4 * q + 1], pp[4 * q + 2], pp[4 * q + 3]);
-          *reinterpret_cast<uint4*>(srow + phys) = make_uint4(ss[4 * q], ss[4 * q + 1], ss[4 * q + 2], ss[4 * q + 3]);
-        }
+      for (int q = 0; q < 4; ++q) {
+        const int chunk = half * 4 + q;
+        const int phys = (chunk ^ (r & 7)) << 4;
+        *reinterpret_cast<uint4*>(prow + phys) = make_uint4(pp[4 * q], pp[4 * q + 1], pp[4 * q + 2], pp[4 * q + 3]);
+        *reinterpret_cast<uint4*>(srow + phys) = make_uint4(ss[4 * q], ss[4 * q + 1], ss[4 * q + 2], ss[4 * q + 3]);
       }
       fence_async_smem();
       tc_fence_before();
@@ -748,17 +741,16 @@ __global__ void __launch_bounds__(192, 1)
     }
     if (ok && mbar_wait_warp(done, 0, kBudgetNs, abort_flag, p.status)) {
       tc_fence_after();
-      __nv_bfloat16* vrow = p.dv + ((int64_t)b * p.T + kj) * p.lddv + kvh * HD;
-      __nv_bfloat16* krow = p.dk + ((int64_t)b * p.T + kj) * p.lddk + kvh * HD;
+      // half 0 writes dV, half 1 writes dK
+      const bool isk = half == 1;
+      __nv_bfloat16* row = isk ? p.dk + ((int64_t)b * p.T + kj) * p.lddk + kvh * HD
+                               : p.dv + ((int64_t)b * p.T + kj) * p.lddv + kvh * HD;
+      const float sc = isk ? p.scale : 1.f;
 #pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
+      for (int cc = 0; cc < 4; ++cc) {
         uint32_t v[32];
-        const bool isk = c >= 4;
-        const int cc = c & 3;
         tmem_ld32(lane_base + (isk ? 384 : 256) + cc * 32, v);
         tmem_ld_wait();
-        const float sc = isk ? p.scale : 1.f;
-        __nv_bfloat16* row = isk ? krow : vrow;
         if (kj < p.T) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -871,11 +863,11 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::
   }
   auto st = at::cuda::getCurrentCUDAStream();
   if (which != 2) {
-    attn_dq_tc_kernel<<<dim3((unsigned)(T / BQ), (unsigned)H, (unsigned)B), 192, DQ_SMEM, st>>>(tq, td, tq64, p);
+    attn_dq_tc_kernel<<<dim3((unsigned)(T / BQ), (unsigned)H, (unsigned)B), 320, DQ_SMEM, st>>>(tq, td, tq64, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   if (which != 1) {
-    attn_dkdv_tc_kernel<<<dim3((unsigned)(T / BKV), (unsigned)KV, (unsigned)B), 192, DK_SMEM, st>>>(tq, tq64, td64, p);
+    attn_dkdv_tc_kernel<<<dim3((unsigned)(T / BKV), (unsigned)KV, (unsigned)B), 320, DK_SMEM, st>>>(tq, tq64, td64, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
