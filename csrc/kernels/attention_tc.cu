@@ -358,9 +358,10 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* kv_full = bars + 1;   // [4]
   uint64_t* kv_empty = bars + 5;  // [4]
   uint64_t* s_full = bars + 9;    // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* done = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* p_full = bars + 11;   // [2]: by iteration parity, so a warp group running one block ahead
+                                  // arrives on the other barrier and never completes the current phase
+  uint64_t* done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -380,7 +381,8 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 256);
+    mbar_init(&p_full[0], 256);
+    mbar_init(&p_full[1], 256);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -447,7 +449,7 @@ __global__ void __launch_bounds__(320, 1)
           ok = false;
           break;
         }
-        if (!mbar_wait(p_full, j & 1, kBudgetNs, abort_flag, p.status)) {
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
           ok = false;
           break;
         }
@@ -509,7 +511,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j & 1]);
     }
     if (ok && mbar_wait_warp(done, 0, kBudgetNs, abort_flag, p.status)) {
       tc_fence_after();
@@ -570,9 +572,9 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* qd_full = bars + 1;   // [3]
   uint64_t* qd_empty = bars + 4;  // [3]
   uint64_t* s_full = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* done = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* p_full = bars + 9;    // [2], by iteration parity (see the dQ kernel)
+  uint64_t* done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* stat = reinterpret_cast<float*>(smem + DK_STAT);
 
@@ -594,7 +596,8 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 256);
+    mbar_init(&p_full[0], 256);
+    mbar_init(&p_full[1], 256);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -667,7 +670,7 @@ __global__ void __launch_bounds__(320, 1)
           ok = false;
           break;
         }
-        if (!mbar_wait(p_full, it & 1, kBudgetNs, abort_flag, p.status)) {
+        if (!mbar_wait(&p_full[it & 1], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
           ok = false;
           break;
         }
@@ -737,7 +740,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[it & 1]);
     }
     if (ok && mbar_wait_warp(done, 0, kBudgetNs, abort_flag, p.status)) {
       tc_fence_after();

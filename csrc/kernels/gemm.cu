@@ -471,9 +471,25 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
   p.n_tiles = (int)((N + BN - 1) / BN);
   p.k_blocks = (int)((K + BK - 1) / BK);
   int splits = (int)std::max<int64_t>(1, k_splits);
-  if (k_splits <= 0) {  // auto: fill ~2 waves when the tile count is small, keep >= 8 k-blocks per split
+  if (k_splits <= 0) {
+    // auto split-K: among split counts that keep >= 16 k-blocks per split, pick the one whose work
+    // units fill the persistent grid's waves best (least idle fraction in the last wave), preferring
+    // fewer splits (less reduce-add traffic) on ties
     const int tiles = p.m_tiles * p.n_tiles * p.batch;
-    splits = std::max(1, std::min(p.k_blocks / 8, (2 * num_sms() + tiles - 1) / tiles));
+    const int sms = num_sms();
+    splits = 1;
+    double best = 1e9;
+    const int max_s = std::max(1, std::min(64, p.k_blocks / 16));
+    for (int sp = 1; sp <= max_s; ++sp) {
+      const int64_t units = (int64_t)tiles * sp;
+      const int64_t waves = (units + sms - 1) / sms;
+      const double waste = (double)(waves * sms - units) / (double)(waves * sms);
+      const double cost = waste + (units < sms ? 1.0 : 0.0) + 0.002 * sp;
+      if (cost < best - 1e-9) {
+        best = cost;
+        splits = sp;
+      }
+    }
     if (epi != EPI_ATOMIC_F32) splits = 1;
   }
   TORCH_CHECK(splits == 1 || epi == EPI_ATOMIC_F32, "k_splits > 1 needs the accumulating epilogue");
