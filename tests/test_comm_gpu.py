@@ -206,3 +206,50 @@ def test_p2p_trainer_matches_nccl_2gpu():
             assert frac_bad < (5e-2 if adam else 1e-3), (n, frac_bad)
     for n in res[0]["p2p"][1]:
         assert torch.equal(res[0]["p2p"][1][n], res[1]["p2p"][1][n]), n  # ranks hold identical replicas
+
+
+def _topk(rank, world):
+    """One bucket of n elements; rank 0 owns the first half, rank 1 the second."""
+    from bitresearch_b200.ops._ext import check_status, ext
+    from bitresearch_b200.parallel.comm import SymmetricBuffer
+    E = ext()
+    n, half, k = 65536, 32768, 0.05
+    g = torch.randn(n, generator=torch.Generator().manual_seed(10 + rank)).cuda()
+    err = torch.zeros(n, device="cuda")
+    thr = torch.zeros(1, device="cuda")
+    idx = SymmetricBuffer(n * 4)
+    val = SymmetricBuffer(n * 2)
+    cnt = SymmetricBuffer(64)
+    flags = SymmetricBuffer(64)
+    # list regions: owner 0 at [0, half), owner 1 at [half, n); counters 0 and 1
+    chunks = torch.tensor([[0, half, 0, 0], [half, half, half, 1]], dtype=torch.int64, device="cuda")
+    E.topk_threshold(g, err, None, 0, n, 1.0, 0.0, 10000, k, 1234 + rank, thr)
+    E.topk_select(g, err, None, chunks, 1.0, 0.0, thr, idx.ptr, val.ptr, cnt.ptr)
+    E.comm_signal(flags.ptr, 5)
+    peers = torch.tensor([[idx.peer_ptrs[r], val.peer_ptrs[r], cnt.peer_ptrs[r]] for r in range(world)],
+                         dtype=torch.int64, device="cuda")
+    fp = torch.tensor(flags.peer_ptrs, dtype=torch.int64, device="cuda")
+    red = torch.zeros(n, device="cuda")
+    E.topk_reduce(peers, fp, 0, 5, rank * half, rank, red, 1.0 / world, 16, 10.0)
+    torch.cuda.synchronize()
+    out = (g.cpu(), err.cpu(), float(thr.item()), red.cpu(), check_status())
+    torch.distributed.barrier()
+    for b in (idx, val, cnt, flags):
+        b.close()
+    return out
+
+
+def test_topk_sparse_reduce_2gpu():
+    res = _run(_topk)
+    n, half = 65536, 32768
+    kept = []
+    for g, err, thr, _, st in res:
+        assert st == 0
+        keep = g.abs() >= thr
+        assert 0.03 < keep.float().mean().item() < 0.07  # about k = 5% from a 10000-sample threshold
+        torch.testing.assert_close(err, torch.where(keep, torch.zeros_like(g), g))  # residual = what was dropped
+        kept.append(torch.where(keep, g, torch.zeros_like(g)).half().float())
+    mean = (kept[0] + kept[1]) / 2
+    for r, (_, _, _, red, _) in enumerate(res):
+        sl = slice(r * half, (r + 1) * half)
+        torch.testing.assert_close(red[sl], mean[sl], rtol=1e-3, atol=1e-3)
