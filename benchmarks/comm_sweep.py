@@ -101,23 +101,33 @@ class P2PBench:
         self.E.comm_signal(self.flags.ptr + 8 * slot, epoch)
         self.last[slot] = epoch
 
-    def rs(self, src: torch.Tensor, wire: int, out: torch.Tensor):
+    def rs(self, src: torch.Tensor, wire: int, out: torch.Tensor, mark=None):
+        mark = mark or (lambda name: None)
         e = self.epoch = self.epoch + 1
         self._wait(SLOT_READ)  # every peer has read last iteration's send buffer
+        mark("wait_read")
         self.E.comm_pack(src, self.send.ptr, wire, 0, self.n, 1.0, self.bad)
+        mark("pack")
         self._signal(SLOT_READY, e)
+        mark("signal")
         self.E.comm_reduce(self.send.peers_dev, self.flag_ptrs, SLOT_READY, e, self.chunks, out, wire,
                            1.0 / self.world, self.blocks, self.budget)
+        mark("reduce")
         self._signal(SLOT_READ, e)
 
-    def ar(self, src: torch.Tensor, wire: int):
+    def ar(self, src: torch.Tensor, wire: int, mark=None):
+        mark = mark or (lambda name: None)
         e = self.epoch + 1
         self._wait(SLOT_GATHERED)  # every peer has gathered last iteration's result
-        self.rs(src, wire, self.res_view)
+        mark("wait_gathered")
+        self.rs(src, wire, self.res_view, mark)
         self._signal(SLOT_RES, e)
+        mark("signal2")
         self.E.comm_gather(self.res.peers_dev, self.flag_ptrs, SLOT_RES, e, self.segs, self.res_view, self.blocks,
                            self.budget)
+        mark("gather")
         self._signal(SLOT_GATHERED, e)
+        mark("signal3")
 
     def topk(self, src: torch.Tensor, ratio: float, out: torch.Tensor):
         e = self.epoch = self.epoch + 1
@@ -154,6 +164,35 @@ def time_iters(fn, iters: int, warm: int = 3) -> float:
     return float(t.item())
 
 
+def breakdown(bench: P2PBench, nbytes: int, wire: str, iters: int = 20) -> dict:
+    """Device time of each phase of one p2p all-reduce iteration (median over iterations, max over ranks)."""
+    code, _, esz = WIRE[wire]
+    n = max(8 * bench.world, (nbytes // esz) // (8 * bench.world) * (8 * bench.world))
+    bench.setup(n)
+    src = torch.randn(n, device="cuda")
+    rows = []
+    for it in range(iters + 3):
+        evs = []
+
+        def mark(name, evs=evs):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            evs.append((name, ev))
+
+        mark("start")
+        bench.ar(src, code, mark)
+        torch.cuda.synchronize()
+        if it >= 3:
+            rows.append({evs[i][0]: evs[i - 1][1].elapsed_time(evs[i][1]) * 1e3 for i in range(1, len(evs))})
+    out = {}
+    for k in rows[0]:
+        vals = sorted(r[k] for r in rows)
+        t = torch.tensor([vals[len(vals) // 2]], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out[k] = round(float(t.item()), 2)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--min-bytes", type=int, default=1 << 10)
@@ -162,6 +201,7 @@ def main():
     ap.add_argument("--variants", default="nccl_rs,p2p_rs,nccl_ar,p2p_ar,p2p_topk")
     ap.add_argument("--topk", type=float, default=0.01)
     ap.add_argument("--json", default="")
+    ap.add_argument("--breakdown", default="", help="comma-separated bucket sizes (bytes): per-phase us of p2p_ar")
     args = ap.parse_args()
 
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
@@ -178,6 +218,12 @@ def main():
     max_elems = args.max_bytes // 2 + 8 * world
     bench = P2PBench(max_elems, rank, world)
     variants = args.variants.split(",")
+    if args.breakdown:
+        for nb in args.breakdown.split(","):
+            for wname in args.wires.split(","):
+                ph = breakdown(bench, int(nb), wname)
+                if rank == 0:
+                    print(json.dumps({"breakdown_us": ph, "bytes": int(nb), "wire": wname, "n_gpus": world}), flush=True)
     rows = []
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
     for wname in args.wires.split(","):

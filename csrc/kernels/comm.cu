@@ -70,12 +70,13 @@ struct Chunk {
 
 template <int WIRE>
 __device__ __forceinline__ void load8(const void* base, int64_t i, float (&v)[8]) {
+  // peers' buffers are read with L2-only loads (.cg): L1 is not coherent with another GPU's writes
   if constexpr (WIRE == W_F32) {
-    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i);
-    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i + 4);
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i));
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i + 4));
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   } else {
-    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + i);
+    const uint4 u = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + i));
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -95,9 +96,10 @@ __device__ __forceinline__ void load8(const void* base, int64_t i, float (&v)[8]
 
 template <int WIRE>
 __device__ __forceinline__ float load1(const void* base, int64_t i) {
-  if constexpr (WIRE == W_F32) return reinterpret_cast<const float*>(base)[i];
-  if constexpr (WIRE == W_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[i]);
-  return __half2float(reinterpret_cast<const __half*>(base)[i]);
+  if constexpr (WIRE == W_F32) return __ldcg(reinterpret_cast<const float*>(base) + i);
+  const unsigned short u = __ldcg(reinterpret_cast<const unsigned short*>(base) + i);
+  if constexpr (WIRE == W_BF16) return __bfloat162float(__ushort_as_bfloat16(u));
+  return __half2float(__ushort_as_half(u));
 }
 
 template <int WIRE>
@@ -107,12 +109,43 @@ __device__ __forceinline__ void store_wire(void* base, int64_t i, float x) {
   else reinterpret_cast<__half*>(base)[i] = __float2half(x);
 }
 
-// grid-stride over [lo, hi): send[i] = wire(src[i] * scale); *bad |= any non-finite
+template <int WIRE>
+__device__ __forceinline__ void store_wire4(void* base, int64_t i, float4 x) {
+  if constexpr (WIRE == W_F32) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + i) = x;
+  } else if constexpr (WIRE == W_BF16) {
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(base) + i) = make_uint2(pack_bf16(x.x, x.y), pack_bf16(x.z, x.w));
+  } else {
+    const __half2 a = __floats2half2_rn(x.x, x.y), b = __floats2half2_rn(x.z, x.w);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(base) + i) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+  }
+}
+
+// grid-stride over [lo, hi): send[i] = wire(src[i] * scale); *bad |= any non-finite. The 4-aligned body
+// moves 16-byte loads and 8/16-byte stores; the unaligned head and tail go element by element.
 template <int WIRE>
 __global__ void pack_kernel(const float* __restrict__ src, void* __restrict__ send, int64_t lo, int64_t hi, float scale,
                             int* __restrict__ bad) {
   int nonfinite = 0;
-  for (int64_t i = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < hi; i += (int64_t)gridDim.x * blockDim.x) {
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, nth = (int64_t)gridDim.x * blockDim.x;
+  const int64_t a = min(hi, (lo + 3) & ~int64_t(3));
+  const int64_t b4 = a + ((hi - a) & ~int64_t(3));
+  for (int64_t i = lo + tid; i < a; i += nth) {
+    const float x = src[i] * scale;
+    nonfinite |= !isfinite(x);
+    store_wire<WIRE>(send, i, x);
+  }
+  for (int64_t i = a + tid * 4; i < b4; i += nth * 4) {
+    float4 x = *reinterpret_cast<const float4*>(src + i);
+    x.x *= scale;
+    x.y *= scale;
+    x.z *= scale;
+    x.w *= scale;
+    nonfinite |= !(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w));
+    store_wire4<WIRE>(send, i, x);
+  }
+  for (int64_t i = b4 + tid; i < hi; i += nth) {
     const float x = src[i] * scale;
     nonfinite |= !isfinite(x);
     store_wire<WIRE>(send, i, x);
@@ -125,17 +158,45 @@ __global__ void signal_kernel(int64_t* flag, int64_t value) {
   st_release_sys(flag, value);
 }
 
-// One block per chunk (grid-stride over chunks). out[i] = scale * sum_p send_p[i].
+// One block per chunk (grid-stride over chunks). out[i] = scale * sum_p send_p[i], summed in peer order
+// (the same order on every owner, so results are deterministic). Each thread keeps kRedUnroll 16-byte
+// loads per peer in flight to cover NVLink latency.
+constexpr int kRedUnroll = 4;
+
 template <int WIRE>
 __global__ void __launch_bounds__(256) reduce_kernel(const void* const* __restrict__ peers, const int64_t* const* flags,
                                                      int npeers, int slot, int64_t epoch, const Chunk* __restrict__ chunks,
                                                      int nchunks, float* __restrict__ out, float scale,
                                                      uint64_t budget_ns, int* status) {
   if (!wait_peers(flags, npeers, slot, epoch, budget_ns, status)) return;
+  const int64_t step = (int64_t)blockDim.x * 8;
   for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
     const Chunk ch = chunks[c];
     const int64_t n8 = ch.len & ~int64_t(7);
-    for (int64_t j = threadIdx.x * 8; j < n8; j += blockDim.x * 8) {
+    int64_t j = threadIdx.x * 8;
+    for (; j + (kRedUnroll - 1) * step < n8; j += kRedUnroll * step) {
+      float acc[kRedUnroll][8];
+#pragma unroll
+      for (int u = 0; u < kRedUnroll; ++u)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[u][k] = 0.f;
+      for (int p = 0; p < npeers; ++p) {
+        float v[kRedUnroll][8];
+#pragma unroll
+        for (int u = 0; u < kRedUnroll; ++u) load8<WIRE>(peers[p], ch.off + j + u * step, v[u]);
+#pragma unroll
+        for (int u = 0; u < kRedUnroll; ++u)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[u][k] += v[u][k];
+      }
+#pragma unroll
+      for (int u = 0; u < kRedUnroll; ++u) {
+        float4* o = reinterpret_cast<float4*>(out + ch.off + j + u * step);
+        o[0] = make_float4(acc[u][0] * scale, acc[u][1] * scale, acc[u][2] * scale, acc[u][3] * scale);
+        o[1] = make_float4(acc[u][4] * scale, acc[u][5] * scale, acc[u][6] * scale, acc[u][7] * scale);
+      }
+    }
+    for (; j < n8; j += step) {
       const int64_t i = ch.off + j;
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       for (int p = 0; p < npeers; ++p) {
@@ -148,10 +209,10 @@ __global__ void __launch_bounds__(256) reduce_kernel(const void* const* __restri
       o[0] = make_float4(acc[0] * scale, acc[1] * scale, acc[2] * scale, acc[3] * scale);
       o[1] = make_float4(acc[4] * scale, acc[5] * scale, acc[6] * scale, acc[7] * scale);
     }
-    for (int64_t j = n8 + threadIdx.x; j < ch.len; j += blockDim.x) {
+    for (int64_t jj = n8 + threadIdx.x; jj < ch.len; jj += blockDim.x) {
       float acc = 0.f;
-      for (int p = 0; p < npeers; ++p) acc += load1<WIRE>(peers[p], ch.off + j);
-      out[ch.off + j] = acc * scale;
+      for (int p = 0; p < npeers; ++p) acc += load1<WIRE>(peers[p], ch.off + jj);
+      out[ch.off + jj] = acc * scale;
     }
   }
 }
@@ -171,15 +232,44 @@ __global__ void __launch_bounds__(256) gather_kernel(const float* const* __restr
                                                      const GatherSeg* __restrict__ segs, int nsegs,
                                                      float* __restrict__ local, uint64_t budget_ns, int* status) {
   if (!wait_peers(flags, npeers, slot, epoch, budget_ns, status)) return;
+  constexpr int U = 4;
   for (int s = blockIdx.x; s < nsegs; s += gridDim.x) {
     const GatherSeg g = segs[s];
-    const float* src = peers[g.owner];
-    for (int64_t j = threadIdx.x; j < g.len; j += blockDim.x) {
-      const float x = src[g.off + j];
-      local[g.off + j] = x;
-      if (g.shadow) {
+    const float* src = peers[g.owner] + g.off;
+    float* dst = local + g.off;
+    __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(g.shadow);
+    // 4 consecutive elements stay in one shadow row when the row length, the leading dimension and
+    // the chunk start are multiples of 4
+    const bool vec = (g.off & 3) == 0 && (g.start & 3) == 0 &&
+                     (!sh || ((g.cols & 3) == 0 && (g.shadow_ld & 3) == 0 && (g.shadow & 7) == 0));
+    const int64_t n4 = vec ? (g.len & ~int64_t(3)) : 0;
+    const int64_t step = (int64_t)blockDim.x * 4;
+    for (int64_t j0 = threadIdx.x * 4; j0 < n4; j0 += U * step) {
+      float4 x[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t j = j0 + u * step;
+        if (j < n4) x[u] = __ldcg(reinterpret_cast<const float4*>(src + j));
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t j = j0 + u * step;
+        if (j < n4) {
+          *reinterpret_cast<float4*>(dst + j) = x[u];
+          if (sh) {
+            const int64_t e = g.start + j;
+            *reinterpret_cast<uint2*>(sh + (e / g.cols) * g.shadow_ld + (e % g.cols)) =
+                make_uint2(pack_bf16(x[u].x, x[u].y), pack_bf16(x[u].z, x[u].w));
+          }
+        }
+      }
+    }
+    for (int64_t j = n4 + threadIdx.x; j < g.len; j += blockDim.x) {
+      const float x = __ldcg(src + j);
+      dst[j] = x;
+      if (sh) {
         const int64_t e = g.start + j;
-        reinterpret_cast<__nv_bfloat16*>(g.shadow)[(e / g.cols) * g.shadow_ld + (e % g.cols)] = __float2bfloat16(x);
+        sh[(e / g.cols) * g.shadow_ld + (e % g.cols)] = __float2bfloat16(x);
       }
     }
   }
@@ -298,7 +388,7 @@ __global__ void __launch_bounds__(256) topk_reduce_kernel(const PeerList* __rest
     const __half* vx = reinterpret_cast<const __half*>(peers[p].val) + list_off;
     const int n = reinterpret_cast<const volatile int*>(peers[p].cnt)[cnt_index];
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
-      atomicAdd(red + ix[j], __half2float(vx[j]) * scale);
+      atomicAdd(red + __ldcg(ix + j), __half2float(__ldcg(vx + j)) * scale);
   }
 }
 

@@ -167,6 +167,7 @@ def _train(rank, world):
                                                "log_every=0", "results_tsv=", f"comm={comm}", "wire_dtype=fp32"])
         tr = Trainer(cfg, device=torch.device("cuda", rank), log=lambda m: None)
         tr.initialize()
+        init = {n: p.detach().float().cpu().clone() for n, p in tr.model.named().items()}
         g = torch.Generator(device="cpu").manual_seed(100 + rank)
         losses, grads = [], None
         for step in range(3):
@@ -178,19 +179,24 @@ def _train(rank, world):
                     grads = {n: v.detach().float().cpu().clone() for n, v in tr.grad_views.items()}
                 else:
                     grads = {n: tr.comm.red_views[n].detach().float().cpu().clone() for n in tr.comm.owned_names}
-        out[comm] = (losses, {n: p.detach().float().cpu() for n, p in tr.model.named().items()}, grads)
+        out[comm] = (losses, {n: p.detach().float().cpu() for n, p in tr.model.named().items()}, grads, init)
         tr.destroy()
     return out
 
 
 def test_p2p_trainer_matches_nccl_2gpu():
-    """Same batches through the NCCL all-reduce path and the in-kernel NVLink path: the mean gradients
-    agree to fp32 accumulation-order noise, losses track, replicas stay identical across ranks, and
-    parameters agree except where AdamW (eps 1e-10) amplifies a near-zero gradient's rounding."""
+    """Same batches through the NCCL all-reduce path and the in-kernel NVLink path: ranks hold identical
+    replicas, the mean gradients agree to fp32 accumulation-order noise, losses track, and after three
+    steps each parameter's difference between the paths is small next to the distance it moved. (Muon
+    matrices go through bf16 Newton-Schulz, batched over each rank's owned shard on the p2p path and
+    over all matrices on the replicated path, so the two updates differ by bf16 rounding; AdamW with
+    eps 1e-10 amplifies near-zero gradient differences into sign flips of single elements.)"""
     res = _run(_train)
+    for n in res[0]["p2p"][1]:
+        assert torch.equal(res[0]["p2p"][1][n], res[1]["p2p"][1][n]), n  # ranks hold identical replicas
     for r in range(2):
-        ln, pn, gn = res[r]["nccl"]
-        lp, pp, gp = res[r]["p2p"]
+        ln, pn, gn, init = res[r]["nccl"]
+        lp, pp, gp, _ = res[r]["p2p"]
         for a, b in zip(ln, lp):
             assert abs(a - b) < 2e-3 * abs(a)
         for n, g in gp.items():  # owned parameters of this rank
@@ -198,14 +204,10 @@ def test_p2p_trainer_matches_nccl_2gpu():
             err = (g - ref).abs().max().item()
             assert err <= 1e-4 * (ref.abs().max().item() + 1e-12), (n, err)
         for n in pn:
-            d = (pn[n] - pp[n]).abs()
-            scale = pn[n].abs().max().item() + 1e-6
-            frac_bad = (d > 5e-3 * scale).float().mean().item()
-            # AdamW parameters (embeddings, lm_head, VE, scalars) flip sign on near-zero gradients
+            moved = (pn[n] - init[n]).norm().item() + 1e-12
+            diff = (pn[n] - pp[n]).norm().item()
             adam = not n.startswith("layer")
-            assert frac_bad < (5e-2 if adam else 1e-3), (n, frac_bad)
-    for n in res[0]["p2p"][1]:
-        assert torch.equal(res[0]["p2p"][1][n], res[1]["p2p"][1][n]), n  # ranks hold identical replicas
+            assert diff <= (0.25 if adam else 0.05) * moved, (r, n, diff, moved)
 
 
 def _topk(rank, world):
