@@ -1,26 +1,41 @@
-// tcgen05/TMEM flash attention forward for sm_100a (head_dim 128, causal + sliding window).
+// tcgen05/TMEM flash attention for sm_100a (head_dim 128, causal + sliding window).
 //
-// One CTA per (128-query tile, head, batch); 192 threads:
-//   warp 0      TMA: the Q tile once, then 128-key K and V tiles into a 2-stage ring (128-byte
-//               swizzle, 3-D tensor maps over the fused [B, T, Dq+2Dkv] projection buffer, zero fill
-//               past T; no multicast);
-//   warp 1      TMEM allocation and the single MMA-issuing lane:
-//                 S_j = Q K_j^T  -> TMEM columns [128*(j%2), +128)  (two ping-pong buffers)
-//                 O  += P_j V_j  -> TMEM columns [256, 384)
-//               S_{j+1} is issued before waiting for P_j, so the next scores overlap this softmax;
-//   warps 2-5   softmax, one query row per thread (TMEM lane = row): masked row max, conditional
-//               rescale of O in TMEM (only when the running max grows by more than 2^8, so P stays
-//               below 256), P = exp2(S*scale - m) written as bf16 to shared memory in the K-major
-//               128-byte-swizzled layout the PV MMA reads; finally O / l and the log-sum-exp.
-// Key tiles entirely outside [q - w + 1, q] are never loaded. All mbarrier waits are bounded; on
+// Forward: one CTA per (two 128-query tiles A and B, head, batch); 320 threads:
+//   warp 0      TMA: both Q tiles once, then K tiles into a 3-stage ring and V tiles into a 2-stage
+//               ring (128-byte swizzle, 3-D tensor maps over the fused [B, T, Dq+2Dkv] projection
+//               buffer, zero fill past T; no multicast);
+//   warp 1      TMEM allocation and the single MMA-issuing lane. Per query tile X:
+//                 S_X = Q_X K_t^T  -> TMEM [256X, +128)          (fp32)
+//                 P_X              -> TMEM [256X, +64)           (bf16 pairs, written over S_X)
+//                 O_X += P_X V_t   -> TMEM [256X + 128, +128)    (A operand read from TMEM)
+//               issued in the order S_A S_B | PV_A S_A' PV_B S_B' | ..., so the tensor core works on
+//               one tile while the other tile's softmax runs;
+//   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B: one query row per thread (TMEM lane =
+//               row), masked row max, conditional rescale of O (only when the running max grows by
+//               more than 2^8, so P stays below 256), P = exp2(S*scale - m) packed to bf16 and stored
+//               back to TMEM; finally O / l and the log-sum-exp.
+// S_X(j+1) is issued after PV_X(j), and the tcgen05.mma of one CTA complete in issue order, so when the
+// softmax of S_X(j+1) starts, PV_X(j) has finished reading P_X(j) and writing O_X: the softmax may
+// overwrite P and rescale O without another barrier.
+// Key tiles outside a tile's band [q - w + 1, q] are never loaded. All mbarrier waits are bounded; on
 // timeout the CTA records a status code, drains its MMAs, frees TMEM and exits.
+//
+// Backward: a dQ kernel and a dK/dV kernel (described where they are defined).
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "status.h"
 #include "tma_host.h"
+
+// Pipeline split for profiling only (benchmarks/attn_split.py): 1 removes the softmax arithmetic,
+// 2 decouples the MMA lane from the softmax warps. Both compute wrong values; 0 is the kernel.
+#ifndef ATTN_SPLIT_MODE
+#define ATTN_SPLIT_MODE 0
+#endif
 
 namespace br {
 namespace {
@@ -42,54 +57,84 @@ struct FwdParams {
   int* status;
 };
 
-// smem layout (offsets from a 1024-aligned base)
-constexpr int SM_Q = 0;
-constexpr int SM_K = SM_Q + TILE_BYTES;
-constexpr int SM_V = SM_K + 2 * TILE_BYTES;
-constexpr int SM_P = SM_V + 2 * TILE_BYTES;
-constexpr int SM_BAR = SM_P + TILE_BYTES;
-constexpr int FWD_SMEM = SM_BAR + 256 + 1024;
-
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__global__ void __launch_bounds__(192, 1)
+constexpr int F2_Q = 0;                               // [2] x 32 KB: Q_A, Q_B
+constexpr int F2_KST = 3;                             // K ring depth
+constexpr int F2_VST = 2;                             // V ring depth
+constexpr int F2_K = F2_Q + 2 * TILE_BYTES;           // [3] x 32 KB
+constexpr int F2_V = F2_K + F2_KST * TILE_BYTES;      // [2] x 32 KB
+constexpr int F2_BAR = F2_V + F2_VST * TILE_BYTES;
+constexpr int FWD_SMEM = F2_BAR + 256 + 1024;
+
+struct Band {
+  int lo, n;  // first key tile and number of key tiles of a query tile
+  __device__ bool uses(int t) const { return t >= lo && t < lo + n; }
+};
+
+__device__ __forceinline__ Band band_of(int q0, int T, int w) {
+  Band b;
+  if (q0 >= T) {
+    b.lo = 0;
+    b.n = 0;
+    return b;
+  }
+  b.lo = max(0, q0 - w + 1) / BKV;
+  const int hi = min(q0 + BQ - 1, T - 1) / BKV;
+  b.n = hi - b.lo + 1;
+  return b;
+}
+
+__global__ void __launch_bounds__(320, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM_BAR);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + F2_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2]
-  uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* kv_empty = bars + 5;  // [2]
-  uint64_t* s_full = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* k_full = bars + 1;   // [3]
+  uint64_t* k_empty = bars + 4;  // [3]
+  uint64_t* v_full = bars + 7;   // [2]
+  uint64_t* v_empty = bars + 9;  // [2]
+  uint64_t* s_full = bars + 11;  // [2] per query tile
+  uint64_t* p_full = bars + 13;  // [2] per query tile
+  uint64_t* o_done = bars + 15;  // [2] per query tile
+  uint64_t* drain = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int qp = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (p.H / p.KV);
-  const int q0 = qb * BQ;
+  const int q0 = qp * 2 * BQ;
   const int w = p.window;
-  const int kb_lo = max(0, q0 - w + 1) / BKV;
-  const int kb_hi = min(q0 + BQ - 1, p.T - 1) / BKV;
-  const int nkv = kb_hi - kb_lo + 1;
+  const Band bA = band_of(q0, p.T, w), bB = band_of(q0 + BQ, p.T, w);
+  // key tiles of the CTA: bA.lo .. last tile of B (or of A when B is past T)
+  const int u_lo = bA.lo;
+  const int u_hi = bB.n > 0 ? bB.lo + bB.n - 1 : bA.lo + bA.n - 1;
+  const int nu = u_hi - u_lo + 1;
+  // Last user of key tile t among the two query tiles, in MMA issue order: when both tiles start at
+  // the same key tile, B's MMAs on t come after A's; when B starts one tile later, A's come last.
+  const bool same_start = bB.n > 0 && bB.lo == bA.lo;
+  auto last_is_b = [&](int t) -> bool { return same_start ? bB.uses(t) : !bA.uses(t); };
   const int warp = warp_id();
   if (device_failed(p.status)) return;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < F2_KST; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-      mbar_init(&s_full[i], 1);
+      mbar_init(&k_empty[i], 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
+    for (int i = 0; i < F2_VST; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&s_full[x], 1);
+      mbar_init(&p_full[x], 128);
+      mbar_init(&o_done[x], 1);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -107,127 +152,148 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     if (elect_one()) {
       tma_prefetch_desc(&tm);
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
-      tma_load_3d(&tm, q_full, smem + SM_Q, h * HD, q0, b);
-      tma_load_3d(&tm, q_full, smem + SM_Q + ATOM_BYTES, h * HD + 64, q0, b);
-      for (int j = 0; j < nkv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
-          fail(kErrTimeoutProducer);
-          break;
-        }
-        const int k0 = (kb_lo + j) * BKV;
-        uint8_t* ks = smem + SM_K + st * TILE_BYTES;
-        uint8_t* vs = smem + SM_V + st * TILE_BYTES;
-        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
-        tma_load_3d(&tm, &k_full[st], ks, p.Dq + kvh * HD, k0, b);
-        tma_load_3d(&tm, &k_full[st], ks + ATOM_BYTES, p.Dq + kvh * HD + 64, k0, b);
-        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
-        tma_load_3d(&tm, &v_full[st], vs, p.Dq + p.Dkv + kvh * HD, k0, b);
-        tma_load_3d(&tm, &v_full[st], vs + ATOM_BYTES, p.Dq + p.Dkv + kvh * HD + 64, k0, b);
+      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+      for (int x = 0; x < 2; ++x) {
+        tma_load_3d(&tm, q_full, smem + F2_Q + x * TILE_BYTES, h * HD, q0 + x * BQ, b);
+        tma_load_3d(&tm, q_full, smem + F2_Q + x * TILE_BYTES + ATOM_BYTES, h * HD + 64, q0 + x * BQ, b);
       }
+      // K runs up to two tiles ahead of V (B's next scores need K[t+1] while A still reads V[t]),
+      // so the two rings are filled in one interleaved order: K0, K1, V0, K2, V1, K3, V2, ...
+      int ik = 0, iv = 0;
+      bool ok = true;
+      while (ok && (ik < nu || iv < nu)) {
+        const bool do_k = ik < nu && (ik < iv + 2);
+        if (do_k) {
+          const int st = ik % F2_KST;
+          if (!mbar_wait(&k_empty[st], ((ik / F2_KST) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          const int k0 = (u_lo + ik) * BKV;
+          uint8_t* ks = smem + F2_K + st * TILE_BYTES;
+          mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+          tma_load_3d(&tm, &k_full[st], ks, p.Dq + kvh * HD, k0, b);
+          tma_load_3d(&tm, &k_full[st], ks + ATOM_BYTES, p.Dq + kvh * HD + 64, k0, b);
+          ++ik;
+        } else {
+          const int st = iv % F2_VST;
+          if (!mbar_wait(&v_empty[st], ((iv / F2_VST) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          const int k0 = (u_lo + iv) * BKV;
+          uint8_t* vs = smem + F2_V + st * TILE_BYTES;
+          mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+          tma_load_3d(&tm, &v_full[st], vs, p.Dq + p.Dkv + kvh * HD, k0, b);
+          tma_load_3d(&tm, &v_full[st], vs + ATOM_BYTES, p.Dq + p.Dkv + kvh * HD + 64, k0, b);
+          ++iv;
+        }
+      }
+      if (!ok) fail(kErrTimeoutProducer);
     }
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, false, false);
       constexpr uint32_t idesc_o = umma_idesc_bf16(128, 128, false, true);
-      const uint32_t q_addr = smem_u32(smem + SM_Q);
-      const uint32_t p_addr = smem_u32(smem + SM_P);
       bool ok = mbar_wait(q_full, 0, kBudgetNs, abort_flag, p.status);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) return false;
+      // S_X(j) = Q_X K_t^T for key tile t = lo_X + j
+      auto issue_s = [&](int x, int j) -> bool {
+        const Band& bx = x ? bB : bA;
+        const int t = bx.lo + j, i = t - u_lo, st = i % F2_KST;
+        if (!mbar_wait(&k_full[st], (i / F2_KST) & 1, kBudgetNs, abort_flag, p.status)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + SM_K + st * TILE_BYTES);
+        const uint32_t q_addr = smem_u32(smem + F2_Q + x * TILE_BYTES);
+        const uint32_t k_addr = smem_u32(smem + F2_K + st * TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
-          umma_bf16_ss(tmem + st * 128, umma_desc_sw128(q_addr + off, 16, 1024),
+          umma_bf16_ss(tmem + x * 256, umma_desc_sw128(q_addr + off, 16, 1024),
                        umma_desc_sw128(k_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[st]);
+        umma_commit(&s_full[x]);
+        if (last_is_b(t) == (x == 1)) umma_commit(&k_empty[st]);
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < nkv && ok; ++j) {
-        if (j + 1 < nkv && !issue_s(j + 1)) {
-          ok = false;
-          break;
-        }
-        const int st = j & 1;
-        if (!mbar_wait(p_full, j & 1, kBudgetNs, abort_flag, p.status) ||
-            !mbar_wait(&v_full[st], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
-          ok = false;
-          break;
-        }
+      // O_X += P_X V_t, P from TMEM
+      auto issue_pv = [&](int x, int j) -> bool {
+        const Band& bx = x ? bB : bA;
+        const int t = bx.lo + j, i = t - u_lo, st = i % F2_VST;
+        if ((ATTN_SPLIT_MODE != 2 && !mbar_wait(&p_full[x], j & 1, kBudgetNs, abort_flag, p.status)) ||
+            !mbar_wait(&v_full[st], (i / F2_VST) & 1, kBudgetNs, abort_flag, p.status))
+          return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(smem + SM_V + st * TILE_BYTES);
+        const uint32_t v_addr = smem_u32(smem + F2_V + st * TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * ATOM_BYTES + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = umma_desc_sw128(v_addr + kk * 2048, ATOM_BYTES, 1024);
-          umma_bf16_ss(tmem + 256, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          umma_bf16_ts(tmem + x * 256 + 128, tmem + x * 256 + kk * 8,
+                       umma_desc_sw128(v_addr + kk * 2048, ATOM_BYTES, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        if (last_is_b(t) == (x == 1)) umma_commit(&v_empty[st]);
+        if (j == (x ? bB.n : bA.n) - 1) umma_commit(&o_done[x]);
+        return true;
+      };
+      if (ok && bA.n > 0) ok = issue_s(0, 0);
+      if (ok && bB.n > 0) ok = issue_s(1, 0);
+      for (int j = 0; ok && (j < bA.n || j < bB.n); ++j) {
+        for (int x = 0; x < 2 && ok; ++x) {
+          const int n = x ? bB.n : bA.n;
+          if (j >= n) continue;
+          ok = issue_pv(x, j);
+          if (ok && j + 1 < n) ok = issue_s(x, j + 1);
         }
-        umma_commit(o_done);
-        umma_commit(&kv_empty[st]);
       }
       if (!ok) fail(kErrTimeoutMma);
       umma_commit(drain);
       mbar_wait(drain, 0, 100000000ull, nullptr);
     }
   } else {
-    // softmax warps: row r of the tile
+    // softmax warps: query tile x = (warp - 2) / 4, row r of the tile (TMEM lane group = warp % 4)
+    const int x = (warp - 2) >> 2;
+    const Band bx = x ? bB : bA;
     const int wq = warp & 3;
     const int lane = lane_id();
     const int r = wq * 32 + lane;
-    const int qi = q0 + r;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
-    uint8_t* prow = smem + SM_P + r * 128;
+    const int qt = q0 + x * BQ;
+    const int qi = qt + r;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16) + x * 256;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      const int st = j & 1;
-      if (!mbar_wait_warp(&s_full[st], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+    for (int j = 0; j < bx.n; ++j) {
+      if (ATTN_SPLIT_MODE != 2 && !mbar_wait_warp(&s_full[x], j & 1, kBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
         break;
       }
       tc_fence_after();
-      const int k0 = (kb_lo + j) * BKV;
-      const uint32_t s_addr = lane_base + st * 128;
+      const int k0 = (bx.lo + j) * BKV;
       // interior tiles (every key visible to every row of the tile) skip the per-element mask
-      const bool interior = (k0 + BKV - 1 <= q0) && (k0 > q0 + BQ - 1 - w) && (k0 + BKV <= p.T);
-      // S row -> registers once (log2 domain), masked row max
-      uint32_t sr[4][32];
+      const bool interior = (k0 + BKV - 1 <= qt) && (k0 > qt + BQ - 1 - w) && (k0 + BKV <= p.T);
+      uint32_t sr[4][32];  // raw S row (masked entries set to -inf)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, sr[c]);
+      for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + c * 32, sr[c]);
       tmem_ld_wait();
-      float sv[BKV];
+      // row max of the raw scores (scale > 0, so it is the max of the scaled ones too); query qi sees
+      // key k0 + 32c + i for i in [qi - w + 1 - k0 - 32c, qi + 1 - k0 - 32c) below T - k0 - 32c
       float mx = -INFINITY;
       if (interior) {
 #pragma unroll
-        for (int i = 0; i < BKV; ++i) {
-          sv[i] = __uint_as_float(sr[i >> 5][i & 31]) * p.scale_log2;
-          mx = fmaxf(mx, sv[i]);
-        }
+        for (int i = 0; i < BKV; ++i) mx = fmaxf(mx, __uint_as_float(sr[i >> 5][i & 31]));
       } else {
 #pragma unroll
-        for (int i = 0; i < BKV; ++i) {
-          const int kj = k0 + i;
-          const bool vis = kj <= qi && kj > qi - w && kj < p.T;
-          sv[i] = vis ? __uint_as_float(sr[i >> 5][i & 31]) * p.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, sv[i]);
+        for (int c = 0; c < 4; ++c) {
+          const int kc = k0 + 32 * c;
+          const uint32_t vis = qi < p.T ? range_mask32(qi - w + 1 - kc, min(qi + 1 - kc, p.T - kc)) : 0u;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float v = ((vis >> i) & 1u) ? __uint_as_float(sr[c][i]) : -INFINITY;
+            sr[c][i] = __float_as_uint(v);
+            mx = fmaxf(mx, v);
+          }
         }
       }
-      // PV_{j-1} must be complete before P is overwritten or O is rescaled
-      if (j > 0 && !mbar_wait_warp(o_done, (j - 1) & 1, kBudgetNs, abort_flag, p.status)) {
-        fail(kErrTimeoutEpilogue);
-        ok = false;
-        break;
-      }
-      tc_fence_after();
+      mx *= p.scale_log2;
       // The rescale decision is per row, but tcgen05.ld/st are warp-collective: the warp rescales
-      // together whenever any of its rows needs it, rows that do not use alpha = 1.
+      // together whenever any of its rows needs it, rows that do not use alpha = 1. PV_X(j-1) is
+      // complete here (it was issued before S_X(j)).
       float alpha = 1.f;
       bool mine = false;
       if (j == 0) {
@@ -242,47 +308,48 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t v[32];
-          tmem_ld32(lane_base + 256 + c * 32, v);
+          tmem_ld32(lane_base + 128 + c * 32, v);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-          tmem_st32(lane_base + 256 + c * 32, v);
+          tmem_st32(lane_base + 128 + c * 32, v);
         }
-        tmem_st_wait();
       }
-      // P = exp2(s - m_ref) -> bf16 into the swizzled K-major P tile (masked entries are -inf -> 0)
+      // P = exp2(s * scale_log2 - m_ref) -> bf16 pairs into TMEM columns [0, 64) of this tile (masked
+      // entries are -inf -> 0); the scale-and-subtract and the row sum run on f32x2 pairs
       const float mref = m_ref == -INFINITY ? 0.f : m_ref;
+      const uint64_t sc2 = f32x2(p.scale_log2, p.scale_log2), nm2 = f32x2(-mref, -mref);
+      uint64_t l2 = f32x2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
+      for (int c = 0; c < (ATTN_SPLIT_MODE == 1 ? 0 : 2); ++c) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = exp2f(sv[c * 32 + i] - mref);
-          const float p1 = exp2f(sv[c * 32 + i + 1] - mref);
-          l += p0 + p1;
+        for (int i = 0; i < 64; i += 2) {
+          const int e = c * 64 + i;
+          const float2 t = f32x2_split(
+              fma_f32x2(f32x2(__uint_as_float(sr[e >> 5][e & 31]), __uint_as_float(sr[e >> 5][(e + 1) & 31])), sc2, nm2));
+          const float p0 = exp2f(t.x), p1 = exp2f(t.y);
+          l2 = add_f32x2(l2, f32x2(p0, p1));
           pk[i / 2] = pack_bf16(p0, p1);
         }
-        // columns c*32 .. c*32+31: atom c/2, 16-byte chunks (c%2)*4 .. +3, XOR-swizzled by row
-        uint8_t* atom = prow + (c >> 1) * ATOM_BYTES;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = (c & 1) * 4 + q;
-          *reinterpret_cast<uint4*>(atom + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-        }
+        tmem_st32(lane_base + c * 32, pk);
       }
-      fence_async_smem();
+      {
+        const float2 ls = f32x2_split(l2);
+        l += ls.x + ls.y;
+      }
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[x]);
     }
-    if (ok && mbar_wait_warp(o_done, (nkv - 1) & 1, kBudgetNs, abort_flag, p.status)) {
+    if (bx.n > 0 && ok && mbar_wait_warp(&o_done[x], 0, kBudgetNs, abort_flag, p.status)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = p.out + ((int64_t)b * p.T + qi) * p.ldo + h * HD;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t v[32];
-        tmem_ld32(lane_base + 256 + c * 32, v);
+        tmem_ld32(lane_base + 128 + c * 32, v);
         tmem_ld_wait();
         if (qi < p.T) {
 #pragma unroll
@@ -296,8 +363,8 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      if (qi < p.T) p.lse[((int64_t)b * p.H + h) * p.T + qi] = (m_ref + __log2f(l)) / kLog2e;
-    } else if (ok) {
+      if (qi < p.T) p.lse[((int64_t)b * p.H + h) * p.T + qi] = m_ref + __log2f(l);  // log2 units
+    } else if (bx.n > 0 && ok) {
       fail(kErrTimeoutEpilogue);
     }
   }
@@ -449,7 +516,7 @@ __global__ void __launch_bounds__(320, 1)
           ok = false;
           break;
         }
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+        if (ATTN_SPLIT_MODE != 2 && !mbar_wait(&p_full[j & 1], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
           ok = false;
           break;
         }
@@ -475,12 +542,12 @@ __global__ void __launch_bounds__(320, 1)
     const int qi = q0 + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
     const int qc = min(qi, p.T - 1);
-    const float lse2 = p.lse[((int64_t)b * p.H + h) * p.T + qc] * kLog2e;
+    const float lse2 = p.lse[((int64_t)b * p.H + h) * p.T + qc];  // log2 units
     const float dl = p.delta[((int64_t)b * p.H + h) * p.T + qc];
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int set = j & 1;
-      if (!mbar_wait_warp(&s_full[set], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+      if (ATTN_SPLIT_MODE != 2 && !mbar_wait_warp(&s_full[set], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
         break;
@@ -493,15 +560,32 @@ __global__ void __launch_bounds__(320, 1)
       tmem_ld32(lane_base + set * 128 + 64 + half * 32, dv);
       tmem_ld_wait();
       uint8_t* drow = smem + DQ_DS + set * 16384 + r * 128;
+      // dS = exp2(S * scale_log2 - lse2) (dP - delta); query qi sees key k0 + i for i in
+      // [qi - w + 1 - k0, qi + 1 - k0) below T - k0 (boundary blocks only)
       uint32_t pk[16];
+      auto body = [&](auto masked) {
+        constexpr bool kMasked = decltype(masked)::value;
+        uint32_t vis = 0xffffffffu;
+        if constexpr (kMasked) vis = qi < p.T ? range_mask32(qi - w + 1 - k0, min(qi + 1 - k0, p.T - k0)) : 0u;
+        const uint64_t dl2 = f32x2(dl, dl);
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const int kj = k0 + i;
-        const bool v0 = interior || (kj <= qi && kj > qi - w && kj < p.T);
-        const bool v1 = interior || (kj + 1 <= qi && kj + 1 > qi - w && kj + 1 < p.T);
-        const float p0 = v0 ? exp2f(__uint_as_float(sv[i]) * p.scale_log2 - lse2) : 0.f;
-        const float p1 = v1 ? exp2f(__uint_as_float(sv[i + 1]) * p.scale_log2 - lse2) : 0.f;
-        pk[i / 2] = pack_bf16(p0 * (__uint_as_float(dv[i]) - dl), p1 * (__uint_as_float(dv[i + 1]) - dl));
+        for (int i = 0; i < 32; i += 2) {
+          float p0 = exp2f(fmaf(__uint_as_float(sv[i]), p.scale_log2, -lse2));
+          float p1 = exp2f(fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, -lse2));
+          if constexpr (kMasked) {
+            p0 = ((vis >> i) & 1u) ? p0 : 0.f;
+            p1 = ((vis >> (i + 1)) & 1u) ? p1 : 0.f;
+          }
+          const float2 g = f32x2_split(
+              mul_f32x2(f32x2(p0, p1), sub_f32x2(f32x2(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])), dl2)));
+          pk[i / 2] = pack_bf16(g.x, g.y);
+        }
+      };
+      if (ATTN_SPLIT_MODE == 1) {
+      } else if (interior) {
+        body(std::false_type{});
+      } else {
+        body(std::true_type{});
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -670,7 +754,7 @@ __global__ void __launch_bounds__(320, 1)
           ok = false;
           break;
         }
-        if (!mbar_wait(&p_full[it & 1], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+        if (ATTN_SPLIT_MODE != 2 && !mbar_wait(&p_full[it & 1], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
           ok = false;
           break;
         }
@@ -704,7 +788,7 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
     for (int it = 0; it < iters; ++it) {
       const int set = it & 1, st = it % DK_STAGES;
-      if (!mbar_wait_warp(&s_full[set], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+      if (ATTN_SPLIT_MODE != 2 && !mbar_wait_warp(&s_full[set], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
         break;
@@ -720,16 +804,42 @@ __global__ void __launch_bounds__(320, 1)
       tmem_ld_wait();
       uint8_t* prow = smem + DK_PT + set * 16384 + r * 128;
       uint8_t* srow = smem + DK_DST + set * 16384 + r * 128;
+      // P^T = exp2(S^T * scale_log2 - lse2) and dS^T = P^T (dP^T - delta); key kj sees query q0 + i for
+      // i in [kj - q0, kj - q0 + w) below T - q0 (boundary blocks only; interior blocks skip the mask)
       uint32_t pp[16], ss[16];
+      auto body = [&](auto masked) {
+        constexpr bool kMasked = decltype(masked)::value;
+        uint32_t vis = 0xffffffffu;
+        if constexpr (kMasked) vis = kj < p.T ? range_mask32(kj - q0, min(kj - q0 + w, p.T - q0)) : 0u;
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const int qa = q0 + i;
-        const bool v0 = interior || (kj <= qa && kj > qa - w && qa < p.T && kj < p.T);
-        const bool v1 = interior || (kj <= qa + 1 && kj > qa + 1 - w && qa + 1 < p.T && kj < p.T);
-        const float p0 = v0 ? exp2f(__uint_as_float(sv[i]) * p.scale_log2 - ls[i] * kLog2e) : 0.f;
-        const float p1 = v1 ? exp2f(__uint_as_float(sv[i + 1]) * p.scale_log2 - ls[i + 1] * kLog2e) : 0.f;
-        pp[i / 2] = pack_bf16(p0, p1);
-        ss[i / 2] = pack_bf16(p0 * (__uint_as_float(dv[i]) - ls[64 + i]), p1 * (__uint_as_float(dv[i + 1]) - ls[64 + i + 1]));
+        for (int i = 0; i < 32; i += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(ls + i);
+          const float4 d4 = *reinterpret_cast<const float4*>(ls + 64 + i);
+          float pr[4];
+          pr[0] = exp2f(fmaf(__uint_as_float(sv[i + 0]), p.scale_log2, -l4.x));
+          pr[1] = exp2f(fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, -l4.y));
+          pr[2] = exp2f(fmaf(__uint_as_float(sv[i + 2]), p.scale_log2, -l4.z));
+          pr[3] = exp2f(fmaf(__uint_as_float(sv[i + 3]), p.scale_log2, -l4.w));
+          if constexpr (kMasked) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) pr[k] = ((vis >> (i + k)) & 1u) ? pr[k] : 0.f;
+          }
+          const float2 g0 = f32x2_split(mul_f32x2(
+              f32x2(pr[0], pr[1]), sub_f32x2(f32x2(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])), f32x2(d4.x, d4.y))));
+          const float2 g1 = f32x2_split(mul_f32x2(f32x2(pr[2], pr[3]), sub_f32x2(f32x2(__uint_as_float(dv[i + 2]),
+                                                                                          __uint_as_float(dv[i + 3])),
+                                                                                   f32x2(d4.z, d4.w))));
+          pp[i / 2] = pack_bf16(pr[0], pr[1]);
+          pp[i / 2 + 1] = pack_bf16(pr[2], pr[3]);
+          ss[i / 2] = pack_bf16(g0.x, g0.y);
+          ss[i / 2 + 1] = pack_bf16(g1.x, g1.y);
+        }
+      };
+      if (ATTN_SPLIT_MODE == 1) {
+      } else if (interior) {
+        body(std::false_type{});
+      } else {
+        body(std::true_type{});
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -808,8 +918,8 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse,
     C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
     attr = true;
   }
-  dim3 grid((unsigned)((T + BQ - 1) / BQ), (unsigned)H, (unsigned)B);
-  attn_fwd_tc_kernel<<<grid, 192, FWD_SMEM, at::cuda::getCurrentCUDAStream()>>>(tm, p);
+  dim3 grid((unsigned)((T + 2 * BQ - 1) / (2 * BQ)), (unsigned)H, (unsigned)B);
+  attn_fwd_tc_kernel<<<grid, 320, FWD_SMEM, at::cuda::getCurrentCUDAStream()>>>(tm, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -186,7 +186,8 @@ def _attn_ref(q, k, v, window):
 
 
 @pytest.mark.parametrize("B,T,H,KV,window", [(2, 256, 4, 4, 256), (1, 300, 4, 2, 100), (2, 512, 2, 2, 128),
-                                             (1, 193, 2, 1, 1000), (2, 1024, 2, 1, 300), (1, 2048, 2, 2, 1024)])
+                                             (1, 193, 2, 1, 1000), (2, 1024, 2, 1, 300), (1, 2048, 2, 2, 1024),
+                                             (1, 640, 4, 2, 200), (2, 384, 2, 2, 384)])
 def test_attention_fwd_bwd(cuda, B, T, H, KV, window):
     E = _ext()
     torch.manual_seed(3)
@@ -213,7 +214,7 @@ def test_attention_fwd_bwd(cuda, B, T, H, KV, window):
     _assert(lse, lse_ref, 1e-3)
     if T % 128 == 0:
         _assert(o_tc, ref.reshape(M, D), 2e-2)
-        _assert(lse_tc, lse_ref, 1e-3)
+        _assert(lse_tc * math.log(2.0), lse_ref, 1e-3)  # the tcgen05 kernel reports lse in log2 units
     do = torch.randn(M, D, device=cuda).to(torch.bfloat16)
     (ref.reshape(M, D) * do.float()).sum().backward()
     dqkv = torch.empty_like(qkv)
