@@ -34,6 +34,95 @@ def load_token_bytes(path: str, vocab_size: int) -> np.ndarray:
     return np.fromfile(path, dtype="<i4").astype(np.int32)
 
 
+# ------------------------------------------------------------------ manifest-aware discovery
+# The reference looks for a parity manifest (explicit URL, else <artifact base>/manifest.json), takes
+# every .bin shard it lists from <parity>/bin/, concatenates them into one token stream, and looks for
+# token_bytes.bin / token-bytes.bin / token_bytes.json under <parity>/tokenizer/ then <parity>/bin/
+# (trainer.ts:182-279, :489-511); without a manifest it tries tokens.bin at the data root and finally
+# falls back to synthetic batches (trainer.ts:513-562). Here the locations are filesystem paths.
+TOKEN_BYTES_NAMES = ("token_bytes.bin", "token-bytes.bin", "token_bytes.json")
+
+
+def find_manifest(path: str) -> str | None:
+    """A manifest.json: ``path`` itself, or ``path/manifest.json``, or ``path/parity/manifest.json``."""
+    import os
+    if not path:
+        return None
+    if os.path.isfile(path) and path.endswith(".json"):
+        return path
+    if os.path.isdir(path):
+        for rel in ("manifest.json", os.path.join("parity", "manifest.json")):
+            cand = os.path.join(path, rel)
+            if os.path.isfile(cand):
+                return cand
+    return None
+
+
+def manifest_artifacts(manifest_path: str) -> dict:
+    """Resolves a parity manifest to local files: {"bin": [paths], "token_bytes": path | None,
+    "tokenizer": path | None}. Shards are looked up under <manifest dir>/bin, then the manifest's
+    recorded source directory."""
+    import json
+    import os
+    with open(manifest_path) as f:
+        m = json.load(f)
+    root = os.path.dirname(os.path.abspath(manifest_path))
+    src = m.get("source", {}) or {}
+    bin_dirs = [os.path.join(root, "bin")] + ([src["binDir"]] if src.get("binDir") else [])
+    tok_dirs = [os.path.join(root, "tokenizer")] + ([src["tokenizerDir"]] if src.get("tokenizerDir") else [])
+    bins = []
+    for name in (m.get("files", {}) or {}).get("bin", []):
+        if not name.endswith(".bin"):
+            continue
+        for d in bin_dirs:
+            cand = os.path.join(d, name)
+            if os.path.isfile(cand):
+                bins.append(cand)
+                break
+    token_bytes = tokenizer = None
+    for d in tok_dirs + bin_dirs:
+        for name in TOKEN_BYTES_NAMES:
+            cand = os.path.join(d, name)
+            if token_bytes is None and os.path.isfile(cand):
+                token_bytes = cand
+        cand = os.path.join(d, "tokenizer.json")
+        if tokenizer is None and os.path.isfile(cand):
+            tokenizer = cand
+    return {"bin": bins, "token_bytes": token_bytes, "tokenizer": tokenizer}
+
+
+def load_token_data(path: str) -> np.ndarray:
+    """The token stream behind ``path``: a .bin shard, a manifest (all listed shards concatenated in
+    order), or a directory holding a manifest or tokens.bin."""
+    import os
+    man = find_manifest(path)
+    if man is not None:
+        bins = manifest_artifacts(man)["bin"]
+        if not bins:
+            raise FileNotFoundError(f"manifest {man} lists no .bin shard that exists locally")
+        return np.concatenate([load_tokens_bin(b) for b in bins])
+    if os.path.isdir(path):
+        cand = os.path.join(path, "tokens.bin")
+        if os.path.isfile(cand):
+            return load_tokens_bin(cand)
+        raise FileNotFoundError(f"{path}: no manifest.json, parity/manifest.json or tokens.bin")
+    return load_tokens_bin(path)
+
+
+def discover_token_bytes(path: str) -> str:
+    """token_bytes next to the data of ``path`` (manifest locations, then the data directory); "" if none."""
+    import os
+    man = find_manifest(path)
+    if man is not None:
+        return manifest_artifacts(man)["token_bytes"] or ""
+    d = path if os.path.isdir(path) else os.path.dirname(path)
+    for name in TOKEN_BYTES_NAMES:
+        cand = os.path.join(d, name)
+        if d and os.path.isfile(cand):
+            return cand
+    return ""
+
+
 class TokenDataLoader:
     def __init__(self, tokens: np.ndarray | None = None):
         self.tokens = np.zeros(0, np.int32) if tokens is None else np.ascontiguousarray(tokens, np.int32)

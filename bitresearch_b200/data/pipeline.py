@@ -17,7 +17,7 @@ import numpy as np
 import torch
 
 from ..config import TrainConfig
-from .loader import BestFitDocumentBatcher, TokenDataLoader, load_tokens_bin
+from .loader import BestFitDocumentBatcher, TokenDataLoader, load_token_data
 from .synthetic import UniformBOSStream, ZipfDocumentSource, bos_id
 
 
@@ -98,7 +98,7 @@ def make_batch_source(cfg: TrainConfig, split: str = "train", rank: int = 0, wor
     if cfg.data == "uniform":
         return _Uniform(cfg, seed)
     if cfg.data == "tokens":
-        toks = load_tokens_bin(cfg.data_path)
+        toks = load_token_data(cfg.data_path)
         split_at = int(len(toks) * (1 - cfg.val_fraction))
         part = toks[:split_at] if split == "train" else toks[split_at:]
         if split == "train" and world > 1:  # contiguous per-rank shards of the training stream

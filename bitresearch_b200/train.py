@@ -39,7 +39,7 @@ from . import checkpoint as ckpt
 from .config import TrainConfig, apply_overrides, estimate_params, preset
 from .data.pipeline import PinnedPrefetcher, make_batch_source
 from .data.synthetic import make_token_bytes
-from .data.loader import load_token_bytes
+from .data.loader import discover_token_bytes, load_token_bytes
 from .eval import evaluate_bpb
 from .models.gpt import GPT
 from .optim.muon_adamw import MuonAdamW, lr_multiplier, muon_momentum, weight_decay_at
@@ -173,8 +173,11 @@ class Trainer:
             self.engine.attach_optimizer(self.optimizer)
         # data
         self.train_source = make_batch_source(cfg, "train", self.rank, self.world)
-        if cfg.data == "tokens" and cfg.token_bytes_path:
-            self.token_bytes = load_token_bytes(cfg.token_bytes_path, cfg.model.vocab_size)
+        if cfg.data == "tokens":
+            # explicit table, else the one the manifest / data directory provides, else all ones (the
+            # reference's avgBytesPerToken = 1 fallback)
+            tb_path = cfg.token_bytes_path or discover_token_bytes(cfg.data_path)
+            self.token_bytes = load_token_bytes(tb_path, cfg.model.vocab_size)
         else:
             self.token_bytes = make_token_bytes(cfg.model.vocab_size, cfg.token_bytes_max)
         if self.is_cuda:

@@ -211,7 +211,10 @@ void pack_split(Packer& p, uintptr_t inputs, uintptr_t targets, int64_t batch, i
 
 }  // namespace
 
+void register_bpe(py::module& m);
+
 PYBIND11_MODULE(_native_data, m) {
+  register_bpe(m);
   m.doc() = "native document source + BOS best-fit packer";
   py::class_<Packer, std::shared_ptr<Packer>>(m, "Packer")
       .def_property_readonly("epoch", [](const Packer& p) { return p.epoch; })

@@ -19,7 +19,7 @@ def _ext_modules():
 
     data = Extension(
         "bitresearch_b200._native_data",
-        ["csrc/data/packer.cpp"],
+        ["csrc/data/packer.cpp", "csrc/data/bpe.cpp"],
         include_dirs=[pybind11.get_include()],
         extra_compile_args=["-O3", "-std=c++17"],
         language="c++",
