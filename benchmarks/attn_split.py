@@ -1,7 +1,7 @@
 """Where the tcgen05 attention kernels spend their time: MMA/TMA pipeline versus softmax warps.
 
   python benchmarks/attn_split.py --build        # CPU is enough: compiles the three variants for sm_100a
-  python benchmarks/attn_split.py [--tokens 131072] [--windows 1024,2048]
+  python benchmarks/attn_split.py [--tokens 131072] [--windows 1024,2048]   # times the built variants
 
 Builds ``csrc/kernels/attention_tc.cu`` three times with ``ATTN_SPLIT_MODE``:
 
@@ -63,6 +63,19 @@ def load(mode: int):
                     extra_cflags=["-O3"], extra_ldflags=["-lcuda"], build_directory=d, verbose=False)
 
 
+def load_built(mode: int):
+    """Imports a variant built by ``--build`` (no compiler run: the build tree may come from another machine)."""
+    import glob
+    import importlib.util
+    hits = glob.glob(os.path.join(OUT, f"mode{mode}", f"attn_split{mode}*.so"))
+    if not hits:
+        raise SystemExit(f"variant {mode} is not built: run `python benchmarks/attn_split.py --build` first")
+    spec = importlib.util.spec_from_file_location(f"attn_split{mode}", hits[0])
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def timeit(fn, reps=10, warm=3):
     for _ in range(warm):
         fn()
@@ -84,10 +97,12 @@ def main():
     ap.add_argument("--tokens", type=int, default=131072)
     ap.add_argument("--windows", default="1024,2048")
     args = ap.parse_args()
-    mods = {m: load(m) for m in MODES}
     if args.build:
-        print("built", sorted(mods))
+        for m in MODES:
+            load(m)
+        print("built", sorted(MODES))
         return
+    mods = {m: load_built(m) for m in MODES}
     T, H, KV, hd = 2048, 4, 4, 128
     B = args.tokens // T
     torch.manual_seed(0)

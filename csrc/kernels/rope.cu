@@ -37,38 +37,71 @@ __device__ __forceinline__ void stb2(__nv_bfloat16* p, float a, float b) {
   *reinterpret_cast<uint32_t*>(p) = pack_bf16(a, b);
 }
 
-__global__ void rope_fwd_kernel(__nv_bfloat16* __restrict__ qkv, RopeArgs a, const float* __restrict__ cosT,
-                                const float* __restrict__ sinT, float* __restrict__ rq, float* __restrict__ rk,
-                                const int* __restrict__ idx, const float* __restrict__ ve,
-                                const float* __restrict__ cur, const float* __restrict__ wg, float* __restrict__ gate,
-                                int D) {
+// The q/k heads of a token go in groups of G = 8: every head of a group is loaded before any is
+// transformed, so a warp keeps a group's loads in flight and its warp reductions run side by side.
+constexpr int G = 8;
+
+__global__ void __launch_bounds__(256) rope_fwd_kernel(__nv_bfloat16* __restrict__ qkv, RopeArgs a,
+                                                       const float* __restrict__ cosT, const float* __restrict__ sinT,
+                                                       float* __restrict__ rq, float* __restrict__ rk,
+                                                       const int* __restrict__ idx, const float* __restrict__ ve,
+                                                       const float* __restrict__ cur, const float* __restrict__ wg,
+                                                       float* __restrict__ gate, int D) {
   const int lane = threadIdx.x & 31;
-  const int h2 = a.hd / 2;  // 64
+  constexpr int h2 = 64;  // hd / 2
+  const int nqk = a.H + a.KV;
   for (int m = blockIdx.x * kWarps + (threadIdx.x >> 5); m < a.M; m += gridDim.x * kWarps) {
     __nv_bfloat16* row = qkv + (int64_t)m * a.ld;
     const int t = m % a.T;
     const float2 c = *reinterpret_cast<const float2*>(cosT + t * h2 + 2 * lane);
     const float2 sn = *reinterpret_cast<const float2*>(sinT + t * h2 + 2 * lane);
-    const int nqk = a.H + a.KV;
-#pragma unroll 2
-    for (int s = 0; s < nqk; ++s) {
-      __nv_bfloat16* p = row + s * a.hd;
-      const float2 x1 = ldb2(p + 2 * lane), x2 = ldb2(p + h2 + 2 * lane);
-      const float y1a = x1.x * c.x + x2.x * sn.x, y1b = x1.y * c.y + x2.y * sn.y;
-      const float y2a = -x1.x * sn.x + x2.x * c.x, y2b = -x1.y * sn.y + x2.y * c.y;
-      const float r = rsqrtf(warp_sum(y1a * y1a + y1b * y1b + y2a * y2a + y2b * y2b) / a.hd + kEps);
-      stb2(p + 2 * lane, y1a * r, y1b * r);
-      stb2(p + h2 + 2 * lane, y2a * r, y2b * r);
-      if (lane == 0) (s < a.H ? rq[(int64_t)m * a.H + s] : rk[(int64_t)m * a.KV + (s - a.H)]) = r;
+    for (int s0 = 0; s0 < nqk; s0 += G) {
+      __nv_bfloat16* hrow = row + s0 * 128;
+      const int ng = min(G, nqk - s0);
+      float2 x1[G], x2[G];
+#pragma unroll
+      for (int s = 0; s < G; ++s) {
+        if (s < ng) {
+          x1[s] = ldb2(hrow + s * 128 + 2 * lane);
+          x2[s] = ldb2(hrow + s * 128 + h2 + 2 * lane);
+        }
+      }
+      float ss[G];
+#pragma unroll
+      for (int s = 0; s < G; ++s) {
+        ss[s] = 0.f;
+        if (s < ng) {
+          const float y1a = x1[s].x * c.x + x2[s].x * sn.x, y1b = x1[s].y * c.y + x2[s].y * sn.y;
+          const float y2a = -x1[s].x * sn.x + x2[s].x * c.x, y2b = -x1[s].y * sn.y + x2[s].y * c.y;
+          x1[s] = make_float2(y1a, y1b);
+          x2[s] = make_float2(y2a, y2b);
+          ss[s] = y1a * y1a + y1b * y1b + y2a * y2a + y2b * y2b;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int s = 0; s < G; ++s) ss[s] += __shfl_xor_sync(0xffffffffu, ss[s], o);
+      }
+#pragma unroll
+      for (int s = 0; s < G; ++s) {
+        if (s < ng) {
+          const float r = rsqrtf(ss[s] / 128.f + kEps);
+          stb2(hrow + s * 128 + 2 * lane, x1[s].x * r, x1[s].y * r);
+          stb2(hrow + s * 128 + h2 + 2 * lane, x2[s].x * r, x2[s].y * r);
+          const int hs = s0 + s;
+          if (lane == s) (hs < a.H ? rq[(int64_t)m * a.H + hs] : rk[(int64_t)m * a.KV + (hs - a.H)]) = r;
+        }
+      }
     }
     if (ve != nullptr) {
       const float cz = cur[(int64_t)m * D + lane];
-      const float* e = ve + (int64_t)idx[m] * (a.KV * a.hd);
+      const float* e = ve + (int64_t)idx[m] * (a.KV * 128);
       for (int h = 0; h < a.KV; ++h) {
         const float z = warp_sum(cz * wg[lane * a.KV + h]);
         const float g = 2.f / (1.f + __expf(-z));
-        __nv_bfloat16* p = row + (nqk + h) * a.hd;
-        const float4 ev = *reinterpret_cast<const float4*>(e + h * a.hd + 4 * lane);
+        __nv_bfloat16* p = row + (nqk + h) * 128;
+        const float4 ev = *reinterpret_cast<const float4*>(e + h * 128 + 4 * lane);
         const uint2 u = *reinterpret_cast<const uint2*>(p + 4 * lane);
         const float2 v01 = unpack_bf16(u.x), v23 = unpack_bf16(u.y);
         uint2 o;
@@ -82,41 +115,69 @@ __global__ void rope_fwd_kernel(__nv_bfloat16* __restrict__ qkv, RopeArgs a, con
 }
 
 // dqkv (in: grads of the transformed q,k,v; out: grads of the raw projection output), in place.
-__global__ void rope_bwd_kernel(__nv_bfloat16* __restrict__ dqkv, const __nv_bfloat16* __restrict__ qkv, RopeArgs a,
-                                const float* __restrict__ cosT, const float* __restrict__ sinT,
-                                const float* __restrict__ rq, const float* __restrict__ rk,
-                                const int* __restrict__ idx, const float* __restrict__ ve,
-                                const float* __restrict__ gate, float* __restrict__ dve, float* __restrict__ dz) {
+__global__ void __launch_bounds__(256) rope_bwd_kernel(__nv_bfloat16* __restrict__ dqkv,
+                                                       const __nv_bfloat16* __restrict__ qkv, RopeArgs a,
+                                                       const float* __restrict__ cosT, const float* __restrict__ sinT,
+                                                       const float* __restrict__ rq, const float* __restrict__ rk,
+                                                       const int* __restrict__ idx, const float* __restrict__ ve,
+                                                       const float* __restrict__ gate, float* __restrict__ dve,
+                                                       float* __restrict__ dz) {
   const int lane = threadIdx.x & 31;
-  const int h2 = a.hd / 2;
+  constexpr int h2 = 64;
+  const int nqk = a.H + a.KV;
   for (int m = blockIdx.x * kWarps + (threadIdx.x >> 5); m < a.M; m += gridDim.x * kWarps) {
     const int64_t base = (int64_t)m * a.ld;
     const int t = m % a.T;
     const float2 c = *reinterpret_cast<const float2*>(cosT + t * h2 + 2 * lane);
     const float2 sn = *reinterpret_cast<const float2*>(sinT + t * h2 + 2 * lane);
-    const int nqk = a.H + a.KV;
-#pragma unroll 2
-    for (int s = 0; s < nqk; ++s) {
-      const int64_t off = base + s * a.hd;
-      const float r = s < a.H ? rq[(int64_t)m * a.H + s] : rk[(int64_t)m * a.KV + (s - a.H)];
-      const float2 g1 = ldb2(dqkv + off + 2 * lane), g2 = ldb2(dqkv + off + h2 + 2 * lane);
-      const float2 u1 = ldb2(qkv + off + 2 * lane), u2 = ldb2(qkv + off + h2 + 2 * lane);
-      const float mean = warp_sum(g1.x * u1.x + g1.y * u1.y + g2.x * u2.x + g2.y * u2.y) / a.hd;
-      const float d1a = r * (g1.x - u1.x * mean), d1b = r * (g1.y - u1.y * mean);
-      const float d2a = r * (g2.x - u2.x * mean), d2b = r * (g2.y - u2.y * mean);
-      stb2(dqkv + off + 2 * lane, d1a * c.x - d2a * sn.x, d1b * c.y - d2b * sn.y);
-      stb2(dqkv + off + h2 + 2 * lane, d1a * sn.x + d2a * c.x, d1b * sn.y + d2b * c.y);
+    // lane s < nqk fetches head s's rstd; it is broadcast below
+    const float rl = lane < a.H ? rq[(int64_t)m * a.H + lane]
+                                : (lane < nqk ? rk[(int64_t)m * a.KV + (lane - a.H)] : 0.f);
+    for (int s0 = 0; s0 < nqk; s0 += G) {
+      const int ng = min(G, nqk - s0);
+      float2 g1[G], g2[G], u1[G], u2[G];
+#pragma unroll
+      for (int s = 0; s < G; ++s) {
+        if (s < ng) {
+          const int64_t off = base + (s0 + s) * 128;
+          g1[s] = ldb2(dqkv + off + 2 * lane);
+          g2[s] = ldb2(dqkv + off + h2 + 2 * lane);
+          u1[s] = ldb2(qkv + off + 2 * lane);
+          u2[s] = ldb2(qkv + off + h2 + 2 * lane);
+        }
+      }
+      float dot[G];
+#pragma unroll
+      for (int s = 0; s < G; ++s)
+        dot[s] = s < ng ? g1[s].x * u1[s].x + g1[s].y * u1[s].y + g2[s].x * u2[s].x + g2[s].y * u2[s].y : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int s = 0; s < G; ++s) dot[s] += __shfl_xor_sync(0xffffffffu, dot[s], o);
+      }
+#pragma unroll
+      for (int s = 0; s < G; ++s) {
+        const float r = __shfl_sync(0xffffffffu, rl, s0 + s);  // every lane shuffles (full mask)
+        if (s < ng) {
+          const int64_t off = base + (s0 + s) * 128;
+          const float mean = dot[s] / 128.f;
+          const float d1a = r * (g1[s].x - u1[s].x * mean), d1b = r * (g1[s].y - u1[s].y * mean);
+          const float d2a = r * (g2[s].x - u2[s].x * mean), d2b = r * (g2[s].y - u2[s].y * mean);
+          stb2(dqkv + off + 2 * lane, d1a * c.x - d2a * sn.x, d1b * c.y - d2b * sn.y);
+          stb2(dqkv + off + h2 + 2 * lane, d1a * sn.x + d2a * c.x, d1b * sn.y + d2b * c.y);
+        }
+      }
     }
     if (ve != nullptr) {
-      const int64_t erow = (int64_t)idx[m] * (a.KV * a.hd);
+      const int64_t erow = (int64_t)idx[m] * (a.KV * 128);
       for (int h = 0; h < a.KV; ++h) {
-        const int64_t off = base + (nqk + h) * a.hd + 4 * lane;
+        const int64_t off = base + (nqk + h) * 128 + 4 * lane;
         const float g = gate[(int64_t)m * a.KV + h];
-        const float4 e = *reinterpret_cast<const float4*>(ve + erow + h * a.hd + 4 * lane);
+        const float4 e = *reinterpret_cast<const float4*>(ve + erow + h * 128 + 4 * lane);
         const uint2 u = *reinterpret_cast<const uint2*>(dqkv + off);
         const float2 d01 = unpack_bf16(u.x), d23 = unpack_bf16(u.y);
         const float dg = warp_sum(d01.x * e.x + d01.y * e.y + d23.x * e.z + d23.y * e.w);
-        red_add_v4_f32(dve + erow + h * a.hd + 4 * lane, d01.x * g, d01.y * g, d23.x * g, d23.y * g);
+        red_add_v4_f32(dve + erow + h * 128 + 4 * lane, d01.x * g, d01.y * g, d23.x * g, d23.y * g);
         if (lane == 0) dz[(int64_t)m * a.KV + h] = dg * g * (1.f - 0.5f * g);
       }
     }
@@ -166,7 +227,7 @@ int grid_for(int64_t tasks) {
   int dev, sms;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return (int)std::max<int64_t>(1, std::min<int64_t>((tasks + kWarps - 1) / kWarps, (int64_t)sms * 16));
+  return (int)std::max<int64_t>(1, std::min<int64_t>((tasks + kWarps - 1) / kWarps, (int64_t)sms * 8));
 }
 
 }  // namespace
@@ -181,6 +242,7 @@ void rope_fwd(torch::Tensor& qkv, int64_t T, int64_t H, int64_t KV, int64_t hd, 
   RopeArgs a{(int)M, (int)T, (int)H, (int)KV, (int)hd, (int)qkv.stride(0)};
   const bool has_ve = ve.has_value() && ve->defined();
   c10::cuda::CUDAGuard g(qkv.device());
+  TORCH_CHECK(H + KV <= 32, "rope_fwd: at most 32 q/k heads");
   rope_fwd_kernel<<<grid_for(M), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), a, cosT.data_ptr<float>(), sinT.data_ptr<float>(),
       rq.data_ptr<float>(), rk.data_ptr<float>(), idx.data_ptr<int>(), has_ve ? ve->data_ptr<float>() : nullptr,
@@ -198,6 +260,7 @@ void rope_bwd(torch::Tensor& dqkv, const torch::Tensor& qkv, int64_t T, int64_t 
   RopeArgs a{(int)M, (int)T, (int)H, (int)KV, (int)hd, (int)qkv.stride(0)};
   const bool has_ve = ve.has_value() && ve->defined();
   c10::cuda::CUDAGuard g(qkv.device());
+  TORCH_CHECK(hd == 128 && H + KV <= 32, "rope_bwd: head_dim 128, at most 32 q/k heads");
   rope_bwd_kernel<<<grid_for(M), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), a,
       cosT.data_ptr<float>(), sinT.data_ptr<float>(), rq.data_ptr<float>(), rk.data_ptr<float>(), idx.data_ptr<int>(),
