@@ -56,15 +56,23 @@ constexpr int BK = 64;
 constexpr int CHUNK_BYTES = 32 * 128;  // one epilogue warp's 32 rows x 128 bytes
 constexpr uint64_t kWaitBudgetNs = 2000000000ull;
 
-template <int BN>
+// AUX: the epilogue reads an auxiliary input. Its loads then run through a 4-buffer ring per
+// epilogue warp, issued up to three chunks (across tile boundaries) ahead of the chunk being
+// processed, so the DRAM latency of the aux tile overlaps the epilogue math; the main loop gives up
+// one stage to make room.
+template <int BN, bool AUX>
 struct GemmCfg {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int STAGES = AUX ? (BN == 256 ? 3 : 5) : (BN == 256 ? 4 : 6);
+  static constexpr int NBUF = AUX ? 4 : 2;  // staging buffers per epilogue warp
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int EPI_BYTES = 4 * 2 * CHUNK_BYTES;  // 4 warps x 2 buffers
-  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 256 /*barriers*/ + 1024 /*align*/;
+  static constexpr int EPI_BYTES = 4 * NBUF * CHUNK_BYTES;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024 /*align*/;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+  static_assert((2 * STAGES + 5 + 4 * NBUF) * 8 + 8 <= BAR_BYTES, "barrier region");
 };
 
 constexpr bool epi_f32(int e) { return e == EPI_F32 || e == EPI_ATOMIC_F32; }
@@ -96,6 +104,16 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* m, const vo
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Waits until at most n bulk store groups still read shared memory (n clamped to [0, 2]; waiting for
+// fewer pending groups than allowed is always safe).
+__device__ __forceinline__ void bulk_wait_read_n(int n) {
+  if (n <= 0)
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  else if (n == 1)
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+  else
+    asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory");
+}
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled staging tile.
@@ -118,11 +136,13 @@ __device__ __forceinline__ float epi_op(float acc, float aux, const GemmParams& 
   return v;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool AUX>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, GemmParams p) {
-  using Cfg = GemmCfg<BN>;
+  static_assert(!AUX || epi_reads_aux(EPI), "aux ring for an epilogue without aux");
+  using Cfg = GemmCfg<BN, AUX>;
+  constexpr int NBUF = Cfg::NBUF;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -135,8 +155,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tfull_bar = bars + 2 * STAGES;
   uint64_t* tempty_bar = bars + 2 * STAGES + 2;
   uint64_t* drain_bar = bars + 2 * STAGES + 4;
-  uint64_t* aux_bar = bars + 2 * STAGES + 5;  // [4], one per epilogue warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 9);
+  uint64_t* aux_bar = bars + 2 * STAGES + 5;  // [4][NBUF]: per epilogue warp, one per staging buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5 + 4 * NBUF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -153,7 +173,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&tempty_bar[a], 128);
     }
     mbar_init(drain_bar, 1);
-    for (int w = 0; w < 4; ++w) mbar_init(&aux_bar[w], 1);
+    for (int w = 0; w < 4 * NBUF; ++w) mbar_init(&aux_bar[w], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -272,67 +292,91 @@ __global__ void __launch_bounds__(192, 1)
     const int wq = warp & 3;
     const int lane = lane_id();
     const bool leader = lane == 0;
-    uint8_t* ebuf = sE + wq * 2 * CHUNK_BYTES;
-    uint64_t* xbar = &aux_bar[wq];
-    uint32_t xphase = 0;
-    int nchunk = 0;
+    uint8_t* ebuf = sE + wq * NBUF * CHUNK_BYTES;
+    uint64_t* xbar = &aux_bar[wq * NBUF];
     constexpr int COLS = epi_f32(EPI) ? 32 : 64;  // columns per 128-byte chunk
+    constexpr int CPT = BN / COLS;                 // chunks per tile
+    int nchunk = 0;                                // chunks this warp has processed (ring position)
+    // aux prefetch cursor (AUX only): next chunk to load, its work unit and chunk within the tile
+    int pchunk = 0, pu = blockIdx.x, pc = 0;
+    auto prefetch = [&](int upto) {
+      while (pchunk < upto && pu < total) {
+        if (pchunk >= NBUF) {
+          // buffer pchunk % NBUF last staged chunk pchunk - NBUF: its store must have read it; the
+          // stores of the chunks after it may still be pending (one bulk group per chunk)
+          const int newer = nchunk - 1 - (pchunk - NBUF);
+          if (leader) bulk_wait_read_n(newer);
+        }
+        if (leader) {
+          int m, n, b, kb0, kb1;
+          decode_unit(p, pu, m, n, b, kb0, kb1);
+          const int slot = pchunk % NBUF;
+          mbar_arrive_expect_tx(&xbar[slot], CHUNK_BYTES);
+          tma_load_3d(&tmX, &xbar[slot], ebuf + slot * CHUNK_BYTES, n * BN + pc * COLS, m * BM + wq * 32, b);
+        }
+        ++pchunk;
+        if (++pc == CPT) {
+          pc = 0;
+          pu += gridDim.x;
+        }
+      }
+    };
     int local = 0;
     if (leader) {
       tma_prefetch_desc(&tmC);
-      if (p.has_aux) tma_prefetch_desc(&tmX);
+      if constexpr (AUX) tma_prefetch_desc(&tmX);
     }
-    for (int u = blockIdx.x; u < total; u += gridDim.x, ++local) {
+    bool ok = true;
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++local) {
       int m, n, b, kb0, kb1;
       decode_unit(p, u, m, n, b, kb0, kb1);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      if constexpr (AUX) prefetch(nchunk + NBUF);  // aux of the coming chunks loads during the MMA
       if (!mbar_wait_warp(&tfull_bar[acc], acc_phase, kWaitBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
+        ok = false;
         break;
       }
       tc_fence_after();
       const int row0 = m * BM + wq * 32;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * BN;
-      bool ok = true;
 #pragma unroll 1
-      for (int c = 0; c < BN / COLS; ++c, ++nchunk) {
-        uint8_t* buf = ebuf + (nchunk & 1) * CHUNK_BYTES;
+      for (int c = 0; c < CPT; ++c, ++nchunk) {
+        const int slot = nchunk % NBUF;
+        uint8_t* buf = ebuf + slot * CHUNK_BYTES;
         const int col0 = n * BN + c * COLS;
-        if (leader) bulk_wait_read1();  // the store that last used this buffer has read it
-        __syncwarp();
-        const bool use_aux = epi_reads_aux(EPI) && p.has_aux;
-        if (use_aux) {
-          if (leader) {
-            mbar_arrive_expect_tx(xbar, CHUNK_BYTES);
-            tma_load_3d(&tmX, xbar, buf, col0, row0, b);
-          }
-        }
         uint32_t r[COLS];
         tmem_ld32(taddr + c * COLS, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         if constexpr (COLS == 64) tmem_ld32(taddr + c * COLS + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        if constexpr (AUX) {
+          prefetch(nchunk + NBUF);  // keeps up to NBUF - 1 chunks ahead in flight
+        } else {
+          if (leader) bulk_wait_read1();  // the store that last used this buffer has read it
+        }
+        __syncwarp();
         tmem_ld_wait();
-        if (use_aux) {
-          if (!mbar_wait_warp(xbar, xphase, kWaitBudgetNs, abort_flag, p.status)) {
+        if constexpr (AUX) {
+          if (!mbar_wait_warp(&xbar[slot], (nchunk / NBUF) & 1, kWaitBudgetNs, abort_flag, p.status)) {
             fail(kErrTimeoutEpilogue);
             ok = false;
+            break;
           }
-          xphase ^= 1;
         }
         uint8_t* myrow = buf;  // row `lane` of this warp's 32-row chunk
 #pragma unroll
         for (int q = 0; q < 8; ++q) {  // eight 16-byte chunks per 128-byte row
-          uint4* slot = reinterpret_cast<uint4*>(myrow + swz_off(lane, q));
+          uint4* slotp = reinterpret_cast<uint4*>(myrow + swz_off(lane, q));
           if constexpr (epi_f32(EPI)) {
-            float4 x = use_aux ? *reinterpret_cast<const float4*>(slot) : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 x = AUX ? *reinterpret_cast<const float4*>(slotp) : make_float4(0.f, 0.f, 0.f, 0.f);
             float4 o;
             o.x = epi_op<EPI == EPI_ATOMIC_F32 ? EPI_BF16 : EPI>(__uint_as_float(r[4 * q + 0]), x.x, p);
             o.y = epi_op<EPI == EPI_ATOMIC_F32 ? EPI_BF16 : EPI>(__uint_as_float(r[4 * q + 1]), x.y, p);
             o.z = epi_op<EPI == EPI_ATOMIC_F32 ? EPI_BF16 : EPI>(__uint_as_float(r[4 * q + 2]), x.z, p);
             o.w = epi_op<EPI == EPI_ATOMIC_F32 ? EPI_BF16 : EPI>(__uint_as_float(r[4 * q + 3]), x.w, p);
-            *reinterpret_cast<float4*>(slot) = o;
+            *reinterpret_cast<float4*>(slotp) = o;
           } else {
-            uint4 xv = use_aux ? *slot : make_uint4(0, 0, 0, 0);
+            uint4 xv = AUX ? *slotp : make_uint4(0, 0, 0, 0);
             const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
             uint32_t os[4];
 #pragma unroll
@@ -341,26 +385,28 @@ __global__ void __launch_bounds__(192, 1)
               os[j] = pack_bf16(epi_op<EPI>(__uint_as_float(r[8 * q + 2 * j]), f.x, p),
                                 epi_op<EPI>(__uint_as_float(r[8 * q + 2 * j + 1]), f.y, p));
             }
-            *slot = make_uint4(os[0], os[1], os[2], os[3]);
+            *slotp = make_uint4(os[0], os[1], os[2], os[3]);
           }
         }
         fence_async_smem();
         __syncwarp();
-        if (c == BN / COLS - 1) {
+        if (c == CPT - 1) {
           // accumulator fully read: hand it back to the MMA warp
           tc_fence_before();
           mbar_arrive(&tempty_bar[acc]);
         }
-        if (leader && ok) {
+        if (leader) {
           if constexpr (EPI == EPI_ATOMIC_F32)
             tma_reduce_add_3d(&tmC, buf, col0, row0, b);
           else
             tma_store_3d(&tmC, buf, col0, row0, b);
           bulk_commit();
         }
-        if (!ok) break;
       }
-      if (!ok) break;
+    }
+    if constexpr (AUX) {
+      // on an early exit, let every aux load already issued land before the CTA leaves
+      for (int q = nchunk; q < pchunk; ++q) mbar_wait(&xbar[q % NBUF], (q / NBUF) & 1, 100000000ull, nullptr);
     }
     if (leader) bulk_wait_all();
     __syncwarp();
@@ -390,31 +436,37 @@ struct Maps {
   CUtensorMap a, b, c, x;
 };
 
-template <int BN, bool AMN, bool BMN, int EPI>
+template <int BN, bool AMN, bool BMN, int EPI, bool AUX>
 void launch_t(const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
-  auto k = gemm_kernel<BN, AMN, BMN, EPI>;
+  auto k = gemm_kernel<BN, AMN, BMN, EPI, AUX>;
+  using Cfg = GemmCfg<BN, AUX>;
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     attr = true;
   }
-  k<<<grid, 192, GemmCfg<BN>::SMEM, st>>>(mp.a, mp.b, mp.c, mp.x, p);
+  k<<<grid, 192, Cfg::SMEM, st>>>(mp.a, mp.b, mp.c, mp.x, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 template <int BN, bool AMN, bool BMN>
 void dispatch_epi(int epi, const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
+  const bool aux = p.has_aux != 0;
   switch (epi) {
-    case EPI_BF16: return launch_t<BN, AMN, BMN, EPI_BF16>(mp, p, grid, st);
-    case EPI_F32: return launch_t<BN, AMN, BMN, EPI_F32>(mp, p, grid, st);
-    case EPI_ATOMIC_F32: return launch_t<BN, AMN, BMN, EPI_ATOMIC_F32>(mp, p, grid, st);
+    case EPI_BF16:
+      return aux ? launch_t<BN, AMN, BMN, EPI_BF16, true>(mp, p, grid, st)
+                 : launch_t<BN, AMN, BMN, EPI_BF16, false>(mp, p, grid, st);
+    case EPI_F32:
+      return aux ? launch_t<BN, AMN, BMN, EPI_F32, true>(mp, p, grid, st)
+                 : launch_t<BN, AMN, BMN, EPI_F32, false>(mp, p, grid, st);
+    case EPI_ATOMIC_F32: return launch_t<BN, AMN, BMN, EPI_ATOMIC_F32, false>(mp, p, grid, st);
     default: break;
   }
   if constexpr (BN == 256) {
     switch (epi) {
-      case EPI_RELU2: return launch_t<BN, AMN, BMN, EPI_RELU2>(mp, p, grid, st);
-      case EPI_RELU2_BWD: return launch_t<BN, AMN, BMN, EPI_RELU2_BWD>(mp, p, grid, st);
-      case EPI_SOFTCAP: return launch_t<BN, AMN, BMN, EPI_SOFTCAP>(mp, p, grid, st);
+      case EPI_RELU2: return launch_t<BN, AMN, BMN, EPI_RELU2, false>(mp, p, grid, st);
+      case EPI_RELU2_BWD: return launch_t<BN, AMN, BMN, EPI_RELU2_BWD, true>(mp, p, grid, st);
+      case EPI_SOFTCAP: return launch_t<BN, AMN, BMN, EPI_SOFTCAP, false>(mp, p, grid, st);
       default: break;
     }
   }
@@ -497,6 +549,7 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
   p.k_splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
   if (aux.has_value() && aux->defined()) {
     TORCH_CHECK(aux->scalar_type() == c.scalar_type(), "gemm: aux dtype must match the output");
+    TORCH_CHECK(epi == EPI_BF16 || epi == EPI_F32 || epi == EPI_RELU2_BWD, "gemm: this epilogue takes no aux");
     mp.x = out_map(*aux, M, N, batch, ld_aux, bs_aux);
     p.has_aux = 1;
   } else {
