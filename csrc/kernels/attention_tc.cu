@@ -389,7 +389,11 @@ struct BwdParams {
   int T, H, KV, Dq, Dkv, window;
   float scale_log2, scale;
   const float* lse;
-  const float* delta;
+  float* delta;                 // rowsum(dO * O): written by the dQ kernel, read by the dK/dV kernel
+  const __nv_bfloat16* o;
+  int64_t ldo;
+  const __nv_bfloat16* dout;
+  int64_t lddo;
   __nv_bfloat16* dq;
   int64_t lddq;
   __nv_bfloat16* dk;
@@ -405,14 +409,15 @@ struct BwdParams {
 constexpr int BK64 = 64;
 constexpr int KV64 = 64 * 128 * 2;        // 64 keys x 128 hd: two 8 KB swizzle atoms
 constexpr int KV64_ATOM = 64 * 128;
-constexpr int DQ_STAGES = 4;
+constexpr int DQ_STAGES = 5;
 constexpr int DQ_Q = 0;
 constexpr int DQ_DO = DQ_Q + TILE_BYTES;
-constexpr int DQ_K = DQ_DO + TILE_BYTES;            // [4] x 16 KB
-constexpr int DQ_V = DQ_K + DQ_STAGES * KV64;       // [4] x 16 KB
-constexpr int DQ_DS = DQ_V + DQ_STAGES * KV64;      // [2] x (128 q x 64 keys bf16 = one 16 KB atom)
-constexpr int DQ_BAR = DQ_DS + 2 * 16384;
+constexpr int DQ_K = DQ_DO + TILE_BYTES;            // [5] x 16 KB
+constexpr int DQ_V = DQ_K + DQ_STAGES * KV64;       // [5] x 16 KB
+constexpr int DQ_DSUM = DQ_V + DQ_STAGES * KV64;    // [2][128] floats: half-row sums of dO * O
+constexpr int DQ_BAR = DQ_DSUM + 1024;
 constexpr int DQ_SMEM = DQ_BAR + 256 + 1024;
+static_assert(DQ_SMEM <= 232448, "dQ kernel shared memory");
 
 __global__ void __launch_bounds__(320, 1)
     attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
@@ -422,13 +427,14 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DQ_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [4]
-  uint64_t* kv_empty = bars + 5;  // [4]
-  uint64_t* s_full = bars + 9;    // [2]
-  uint64_t* p_full = bars + 11;   // [2]: by iteration parity, so a warp group running one block ahead
+  uint64_t* kv_full = bars + 1;                   // [DQ_STAGES]
+  uint64_t* kv_empty = kv_full + DQ_STAGES;       // [DQ_STAGES]
+  uint64_t* s_full = kv_empty + DQ_STAGES;        // [2]
+  uint64_t* p_full = s_full + 2;                  // [2]: by iteration parity, so a warp group running one block ahead
                                   // arrives on the other barrier and never completes the current phase
-  uint64_t* done = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* done = p_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  static_assert((2 * DQ_STAGES + 7) * 8 <= 256, "dQ barrier region");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -523,10 +529,11 @@ __global__ void __launch_bounds__(320, 1)
         tc_fence_after();
         const int st = j % DQ_STAGES;
         const uint32_t k_addr = smem_u32(smem + DQ_K + st * KV64);
-        const uint32_t ds_addr = smem_u32(smem + DQ_DS + (j & 1) * 16384);
+        // dS (bf16 pairs) sits in TMEM over the scores it came from: keys 32h .. 32h+31 at columns
+        // 128*set + 32h .. +15, so each 16-key step reads its own 8 columns
 #pragma unroll
         for (int kk = 0; kk < BK64 / 16; ++kk)
-          umma_bf16_ss(tmem + 256, umma_desc_sw128(ds_addr + kk * 32, 16, 1024),
+          umma_bf16_ts(tmem + 256, tmem + (j & 1) * 128 + (kk >> 1) * 32 + (kk & 1) * 8,
                        umma_desc_sw128(k_addr + kk * 2048, KV64_ATOM, 1024), idesc_q, (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&kv_empty[st]);
       }
@@ -543,7 +550,35 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
     const int qc = min(qi, p.T - 1);
     const float lse2 = p.lse[((int64_t)b * p.H + h) * p.T + qc];  // log2 units
-    const float dl = p.delta[((int64_t)b * p.H + h) * p.T + qc];
+    // delta = rowsum(dO * O) over this head: the two warps of a row each reduce 64 of the 128 dims
+    // (while the first tiles load) and meet in shared memory; the kernel writes delta for dK/dV
+    float dl;
+    {
+      float* dsum = reinterpret_cast<float*>(smem + DQ_DSUM);
+      const int64_t row = (int64_t)b * p.T + qc;
+      const uint4* op = reinterpret_cast<const uint4*>(p.o + row * p.ldo + h * HD + half * 64);
+      const uint4* gp = reinterpret_cast<const uint4*>(p.dout + row * p.lddo + h * HD + half * 64);
+      uint4 ov[8], gv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ov[i] = __ldg(op + i);
+        gv[i] = __ldg(gp + i);
+      }
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t oa[4] = {ov[i].x, ov[i].y, ov[i].z, ov[i].w}, ga[4] = {gv[i].x, gv[i].y, gv[i].z, gv[i].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 x = unpack_bf16(oa[k]), y = unpack_bf16(ga[k]);
+          acc = fmaf(x.x, y.x, fmaf(x.y, y.y, acc));
+        }
+      }
+      dsum[half * 128 + r] = acc;
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight softmax warps
+      dl = dsum[r] + dsum[128 + r];
+      if (half == 0 && qi < p.T) p.delta[((int64_t)b * p.H + h) * p.T + qi] = dl;
+    }
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int set = j & 1;
@@ -559,7 +594,6 @@ __global__ void __launch_bounds__(320, 1)
       tmem_ld32(lane_base + set * 128 + half * 32, sv);
       tmem_ld32(lane_base + set * 128 + 64 + half * 32, dv);
       tmem_ld_wait();
-      uint8_t* drow = smem + DQ_DS + set * 16384 + r * 128;
       // dS = exp2(S * scale_log2 - lse2) (dP - delta); query qi sees key k0 + i for i in
       // [qi - w + 1 - k0, qi + 1 - k0) below T - k0 (boundary blocks only)
       uint32_t pk[16];
@@ -587,13 +621,9 @@ __global__ void __launch_bounds__(320, 1)
       } else {
         body(std::true_type{});
       }
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int chunk = half * 4 + q;
-        *reinterpret_cast<uint4*>(drow + ((chunk ^ (r & 7)) << 4)) =
-            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-      }
-      fence_async_smem();
+      // into this warp's own (already read) score columns: the other warp of the row still reads its half
+      tmem_st16(lane_base + set * 128 + half * 32, pk);
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);
     }
@@ -634,16 +664,15 @@ __global__ void __launch_bounds__(320, 1)
 constexpr int KB_Q = 64;
 constexpr int HALF_TILE = 64 * 128 * 2;   // 64 rows x 128 hd, two 8 KB swizzle atoms
 constexpr int HALF_ATOM = 64 * 128;
-constexpr int DK_STAGES = 3;                        // Q/dO ring: block i+1 is issued ahead while i-1 drains
+constexpr int DK_STAGES = 4;                        // Q/dO ring
 constexpr int DK_K = 0;
 constexpr int DK_V = DK_K + TILE_BYTES;
-constexpr int DK_Q = DK_V + TILE_BYTES;            // [3] x HALF_TILE
-constexpr int DK_DO = DK_Q + DK_STAGES * HALF_TILE;  // [3] x HALF_TILE
-constexpr int DK_PT = DK_DO + DK_STAGES * HALF_TILE; // [2] x (128 keys x 64 q bf16 = one 16 KB atom)
-constexpr int DK_DST = DK_PT + 2 * 16384;          // [2] x 16 KB
-constexpr int DK_STAT = DK_DST + 2 * 16384;        // [3] x (lse[64], delta[64]) floats
+constexpr int DK_Q = DK_V + TILE_BYTES;            // [4] x HALF_TILE
+constexpr int DK_DO = DK_Q + DK_STAGES * HALF_TILE;  // [4] x HALF_TILE
+constexpr int DK_STAT = DK_DO + DK_STAGES * HALF_TILE; // [4] x (lse[64], delta[64]) floats
 constexpr int DK_BAR = DK_STAT + DK_STAGES * 512;
 constexpr int DK_SMEM = DK_BAR + 256 + 1024;
+static_assert(DK_SMEM <= 232448, "dK/dV kernel shared memory");
 
 __global__ void __launch_bounds__(320, 1)
     attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_qkv,
@@ -653,12 +682,13 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DK_BAR);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;   // [3]
-  uint64_t* qd_empty = bars + 4;  // [3]
-  uint64_t* s_full = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;    // [2], by iteration parity (see the dQ kernel)
-  uint64_t* done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* qd_full = bars + 1;                   // [DK_STAGES]
+  uint64_t* qd_empty = qd_full + DK_STAGES;       // [DK_STAGES]
+  uint64_t* s_full = qd_empty + DK_STAGES;        // [2]
+  uint64_t* p_full = s_full + 2;                  // [2], by iteration parity (see the dQ kernel)
+  uint64_t* done = p_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  static_assert((2 * DK_STAGES + 7) * 8 <= 256, "dK/dV barrier region");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* stat = reinterpret_cast<float*>(smem + DK_STAT);
 
@@ -762,15 +792,15 @@ __global__ void __launch_bounds__(320, 1)
         const int st = it % DK_STAGES, set = it & 1;
         const uint32_t q_addr = smem_u32(smem + DK_Q + st * HALF_TILE);
         const uint32_t do_addr = smem_u32(smem + DK_DO + st * HALF_TILE);
-        const uint32_t pt_addr = smem_u32(smem + DK_PT + set * 16384);
-        const uint32_t dst_addr = smem_u32(smem + DK_DST + set * 16384);
+        // P^T and dS^T (bf16 pairs) sit in TMEM over S^T and dP^T: queries 32h .. 32h+31 at columns
+        // 32h .. +15 of each, so each 16-query step reads its own 8 columns
 #pragma unroll
         for (int kk = 0; kk < KB_Q / 16; ++kk) {
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          umma_bf16_ss(tmem + 256, umma_desc_sw128(pt_addr + kk * 32, 16, 1024),
-                       umma_desc_sw128(do_addr + kk * 2048, HALF_ATOM, 1024), idesc_g, acc);
-          umma_bf16_ss(tmem + 384, umma_desc_sw128(dst_addr + kk * 32, 16, 1024),
-                       umma_desc_sw128(q_addr + kk * 2048, HALF_ATOM, 1024), idesc_g, acc);
+          const uint32_t col = set * 128 + (kk >> 1) * 32 + (kk & 1) * 8;
+          umma_bf16_ts(tmem + 256, tmem + col, umma_desc_sw128(do_addr + kk * 2048, HALF_ATOM, 1024), idesc_g, acc);
+          umma_bf16_ts(tmem + 384, tmem + col + 64, umma_desc_sw128(q_addr + kk * 2048, HALF_ATOM, 1024), idesc_g,
+                       acc);
         }
         umma_commit(&qd_empty[st]);
       }
@@ -802,8 +832,6 @@ __global__ void __launch_bounds__(320, 1)
       tmem_ld32(lane_base + set * 128 + half * 32, sv);
       tmem_ld32(lane_base + set * 128 + 64 + half * 32, dv);
       tmem_ld_wait();
-      uint8_t* prow = smem + DK_PT + set * 16384 + r * 128;
-      uint8_t* srow = smem + DK_DST + set * 16384 + r * 128;
       // P^T = exp2(S^T * scale_log2 - lse2) and dS^T = P^T (dP^T - delta); key kj sees query q0 + i for
       // i in [kj - q0, kj - q0 + w) below T - q0 (boundary blocks only; interior blocks skip the mask)
       uint32_t pp[16], ss[16];
@@ -841,14 +869,10 @@ __global__ void __launch_bounds__(320, 1)
       } else {
         body(std::true_type{});
       }
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int chunk = half * 4 + q;
-        const int phys = (chunk ^ (r & 7)) << 4;
-        *reinterpret_cast<uint4*>(prow + phys) = make_uint4(pp[4 * q], pp[4 * q + 1], pp[4 * q + 2], pp[4 * q + 3]);
-        *reinterpret_cast<uint4*>(srow + phys) = make_uint4(ss[4 * q], ss[4 * q + 1], ss[4 * q + 2], ss[4 * q + 3]);
-      }
-      fence_async_smem();
+      // into this warp's own (already read) columns of S^T and dP^T
+      tmem_st16(lane_base + set * 128 + half * 32, pp);
+      tmem_st16(lane_base + set * 128 + 64 + half * 32, ss);
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[it & 1]);
     }
@@ -926,20 +950,16 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse,
 }  // namespace br
 
 namespace br {
-void attn_delta(const torch::Tensor& o, const torch::Tensor& dout, torch::Tensor& delta, int64_t B, int64_t T,
-                int64_t H);
-
 // dqkv: [B*T, Dq + 2*Dkv] bf16 output (dq | dk | dv); dout: [B*T, H*hd] bf16; lse, delta: fp32 [B, H, T].
 void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::Tensor& dout, const torch::Tensor& lse,
                  torch::Tensor& dqkv, torch::Tensor& delta, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd,
                  int64_t window, int64_t which) {
-  // which: 0 = delta, dQ and dK/dV; 1 = delta and dQ only; 2 = dK/dV only (delta already computed)
+  // which: 0 = dQ (which also writes delta) and dK/dV; 1 = dQ only; 2 = dK/dV only (delta already written)
   TORCH_CHECK(hd == HD && T % 128 == 0, "attn_bwd_tc: head_dim 128 and T % 128 == 0");
   const int64_t W = qkv.size(1);
   TORCH_CHECK(W == (H + 2 * KV) * hd && dqkv.size(1) == W, "attn_bwd_tc: widths");
   TORCH_CHECK(dout.stride(1) == 1 && dout.size(1) == H * hd, "attn_bwd_tc: dout");
   c10::cuda::CUDAGuard g(qkv.device());
-  if (which != 2) attn_delta(o, dout, delta, B, T, H);
   CUtensorMap tq = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.data_ptr(), W, T, B, qkv.stride(0),
                               qkv.stride(0) * T, 64, 128);
   CUtensorMap td = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dout.data_ptr(), H * hd, T, B, dout.stride(0),
@@ -960,6 +980,11 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::
   p.scale_log2 = kLog2e * p.scale;
   p.lse = lse.data_ptr<float>();
   p.delta = delta.data_ptr<float>();
+  TORCH_CHECK(o.stride(1) == 1 && o.stride(0) % 8 == 0 && dout.stride(0) % 8 == 0, "attn_bwd_tc: o / dout rows");
+  p.o = reinterpret_cast<const __nv_bfloat16*>(o.data_ptr());
+  p.ldo = o.stride(0);
+  p.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  p.lddo = dout.stride(0);
   auto* base = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   p.dq = base;
   p.lddq = dqkv.stride(0);
