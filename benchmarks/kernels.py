@@ -161,6 +161,28 @@ def main():
             ms = timeit(lambda: E.attn_bwd_tc(qkv, o2, do, lse, dqkv, delta, B, T, H, H, 128, window, 2), reps=5)
             report(f"  attn_bwd_tc dkdv only (2x fwd)", ms, flops=2.0 * f_fwd)
 
+    # ------------------------------------------------------------------ RoPE fusion A/B
+    if want("fusion"):
+        # QKV projection + RoPE/QK-norm (+ value embedding): one GEMM with the epilogue vs GEMM + kernel
+        xq = torch.randn(M, D, **bf)
+        wq = torch.randn(D, 3 * D, **bf) * D ** -0.5
+        qkv = torch.empty(M, 3 * D, **bf)
+        pos = torch.arange(T, device=dev, dtype=torch.float32)[:, None]
+        inv = 10000.0 ** (-torch.arange(0, 128, 2, device=dev, dtype=torch.float32) / 128)
+        cos, sin = torch.cos(pos * inv).contiguous(), torch.sin(pos * inv).contiguous()
+        idx = torch.randint(0, V, (M,), device=dev, dtype=torch.int32)
+        rq, rk = torch.empty(M, H, device=dev), torch.empty(M, H, device=dev)
+        ve = torch.randn(V, D, device=dev)
+        curx = torch.randn(M, D, device=dev)
+        wg = torch.randn(32, H, device=dev) * 0.3
+        gate = torch.empty(M, H, device=dev)
+        for tag, vea in (("", (idx, None, None, None, None)), (" +VE", (idx, ve, curx, wg, gate))):
+            ms_sep = timeit(lambda: (gemm.matmul(xq, wq, out=qkv),
+                                     E.rope_fwd(qkv, T, H, H, 128, cos, sin, rq, rk, *vea)))
+            ms_fused = timeit(lambda: gemm.qkv_rope(xq, wq, qkv, cos, sin, rq, rk, T, H, H, *vea))
+            report(f"qkv+rope{tag}: gemm then rope_fwd", ms_sep, flops=2.0 * M * D * 3 * D)
+            report(f"qkv+rope{tag}: fused epilogue", ms_fused, flops=2.0 * M * D * 3 * D)
+
     # ------------------------------------------------------------------ row kernels
     if want("rows"):
         x = torch.randn(M, D, device=dev)

@@ -58,6 +58,8 @@ class FusedGPTEngine:
         self.bucket_hook = None
         # tcgen05 attention needs whole 128-row tiles; other lengths use the register-tiled kernels
         self.tc_attention = seq % 128 == 0
+        # the QKV GEMM applies RoPE/QK-norm/VE in its epilogue when each 256-column tile holds two heads
+        self.fused_rope = self.hd == 128 and self.H % 2 == 0 and self.KV % 2 == 0
         self._hook_on = False
         self._grad_scale = 1.0
 
@@ -138,12 +140,13 @@ class FusedGPTEngine:
             cur, xn = b["cur"][i], b["xn"][i]
             E.ladder_rms_fwd(x, b["x0"], P["residLambdas"], P["x0Lambdas"], i, cur, xn, b["rstd1"][i])
             qkv = b["qkv"][i]
-            gemm.matmul(xn, self.wqkv[i], out=qkv)
-            if i in b["gate"]:
-                E.rope_fwd(qkv, T, H, KV, hd, self.cos, self.sin, b["rq"][i], b["rk"][i], idx,
-                           P[f"ve_{i}"], cur, P[f"layer{i}_ve_gate"], b["gate"][i])
+            ve_args = ((idx, P[f"ve_{i}"], cur, P[f"layer{i}_ve_gate"], b["gate"][i]) if i in b["gate"]
+                       else (idx, None, None, None, None))
+            if self.fused_rope:  # RoPE + QK-norm (+ VE) in the QKV GEMM's epilogue
+                gemm.qkv_rope(xn, self.wqkv[i], qkv, self.cos, self.sin, b["rq"][i], b["rk"][i], T, H, KV, *ve_args)
             else:
-                E.rope_fwd(qkv, T, H, KV, hd, self.cos, self.sin, b["rq"][i], b["rk"][i], idx, None, None, None, None)
+                gemm.matmul(xn, self.wqkv[i], out=qkv)
+                E.rope_fwd(qkv, T, H, KV, hd, self.cos, self.sin, b["rq"][i], b["rk"][i], *ve_args)
             o = b["o"][i]
             if self.tc_attention:
                 E.attn_fwd_tc(qkv, o, b["lse"][i], B, T, H, KV, hd, self.windows[i])
@@ -185,31 +188,30 @@ class FusedGPTEngine:
             gemm.matmul(b["o"][i].t(), b["dmid_b"], out=G[f"layer{i}_proj"], epi=A, k_splits=0)
             gemm.matmul(b["dmid_b"], self.shadows[f"layer{i}_proj"].t(), out=b["do"])
             qkv, dqkv = b["qkv"][i], b["dqkv"]
+            ve = i in b["gate"]
             if self.tc_attention:
                 E.attn_bwd_tc(qkv, b["o"][i], b["do"], b["lse"][i], dqkv, b["delta"], B, T, H, KV, hd, self.windows[i])
             else:
                 E.attn_bwd(qkv[:, :Dq], qkv[:, Dq:Dq + Dkv], qkv[:, Dq + Dkv:], b["o"][i], b["do"], b["lse"][i],
                            dqkv[:, :Dq], dqkv[:, Dq:Dq + Dkv], dqkv[:, Dq + Dkv:], b["delta"], b["delta"], B, T, H, KV,
                            hd, self.windows[i])
-            ve = i in b["gate"]
+            # RoPE + QK-norm (+ VE) backward as its own pass: folding it into the attention epilogues put
+            # its global loads on every CTA's tail and measured slower
+            ve_b = (P[f"ve_{i}"], b["gate"][i], G[f"ve_{i}"], b["dz"]) if ve else (None, None, None, None)
+            E.rope_bwd(dqkv, qkv, T, H, KV, hd, self.cos, self.sin, b["rq"][i], b["rk"][i], idx, *ve_b)
             if ve:
-                E.rope_bwd(dqkv, qkv, T, H, KV, hd, self.cos, self.sin, b["rq"][i], b["rk"][i], idx, P[f"ve_{i}"],
-                           b["gate"][i], G[f"ve_{i}"], b["dz"])
                 E.ve_gate_bwd(b["cur"][i], b["dz"], P[f"layer{i}_ve_gate"], G[f"layer{i}_ve_gate"], b["dgate_in"])
-            else:
-                E.rope_bwd(dqkv, qkv, T, H, KV, hd, self.cos, self.sin, b["rq"][i], b["rk"][i], idx, None, None, None,
-                           None)
             xn = b["xn"][i]
             gemm.matmul(xn.t(), dqkv[:, :Dq], out=G[f"layer{i}_q"], epi=A, k_splits=0)
             gemm.matmul(xn.t(), dqkv[:, Dq:Dq + Dkv], out=G[f"layer{i}_k"], epi=A, k_splits=0)
             gemm.matmul(xn.t(), dqkv[:, Dq + Dkv:], out=G[f"layer{i}_v"], epi=A, k_splits=0)
             gemm.matmul(dqkv, self.wqkv[i].t(), out=b["dxn"])
             x_in = b["xs"][i - 1] if i > 0 else b["x0"]
+            # also writes the bf16 copy of dx that layer i-1's backward GEMMs read
             E.ladder_bwd(x_in, b["x0"], P["residLambdas"], P["x0Lambdas"], i, b["rstd1"][i], b["dxn"], b["dmid"],
-                         b["dgate_in"] if ve else None, b["dx"], b["dx0"], G["residLambdas"], G["x0Lambdas"], i == 0)
+                         b["dgate_in"] if ve else None, b["dx"], b["dx0"], G["residLambdas"], G["x0Lambdas"], i == 0,
+                         b["dx_b"] if i > 0 else None)
             self._ready(self.L - i)
-            if i > 0:
-                E.cast_bf16(b["dx"], b["dx_b"])
         E.embed_bwd(idx, P["wte"], b["rstd0"], b["dx0"], G["wte"])
         self._ready(self.L + 1)
 

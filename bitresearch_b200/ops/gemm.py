@@ -67,3 +67,14 @@ def matmul(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, ep
     ext().gemm(a, a_mn, lda, bsa, b, b_mn, ldb, bsb, out, out.stride(-2), bsc, M, N, K, batch, epi, aux, ld_aux,
                bs_aux, alpha, beta, k_splits, block_n)
     return out
+
+
+def qkv_rope(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+             rq: torch.Tensor, rk: torch.Tensor, T: int, H: int, KV: int, idx: torch.Tensor | None = None,
+             ve: torch.Tensor | None = None, cur: torch.Tensor | None = None, wg: torch.Tensor | None = None,
+             gate: torch.Tensor | None = None) -> torch.Tensor:
+    """``out = x @ w`` for the fused QKV projection with RoPE + QK-norm on the q/k heads (rstd into
+    ``rq``/``rk``) and, when ``ve`` is given, the value-embedding add on the v heads (gate into
+    ``gate``), all in the GEMM epilogue. Needs head_dim 128 and even H and KV."""
+    ext().gemm_qkv_rope(x, w, out, cos, sin, rq, rk, T, H, KV, idx, ve, cur, wg, gate)
+    return out

@@ -394,6 +394,8 @@ struct BwdParams {
   int64_t ldo;
   const __nv_bfloat16* dout;
   int64_t lddo;
+  const __nv_bfloat16* qkv;  // the fused projection buffer (the dQ kernel reads its Q rows)
+  int64_t ldqkv;
   __nv_bfloat16* dq;
   int64_t lddq;
   __nv_bfloat16* dk;
@@ -403,26 +405,25 @@ struct BwdParams {
   int* status;
 };
 
-// ---- dQ: one CTA per (128 queries, head, batch), 64-key blocks in a 4-stage K/V ring.
+// ---- dQ: one CTA per (128 queries, head, batch), 64-key blocks in a 6-stage K/V ring.
 // TMEM: two S/dP sets (set s: S at [128s, +64), dP at [128s+64, +64)) so block j+1's scores are
-// computed while the softmax warps turn block j into dS; dQ accumulates at [256, 384).
+// computed while the softmax warps turn block j into dS; dQ accumulates at [256, 384); the CTA's Q and
+// dO rows sit at [384, 448) and [448, 512) as bf16 pairs, so the S and dP MMAs read only K and V from
+// shared memory.
 constexpr int BK64 = 64;
 constexpr int KV64 = 64 * 128 * 2;        // 64 keys x 128 hd: two 8 KB swizzle atoms
 constexpr int KV64_ATOM = 64 * 128;
-constexpr int DQ_STAGES = 5;
-constexpr int DQ_Q = 0;
-constexpr int DQ_DO = DQ_Q + TILE_BYTES;
-constexpr int DQ_K = DQ_DO + TILE_BYTES;            // [5] x 16 KB
-constexpr int DQ_V = DQ_K + DQ_STAGES * KV64;       // [5] x 16 KB
+constexpr int DQ_STAGES = 6;
+constexpr int DQ_K = 0;                             // [6] x 16 KB
+constexpr int DQ_V = DQ_K + DQ_STAGES * KV64;       // [6] x 16 KB
 constexpr int DQ_DSUM = DQ_V + DQ_STAGES * KV64;    // [2][128] floats: half-row sums of dO * O
 constexpr int DQ_BAR = DQ_DSUM + 1024;
 constexpr int DQ_SMEM = DQ_BAR + 256 + 1024;
 static_assert(DQ_SMEM <= 232448, "dQ kernel shared memory");
 
 __global__ void __launch_bounds__(320, 1)
-    attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
-                      const __grid_constant__ CUtensorMap tm_kv, BwdParams p) {
-  // tm_q / tm_do: 128-row boxes; tm_kv: 64-row boxes
+    attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, BwdParams p) {
+  // tm_kv: 64-row boxes of the fused QKV buffer
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DQ_BAR);
@@ -447,7 +448,7 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = warp_id();
   if (device_failed(p.status)) return;
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    mbar_init(q_full, 256);  // every softmax thread has stored its Q or dO row in TMEM
     for (int i = 0; i < DQ_STAGES; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
@@ -472,11 +473,6 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 0) {
     if (elect_one()) {
-      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
-      tma_load_3d(&tm_q, q_full, smem + DQ_Q, h * HD, q0, b);
-      tma_load_3d(&tm_q, q_full, smem + DQ_Q + ATOM_BYTES, h * HD + 64, q0, b);
-      tma_load_3d(&tm_do, q_full, smem + DQ_DO, h * HD, q0, b);
-      tma_load_3d(&tm_do, q_full, smem + DQ_DO + ATOM_BYTES, h * HD + 64, q0, b);
       for (int j = 0; j < nkv; ++j) {
         const int st = j % DQ_STAGES;
         if (!mbar_wait(&kv_empty[st], ((j / DQ_STAGES) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
@@ -497,7 +493,6 @@ __global__ void __launch_bounds__(320, 1)
     if (elect_one()) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, 64, false, false);
       constexpr uint32_t idesc_q = umma_idesc_bf16(128, 128, false, true);
-      const uint32_t q_addr = smem_u32(smem + DQ_Q), do_addr = smem_u32(smem + DQ_DO);
       bool ok = mbar_wait(q_full, 0, kBudgetNs, abort_flag, p.status);
       auto issue_sdp = [&](int j) -> bool {
         const int st = j % DQ_STAGES, set = j & 1;
@@ -506,12 +501,11 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t k_addr = smem_u32(smem + DQ_K + st * KV64), v_addr = smem_u32(smem + DQ_V + st * KV64);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t offa = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
           const uint32_t offb = (kk >> 2) * KV64_ATOM + (kk & 3) * 32;
-          umma_bf16_ss(tmem + set * 128, umma_desc_sw128(q_addr + offa, 16, 1024),
-                       umma_desc_sw128(k_addr + offb, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-          umma_bf16_ss(tmem + set * 128 + 64, umma_desc_sw128(do_addr + offa, 16, 1024),
-                       umma_desc_sw128(v_addr + offb, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          umma_bf16_ts(tmem + set * 128, tmem + 384 + kk * 8, umma_desc_sw128(k_addr + offb, 16, 1024), idesc_s,
+                       kk > 0 ? 1u : 0u);
+          umma_bf16_ts(tmem + set * 128 + 64, tmem + 448 + kk * 8, umma_desc_sw128(v_addr + offb, 16, 1024), idesc_s,
+                       kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[set]);
         return true;
@@ -549,6 +543,31 @@ __global__ void __launch_bounds__(320, 1)
     const int qi = q0 + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
     const int qc = min(qi, p.T - 1);
+    {
+      // this row's Q (first warp of the row) or dO (second warp) into TMEM as bf16 pairs: the A operands
+      // of the S and dP MMAs
+      const int64_t m = (int64_t)b * p.T + qc;
+      const uint4* src = reinterpret_cast<const uint4*>(half == 0 ? p.qkv + m * p.ldqkv + h * HD
+                                                                  : p.dout + m * p.lddo + h * HD);
+      uint32_t w0[32], w1[32];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 a = __ldg(src + i), c = __ldg(src + 8 + i);
+        w0[4 * i] = a.x;
+        w0[4 * i + 1] = a.y;
+        w0[4 * i + 2] = a.z;
+        w0[4 * i + 3] = a.w;
+        w1[4 * i] = c.x;
+        w1[4 * i + 1] = c.y;
+        w1[4 * i + 2] = c.z;
+        w1[4 * i + 3] = c.w;
+      }
+      tmem_st32(lane_base + 384 + 64 * half, w0);
+      tmem_st32(lane_base + 384 + 64 * half + 32, w1);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(q_full);
+    }
     const float lse2 = p.lse[((int64_t)b * p.H + h) * p.T + qc];  // log2 units
     // delta = rowsum(dO * O) over this head: the two warps of a row each reduce 64 of the 128 dims
     // (while the first tiles load) and meet in shared memory; the kernel writes delta for dK/dV
@@ -659,7 +678,7 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
-// ---- dK, dV: one CTA per (128 keys, kv head, batch), 64-query blocks in a 2-stage Q/dO ring.
+// ---- dK, dV: one CTA per (128 keys, kv head, batch), 64-query blocks in a 4-stage Q/dO ring.
 // TMEM: two S^T/dP^T sets (set s: S^T at [128s, +64), dP^T at [128s+64, +64)), dV [256,384), dK [384,512).
 constexpr int KB_Q = 64;
 constexpr int HALF_TILE = 64 * 128 * 2;   // 64 rows x 128 hd, two 8 KB swizzle atoms
@@ -951,9 +970,10 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse,
 
 namespace br {
 // dqkv: [B*T, Dq + 2*Dkv] bf16 output (dq | dk | dv); dout: [B*T, H*hd] bf16; lse, delta: fp32 [B, H, T].
-void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::Tensor& dout, const torch::Tensor& lse,
-                 torch::Tensor& dqkv, torch::Tensor& delta, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd,
-                 int64_t window, int64_t which) {
+namespace {
+void attn_bwd_tc_impl(const torch::Tensor& qkv, const torch::Tensor& o, const torch::Tensor& dout,
+                      const torch::Tensor& lse, torch::Tensor& dqkv, torch::Tensor& delta, int64_t B, int64_t T,
+                      int64_t H, int64_t KV, int64_t hd, int64_t window, int64_t which) {
   // which: 0 = dQ (which also writes delta) and dK/dV; 1 = dQ only; 2 = dK/dV only (delta already written)
   TORCH_CHECK(hd == HD && T % 128 == 0, "attn_bwd_tc: head_dim 128 and T % 128 == 0");
   const int64_t W = qkv.size(1);
@@ -962,8 +982,6 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::
   c10::cuda::CUDAGuard g(qkv.device());
   CUtensorMap tq = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.data_ptr(), W, T, B, qkv.stride(0),
                               qkv.stride(0) * T, 64, 128);
-  CUtensorMap td = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dout.data_ptr(), H * hd, T, B, dout.stride(0),
-                              dout.stride(0) * T, 64, 128);
   // the dK/dV kernel loads 64-query tiles of Q and dO
   CUtensorMap tq64 = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.data_ptr(), W, T, B, qkv.stride(0),
                                 qkv.stride(0) * T, 64, 64);
@@ -985,6 +1003,8 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::
   p.ldo = o.stride(0);
   p.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
   p.lddo = dout.stride(0);
+  p.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  p.ldqkv = qkv.stride(0);
   auto* base = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   p.dq = base;
   p.lddq = dqkv.stride(0);
@@ -1001,7 +1021,7 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::
   }
   auto st = at::cuda::getCurrentCUDAStream();
   if (which != 2) {
-    attn_dq_tc_kernel<<<dim3((unsigned)(T / BQ), (unsigned)H, (unsigned)B), 320, DQ_SMEM, st>>>(tq, td, tq64, p);
+    attn_dq_tc_kernel<<<dim3((unsigned)(T / BQ), (unsigned)H, (unsigned)B), 320, DQ_SMEM, st>>>(tq64, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   if (which != 1) {
@@ -1009,4 +1029,12 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
+}  // namespace
+
+void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::Tensor& dout, const torch::Tensor& lse,
+                 torch::Tensor& dqkv, torch::Tensor& delta, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd,
+                 int64_t window, int64_t which) {
+  attn_bwd_tc_impl(qkv, o, dout, lse, dqkv, delta, B, T, H, KV, hd, window, which);
+}
+
 }  // namespace br

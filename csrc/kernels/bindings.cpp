@@ -4,6 +4,11 @@
 namespace br {
 int64_t read_status(int64_t device);
 void reset_status(int64_t device);
+void gemm_qkv_rope(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, const torch::Tensor& cosT,
+                   const torch::Tensor& sinT, torch::Tensor& rq, torch::Tensor& rk, int64_t T, int64_t H, int64_t KV,
+                   c10::optional<torch::Tensor> idx, c10::optional<torch::Tensor> ve,
+                   c10::optional<torch::Tensor> cur, c10::optional<torch::Tensor> wg,
+                   c10::optional<torch::Tensor> gate);
 void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, const torch::Tensor& b, bool b_mn,
                  int64_t ldb, int64_t bsb, torch::Tensor& c, int64_t ldc, int64_t bsc, int64_t M, int64_t N,
                  int64_t K, int64_t batch, int64_t epi, c10::optional<torch::Tensor> aux, int64_t ld_aux,
@@ -18,7 +23,8 @@ void rms_bwd(const torch::Tensor& x, const torch::Tensor& rstd, const torch::Ten
 void ladder_bwd(const torch::Tensor& x, const torch::Tensor& x0, const torch::Tensor& lam_r,
                 const torch::Tensor& lam_0, int64_t layer, const torch::Tensor& rstd, const torch::Tensor& dxn,
                 const torch::Tensor& dres, c10::optional<torch::Tensor> dgate_in, torch::Tensor& dx,
-                torch::Tensor& dx0_acc, torch::Tensor& dlam_r, torch::Tensor& dlam_0, bool first_layer);
+                torch::Tensor& dx0_acc, torch::Tensor& dlam_r, torch::Tensor& dlam_0, bool first_layer,
+                c10::optional<torch::Tensor> dx_b);
 void embed_bwd(const torch::Tensor& idx, const torch::Tensor& wte, const torch::Tensor& rstd, const torch::Tensor& dx0,
                torch::Tensor& dwte);
 void cast_bf16(const torch::Tensor& x, torch::Tensor& y);
@@ -54,6 +60,8 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse,
 void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::Tensor& dout, const torch::Tensor& lse,
                  torch::Tensor& dqkv, torch::Tensor& delta, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd,
                  int64_t window, int64_t which);
+torch::Tensor mc_sharpe(int64_t n_paths, int64_t steps, double mu, double sigma, double annual, int64_t seed,
+                        int64_t device);
 std::tuple<int64_t, torch::Tensor> sym_alloc(int64_t bytes);
 int64_t sym_open(const torch::Tensor& handle);
 void sym_close(int64_t ptr);
@@ -82,11 +90,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_status", &br::read_status);
   m.def("reset_status", &br::reset_status);
   m.def("gemm", &br::gemm_launch);
+  m.def("gemm_qkv_rope", &br::gemm_qkv_rope);
   m.def("embed_rms_fwd", &br::embed_rms_fwd);
   m.def("ladder_rms_fwd", &br::ladder_rms_fwd);
   m.def("rms_fwd", &br::rms_fwd);
   m.def("rms_bwd", &br::rms_bwd);
-  m.def("ladder_bwd", &br::ladder_bwd);
+  m.def("ladder_bwd", &br::ladder_bwd, pybind11::arg("x"), pybind11::arg("x0"), pybind11::arg("lam_r"),
+        pybind11::arg("lam_0"), pybind11::arg("layer"), pybind11::arg("rstd"), pybind11::arg("dxn"),
+        pybind11::arg("dres"), pybind11::arg("dgate_in"), pybind11::arg("dx"), pybind11::arg("dx0_acc"),
+        pybind11::arg("dlam_r"), pybind11::arg("dlam_0"), pybind11::arg("first_layer"),
+        pybind11::arg("dx_b") = pybind11::none());
   m.def("embed_bwd", &br::embed_bwd);
   m.def("cast_bf16", &br::cast_bf16);
   m.def("rope_fwd", &br::rope_fwd);
@@ -103,6 +116,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("lse"), pybind11::arg("dqkv"), pybind11::arg("delta"), pybind11::arg("B"), pybind11::arg("T"),
         pybind11::arg("H"), pybind11::arg("KV"), pybind11::arg("hd"), pybind11::arg("window"),
         pybind11::arg("which") = 0);
+  m.def("mc_sharpe", &br::mc_sharpe);
   m.def("sym_alloc", &br::sym_alloc);
   m.def("sym_open", &br::sym_open);
   m.def("sym_close", &br::sym_close);

@@ -40,6 +40,26 @@ enum GemmEpi : int {
   EPI_RELU2_BWD = 3,   // C(bf16) = alpha*acc * 2*sqrt(aux(bf16))   (d/du of relu(u)^2 given h = relu(u)^2)
   EPI_ATOMIC_F32 = 4,  // C(f32) += alpha*acc                       (TMA reduce-add)
   EPI_SOFTCAP = 5,     // C(bf16) = beta*tanh(alpha*acc)             (alpha = 1/cap, beta = cap)
+  EPI_QKV_ROPE = 6,    // fused QKV projection output (see QkvRope), BN = 256
+};
+
+// The QKV projection's epilogue: the output columns are [q heads | k heads | v heads] of 128 columns
+// each, and a 256-column tile holds exactly two heads (H and KV even). Per row of a q/k head: half-split
+// RoPE (y1 = x1 c + x2 s, y2 = -x1 s + x2 c with c, s = cos/sin tables [T, 64] at the row's position)
+// then RMSNorm over the 128 head dims (QK-norm after RoPE, gpt.ts:159-177, :239-244), saving the rstd.
+// Per row of a v head on value-embedding layers: v += ve[idx] * 2 sigmoid(cur[:, :32] . Wg[:, h])
+// (gpt.ts:225-236), saving the gate.
+struct QkvRope {
+  const float* cosT;
+  const float* sinT;
+  float* rq;             // [M, H]
+  float* rk;             // [M, KV]
+  const int* idx;        // token ids [M]             (value-embedding layers only, else null)
+  const float* ve;       // [V, KV*128] fp32 table
+  const float* cur;      // [M, ld_cur] ladder output (the gate reads its first 32 columns)
+  const float* wg;       // [32, KV]
+  float* gate;           // [M, KV]
+  int T, H, KV, ld_cur;
 };
 
 struct GemmParams {
@@ -49,6 +69,7 @@ struct GemmParams {
   int has_aux;
   float alpha, beta;
   int* status;
+  QkvRope rope;
 };
 
 constexpr int BM = 128;
@@ -341,6 +362,100 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int row0 = m * BM + wq * 32;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * BN;
+      if constexpr (EPI == EPI_QKV_ROPE) {
+        // two heads per tile; thread = row. Each head: 128 accumulator columns -> RoPE + QK-norm
+        // (q, k heads) or the value-embedding add (v heads) -> two 64-column bf16 chunks.
+        const QkvRope& rp = p.rope;
+        const int mrow = row0 + lane;
+        const bool valid = mrow < p.M;
+        const int64_t msafe = valid ? mrow : 0;
+        const int nqk = rp.H + rp.KV;
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          const int head = n * 2 + hh;
+          uint32_t v[4][32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tmem_ld32(taddr + hh * 128 + c * 32, v[c]);
+          tmem_ld_wait();
+          if (hh == 1) {  // accumulator fully read: hand it back to the MMA warp
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[acc]);
+          }
+          float x[128];
+#pragma unroll
+          for (int i = 0; i < 128; ++i) x[i] = __uint_as_float(v[i >> 5][i & 31]);
+          if (head < nqk) {
+            const float4* cr = reinterpret_cast<const float4*>(rp.cosT + (int64_t)(mrow % rp.T) * 64);
+            const float4* sr = reinterpret_cast<const float4*>(rp.sinT + (int64_t)(mrow % rp.T) * 64);
+            float ss = 0.f;
+#pragma unroll
+            for (int j4 = 0; j4 < 16; ++j4) {
+              const float4 c4 = __ldg(cr + j4), s4 = __ldg(sr + j4);
+              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int j = 4 * j4 + k;
+                const float x1 = x[j], x2 = x[64 + j];
+                const float y1 = x1 * cc[k] + x2 * sn[k], y2 = x2 * cc[k] - x1 * sn[k];
+                x[j] = y1;
+                x[64 + j] = y2;
+                ss = fmaf(y1, y1, fmaf(y2, y2, ss));
+              }
+            }
+            const float r = rsqrtf(ss * (1.f / 128.f) + 1e-5f);
+#pragma unroll
+            for (int i = 0; i < 128; ++i) x[i] *= r;
+            if (valid) {
+              if (head < rp.H) rp.rq[(int64_t)mrow * rp.H + head] = r;
+              else rp.rk[(int64_t)mrow * rp.KV + (head - rp.H)] = r;
+            }
+          } else if (rp.ve != nullptr) {
+            const int kvh = head - nqk;
+            const float4* cz = reinterpret_cast<const float4*>(rp.cur + msafe * rp.ld_cur);
+            float z = 0.f;
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const float4 cv = __ldg(cz + c4);
+              z = fmaf(cv.x, __ldg(rp.wg + (4 * c4 + 0) * rp.KV + kvh), z);
+              z = fmaf(cv.y, __ldg(rp.wg + (4 * c4 + 1) * rp.KV + kvh), z);
+              z = fmaf(cv.z, __ldg(rp.wg + (4 * c4 + 2) * rp.KV + kvh), z);
+              z = fmaf(cv.w, __ldg(rp.wg + (4 * c4 + 3) * rp.KV + kvh), z);
+            }
+            const float g = 2.f / (1.f + __expf(-z));
+            const float4* e =
+                reinterpret_cast<const float4*>(rp.ve + (int64_t)__ldg(rp.idx + msafe) * (rp.KV * 128) + kvh * 128);
+#pragma unroll
+            for (int d4 = 0; d4 < 32; ++d4) {
+              const float4 ev = __ldg(e + d4);
+              x[4 * d4 + 0] = fmaf(ev.x, g, x[4 * d4 + 0]);
+              x[4 * d4 + 1] = fmaf(ev.y, g, x[4 * d4 + 1]);
+              x[4 * d4 + 2] = fmaf(ev.z, g, x[4 * d4 + 2]);
+              x[4 * d4 + 3] = fmaf(ev.w, g, x[4 * d4 + 3]);
+            }
+            if (valid) rp.gate[(int64_t)mrow * rp.KV + kvh] = g;
+          }
+#pragma unroll
+          for (int hc = 0; hc < 2; ++hc, ++nchunk) {
+            uint8_t* buf = ebuf + (nchunk & 1) * CHUNK_BYTES;
+            if (leader) bulk_wait_read1();  // the store that last used this buffer has read it
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float* xs = x + 64 * hc + 8 * q;
+              *reinterpret_cast<uint4*>(buf + swz_off(lane, q)) =
+                  make_uint4(pack_bf16(xs[0], xs[1]), pack_bf16(xs[2], xs[3]), pack_bf16(xs[4], xs[5]),
+                             pack_bf16(xs[6], xs[7]));
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (leader) {
+              tma_store_3d(&tmC, buf, n * BN + hh * 128 + hc * 64, row0, b);
+              bulk_commit();
+            }
+          }
+        }
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < CPT; ++c, ++nchunk) {
         const int slot = nchunk % NBUF;
@@ -567,6 +682,69 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
     dispatch_major<256>(a_mn, b_mn, (int)epi, mp, p, grid, st);
   else
     dispatch_major<128>(a_mn, b_mn, (int)epi, mp, p, grid, st);
+}
+
+// out[M, (H+2KV)*128] = x[M, K] @ w[K, N] with the QKV epilogue (RoPE + QK-norm on q/k heads, the
+// value-embedding add on v heads when `ve` is given). x, w, out: bf16 with contiguous rows.
+void gemm_qkv_rope(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, const torch::Tensor& cosT,
+                   const torch::Tensor& sinT, torch::Tensor& rq, torch::Tensor& rk, int64_t T, int64_t H, int64_t KV,
+                   c10::optional<torch::Tensor> idx, c10::optional<torch::Tensor> ve,
+                   c10::optional<torch::Tensor> cur, c10::optional<torch::Tensor> wg,
+                   c10::optional<torch::Tensor> gate) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16, "gemm_qkv_rope: bf16 tensors");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "gemm_qkv_rope: contiguous rows");
+  TORCH_CHECK(H % 2 == 0 && KV % 2 == 0, "gemm_qkv_rope: even head counts (two heads per 256-column tile)");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(1);
+  TORCH_CHECK(w.size(0) == K && N == (H + 2 * KV) * 128 && out.size(0) == M && out.size(1) == N,
+              "gemm_qkv_rope: shapes");
+  TORCH_CHECK(cosT.scalar_type() == at::kFloat && cosT.is_contiguous() && cosT.size(-1) == 64 &&
+                  sinT.is_contiguous() && cosT.numel() >= T * 64, "gemm_qkv_rope: cos/sin tables [T, 64] fp32");
+  TORCH_CHECK(rq.numel() >= M * H && rk.numel() >= M * KV, "gemm_qkv_rope: rstd buffers");
+  c10::cuda::CUDAGuard guard(x.device());
+  Maps mp;
+  mp.a = bf16_map(x.data_ptr(), K, M, 1, x.stride(0), 0, BM);
+  mp.b = bf16_map(w.data_ptr(), N, K, 1, w.stride(0), 0, 64);
+  mp.c = out_map(out, M, N, 1, out.stride(0), 0);
+  mp.x = mp.c;
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.batch = 1;
+  p.m_tiles = (int)((M + BM - 1) / BM);
+  p.n_tiles = (int)(N / 256);
+  p.k_blocks = (int)((K + BK - 1) / BK);
+  p.k_splits = 1;
+  p.kb_per_split = p.k_blocks;
+  p.has_aux = 0;
+  p.alpha = 1.f;
+  p.beta = 0.f;
+  p.status = status_ptr(x.device().index());
+  QkvRope& r = p.rope;
+  r.cosT = cosT.data_ptr<float>();
+  r.sinT = sinT.data_ptr<float>();
+  r.rq = rq.data_ptr<float>();
+  r.rk = rk.data_ptr<float>();
+  r.T = (int)T;
+  r.H = (int)H;
+  r.KV = (int)KV;
+  const bool has_ve = ve.has_value() && ve->defined();
+  if (has_ve) {
+    TORCH_CHECK(idx.has_value() && cur.has_value() && wg.has_value() && gate.has_value(), "gemm_qkv_rope: VE args");
+    TORCH_CHECK(idx->scalar_type() == at::kInt && ve->scalar_type() == at::kFloat && cur->scalar_type() == at::kFloat &&
+                    wg->scalar_type() == at::kFloat && wg->size(0) == 32 && wg->size(1) == KV,
+                "gemm_qkv_rope: VE dtypes/shapes");
+    TORCH_CHECK(cur->stride(-1) == 1 && cur->stride(0) % 4 == 0 && ve->size(-1) == KV * 128, "gemm_qkv_rope: VE layout");
+    r.idx = idx->data_ptr<int>();
+    r.ve = ve->data_ptr<float>();
+    r.cur = cur->data_ptr<float>();
+    r.ld_cur = (int)cur->stride(0);
+    r.wg = wg->data_ptr<float>();
+    r.gate = gate->data_ptr<float>();
+  }
+  const int total = p.m_tiles * p.n_tiles;
+  launch_t<256, false, true, EPI_QKV_ROPE, false>(mp, p, std::min(total, num_sms()), at::cuda::getCurrentCUDAStream());
 }
 
 }  // namespace br

@@ -139,7 +139,8 @@ __global__ void ladder_bwd_kernel(const float* __restrict__ x, const float* __re
                                   const float* __restrict__ rstd, const TD* __restrict__ dxn,
                                   const float* __restrict__ dres, const float* __restrict__ dgate_in,
                                   float* __restrict__ dx, float* __restrict__ dx0_acc, float* __restrict__ dlam_r,
-                                  float* __restrict__ dlam_0, int M, int D, int first_layer) {
+                                  float* __restrict__ dlam_0, int M, int D, int first_layer,
+                                  __nv_bfloat16* __restrict__ dx_b) {
   __shared__ float red[2][kWarps];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const float a = lam_r[layer], b = lam_0[layer];
@@ -184,6 +185,8 @@ __global__ void ladder_bwd_kernel(const float* __restrict__ x, const float* __re
         add0.w += dxa.w;
       } else {
         st4(dx + off + c, dxa);
+        if (dx_b)  // the bf16 copy the previous layer's GEMMs read
+          *reinterpret_cast<uint2*>(dx_b + off + c) = make_uint2(pack_bf16(dxa.x, dxa.y), pack_bf16(dxa.z, dxa.w));
       }
       st4(dx0_acc + off + c, make_float4(acc.x + add0.x, acc.y + add0.y, acc.z + add0.z, acc.w + add0.w));
     }
@@ -301,8 +304,11 @@ void rms_bwd(const torch::Tensor& x, const torch::Tensor& rstd, const torch::Ten
 void ladder_bwd(const torch::Tensor& x, const torch::Tensor& x0, const torch::Tensor& lam_r,
                 const torch::Tensor& lam_0, int64_t layer, const torch::Tensor& rstd, const torch::Tensor& dxn,
                 const torch::Tensor& dres, c10::optional<torch::Tensor> dgate_in, torch::Tensor& dx,
-                torch::Tensor& dx0_acc, torch::Tensor& dlam_r, torch::Tensor& dlam_0, bool first_layer) {
+                torch::Tensor& dx0_acc, torch::Tensor& dlam_r, torch::Tensor& dlam_0, bool first_layer,
+                c10::optional<torch::Tensor> dx_b) {
   const int64_t D = x.size(-1), M = x.numel() / D;
+  __nv_bfloat16* dxb = dx_b.has_value() && dx_b->defined() ? reinterpret_cast<__nv_bfloat16*>(dx_b->data_ptr()) : nullptr;
+  TORCH_CHECK(!dxb || (dx_b->scalar_type() == at::kBFloat16 && dx_b->is_contiguous()), "ladder_bwd: dx_b bf16");
   c10::cuda::CUDAGuard g(x.device());
   auto st = at::cuda::getCurrentCUDAStream();
   const float* dgi = dgate_in.has_value() ? dgate_in->data_ptr<float>() : nullptr;
@@ -311,13 +317,14 @@ void ladder_bwd(const torch::Tensor& x, const torch::Tensor& x0, const torch::Te
     ladder_bwd_kernel<float><<<grid, 32 * kWarps, 0, st>>>(
         x.data_ptr<float>(), x0.data_ptr<float>(), lam_r.data_ptr<float>(), lam_0.data_ptr<float>(), (int)layer,
         rstd.data_ptr<float>(), dxn.data_ptr<float>(), dres.data_ptr<float>(), dgi, dx.data_ptr<float>(),
-        dx0_acc.data_ptr<float>(), dlam_r.data_ptr<float>(), dlam_0.data_ptr<float>(), (int)M, (int)D, first_layer);
+        dx0_acc.data_ptr<float>(), dlam_r.data_ptr<float>(), dlam_0.data_ptr<float>(), (int)M, (int)D, first_layer,
+        dxb);
   else
     ladder_bwd_kernel<__nv_bfloat16><<<grid, 32 * kWarps, 0, st>>>(
         x.data_ptr<float>(), x0.data_ptr<float>(), lam_r.data_ptr<float>(), lam_0.data_ptr<float>(), (int)layer,
         rstd.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(dxn.data_ptr()), dres.data_ptr<float>(), dgi,
         dx.data_ptr<float>(), dx0_acc.data_ptr<float>(), dlam_r.data_ptr<float>(), dlam_0.data_ptr<float>(), (int)M,
-        (int)D, first_layer);
+        (int)D, first_layer, dxb);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

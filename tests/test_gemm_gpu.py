@@ -81,3 +81,40 @@ def test_gemm_batched(cuda):
     _close(Bm, 0.5 * (A.float() @ A.float()) - A.float(), c)
     torch.cuda.synchronize()
     assert check_status() == 0
+
+
+@pytest.mark.parametrize("with_ve", [False, True])
+def test_qkv_rope_epilogue_matches_gemm_then_rope(cuda, with_ve):
+    """The fused QKV GEMM epilogue (RoPE + QK-norm on q/k heads, VE add on v heads) against the plain
+    GEMM followed by the separate RoPE kernel; M = 3 x 100 leaves a partial last row tile."""
+    from bitresearch_b200.ops import gemm
+    from bitresearch_b200.ops._ext import check_status, ext
+    E = ext()
+    torch.manual_seed(11)
+    T, B, H, KV, D, V = 100, 3, 4, 2, 256, 64
+    M, N = B * T, (H + 2 * KV) * 128
+    x = torch.randn(M, D, device=cuda).to(torch.bfloat16)
+    w = (torch.randn(D, N, device=cuda) * D ** -0.5).to(torch.bfloat16)
+    pos = torch.arange(T, device=cuda, dtype=torch.float32)[:, None]
+    inv = 10000.0 ** (-torch.arange(0, 128, 2, device=cuda, dtype=torch.float32) / 128)
+    cos, sin = torch.cos(pos * inv).contiguous(), torch.sin(pos * inv).contiguous()
+    idx = torch.randint(0, V, (M,), device=cuda, dtype=torch.int32)
+    ve = torch.randn(V, KV * 128, device=cuda) if with_ve else None
+    cur = torch.randn(M, D, device=cuda) if with_ve else None
+    wg = torch.randn(32, KV, device=cuda) * 0.3 if with_ve else None
+    ref = gemm.matmul(x, w)
+    rq0, rk0 = torch.empty(M, H, device=cuda), torch.empty(M, KV, device=cuda)
+    gate0 = torch.empty(M, KV, device=cuda) if with_ve else None
+    E.rope_fwd(ref, T, H, KV, 128, cos, sin, rq0, rk0, idx, ve, cur, wg, gate0)
+    out = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    rq, rk = torch.empty(M, H, device=cuda), torch.empty(M, KV, device=cuda)
+    gate = torch.empty(M, KV, device=cuda) if with_ve else None
+    gemm.qkv_rope(x, w, out, cos, sin, rq, rk, T, H, KV, idx, ve, cur, wg, gate)
+    torch.cuda.synchronize()
+    assert check_status() == 0
+    # both round the GEMM result to bf16 at different points (before RoPE in the reference path)
+    torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(rq, rq0, rtol=1e-2, atol=1e-3)
+    torch.testing.assert_close(rk, rk0, rtol=1e-2, atol=1e-3)
+    if with_ve:
+        torch.testing.assert_close(gate, gate0, rtol=1e-5, atol=1e-5)

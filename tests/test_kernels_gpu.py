@@ -1,6 +1,8 @@
 """Row kernels, RoPE/QK-norm/VE, fused cross-entropy, attention and optimizer kernels vs fp32 PyTorch."""
 import math
 
+import numpy as np
+
 import pytest
 import torch
 import torch.nn.functional as F
@@ -270,3 +272,16 @@ def test_adamw_and_muon_kernels_match_torch_optimizer(cuda):
             assert err_fused <= 1e-4 * moved + 1e-6, (n, err_fused, moved)
     for n, s in shadows.items():
         _assert(s, models[2].named()[n], 1e-2)
+
+
+def test_monte_carlo_sharpe_kernel_distribution(cuda):
+    """The GPU Monte-Carlo Sharpe kernel against the numpy restatement: different random streams, so
+    the distribution statistics are compared (200k paths: standard errors about 0.002)."""
+    from bitresearch_b200.swarm.strategy import mc_sharpes, mc_sharpes_numpy
+    for mu, sigma in ((0.0, 0.2), (0.15, 0.1)):
+        g = mc_sharpes(mu, sigma, 200_000, seed=7, device=cuda)
+        c = mc_sharpes_numpy(mu, sigma, 200_000, seed=7)
+        assert abs(g.mean() - c.mean()) < 0.02, (mu, sigma, g.mean(), c.mean())
+        assert abs(g.std() - c.std()) < 0.02
+        assert abs(np.percentile(g, 5) - np.percentile(c, 5)) < 0.03
+        assert abs(np.percentile(g, 95) - np.percentile(c, 95)) < 0.03
