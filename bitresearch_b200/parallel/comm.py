@@ -306,6 +306,15 @@ class P2PGradSync:
             self.tr.log(f"p2p collective timed out (status {status}); step {step_idx} skipped")
         return ok
 
+    def grad_norm(self) -> float:
+        """L2 norm of the step's mean gradient: each rank sums the squares of the reduced gradients it
+        owns, one scalar all-reduce adds them up (a collective: every rank calls it on the same steps)."""
+        sq = torch.zeros((), device=self.red.device)
+        for n in self.owned_names:
+            sq = sq + self.red_views[n].float().square().sum()
+        dist.all_reduce(sq)
+        return float(sq.sqrt())
+
     def close(self):
         torch.cuda.synchronize()
         dist.barrier()

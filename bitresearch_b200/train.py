@@ -245,8 +245,11 @@ class Trainer:
 
     def _sync_and_update(self, progress: float, scale: float) -> bool:
         cfg = self.cfg
+        log_step = bool(cfg.log_every) and self.metrics.step % cfg.log_every == 0
         if self.comm is not None and hasattr(self.comm, "step"):  # in-kernel p2p path
             ok = self.comm.step(self.metrics.step, scale, self._set_schedules(progress))
+            if log_step:
+                self.metrics.grad_norm = self.comm.grad_norm()
             return ok
         g = self.flat_grad
         finite = torch.isfinite(g).all()
@@ -286,6 +289,8 @@ class Trainer:
         if self.is_cuda:
             torch.cuda.synchronize(self.device) if cfg.log_every and self.metrics.step % cfg.log_every == 0 else None
         self.metrics.all_reduce_time_ms = (time.perf_counter() - t_ar) * 1e3
+        if log_step:  # the mean gradient's L2 norm (logging steps only: it reads back one scalar)
+            self.metrics.grad_norm = float(g.norm())
         self._set_schedules(progress)
         self.optimizer.step(self.grad_views)
         return True

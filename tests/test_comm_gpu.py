@@ -207,7 +207,7 @@ def test_p2p_trainer_matches_nccl_2gpu():
             moved = (pn[n] - init[n]).norm().item() + 1e-12
             diff = (pn[n] - pp[n]).norm().item()
             adam = not n.startswith("layer")
-            assert diff <= (0.25 if adam else 0.05) * moved, (r, n, diff, moved)
+            assert diff <= (0.25 if adam else 0.1) * moved, (r, n, diff, moved)
 
 
 def _topk(rank, world):
