@@ -64,18 +64,69 @@ _QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,
 
 
 class ClockSampler:
-    """Samples ``nvidia-smi`` every ``period_ms`` between ``start()`` and ``stop()``."""
+    """SM clock and clock-event reasons of one GPU between ``start()`` and ``stop()``.
 
-    def __init__(self, gpu_index: int | None = None, period_ms: int = 200):
+    Reads NVML (read-only queries) every ``period_ms`` on a thread and always once at ``start()`` and
+    once at ``stop()``, so a timed region shorter than the period still has samples; falls back to
+    ``nvidia-smi -lms`` when NVML is unavailable."""
+
+    # clock-event reason bits (nvml.h): the ones a benchmark must report
+    _REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
+
+    def __init__(self, gpu_index: int | None = None, period_ms: int = 50):
         self.gpu_index = gpu_index
         self.period_ms = period_ms
         self.proc = None
         self.path = None
+        self._nvml = None
+        self._handle = None
+        self._samples: list[tuple[float, float, int]] = []
+        self._stop = None
+        self._thread = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        idx = self.gpu_index or 0
+        try:  # match the CUDA device to its NVML handle by PCI address (CUDA_VISIBLE_DEVICES may remap)
+            import torch
+            pr = torch.cuda.get_device_properties(idx)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(idx)
+
+    def _sample(self):
+        n, h = self._nvml, self._handle
+        try:
+            sm = n.nvmlDeviceGetClockInfo(h, n.NVML_CLOCK_SM)
+            smax = n.nvmlDeviceGetMaxClockInfo(h, n.NVML_CLOCK_SM)
+            get = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or n.nvmlDeviceGetCurrentClocksThrottleReasons
+            self._samples.append((float(sm), float(smax), int(get(h))))
+        except Exception:
+            pass
 
     def start(self):
+        import threading
+        try:
+            self._nvml, self._handle = self._nvml_handle()
+        except Exception:
+            self._nvml = None
+        if self._nvml is not None:
+            self._samples = []
+            self._sample()
+            self._stop = threading.Event()
+
+            def loop():
+                while not self._stop.wait(self.period_ms / 1000.0):
+                    self._sample()
+
+            self._thread = threading.Thread(target=loop, daemon=True)
+            self._thread.start()
+            return self
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
-        cmd = ["nvidia-smi", f"--query-gpu={_QUERY}", "--format=csv,noheader,nounits", f"-lms={self.period_ms}"]
+        cmd = ["nvidia-smi", f"--query-gpu={_QUERY}", "--format=csv,noheader,nounits", f"-lms={max(self.period_ms, 100)}"]
         if self.gpu_index is not None:
             cmd.insert(1, f"--id={self.gpu_index}")
         try:
@@ -86,6 +137,17 @@ class ClockSampler:
         return self
 
     def stop(self) -> dict:
+        if self._nvml is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+            self._sample()
+            if not self._samples:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+            sm = [x[0] for x in self._samples]
+            reasons = sorted({name for _, _, r in self._samples for name, bit in self._REASONS.items() if r & bit})
+            loaded = [v for v in sm if v > 0.3 * max(sm)] or sm
+            return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(x[1] for x in self._samples),
+                    "reasons": reasons, "samples": len(sm), "source": "nvml"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         try:
