@@ -10,8 +10,9 @@ Bucket sizes 1 KB .. 256 MB (powers of 4) of N(0,1) values from a seed, for ever
 * ``p2p_rs``: the trainer's path for one bucket: ``comm_pack`` (fp32 -> wire dtype, 1/N scale and the
   non-finite check fused), a release flag, and ``comm_reduce`` where each owner reads its slice from
   every peer's buffer over NVLink and sums in fp32.
-* ``p2p_ar``: ``p2p_rs`` into a symmetric result buffer, then ``comm_gather`` of the other owners'
-  slices (fp32), which is the reduce-scatter + parameter-gather pair the trainer runs per step.
+* ``p2p_ar``: ``p2p_rs`` into a symmetric result buffer, then every owner pushes its reduced slice
+  (fp32) into each peer's buffer with posted NVLink stores (``comm_push``), the pair the trainer runs
+  per step (gradient reduce-scatter, parameter push).
 * ``p2p_topk``: top-k (1%) select with error feedback fused into the (u32 index, f16 value) list
   writer, and the owners' sparse merge (``topk_reduce``); compared against the dense rows.
 
@@ -53,6 +54,8 @@ class P2PBench:
         self.send = SymmetricBuffer(max_elems * 4)
         self.res = SymmetricBuffer(max_elems * 4)
         self.flags = SymmetricBuffer(64 * 8)
+        self.push_flags = SymmetricBuffer(world * 8)
+        self.no_segs = torch.zeros(0, 7, dtype=torch.int64, device="cuda")
         self.idx = SymmetricBuffer(max_elems * 4)
         self.val = SymmetricBuffer(max_elems * 2)
         self.cnt = SymmetricBuffer(64 * 4)
@@ -116,16 +119,19 @@ class P2PBench:
         self._signal(SLOT_READ, e)
 
     def ar(self, src: torch.Tensor, wire: int, mark=None):
+        """Reduce-scatter, then each owner pushes its reduced slice into every peer's result buffer
+        (posted NVLink stores) and flags them; a rank is done when all owners' flags arrived."""
         mark = mark or (lambda name: None)
         e = self.epoch + 1
-        self._wait(SLOT_GATHERED)  # every peer has gathered last iteration's result
+        self._wait(SLOT_GATHERED)  # every peer has consumed last iteration's result
         mark("wait_gathered")
         self.rs(src, wire, self.res_view, mark)
-        self._signal(SLOT_RES, e)
-        mark("signal2")
-        self.E.comm_gather(self.res.peers_dev, self.flag_ptrs, SLOT_RES, e, self.segs, self.res_view, self.blocks,
-                           self.budget)
-        mark("gather")
+        self.E.comm_push(self.res_view, self.res.peers_dev, self.rank, self.chunks, self.blocks)
+        self.E.comm_signal_peers(self.push_flags.peers_dev, self.rank, e)
+        mark("push")
+        self.E.comm_shadow_refresh(self.res_view, self.push_flags.ptr, self.world, self.rank, e, self.no_segs, 1,
+                                   self.budget)
+        mark("wait_pushes")
         self._signal(SLOT_GATHERED, e)
         mark("signal3")
 
@@ -142,7 +148,7 @@ class P2PBench:
         self._signal(SLOT_READ, e)
 
     def close(self):
-        for b in (self.send, self.res, self.flags, self.idx, self.val, self.cnt):
+        for b in (self.send, self.res, self.flags, self.push_flags, self.idx, self.val, self.cnt):
             b.close()
 
 

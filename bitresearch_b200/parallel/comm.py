@@ -181,6 +181,13 @@ class P2PGradSync:
                     ch += [(o, ln) for o, ln, _ in chunk_ranges(off, numel)]
             self.reduce_chunks.append(torch.tensor(ch, dtype=torch.int64, device=dev).view(-1, 2))
         self.flag_ptrs = torch.tensor([p for p in self.flags.peer_ptrs], dtype=torch.int64, device=dev)
+        # parameter push: the chunks this rank owns, and one flag slot per source rank on every rank
+        rows = []
+        for n in self.owned_names:
+            off, numel, _ = self.layout[n]
+            rows += [(o, ln) for o, ln, _ in chunk_ranges(off, numel)]
+        self.push_chunks = torch.tensor(sorted(rows), dtype=torch.int64, device=dev).view(-1, 2)
+        self.push_flags = SymmetricBuffer(self.world * 8)
         self._build_gather_table(trainer)
         self.sparse = cfg.sparsify.enabled
         if self.sparse:
@@ -297,10 +304,14 @@ class P2PGradSync:
         ok = status == 0 and float(flag.item()) == 0.0
         if ok:
             opt.step({n: self.red_views[n] for n in self.owned_names})
-        # publish (possibly unchanged) parameters and pull the ones owned elsewhere
-        self.E.comm_signal(self.flags.ptr + 8 * (self.nflags - 1), epoch)
-        self.E.comm_gather(self.param_buf.peers_dev, self.flag_ptrs, self.nflags - 1, epoch, self.gather_segs,
-                           self.params_flat, 64, self.budget)
+        # push (possibly unchanged) owned parameters into every peer's buffer with posted NVLink stores,
+        # flag each peer, then wait for the other owners' pushes and refresh the bf16 shadows locally.
+        # Every rank finished its backward before the skip agreement above, so no peer still reads the
+        # values being overwritten; pushes only touch a peer's non-owned regions.
+        self.E.comm_push(self.params_flat, self.param_buf.peers_dev, self.rank, self.push_chunks, 0)
+        self.E.comm_signal_peers(self.push_flags.peers_dev, self.rank, epoch)
+        self.E.comm_shadow_refresh(self.params_flat, self.push_flags.ptr, self.world, self.rank, epoch,
+                                   self.gather_segs, 0, self.budget)
         self.epoch = epoch
         if status:
             self.tr.log(f"p2p collective timed out (status {status}); step {step_idx} skipped")
@@ -318,7 +329,7 @@ class P2PGradSync:
     def close(self):
         torch.cuda.synchronize()
         dist.barrier()
-        bufs = [self.send, self.param_buf, self.flags]
+        bufs = [self.send, self.param_buf, self.flags, self.push_flags]
         if self.sparse:
             bufs += [self.sp_idx, self.sp_val, self.sp_cnt]
         for b in bufs:

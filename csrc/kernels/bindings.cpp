@@ -62,6 +62,11 @@ void attn_bwd_tc(const torch::Tensor& qkv, const torch::Tensor& o, const torch::
                  int64_t window, int64_t which);
 torch::Tensor mc_sharpe(int64_t n_paths, int64_t steps, double mu, double sigma, double annual, int64_t seed,
                         int64_t device);
+void comm_push(const torch::Tensor& params, const torch::Tensor& peers, int64_t me, const torch::Tensor& chunks,
+               int64_t max_blocks);
+void comm_signal_peers(const torch::Tensor& flag_peers, int64_t me, int64_t epoch);
+void comm_shadow_refresh(const torch::Tensor& params, int64_t push_flags_ptr, int64_t npeers, int64_t me,
+                         int64_t epoch, const torch::Tensor& segs, int64_t max_blocks, double budget_s);
 std::tuple<int64_t, torch::Tensor> sym_alloc(int64_t bytes);
 int64_t sym_open(const torch::Tensor& handle);
 void sym_close(int64_t ptr);
@@ -117,6 +122,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("H"), pybind11::arg("KV"), pybind11::arg("hd"), pybind11::arg("window"),
         pybind11::arg("which") = 0);
   m.def("mc_sharpe", &br::mc_sharpe);
+  m.def("comm_push", &br::comm_push);
+  m.def("comm_signal_peers", &br::comm_signal_peers);
+  m.def("comm_shadow_refresh", &br::comm_shadow_refresh);
   m.def("sym_alloc", &br::sym_alloc);
   m.def("sym_open", &br::sym_open);
   m.def("sym_close", &br::sym_close);

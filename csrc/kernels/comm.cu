@@ -11,9 +11,13 @@
 //             the pack kernel on the same stream, so all of the bucket is written first);
 //   reduce    for every element of the segments this rank owns inside the bucket: wait (acquire,
 //             bounded) until every peer's flags[slot] >= epoch, then out = scale * sum_p send_p;
-//   gather    after the owners' optimizer steps, each rank pulls the parameters it does not own from
-//             the owners' symmetric parameter buffers (again after an acquire on the owner's flag),
-//             writing the fp32 master and, for GEMM weights, the bf16 shadow.
+//   push      after its optimizer step, each owner writes its parameters into every peer's symmetric
+//             parameter buffer with posted stores and release-stores its slot of each peer's
+//             push-flag array; a receiver acquires its local flags, then refreshes the bf16 GEMM
+//             shadows of the parameters it does not own (the training path);
+//   gather    the pull form of the same exchange: each rank reads the parameters it does not own from
+//             the owners' buffers after an acquire on the owner's flag (remote loads pay a round trip
+//             each, which caps them well below the stores' bandwidth at 8 ranks).
 // A wait that exceeds its budget records kErrTimeoutPeer in the device status word and the block
 // skips its work; the host treats the step as aborted (the reference's abort-and-skip), so nothing
 // spins forever and nothing traps.
@@ -275,6 +279,99 @@ __global__ void __launch_bounds__(256) gather_kernel(const float* const* __restr
   }
 }
 
+// ------------------------------------------------------------------------------ parameter push
+// The owner of each parameter writes its updated values into every peer's symmetric parameter buffer
+// (posted NVLink stores: no round trip per load, unlike a pull), then stores `epoch` into its slot of
+// each peer's push-flag array. A receiver waits on its own (local) flag slots, then refreshes the bf16
+// GEMM shadows of the parameters it does not own from local memory.
+
+// grid-stride over owned chunks: peers[p][off + j] = src[off + j] for every peer p != me
+__global__ void __launch_bounds__(256) push_kernel(const float* __restrict__ src, float* const* __restrict__ peers,
+                                                   int npeers, int me, const Chunk* __restrict__ chunks, int nchunks) {
+  constexpr int U = 4;
+  const int64_t step = (int64_t)blockDim.x * 4;
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    const Chunk ch = chunks[c];
+    const float* s = src + ch.off;
+    const int64_t n4 = ch.len & ~int64_t(3);
+    for (int64_t j0 = threadIdx.x * 4; j0 < n4; j0 += U * step) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t j = j0 + u * step;
+        if (j < n4) v[u] = *reinterpret_cast<const float4*>(s + j);
+      }
+      for (int p = 0; p < npeers; ++p) {
+        if (p == me) continue;
+        float* d = peers[p] + ch.off;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t j = j0 + u * step;
+          if (j < n4) *reinterpret_cast<float4*>(d + j) = v[u];
+        }
+      }
+    }
+    for (int64_t j = n4 + threadIdx.x; j < ch.len; j += blockDim.x) {
+      const float x = s[j];
+      for (int p = 0; p < npeers; ++p)
+        if (p != me) peers[p][ch.off + j] = x;
+    }
+  }
+}
+
+// flags[p][me] = epoch on every peer p != me, after this GPU's earlier writes (release, system scope)
+__global__ void signal_peers_kernel(int64_t* const* flags, int npeers, int me, int64_t epoch) {
+  __threadfence_system();
+  for (int p = 0; p < npeers; ++p)
+    if (p != me) st_release_sys(flags[p] + me, epoch);
+}
+
+// Every block first waits (bounded) until each other rank's slot of this rank's push-flag array holds
+// `epoch`, then writes the bf16 shadows of the listed (non-owned) segments from the local fp32 values.
+__global__ void __launch_bounds__(256) shadow_refresh_kernel(const float* __restrict__ params,
+                                                             const int64_t* __restrict__ push_flags, int npeers,
+                                                             int me, int64_t epoch,
+                                                             const GatherSeg* __restrict__ segs, int nsegs,
+                                                             uint64_t budget_ns, int* status) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (int p = 0; p < npeers && ok; ++p) {
+      if (p == me) continue;
+      uint32_t it = 0;
+      while (ld_acquire_sys(push_flags + p) < epoch) {
+        if ((++it & 63u) == 0 && globaltimer_ns() - t0 > budget_ns) {
+          ok = 0;
+          if (status) atomicCAS(status, 0, kErrTimeoutPeer);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (!ok) return;
+  for (int s = blockIdx.x; s < nsegs; s += gridDim.x) {
+    const GatherSeg g = segs[s];
+    if (!g.shadow) continue;
+    const float* src = params + g.off;
+    __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(g.shadow);
+    const bool vec = (g.off & 3) == 0 && (g.start & 3) == 0 && (g.cols & 3) == 0 && (g.shadow_ld & 3) == 0 &&
+                     (g.shadow & 7) == 0;
+    const int64_t n4 = vec ? (g.len & ~int64_t(3)) : 0;
+    for (int64_t j = threadIdx.x * 4; j < n4; j += (int64_t)blockDim.x * 4) {
+      const float4 x = *reinterpret_cast<const float4*>(src + j);
+      const int64_t e = g.start + j;
+      *reinterpret_cast<uint2*>(sh + (e / g.cols) * g.shadow_ld + (e % g.cols)) =
+          make_uint2(pack_bf16(x.x, x.y), pack_bf16(x.z, x.w));
+    }
+    for (int64_t j = n4 + threadIdx.x; j < g.len; j += blockDim.x) {
+      const int64_t e = g.start + j;
+      sh[(e / g.cols) * g.shadow_ld + (e % g.cols)] = __float2bfloat16(src[j]);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------ top-k + error feedback
 // Deep Gradient Compression as in the reference sparsifier (gradient-sparsifier.ts:82-144), per bucket:
 //   g = grad * scale + e (+ momentum correction v = mu*v + g, g = v); thr = the floor(S*(1-k))-th
@@ -500,6 +597,42 @@ void comm_gather(const torch::Tensor& peers, const torch::Tensor& flags, int64_t
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+}  // namespace br
+
+namespace br {
+// chunks: int64 [n, 2] (offset, length) of the parameters this rank owns; peers: int64 [N] param buffers
+void comm_push(const torch::Tensor& params, const torch::Tensor& peers, int64_t me, const torch::Tensor& chunks,
+               int64_t max_blocks) {
+  c10::cuda::CUDAGuard g(params.device());
+  const int n = (int)chunks.size(0);
+  if (n == 0) return;
+  const int grid = (int)std::min<int64_t>(n, max_blocks > 0 ? max_blocks : 2 * sm_count());
+  push_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      params.data_ptr<float>(), reinterpret_cast<float* const*>(peers.data_ptr<int64_t>()), (int)peers.numel(),
+      (int)me, reinterpret_cast<const Chunk*>(chunks.data_ptr<int64_t>()), n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// flag_peers: int64 [N] pointers to every rank's push-flag array (N int64 slots each)
+void comm_signal_peers(const torch::Tensor& flag_peers, int64_t me, int64_t epoch) {
+  c10::cuda::CUDAGuard g(flag_peers.device());
+  signal_peers_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<int64_t* const*>(flag_peers.data_ptr<int64_t>()), (int)flag_peers.numel(), (int)me, epoch);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// waits for every other rank's push (this rank's flag slots >= epoch), then refreshes bf16 shadows
+void comm_shadow_refresh(const torch::Tensor& params, int64_t push_flags_ptr, int64_t npeers, int64_t me,
+                         int64_t epoch, const torch::Tensor& segs, int64_t max_blocks, double budget_s) {
+  c10::cuda::CUDAGuard g(params.device());
+  const int ns = (int)segs.size(0);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ns, max_blocks > 0 ? max_blocks : sm_count()));
+  shadow_refresh_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      params.data_ptr<float>(), reinterpret_cast<const int64_t*>(push_flags_ptr), (int)npeers, (int)me, epoch,
+      reinterpret_cast<const GatherSeg*>(segs.data_ptr<int64_t>()), ns, (uint64_t)(budget_s * 1e9),
+      status_ptr(params.device().index()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 }  // namespace br
 
 namespace br {

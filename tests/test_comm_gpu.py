@@ -3,8 +3,9 @@
 * 1 GPU: a reduce whose peer flag is never set gives up after its budget, records the timeout in the
   device status word and leaves the context usable.
 * 2 GPUs (one process each, NCCL only for rendezvous): packed bf16/fp32 gradients reduced by their
-  owners equal the mean of the ranks' inputs; the parameter gather returns the owners' values and
-  refreshes bf16 shadows; the trainer's p2p path tracks the NCCL path step for step.
+  owners equal the mean of the ranks' inputs; the parameter gather (pull) and the parameter push
+  deliver the owners' values and refresh bf16 shadows; the fused top-k path reduces the kept entries;
+  the trainer's p2p path tracks the NCCL path step for step.
 """
 import datetime
 import os
@@ -155,6 +156,51 @@ def test_p2p_reduce_and_gather_2gpu():
         assert torch.all(local[other * half:(other + 1) * half] == other + 1)
         assert torch.all(local[r * half:(r + 1) * half] == r + 1)
         assert torch.all(shadow == other + 1)
+
+
+def _push(rank, world):
+    """Rank r owns half of a symmetric fp32 buffer; each pushes its half into the other and flags it;
+    the shadow refresh waits for the flag and writes the bf16 shadow of the half it does not own."""
+    from bitresearch_b200.ops._ext import check_status, ext
+    from bitresearch_b200.parallel.comm import SymmetricBuffer
+    E = ext()
+    n, half = 40000, 20000
+    pbuf = SymmetricBuffer(n * 4)
+    pflags = SymmetricBuffer(world * 8)
+    local = E.sym_view(pbuf.ptr, n, 0, rank)
+    out = {}
+    for epoch in (1, 2):  # two rounds: the flag protocol across steps
+        local.copy_(torch.full((n,), 0.0, device="cuda"))
+        local[rank * half:(rank + 1) * half] = float(10 * epoch + rank + 1)
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        mine = torch.tensor([[rank * half, half]], dtype=torch.int64, device="cuda")
+        E.comm_push(local, pbuf.peers_dev, rank, mine, 0)
+        E.comm_signal_peers(pflags.peers_dev, rank, epoch)
+        other = 1 - rank
+        shadow = torch.zeros(100, 200, dtype=torch.bfloat16, device="cuda")
+        seg = torch.tensor([[other * half, half, other, 200, 200, shadow.data_ptr(), 0]], dtype=torch.int64,
+                           device="cuda")
+        E.comm_shadow_refresh(local, pflags.ptr, world, rank, epoch, seg, 0, 10.0)
+        torch.cuda.synchronize()
+        out[epoch] = (local.cpu(), shadow.float().cpu(), check_status())
+        torch.distributed.barrier()
+    pbuf.close()
+    pflags.close()
+    return out
+
+
+def test_parameter_push_and_shadow_refresh_2gpu():
+    res = _run(_push)
+    n, half = 40000, 20000
+    for r in range(2):
+        o = 1 - r
+        for epoch in (1, 2):
+            local, shadow, st = res[r][epoch]
+            assert st == 0
+            assert torch.all(local[r * half:(r + 1) * half] == 10 * epoch + r + 1)
+            assert torch.all(local[o * half:(o + 1) * half] == 10 * epoch + o + 1)  # pushed by the owner
+            assert torch.all(shadow == 10 * epoch + o + 1)
 
 
 def _train(rank, world):
