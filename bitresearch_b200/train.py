@@ -346,6 +346,16 @@ class Trainer:
         return bpb
 
     # ------------------------------------------------------------------ loop
+    def _agreed_time(self, local_s: float) -> float:
+        """The slowest rank's training time, so every rank stops on the same step and follows the
+        same learning-rate schedule. Each browser peer of the reference keeps its own clock
+        (src/distributed/trainer.ts:986-1005) and its ring tolerates a peer that stops early; here the
+        ranks' collectives must stay matched, so the stop decision is collective."""
+        dev = self.device if self.is_cuda and dist.get_backend() == "nccl" else torch.device("cpu")
+        t = torch.tensor([local_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     def start_training(self) -> TrainerMetrics:
         cfg = self.cfg
         if self.model is None:
@@ -362,6 +372,8 @@ class Trainer:
             dt = time.perf_counter() - t0
             if self.metrics.step > cfg.warmup_steps_excluded:
                 self.total_training_time += dt
+            if self.world > 1:
+                self.total_training_time = self._agreed_time(self.total_training_time)
             m = self.metrics
             if cfg.log_every and m.step % cfg.log_every == 0:
                 lrm = lr_multiplier(min(self.total_training_time / cfg.time_budget, 1), cfg.warmup_ratio,

@@ -51,6 +51,32 @@ def test_gloo_dp_topk_sparsified_ring():
         assert np.array_equal(r0[n], r1[n]), n
 
 
+def _time_budget(rank, world):
+    import time
+    cfg = _cfg(max_steps=10_000, comm="ring", total_batch_tokens=128 * world, time_budget=1.5,
+               warmup_steps_excluded=2)
+    tr = Trainer(cfg, device="cpu", log=lambda m: None)
+    tr.initialize()
+    step = tr.train_step
+    if rank == 1:  # the slower rank: its clock alone would keep it training after rank 0 stops
+
+        def slow(*a, **k):
+            time.sleep(0.02)
+            return step(*a, **k)
+
+        tr.train_step = slow
+    m = tr.start_training()
+    p = np.concatenate([v.detach().numpy().ravel() for v in tr.model.named().values()])
+    return m.step, tr.total_training_time, p
+
+
+def test_gloo_time_budget_stops_every_rank_on_the_same_step():
+    (s0, t0, p0), (s1, t1, p1) = run_world(_time_budget, 2, timeout=120)
+    assert s0 == s1 and s0 > 3
+    assert t0 == t1 >= 1.5
+    assert np.array_equal(p0, p1)
+
+
 def test_checkpoint_resume_reproduces_trajectory(tmp_path):
     cfg = _cfg(max_steps=10)
     a = Trainer(cfg, device="cpu", log=lambda m: None)
