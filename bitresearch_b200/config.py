@@ -183,12 +183,16 @@ class TrainConfig:
     # eval
     eval_tokens: int = 40 * 524288
     val_fraction: float = 0.1
-    # data: "zipf" (BOS-packed Zipf docs), "uniform" (uniform + BOS every 64), "tokens" (a .bin file)
+    # data: "zipf" (BOS-packed Zipf docs), "markov" (Zipf docs whose tokens follow hashed order-1 /
+    # order-2 successor tables), "uniform" (uniform + BOS every 64), "tokens" (a .bin file)
     data: str = "zipf"
     data_path: str = ""
     token_bytes_path: str = ""
     zipf_s: float = 1.1
     doc_mean_len: int = 512
+    markov_p1: float = 0.4  # P(next token is a successor of the previous token)
+    markov_p2: float = 0.4  # P(next token is a successor of the previous two tokens)
+    markov_branch: int = 4  # successors per context, picked with weights 2^-k
     token_bytes_max: int = 16
     bos_every: int = 64
     document_buffer_size: int = 1000

@@ -4,12 +4,15 @@
 host int32 ``(inputs, targets)`` arrays and an ``epoch`` attribute. Each rank draws from its own
 seeded stream (seed, split and rank mixed), so data-parallel ranks see disjoint data, like separate
 browser tabs in the reference. The validation split uses a different seed, i.e. a held-out stream.
+The synthetic distribution itself (which id is frequent, the Markov successors) comes from a
+separate table seed shared by all ranks and both splits.
 
 ``PinnedPrefetcher`` produces the next batch on a host thread into page-locked buffers and copies
 it to the device on a side stream, so the host->device transfer overlaps the previous step.
 """
 from __future__ import annotations
 
+import math
 import threading
 from queue import Queue
 
@@ -30,15 +33,27 @@ def _native():
 
 
 def _seed(cfg: TrainConfig, split: str, rank: int) -> int:
+    """Sampling seed of one rank's stream of one split."""
     return (cfg.seed * 1_000_003 + (0 if split == "train" else 7_777_777) + rank * 9176) & 0x7FFFFFFF
+
+
+def _table_seed(cfg: TrainConfig) -> int:
+    """Seed of the token distribution itself (id permutation, Markov successors): one per run, shared
+    by every rank and by the validation split."""
+    return (cfg.seed * 2_654_435_761 + 0x51A7) & 0x7FFFFFFF
 
 
 class _ZipfNative:
     def __init__(self, cfg: TrainConfig, seed: int):
         mod = _native()
         self.mod = mod
-        self.p = mod.zipf_packer(cfg.model.vocab_size, cfg.zipf_s, float(cfg.doc_mean_len), seed,
-                                 cfg.document_buffer_size, 0)
+        if cfg.data == "markov":
+            self.p = mod.markov_packer(cfg.model.vocab_size, cfg.zipf_s, float(cfg.doc_mean_len), seed,
+                                       _table_seed(cfg), cfg.markov_p1, cfg.markov_p2, cfg.markov_branch,
+                                       cfg.document_buffer_size, 0)
+        else:
+            self.p = mod.zipf_packer(cfg.model.vocab_size, cfg.zipf_s, float(cfg.doc_mean_len), seed,
+                                     cfg.document_buffer_size, 0, _table_seed(cfg))
 
     @property
     def epoch(self):
@@ -55,7 +70,8 @@ class _ZipfNative:
 
 class _ZipfPython:
     def __init__(self, cfg: TrainConfig, seed: int):
-        src = ZipfDocumentSource(cfg.model.vocab_size, cfg.zipf_s, cfg.doc_mean_len, seed)
+        src = ZipfDocumentSource(cfg.model.vocab_size, cfg.zipf_s, cfg.doc_mean_len, seed,
+                                 table_seed=_table_seed(cfg))
         self.b = BestFitDocumentBatcher(src.documents, bos_id(cfg.model.vocab_size), cfg.document_buffer_size)
 
     @property
@@ -95,6 +111,10 @@ def make_batch_source(cfg: TrainConfig, split: str = "train", rank: int = 0, wor
         if native and _native() is not None:
             return _ZipfNative(cfg, seed)
         return _ZipfPython(cfg, seed)
+    if cfg.data == "markov":
+        if _native() is None:
+            raise RuntimeError("data=markov needs the native data module (python setup.py build_ext --inplace)")
+        return _ZipfNative(cfg, seed)
     if cfg.data == "uniform":
         return _Uniform(cfg, seed)
     if cfg.data == "tokens":
@@ -106,6 +126,28 @@ def make_batch_source(cfg: TrainConfig, split: str = "train", rank: int = 0, wor
             part = part[rank * n:(rank + 1) * n]
         return _Tokens(part)
     raise ValueError(f"unknown data source {cfg.data!r}")
+
+
+def markov_floor(cfg: TrainConfig, token_bytes: np.ndarray, n_tokens: int, batch: int) -> tuple[float, float]:
+    """Loss floor of ``data=markov`` on the validation stream: the exact negative log-likelihood of its
+    first ``n_tokens`` targets under the generating process, as (bits per byte, nats per token). A model
+    that had learned the process exactly would score this ``val_bpb``."""
+    if cfg.data != "markov":
+        raise ValueError("markov_floor needs data=markov")
+    mod = _native()
+    T = cfg.model.sequence_len
+    src = _ZipfNative(cfg, _seed(cfg, "val", 0))
+    rows = np.empty((batch, T + 1), np.int32)
+    nats = nbytes = count = 0.0
+    for _ in range(max(1, n_tokens // (batch * T))):
+        mod.pack_rows(src.p, rows, batch, T)
+        nll = mod.markov_nll(src.p, rows, batch, T)
+        tb = token_bytes[rows[:, 1:]]
+        keep = tb > 0
+        nats += float(nll[keep].sum())
+        nbytes += float(tb[keep].sum())
+        count += float(keep.sum())
+    return nats / (math.log(2) * nbytes), nats / count
 
 
 class PinnedPrefetcher:

@@ -48,7 +48,7 @@ class ZipfDocumentSource:
     """Infinite seeded source of documents (without BOS) with Zipf(s)-distributed tokens."""
 
     def __init__(self, vocab_size: int, s: float = 1.1, mean_len: int = 512, seed: int = 0,
-                 max_len: int | None = None):
+                 max_len: int | None = None, table_seed: int | None = None):
         self.V = vocab_size
         self.rng = np.random.default_rng(seed)
         n = vocab_size - 1  # BOS excluded
@@ -57,7 +57,8 @@ class ZipfDocumentSource:
         self.cdf = np.cumsum(w / w.sum())
         self.cdf[-1] = 1.0
         # seeded rank -> id permutation so frequent ids are spread over the table
-        self.perm = np.random.default_rng(seed ^ 0x5EED).permutation(n).astype(np.int32)
+        ts = seed if table_seed is None else table_seed  # the permutation is the distribution, not the sample
+        self.perm = np.random.default_rng(ts ^ 0x5EED).permutation(n).astype(np.int32)
         self.p_geom = 1.0 / mean_len
         self.max_len = max_len
 

@@ -343,6 +343,10 @@ class Trainer:
             nats, nbytes = float(t[0]), float(t[1])
             bpb = nats / (math.log(2) * nbytes) if nbytes > 0 else 0.0
         self.metrics.val_bpb = bpb
+        if cfg.data == "markov" and self.rank == 0 and "val_bpb_floor" not in self.metrics.extra:
+            from .data.pipeline import markov_floor
+            fb, fn = markov_floor(cfg, self.token_bytes, min(cfg.eval_tokens, 1 << 22), B)
+            self.metrics.extra.update(val_bpb_floor=fb, val_nats_floor=fn)
         return bpb
 
     # ------------------------------------------------------------------ loop

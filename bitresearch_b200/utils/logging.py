@@ -43,6 +43,8 @@ class TrainerMetrics:
 
 def summary_block(m: TrainerMetrics, training_seconds: float, total_seconds: float, peak_vram_mb: float,
                   depth: int) -> str:
+    # synthetic Markov data knows its own loss floor; it follows the reference's fields as an extra line
+    floor = [f"val_bpb_floor:    {m.extra['val_bpb_floor']:.6f}"] if "val_bpb_floor" in m.extra else []
     return "\n".join([
         "---",
         f"val_bpb:          {m.val_bpb:.6f}",
@@ -54,7 +56,7 @@ def summary_block(m: TrainerMetrics, training_seconds: float, total_seconds: flo
         f"num_steps:        {m.step}",
         f"num_params_M:     {m.num_params_m:.1f}",
         f"depth:            {depth}",
-    ])
+    ] + floor)
 
 
 def git_commit_short() -> str:

@@ -78,3 +78,80 @@ def test_pipeline_ranks_get_distinct_streams():
     b = make_batch_source(cfg, "train", 1, 2).next(2, 16)[0]
     v = make_batch_source(cfg, "val", 0, 2).next(2, 16)[0]
     assert not np.array_equal(a, b) and not np.array_equal(a, v)
+
+
+@pytest.mark.parametrize("data", ["zipf", "markov"])
+def test_ranks_and_splits_sample_one_distribution(data):
+    pytest.importorskip("bitresearch_b200._native_data")
+    from bitresearch_b200.config import apply_overrides
+    cfg = apply_overrides(preset("d512"), [f"data={data}"])
+    tops, firsts = [], []
+    for split, rank in [("train", 0), ("train", 1), ("val", 0)]:
+        x, _ = make_batch_source(cfg, split, rank, 2).next(16, 2048)
+        ids, c = np.unique(x, return_counts=True)
+        tops.append(set(ids[np.argsort(-c)[:3]].tolist()))
+        firsts.append(x[:, :64].copy())
+    assert tops[0] == tops[1] == tops[2]  # the same frequent ids everywhere
+    assert not np.array_equal(firsts[0], firsts[1]) and not np.array_equal(firsts[0], firsts[2])
+
+
+def _pairs(rows, bos, order):
+    succ = {}
+    for r in rows:
+        for t in range(order, len(r)):
+            ctx = tuple(r[t - order:t])
+            if r[t] == bos or any(c == bos for c in ctx[-1:]):
+                continue
+            if order == 2 and ctx[0] == bos:
+                continue
+            succ.setdefault(ctx, set()).add(int(r[t]))
+    return succ
+
+
+@pytest.mark.parametrize("p1,p2,order", [(1.0, 0.0, 1), (0.0, 1.0, 2)])
+def test_markov_successor_tables(p1, p2, order):
+    nd = pytest.importorskip("bitresearch_b200._native_data")
+    V, K = 256, 3
+    p = nd.markov_packer(V, 1.1, 128.0, 5, 77, p1, p2, K, 100, 0)
+    rows = np.empty((32, 513), np.int32)
+    nd.pack_rows(p, rows, 32, 512)
+    succ = _pairs(rows, V - 1, order)
+    assert max(len(s) for s in succ.values()) <= K
+    assert sum(len(s) > 1 for s in succ.values()) > 10  # several successors are actually used
+    # same table seed -> same successors from a different stream
+    q = nd.markov_packer(V, 1.1, 128.0, 6, 77, p1, p2, K, 100, 0)
+    rows2 = np.empty((32, 513), np.int32)
+    nd.pack_rows(q, rows2, 32, 512)
+    both = _pairs(rows2, V - 1, order)
+    shared = [c for c in both if c in succ]
+    assert shared and all(len(succ[c] | both[c]) <= K for c in shared)
+
+
+def test_markov_nll_matches_sampled_frequencies():
+    nd = pytest.importorskip("bitresearch_b200._native_data")
+    V, K = 8192, 4
+    p = nd.markov_packer(V, 1.1, 4096.0, 1, 2, 1.0, 0.0, K, 100, 0)
+    rows = np.empty((64, 4097), np.int32)
+    nd.pack_rows(p, rows, 64, 4096)
+    nll = nd.markov_nll(p, rows, 64, 4096)
+    keep = rows[:, 1:] != V - 1
+    assert nll[~keep].sum() == 0 and np.isfinite(nll).all() and (nll[keep] > 0).all()
+    w = 2.0 ** -np.arange(K)
+    w /= w.sum()
+    # pure order-1 chain: at most the branch entropy (two branches of a context may name the same id)
+    assert nll[keep].mean() < -(w * np.log(w)).sum() + 0.1
+    # exp(-nll) of a transition is its probability: compare with sampled frequencies of frequent contexts
+    prev, nxt, q = rows[:, :-1].ravel(), rows[:, 1:].ravel(), np.exp(-nll.ravel())
+    inner = (prev != V - 1) & (nxt != V - 1)
+    ids, counts = np.unique(prev[inner], return_counts=True)
+    checked = 0
+    for c in ids[np.argsort(-counts)[:5]]:
+        sel = inner & (prev == c)
+        n = sel.sum()
+        for x in np.unique(nxt[sel]):
+            m = sel & (nxt == x)
+            assert np.allclose(q[m], q[m][0])  # one probability per transition
+            assert abs(m.sum() / n - q[m][0]) < 4 * np.sqrt(0.25 / n) + 1e-3, (c, x)
+            checked += 1
+        assert abs(sum(q[sel & (nxt == x)][0] for x in np.unique(nxt[sel])) - 1.0) < 1e-9
+    assert checked > 10

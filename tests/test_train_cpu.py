@@ -28,6 +28,17 @@ def test_loss_decreases_and_summary(capsys):
     assert "\nval_bpb:" in out and "num_params_M:" in out and m.val_bpb > 0
 
 
+def test_markov_data_reports_its_loss_floor(capsys):
+    cfg = _cfg(max_steps=30, time_budget=1e9, data="markov", doc_mean_len=32)
+    tr = Trainer(cfg, device="cpu")
+    tr.initialize()
+    m = tr.start_training()
+    out = capsys.readouterr().out
+    floor = float(out.split("val_bpb_floor:")[1].split()[0])
+    assert 0 < floor < m.val_bpb
+    assert m.extra["val_nats_floor"] < m.loss
+
+
 def _dp(rank, world, comm, sparsify):
     cfg = _cfg(max_steps=4, comm=comm, total_batch_tokens=128 * world)
     cfg.sparsify.enabled = sparsify
