@@ -33,7 +33,11 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "tokens/s (device-timed, max over ranks)"
-MODEL = "autoresearch GPT d512 depth-8 (4x128 heads, vocab 8192, SSSL windows 1024/2048, VE, ReLU^2, QK-norm)"
+def model_desc(m) -> str:
+    """e.g. 'autoresearch GPT d512 depth-8 (4x128 heads, vocab 8192, SSSL windows 1024/2048, VE, ReLU^2, QK-norm)'."""
+    hd = m.n_embd // m.n_head
+    return (f"autoresearch GPT d{m.n_embd} depth-{m.n_layer} ({m.n_head}x{hd} heads, vocab {m.vocab_size}, "
+            f"{m.window_pattern} windows {m.sequence_len // 2}/{m.sequence_len}, VE, ReLU^2, QK-norm)")
 REF_UNAVAILABLE = ("the reference (gauravsaini/bitresearch) is a TypeScript/TensorFlow.js browser trainer with no "
                    "setup.py/pyproject (pip: 'Directory is not installable'); its GPU path is WebGPU and no Node "
                    "runtime is present")
@@ -174,7 +178,7 @@ def main():
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic: seeded random token ids; random-init weights",
-            "config": {"model": MODEL, "global_batch": global_tokens, "global_batch_unit": "tokens",
+            "config": {"model": model_desc(cfg.model), "global_batch": global_tokens, "global_batch_unit": "tokens",
                        "seq_len": T, "device_batch": B, "grad_accum": accum, "parallelism": f"dp{world}",
                        "comm": (args.comm if args.impl == "ours" else "nccl-ddp") if world > 1 else "none",
                        "l2": "inputs larger than L2 (activations tens of GB per step); no flush"},
