@@ -139,8 +139,8 @@ class P2PBench:
         e = self.epoch = self.epoch + 1
         self._wait(SLOT_READ)  # every peer has read last iteration's lists and counters
         self.cnt_view.zero_()
-        self.E.topk_threshold(src, self.err, None, 0, self.n, 1.0, 0.0, 10000, ratio, e * 7919 + self.rank, self.thr)
-        self.E.topk_select(src, self.err, None, self.sel, 1.0, 0.0, self.thr, self.idx.ptr, self.val.ptr, self.cnt.ptr)
+        self.E.topk_threshold(src, self.err, None, 0, self.n, 1.0, 0.0, 10000, ratio, e * 7919 + self.rank, False, self.thr)
+        self.E.topk_select(src, self.err, None, self.sel, 1.0, 0.0, False, self.thr, self.idx.ptr, self.val.ptr, self.cnt.ptr)
         self._signal(SLOT_READY, e)
         out[self.rank * self.per:(self.rank + 1) * self.per].zero_()
         self.E.topk_reduce(self.sp_peers, self.flag_ptrs, SLOT_READY, e, self.rank * self.per, self.rank, out,

@@ -153,6 +153,10 @@ class SparsifyConfig:
     sample_size: int = 10000
     momentum_factor: float = 0.9
     value_dtype: str = "fp16"  # wire dtype of the kept values
+    # False: the reference's update (residual = the whole velocity, velocity never cleared), whose
+    # unsent residuals grow by (1 + momentum) per step; True: Deep Gradient Compression's momentum
+    # correction with factor masking (u = m u + g, v += u, send top-k of v, clear v and u where sent)
+    momentum_masking: bool = False
 
 
 @dataclass
@@ -253,8 +257,10 @@ def _d1280() -> TrainConfig:
 
 
 def _d512_topk() -> TrainConfig:
+    # error feedback without sender-side momentum: Muon and AdamW apply momentum to what arrives
     c = _d512()
-    c.sparsify = SparsifyConfig(enabled=True, top_k_ratio=0.01, warmup_steps=0, value_dtype="fp16")
+    c.sparsify = SparsifyConfig(enabled=True, top_k_ratio=0.01, warmup_steps=0, value_dtype="fp16",
+                                momentum_factor=0.0)
     return c
 
 

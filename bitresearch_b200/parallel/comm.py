@@ -259,9 +259,9 @@ class P2PGradSync:
         mu = sp.momentum_factor
         seed = (self.epoch * 1000003 + b * 7919 + self.rank * 104729) & 0x7FFFFFFF
         self.E.topk_threshold(self.tr.flat_grad, self.err, self.vel, lo, hi, 1.0 / loss_scale, mu, sp.sample_size,
-                              sp.top_k_ratio, seed, self.thr[b:b + 1])
+                              sp.top_k_ratio, seed, sp.momentum_masking, self.thr[b:b + 1])
         self.E.topk_select(self.tr.flat_grad, self.err, self.vel, self.sel_chunks[b], 1.0 / loss_scale, mu,
-                           self.thr[b:b + 1], self.sp_idx.ptr, self.sp_val.ptr, self.sp_cnt.ptr)
+                           sp.momentum_masking, self.thr[b:b + 1], self.sp_idx.ptr, self.sp_val.ptr, self.sp_cnt.ptr)
         self.E.comm_signal(self.flags.ptr + 8 * b, self.epoch + 1)
         self.E.topk_reduce(self.sp_peers, self.flag_ptrs, b, self.epoch + 1, self.list_base[(b, self.rank)],
                            b * self.world + self.rank, self.red, 1.0 / self.world, 32, self.budget)

@@ -10,6 +10,12 @@ Semantics follow src/distributed/gradient-sparsifier.ts:
   the rest go to the residual and are zeroed (gradient-sparsifier.ts:124-137);
 * wire codec ``[length u32 | count u32 | indices u32[] | values f32[]]`` (gradient-sparsifier.ts:161-193).
 
+With momentum the reference's residual is the whole velocity and the velocity is never cleared, so an
+entry that stays below the threshold grows as ``e <- (1 + mu) e + g`` (1.9x per step at mu = 0.9).
+``momentum_masking=True`` runs Deep Gradient Compression as published instead (Lin et al., 2018):
+``u = mu u + g``, ``v = v + u``, send the top-k of ``v``, clear ``v`` and ``u`` where sent. The default
+keeps the reference's update.
+
 ``GradientSparsifier`` is the torch implementation (any device). On B200 the same math runs fused in
 one kernel pass (threshold from a device-side sample, select, EF update, compaction to an
 index/f16-value payload) in :mod:`bitresearch_b200.parallel.comm`, and this class is its oracle.
@@ -33,13 +39,14 @@ class SparseGradient:
 
 class GradientSparsifier:
     def __init__(self, top_k_ratio: float = 0.10, warmup_steps: int = 100, sample_size: int = 10000,
-                 momentum_factor: float = 0.9, seed: int = 0):
+                 momentum_factor: float = 0.9, seed: int = 0, momentum_masking: bool = False):
         if not (0 < top_k_ratio <= 1):
             raise ValueError(f"topKRatio must be in (0, 1], got {top_k_ratio}")
         self.k = top_k_ratio
         self.warmup_steps = warmup_steps
         self.sample_size = sample_size
         self.mu = momentum_factor
+        self.masking = momentum_masking
         self.error: torch.Tensor | None = None
         self.velocity: torch.Tensor | None = None
         self.step = 0
@@ -73,13 +80,19 @@ class GradientSparsifier:
             self.error = torch.zeros_like(g)
         if self.mu > 0 and (self.velocity is None or self.velocity.numel() != N):
             self.velocity = torch.zeros_like(g)
-        g.add_(self.error)
-        if self.velocity is not None and self.mu > 0:
-            self.velocity.mul_(self.mu).add_(g)
-            g.copy_(self.velocity)
+        if self.masking and self.velocity is not None and self.mu > 0:
+            self.velocity.mul_(self.mu).add_(g)  # u = m u + g
+            g.copy_(self.error).add_(self.velocity)  # v = v + u
+        else:
+            g.add_(self.error)
+            if self.velocity is not None and self.mu > 0:
+                self.velocity.mul_(self.mu).add_(g)
+                g.copy_(self.velocity)
         thr = self.find_threshold(g)
         keep = g.abs() >= thr
         self.error.copy_(torch.where(keep, torch.zeros_like(g), g))
+        if self.masking and self.velocity is not None and self.mu > 0:
+            self.velocity.mul_(~keep)
         g.mul_(keep)
         idx = keep.nonzero().squeeze(1)
         return SparseGradient(N, idx, g[idx].clone())

@@ -161,7 +161,8 @@ class Trainer:
         if cfg.sparsify.enabled and not fused_comm:
             self.sparsifier = GradientSparsifier(cfg.sparsify.top_k_ratio, cfg.sparsify.warmup_steps,
                                                  cfg.sparsify.sample_size, cfg.sparsify.momentum_factor,
-                                                 seed=cfg.seed + self.rank)
+                                                 seed=cfg.seed + self.rank,
+                                                 momentum_masking=cfg.sparsify.momentum_masking)
         self.optimizer = MuonAdamW(
             self.model.named(), self.model.param_groups(), model_dim=cfg.model.n_embd,
             unembedding_lr=cfg.unembedding_lr, embedding_lr=cfg.embedding_lr, matrix_lr=cfg.matrix_lr,

@@ -82,10 +82,10 @@ void comm_gather(const torch::Tensor& peers, const torch::Tensor& flags, int64_t
                  const torch::Tensor& segs, torch::Tensor& local, int64_t max_blocks, double budget_s);
 void topk_threshold(const torch::Tensor& grad, const torch::Tensor& err, c10::optional<torch::Tensor> vel, int64_t lo,
                     int64_t hi, double scale, double mu, int64_t sample, double keep_ratio, int64_t seed,
-                    torch::Tensor& thr_out);
+                    bool masking, torch::Tensor& thr_out);
 void topk_select(const torch::Tensor& grad, torch::Tensor& err, c10::optional<torch::Tensor> vel,
-                 const torch::Tensor& chunks, double scale, double mu, const torch::Tensor& thr, int64_t idx_ptr,
-                 int64_t val_ptr, int64_t cnt_ptr);
+                 const torch::Tensor& chunks, double scale, double mu, bool masking, const torch::Tensor& thr,
+                 int64_t idx_ptr, int64_t val_ptr, int64_t cnt_ptr);
 void topk_reduce(const torch::Tensor& peers, const torch::Tensor& flags, int64_t slot, int64_t epoch, int64_t list_off,
                  int64_t cnt_index, torch::Tensor& red, double scale, int64_t max_blocks, double budget_s);
 }  // namespace br

@@ -377,6 +377,8 @@ __global__ void __launch_bounds__(256) shadow_refresh_kernel(const float* __rest
 //   g = grad * scale + e (+ momentum correction v = mu*v + g, g = v); thr = the floor(S*(1-k))-th
 //   smallest of S sampled |g|; keep |g| >= thr (e = 0) else e = g. Kept entries go on the wire as
 //   (u32 index, f16 value) pairs, appended to the list of the element's owner.
+// masking != 0 (with a velocity) runs the published form instead: u = mu*u + grad*scale, g = e + u,
+// and both e and u are cleared where the entry is sent.
 
 __device__ __forceinline__ uint32_t hash_u32(uint32_t x) {
   x ^= x >> 16;
@@ -391,13 +393,18 @@ __device__ __forceinline__ uint32_t hash_u32(uint32_t x) {
 __global__ void __launch_bounds__(1024) topk_threshold_kernel(const float* __restrict__ grad, const float* __restrict__ err,
                                                               const float* __restrict__ vel, int64_t lo, int64_t hi,
                                                               float scale, float mu, int S, float keep_ratio,
-                                                              uint32_t seed, float* __restrict__ thr_out) {
+                                                              uint32_t seed, int masking, float* __restrict__ thr_out) {
   extern __shared__ float smp[];  // S (power of two)
   const int64_t n = hi - lo;
   for (int i = threadIdx.x; i < S; i += blockDim.x) {
     const int64_t j = lo + (int64_t)(hash_u32(seed ^ (uint32_t)(i * 2654435761u)) % (uint64_t)n);
-    float g = grad[j] * scale + err[j];
-    if (vel) g = mu * vel[j] + g;
+    float g;
+    if (vel && masking) {
+      g = err[j] + (mu * vel[j] + grad[j] * scale);
+    } else {
+      g = grad[j] * scale + err[j];
+      if (vel) g = mu * vel[j] + g;
+    }
     smp[i] = fabsf(g);
   }
   __syncthreads();
@@ -434,7 +441,7 @@ struct SelChunk {
 // counts: this rank's per-(bucket, owner) counters (symmetric memory); idx/val: this rank's lists.
 __global__ void __launch_bounds__(256) topk_select_kernel(const float* __restrict__ grad, float* __restrict__ err,
                                                           float* __restrict__ vel, const SelChunk* __restrict__ chunks,
-                                                          int nchunks, float scale, float mu,
+                                                          int nchunks, float scale, float mu, int masking,
                                                           const float* __restrict__ thr_p, uint32_t* __restrict__ idx,
                                                           __half* __restrict__ val, int* __restrict__ counts) {
   const float thr = *thr_p;
@@ -447,12 +454,19 @@ __global__ void __launch_bounds__(256) topk_select_kernel(const float* __restric
       float g = 0.f;
       const int64_t i = ch.off + j;
       if (j < ch.len) {
-        g = grad[i] * scale + err[i];
-        if (vel) {
-          g = mu * vel[i] + g;
-          vel[i] = g;
+        if (vel && masking) {
+          const float u = mu * vel[i] + grad[i] * scale;
+          g = err[i] + u;
+          keep = fabsf(g) >= thr;
+          vel[i] = keep ? 0.f : u;
+        } else {
+          g = grad[i] * scale + err[i];
+          if (vel) {
+            g = mu * vel[i] + g;
+            vel[i] = g;
+          }
+          keep = fabsf(g) >= thr;
         }
-        keep = fabsf(g) >= thr;
         err[i] = keep ? 0.f : g;
       }
       const unsigned m = __ballot_sync(0xffffffffu, keep);
@@ -638,7 +652,7 @@ void comm_shadow_refresh(const torch::Tensor& params, int64_t push_flags_ptr, in
 namespace br {
 void topk_threshold(const torch::Tensor& grad, const torch::Tensor& err, c10::optional<torch::Tensor> vel, int64_t lo,
                     int64_t hi, double scale, double mu, int64_t sample, double keep_ratio, int64_t seed,
-                    torch::Tensor& thr_out) {
+                    bool masking, torch::Tensor& thr_out) {
   int S = 1;
   while (S < std::min<int64_t>(sample, hi - lo)) S <<= 1;
   TORCH_CHECK(S <= 16384, "topk_threshold: sample size must be <= 16384");
@@ -648,21 +662,22 @@ void topk_threshold(const torch::Tensor& grad, const torch::Tensor& err, c10::op
     C10_CUDA_CHECK(cudaFuncSetAttribute(topk_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
   topk_threshold_kernel<<<1, 1024, sm, at::cuda::getCurrentCUDAStream()>>>(
       grad.data_ptr<float>(), err.data_ptr<float>(), vel.has_value() ? vel->data_ptr<float>() : nullptr, lo, hi,
-      (float)scale, (float)mu, S, (float)keep_ratio, (uint32_t)seed, thr_out.data_ptr<float>());
+      (float)scale, (float)mu, S, (float)keep_ratio, (uint32_t)seed, masking ? 1 : 0, thr_out.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // chunks: int64 [n, 4] = (off, len, list_slot, counter_index)
 void topk_select(const torch::Tensor& grad, torch::Tensor& err, c10::optional<torch::Tensor> vel,
-                 const torch::Tensor& chunks, double scale, double mu, const torch::Tensor& thr, int64_t idx_ptr,
-                 int64_t val_ptr, int64_t cnt_ptr) {
+                 const torch::Tensor& chunks, double scale, double mu, bool masking, const torch::Tensor& thr,
+                 int64_t idx_ptr, int64_t val_ptr, int64_t cnt_ptr) {
   static_assert(sizeof(SelChunk) == 32, "SelChunk layout");
   c10::cuda::CUDAGuard g(grad.device());
   const int n = (int)chunks.size(0);
   if (n == 0) return;
   topk_select_kernel<<<std::min(n, 4 * sm_count()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       grad.data_ptr<float>(), err.data_ptr<float>(), vel.has_value() ? vel->data_ptr<float>() : nullptr,
-      reinterpret_cast<const SelChunk*>(chunks.data_ptr<int64_t>()), n, (float)scale, (float)mu, thr.data_ptr<float>(),
+      reinterpret_cast<const SelChunk*>(chunks.data_ptr<int64_t>()), n, (float)scale, (float)mu, masking ? 1 : 0,
+      thr.data_ptr<float>(),
       reinterpret_cast<uint32_t*>(idx_ptr), reinterpret_cast<__half*>(val_ptr), reinterpret_cast<int*>(cnt_ptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

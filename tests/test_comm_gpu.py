@@ -256,6 +256,53 @@ def test_p2p_trainer_matches_nccl_2gpu():
             assert diff <= (0.25 if adam else 0.1) * moved, (r, n, diff, moved)
 
 
+@pytest.mark.parametrize("masking", [False, True])
+def test_topk_select_momentum_modes_match_oracle(cuda, masking):
+    """Three steps of threshold + select with a velocity, against an fp64 statement of the same update
+    (reference form or the masked DGC form); entries within 1e-5 of the threshold may go either way."""
+    from bitresearch_b200.ops._ext import ext
+    E = ext()
+    n, k, mu = 1 << 16, 0.01, 0.9
+    gen = torch.Generator().manual_seed(3)
+    err = torch.zeros(n, device="cuda")
+    vel = torch.zeros(n, device="cuda")
+    e64 = torch.zeros(n, dtype=torch.float64)
+    v64 = torch.zeros(n, dtype=torch.float64)
+    thr = torch.zeros(1, device="cuda")
+    chunks = torch.tensor([[0, n, 0, 0]], dtype=torch.int64, device="cuda")
+    for step in range(3):
+        g = torch.randn(n, generator=gen)
+        idx = torch.zeros(n, dtype=torch.int32, device="cuda")
+        val = torch.zeros(n, dtype=torch.float16, device="cuda")
+        cnt = torch.zeros(4, dtype=torch.int32, device="cuda")
+        gd = g.cuda()
+        E.topk_threshold(gd, err, vel, 0, n, 1.0, mu, 10000, k, 77 + step, masking, thr)
+        E.topk_select(gd, err, vel, chunks, 1.0, mu, masking, thr, idx.data_ptr(), val.data_ptr(), cnt.data_ptr())
+        torch.cuda.synchronize()
+        t = float(thr.item())
+        g64 = g.double()
+        if masking:
+            u = mu * v64 + g64
+            a = e64 + u
+        else:
+            a = mu * v64 + (g64 + e64)
+            u = a
+        keep = a.abs() >= t
+        sure = (a.abs() - t).abs() > 1e-5 * max(t, 1.0)
+        m = int(cnt[0])
+        sent = torch.zeros(n, dtype=torch.bool)
+        sent[idx[:m].long().cpu()] = True
+        assert m == int(sent.sum())  # no index twice
+        assert torch.equal(sent[sure], keep[sure]), step
+        assert 0.005 < keep.double().mean() < 0.02  # about k from a 10000-sample threshold
+        torch.testing.assert_close(val[:m].float().cpu(), a[idx[:m].long().cpu()].half().float(), rtol=2e-3, atol=1e-4)
+        # carry the kernel's own keep decision into the oracle (borderline entries included)
+        e64 = torch.where(sent, torch.zeros_like(a), a)
+        v64 = torch.where(sent, torch.zeros_like(u), u) if masking else u
+        torch.testing.assert_close(err.cpu().double(), e64, rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(vel.cpu().double(), v64, rtol=1e-5, atol=1e-5)
+
+
 def _topk(rank, world):
     """One bucket of n elements; rank 0 owns the first half, rank 1 the second."""
     from bitresearch_b200.ops._ext import check_status, ext
@@ -271,8 +318,8 @@ def _topk(rank, world):
     flags = SymmetricBuffer(64)
     # list regions: owner 0 at [0, half), owner 1 at [half, n); counters 0 and 1
     chunks = torch.tensor([[0, half, 0, 0], [half, half, half, 1]], dtype=torch.int64, device="cuda")
-    E.topk_threshold(g, err, None, 0, n, 1.0, 0.0, 10000, k, 1234 + rank, thr)
-    E.topk_select(g, err, None, chunks, 1.0, 0.0, thr, idx.ptr, val.ptr, cnt.ptr)
+    E.topk_threshold(g, err, None, 0, n, 1.0, 0.0, 10000, k, 1234 + rank, False, thr)
+    E.topk_select(g, err, None, chunks, 1.0, 0.0, False, thr, idx.ptr, val.ptr, cnt.ptr)
     E.comm_signal(flags.ptr, 5)
     peers = torch.tensor([[idx.peer_ptrs[r], val.peer_ptrs[r], cnt.peer_ptrs[r]] for r in range(world)],
                          dtype=torch.int64, device="cuda")

@@ -31,3 +31,36 @@ def test_momentum_correction_and_codec():
     r = GradientSparsifier.decode(buf)
     assert r.length == 1000 and torch.equal(r.indices, s.indices) and torch.equal(r.values, s.values)
     assert abs(GradientSparsifier.compression_ratio(s) - len(buf) / 4000) < 1e-12
+
+
+def _residual_after(masking, steps=12):
+    sp = GradientSparsifier(top_k_ratio=0.01, warmup_steps=0, sample_size=1000, momentum_factor=0.9, seed=0,
+                            momentum_masking=masking)
+    n = 1000
+    for _ in range(steps):
+        g = torch.full((n,), 1e-3)
+        g[:20] = 1.0  # these fill the top 1% every step, the constant small gradient is never sent
+        sp.sparsify(g)
+    return float(sp.error[20:].abs().max())
+
+
+def test_reference_momentum_residual_grows_geometrically_masked_one_linearly():
+    # reference update: e <- (1 + mu) e + g for an unsent entry; DGC: v grows by u -> g / (1 - mu) per step
+    ref = _residual_after(False)
+    dgc = _residual_after(True)
+    assert ref > 1e-3 * 1.9 ** 11
+    assert dgc < 1e-3 * 12 / (1 - 0.9)
+
+
+def test_momentum_masking_clears_sent_velocity():
+    sp = GradientSparsifier(top_k_ratio=0.1, warmup_steps=0, sample_size=100, momentum_factor=0.5, seed=0,
+                            momentum_masking=True)
+    g = torch.full((100,), 0.01)
+    g[:20] = 1.0  # 20% large entries hold the 10% threshold at 1.0
+    for step in range(2):
+        s = sp.sparsify(g.clone())
+        assert sorted(s.indices.tolist()) == list(range(20))
+        assert (sp.velocity[:20] == 0).all() and (sp.error[:20] == 0).all()
+    # unsent: u1 = 0.01, v1 = 0.01; u2 = 0.5 u1 + 0.01 = 0.015, v2 = v1 + u2 = 0.025
+    assert torch.allclose(sp.velocity[20:], torch.full((80,), 0.015))
+    assert torch.allclose(sp.error[20:], torch.full((80,), 0.025))
