@@ -34,9 +34,21 @@ from ..ops._ext import check_status, ext
 
 
 class FusedGPTEngine:
+    @staticmethod
+    def unsupported(cfg) -> str | None:
+        """Why the sm_100a engine cannot run this model config, or None. Its attention kernels and the
+        QKV epilogue are built for 128-wide heads (every benchmark config has them); other widths train
+        through the eager path (``impl=torch``) on the same GPU."""
+        if cfg.head_dim != 128:
+            return f"head_dim {cfg.head_dim} (n_embd {cfg.n_embd} / n_head {cfg.n_head}); the kernels need 128"
+        return None
+
     def __init__(self, model, grad_views: dict, batch: int, seq: int, flat_grad: torch.Tensor | None = None):
         self.model = model
         self.cfg = cfg = model.cfg
+        why = self.unsupported(cfg)
+        if why is not None:
+            raise ValueError(f"impl=cuda cannot run this model: {why}; use impl=torch")
         self.grads = grad_views
         self.flat_grad = flat_grad
         self.dev = next(model.parameters()).device
