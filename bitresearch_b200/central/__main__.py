@@ -10,6 +10,7 @@ from __future__ import annotations
 import argparse
 import asyncio
 import multiprocessing as mp
+import os
 import sys
 
 
@@ -26,9 +27,10 @@ def _coordinator(args):
 
 def _serve_args(ap):
     ap.add_argument("--host", default="127.0.0.1")
-    ap.add_argument("--port", type=int, default=8787)
+    # PORT and BATCH_SIZE from the environment, as the reference's coordinator reads them (server/index.ts:42-43)
+    ap.add_argument("--port", type=int, default=int(os.environ.get("PORT", "8787")))
     ap.add_argument("--preset", default="ref-default")
-    ap.add_argument("--batch-size", type=int, default=0)
+    ap.add_argument("--batch-size", type=int, default=int(os.environ.get("BATCH_SIZE", "0")))
     ap.add_argument("--data", default="reference", help="reference | zipf | markov | uniform | tokens")
     ap.add_argument("--straggler-timeout", type=float, default=30.0)
     ap.add_argument("--start-delay", type=float, default=2.0)

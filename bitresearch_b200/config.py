@@ -215,6 +215,7 @@ class TrainConfig:
     checkpoint_dir: str = "checkpoints"
     results_tsv: str = "results.tsv"
     metrics_jsonl: str = ""
+    status_port: int = -1  # >= 0: rank 0 serves GET /status and GET /metrics on this port (0 picks one)
     log_every: int = 5
 
     def to_dict(self) -> dict[str, Any]:

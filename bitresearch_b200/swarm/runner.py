@@ -10,7 +10,7 @@ assigned to a worker that exits before reporting them are put back in the queue 
 them assigned, so they would never complete).
 
   python -m bitresearch_b200.swarm [--workers N] [--paths 50000] [--variants config.json]
-                                   [--data val.json] [--out results.json]
+                                   [--data val.json] [--out results.json] [--status-port P]
 """
 from __future__ import annotations
 
@@ -68,6 +68,12 @@ class SwarmQueue:
     def done(self) -> bool:
         return len(self.completed) >= len(self.variants)
 
+    def status(self) -> dict:
+        """Progress in the signalling server's ``swarms`` form (server/signaling.ts:142-151)."""
+        best = self.results[0]["metrics"].get("sharpe") if self.results else None
+        return {"totalVariants": len(self.variants), "completed": len(self.completed), "results": len(self.results),
+                "bestScore": best, "elapsedMs": (time.time() - self.start) * 1e3}
+
 
 def _worker(name: str, device: str | None, data: dict, n_paths: int, seed: int, req_q, work_q, res_q) -> None:
     from .strategy import run_variant
@@ -94,10 +100,26 @@ def _worker(name: str, device: str | None, data: dict, n_paths: int, seed: int, 
 
 
 def run_swarm(variants: list[dict], data: dict, workers: int = 1, n_paths: int = 50_000, seed: int = 0,
-              devices: list[str] | None = None, chunk_size: int = 5, log=print, timeout_s: float = 3600.0) -> list[dict]:
-    """Runs every variant on ``workers`` processes; returns the results sorted by Sharpe (best first)."""
+              devices: list[str] | None = None, chunk_size: int = 5, log=print, timeout_s: float = 3600.0,
+              status_port: int = -1) -> list[dict]:
+    """Runs every variant on ``workers`` processes; returns the results sorted by Sharpe (best first).
+    ``status_port >= 0`` serves the progress at ``GET /status`` and ``GET /metrics`` meanwhile."""
     ctx = mp.get_context("spawn")
     q = SwarmQueue(variants, chunk_size)
+    server = None
+    if status_port >= 0:
+        from ..utils.status import StatusServer
+        t0 = time.time() * 1e3
+
+        def status():
+            peers = [{"id": f"worker-{w}", "room": "swarm", "position": w, "peerType": "compute", "joinedAt": t0}
+                     for w in range(workers)]
+            return {"rooms": ["swarm"], "peers": peers, "ringVersion": 0, "totalPeers": workers,
+                    "computePeers": workers, "observerPeers": 0, "swarms": {"swarm": q.status()}}
+
+        server = StatusServer(status, q.status, port=status_port, prefix="bitresearch_swarm")
+        server.start()
+        log(f"[swarm] status: {server.url}/status")
     req_q, res_q = ctx.Queue(), ctx.Queue()
     work_qs, procs = {}, {}
     devices = devices or [None] * workers
@@ -150,6 +172,8 @@ def run_swarm(variants: list[dict], data: dict, workers: int = 1, n_paths: int =
             p.join(timeout=30)
             if p.is_alive():
                 p.kill()
+        if server is not None:
+            server.stop()
     if not q.done:
         raise TimeoutError(f"swarm finished {len(q.completed)} of {len(variants)} variants before the deadline")
     return q.results
@@ -165,6 +189,7 @@ def main(argv=None) -> int:
     ap.add_argument("--limit", type=int, default=0, help="only the first N variants")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--out", default="")
+    ap.add_argument("--status-port", type=int, default=-1, help=">= 0: serve GET /status and /metrics")
     args = ap.parse_args(argv)
     import torch
     ngpu = torch.cuda.device_count()
@@ -184,7 +209,8 @@ def main(argv=None) -> int:
     else:
         data = synthetic_market(seed=args.seed)
     t0 = time.time()
-    results = run_swarm(variants, data, workers=workers, n_paths=args.paths, seed=args.seed, devices=devices)
+    results = run_swarm(variants, data, workers=workers, n_paths=args.paths, seed=args.seed, devices=devices,
+                        status_port=args.status_port)
     print(f"[swarm] {len(results)} variants in {time.time() - t0:.1f}s on {workers} worker(s)")
     for i, r in enumerate(results[:15]):
         m = r["metrics"]

@@ -102,6 +102,7 @@ class Trainer:
         self.metrics = TrainerMetrics()
         self.total_training_time = 0.0
         self.start_time = 0.0
+        self.status_server = None
         self.running = False
         self.scaler = LossScaler(cfg.dtype == "fp16")
         self.skipped = 0
@@ -367,6 +368,11 @@ class Trainer:
             self.initialize()
         self.running = True
         self.start_time = time.perf_counter()
+        if cfg.status_port >= 0 and self.rank == 0 and self.status_server is None:
+            from .utils.status import StatusServer
+            self.status_server = StatusServer(self.status, lambda: self.metrics.to_dict(), port=cfg.status_port)
+            self.status_server.start()
+            self.log(f"status: {self.status_server.url}/status and /metrics")
         jl = MetricsLog(cfg.metrics_jsonl if self.rank == 0 else "")
         while self.running and self.metrics.step < cfg.max_steps:
             if self.metrics.step > cfg.warmup_steps_excluded and self.total_training_time >= cfg.time_budget:
@@ -402,11 +408,27 @@ class Trainer:
                     f"step {self.metrics.step} | {self.metrics.num_params_m:.1f}M params | depth={cfg.model.n_layer}")
         return self.metrics
 
+    def status(self) -> dict:
+        """The reference's signalling-server status fields (one room, one compute peer per rank, a static
+        ring) with this job's metrics under ``training``."""
+        joined = getattr(self, "_joined_ms", None) or time.time() * 1e3
+        self._joined_ms = joined
+        peers = [{"id": f"rank{r}", "room": "default", "position": r, "peerType": "compute", "joinedAt": joined}
+                 for r in range(self.world)]
+        m = self.metrics.to_dict()
+        m.update(time_budget=self.cfg.time_budget, training_seconds=self.total_training_time,
+                 running=self.running)
+        return {"rooms": ["default"], "peers": peers, "ringVersion": 1, "totalPeers": self.world,
+                "computePeers": self.world, "observerPeers": 0, "swarms": {}, "training": m}
+
     def stop(self) -> None:
         self.running = False
 
     def destroy(self) -> None:
         self.stop()
+        if self.status_server is not None:
+            self.status_server.stop()
+            self.status_server = None
         if self.prefetch is not None:
             self.prefetch.close()
         if self.comm is not None and hasattr(self.comm, "close"):
