@@ -210,6 +210,11 @@ class TrainConfig:
     overlap: bool = True
     sparsify: SparsifyConfig = field(default_factory=SparsifyConfig)
     comm_timeout_s: float = 10.0
+    # ring path only: re-form the ring without a lost rank (store heartbeats + a new gloo group)
+    elastic: bool = False
+    heartbeat_s: float = 2.0  # the reference pings every 2 s (webrtc-mesh.ts:173-196)
+    dead_after_s: float = 10.0  # a peer silent this long is dropped at the next re-formation
+    reform_timeout_s: float = 60.0
     # checkpoints / logging
     checkpoint_interval: int = 0
     checkpoint_dir: str = "checkpoints"

@@ -11,15 +11,21 @@ This replaces the reference's WebSocket signalling server and WebRTC keep-alive:
 * a peer whose heartbeat is older than ``dead_after_s`` is dropped at the next ``form_ring``, the
   equivalent of the server's ``peer-left`` + re-formation (server/signaling.ts:264-295).
 
-Within one NVSwitch node the data path does not depend on the ring (the in-kernel collectives are
-direct), but the trainer uses membership to detect a lost rank between steps and to skip or stop,
-since a NCCL/P2P collective cannot continue with a missing rank.
+``ElasticGroup`` is a gloo process group over the members of one ring version, built from the job's
+store under a per-version prefix. Forming it needs no collective over the old group, so the survivors
+of a lost rank can build it on their own; the trainer's ``elastic`` ring path re-forms this way
+(``Trainer._reform``). The in-kernel NVLink path and NCCL keep a fixed group: a lost rank there ends the
+job with an error at the next collective's timeout.
 """
 from __future__ import annotations
 
+import datetime
 import threading
 import time
 from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
 
 
 @dataclass
@@ -34,8 +40,12 @@ class RingTopology:
 
 class Membership:
     def __init__(self, store, peer_id: str, room: str = "default", heartbeat_s: float = 2.0,
-                 dead_after_s: float = 10.0, peer_type: str = "compute"):
+                 dead_after_s: float = 10.0, peer_type: str = "compute", heartbeat_store=None):
         self.store = store
+        # the heartbeat thread writes through its own store client when given one, so a long blocking
+        # store call of the main thread never delays a beat
+        self.hb_store = heartbeat_store if heartbeat_store is not None else store
+        self.beat_errors = 0
         self.peer_id = peer_id
         self.room = room
         self.heartbeat_s = heartbeat_s
@@ -54,10 +64,11 @@ class Membership:
         self.beat()
         return idx
 
-    def beat(self) -> None:
+    def beat(self, store=None) -> None:
+        store = self.store if store is None else store
         t0 = time.time()
-        self.store.set(self._k("hb", self.peer_id), repr(t0))
-        self.store.get(self._k("hb", self.peer_id))
+        store.set(self._k("hb", self.peer_id), repr(t0))
+        store.get(self._k("hb", self.peer_id))
         rtt = time.time() - t0
         self.smoothed_rtt_s = rtt if self.smoothed_rtt_s == 0 else 0.9 * self.smoothed_rtt_s + 0.1 * rtt
 
@@ -69,9 +80,9 @@ class Membership:
         def run():
             while not self._stop.wait(self.heartbeat_s):
                 try:
-                    self.beat()
-                except Exception:
-                    return
+                    self.beat(self.hb_store)
+                except Exception:  # a transient store error skips one beat; peers tolerate dead_after_s
+                    self.beat_errors += 1
         self._thread = threading.Thread(target=run, daemon=True)
         self._thread.start()
 
@@ -115,3 +126,77 @@ class Membership:
         if self.smoothed_rtt_s <= 0:
             return 10.0
         return max(10.0, 3 * self.smoothed_rtt_s + 5.0)
+
+    def wait_for(self, n: int, timeout_s: float = 60.0) -> RingTopology:
+        """Waits until ``n`` compute peers are registered and alive, then forms the ring."""
+        deadline = time.time() + timeout_s
+        while True:
+            if len(self.alive_peers()) >= n:
+                ring = self.form_ring()
+                if ring is not None and ring.total >= n:
+                    return ring
+            if time.time() > deadline:
+                raise TimeoutError(f"only {len(self.alive_peers())} of {n} peers joined room {self.room!r}")
+            time.sleep(min(0.05, self.heartbeat_s))
+
+    def wait_for_change(self, peers: list[str], timeout_s: float = 60.0) -> RingTopology:
+        """After a failed step: waits until the alive set differs from ``peers`` (the lost peer's heartbeat
+        has aged past ``dead_after_s``), then forms the new ring."""
+        deadline = time.time() + timeout_s
+        while True:
+            alive = self.alive_peers()
+            if alive != sorted(peers) and self.peer_id in alive:
+                ring = self.form_ring()
+                if ring is not None:
+                    return ring
+            if time.time() > deadline:
+                raise TimeoutError(f"ring did not re-form within {timeout_s:.0f} s (alive: {alive})")
+            time.sleep(min(0.1, self.heartbeat_s))
+
+
+def store_client(prefix: str = "bitresearch/elastic", timeout_s: float = 60.0):
+    """A fresh client connection to the job's TCPStore (``MASTER_ADDR:MASTER_PORT``) under ``prefix``."""
+    import os
+    host = os.environ.get("MASTER_ADDR", "127.0.0.1")
+    port = int(os.environ["MASTER_PORT"])
+    raw = dist.TCPStore(host, port, is_master=False, timeout=datetime.timedelta(seconds=timeout_s))
+    return dist.PrefixStore(prefix, raw)
+
+
+class ElasticGroup:
+    """A gloo group over one ring version's members (rank = ring position)."""
+
+    def __init__(self, store, ring: RingTopology, room: str = "default", timeout_s: float = 30.0,
+                 host: str = "127.0.0.1"):
+        opts = dist.ProcessGroupGloo._Options()
+        opts._timeout = datetime.timedelta(seconds=timeout_s)
+        opts._devices = [dist.ProcessGroupGloo.create_device(hostname=host)]
+        self.pg = dist.ProcessGroupGloo(dist.PrefixStore(f"{room}/pg/v{ring.version}", store), ring.position,
+                                        ring.total, opts)
+        self.ring = ring
+        self.rank, self.size, self.version = ring.position, ring.total, ring.version
+        self.timeout_s = timeout_s
+
+    def isend(self, t: torch.Tensor, dst: int):
+        return self.pg.send([t], dst, 0)
+
+    def irecv(self, t: torch.Tensor, src: int):
+        return self.pg.recv([t], src, 0)
+
+    def all_reduce(self, t: torch.Tensor, op=dist.ReduceOp.SUM) -> bool:
+        """In place on a CPU tensor; False if a member is gone (error or timeout)."""
+        o = dist.AllreduceOptions()
+        o.reduceOp = op
+        return self._wait(self.pg.allreduce([t], o))
+
+    def broadcast(self, t: torch.Tensor, root: int = 0) -> bool:
+        o = dist.BroadcastOptions()
+        o.rootRank = root
+        o.rootTensor = 0
+        return self._wait(self.pg.broadcast([t], o))
+
+    def _wait(self, work) -> bool:
+        try:
+            return bool(work.wait(timeout=datetime.timedelta(seconds=self.timeout_s)))
+        except Exception:
+            return False

@@ -32,8 +32,10 @@ _WIRE = {"fp16": torch.float16, "f16": torch.float16, "bf16": torch.bfloat16, "f
 
 
 class RingAllReduce:
-    def __init__(self, group=None, wire_dtype: str = "fp16", timeout_s: float = 10.0, on_progress=None, log=None):
+    def __init__(self, group=None, wire_dtype: str = "fp16", timeout_s: float = 10.0, on_progress=None, log=None,
+                 elastic=None):
         self.group = group
+        self.elastic = elastic  # an ElasticGroup: ranks are ring positions, sends go through its gloo group
         self.wire = _WIRE[wire_dtype]
         self.timeout_s = timeout_s
         self.on_progress = on_progress
@@ -53,15 +55,22 @@ class RingAllReduce:
 
     def all_reduce(self, flat: torch.Tensor, step_id: int = 0) -> torch.Tensor | None:
         """Mean of ``flat`` over the group; ``None`` if aborted. ``flat`` is not modified."""
-        if not dist.is_initialized():
+        if self.elastic is None and not dist.is_initialized():
             return flat.clone()
-        N = dist.get_world_size(self.group)
+        N = self.elastic.size if self.elastic is not None else dist.get_world_size(self.group)
         if N <= 1:
             return flat.clone()
         self.aborted = False
-        r = dist.get_rank(self.group)
-        ranks = dist.get_process_group_ranks(self.group) if self.group is not None else list(range(N))
-        right, left = ranks[(r + 1) % N], ranks[(r - 1) % N]
+        if self.elastic is not None:
+            r = self.elastic.rank
+            right, left = (r + 1) % N, (r - 1) % N
+            isend, irecv = self.elastic.isend, self.elastic.irecv
+        else:
+            r = dist.get_rank(self.group)
+            ranks = dist.get_process_group_ranks(self.group) if self.group is not None else list(range(N))
+            right, left = ranks[(r + 1) % N], ranks[(r - 1) % N]
+            isend = lambda t, d: dist.isend(t, d, group=self.group)  # noqa: E731
+            irecv = lambda t, s: dist.irecv(t, s, group=self.group)  # noqa: E731
         P = flat.numel()
         cs = math.ceil(P / N)
         work = torch.zeros(N * cs, dtype=torch.float32)
@@ -74,9 +83,13 @@ class RingAllReduce:
         def exchange(send_idx: int, recv_idx: int, phase: int) -> torch.Tensor | None:
             hdr_out[0], hdr_out[1], hdr_out[2] = step_id, phase, send_idx
             payload = chunks[send_idx].to(self.wire)
-            reqs = [dist.isend(hdr_out, right, group=self.group), dist.isend(payload, right, group=self.group)]
-            rh = dist.irecv(hdr_in, left, group=self.group)
-            rb = dist.irecv(buf_in, left, group=self.group)
+            try:
+                reqs = [isend(hdr_out, right), isend(payload, right)]
+                rh = irecv(hdr_in, left)
+                rb = irecv(buf_in, left)
+            except Exception as e:  # a closed connection to a lost peer can raise at post time
+                self.log(f"send/recv failed: {e}")
+                return None
             if not (self._wait(rh) and self._wait(rb)):
                 return None
             for q in reqs:

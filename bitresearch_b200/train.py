@@ -103,6 +103,9 @@ class Trainer:
         self.total_training_time = 0.0
         self.start_time = 0.0
         self.status_server = None
+        self.membership = None
+        self.egroup = None  # ElasticGroup of the current ring (elastic ring path)
+        self._comm_failed = False
         self.running = False
         self.scaler = LossScaler(cfg.dtype == "fp16")
         self.skipped = 0
@@ -157,7 +160,10 @@ class Trainer:
             for name, p in self.model.named().items():
                 p.grad = self.grad_views[name]
         if self.world > 1 and cfg.comm == "ring":
-            self.comm = RingAllReduce(wire_dtype=cfg.wire_dtype, timeout_s=cfg.comm_timeout_s, log=self.log)
+            if cfg.elastic:
+                self._init_elastic()
+            self.comm = RingAllReduce(wire_dtype=cfg.wire_dtype, timeout_s=cfg.comm_timeout_s, log=self.log,
+                                      elastic=self.egroup)
         fused_comm = cfg.impl == "cuda" and cfg.comm == "p2p" and self.world > 1
         if cfg.sparsify.enabled and not fused_comm:
             self.sparsifier = GradientSparsifier(cfg.sparsify.top_k_ratio, cfg.sparsify.warmup_steps,
@@ -264,7 +270,10 @@ class Trainer:
             flag = torch.tensor([1.0 if overflow else 0.0], device=self.device)
             if isinstance(self.comm, RingAllReduce):
                 flag = flag.cpu()
-            dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+            if not self._group_all_reduce(flag, dist.ReduceOp.MAX):
+                self.log(f"peer lost at step {self.metrics.step}, skipping optimizer update")
+                self.skipped += 1
+                return False
             overflow = bool(flag.item() > 0)
         self.scaler.update(overflow)
         if overflow:
@@ -282,6 +291,7 @@ class Trainer:
                 if red is None:
                     self.log(f"all-reduce aborted at step {self.metrics.step}, skipping optimizer update")
                     self.skipped += 1
+                    self._comm_failed = self.egroup is not None
                     return False
                 g.copy_(red)
             else:
@@ -340,9 +350,12 @@ class Trainer:
         bpb, nats, nbytes = evaluate_bpb(self.per_token_nats, _Skip(val, self.rank, self.world, B, cfg.model.sequence_len),
                                          self.token_bytes, B, cfg.model.sequence_len, tokens, self.device)
         if self.world > 1:
-            t = torch.tensor([nats, nbytes], dtype=torch.float64, device=self.device if self.is_cuda else "cpu")
-            dist.all_reduce(t)
-            nats, nbytes = float(t[0]), float(t[1])
+            t = torch.tensor([nats, nbytes], dtype=torch.float64,
+                             device=self.device if self.is_cuda and self.egroup is None else "cpu")
+            if self._group_all_reduce(t, dist.ReduceOp.SUM):
+                nats, nbytes = float(t[0]), float(t[1])
+            else:
+                self.log("evaluation sums could not be reduced (peer lost); val_bpb is this rank's share")
             bpb = nats / (math.log(2) * nbytes) if nbytes > 0 else 0.0
         self.metrics.val_bpb = bpb
         if cfg.data == "markov" and self.rank == 0 and "val_bpb_floor" not in self.metrics.extra:
@@ -352,15 +365,80 @@ class Trainer:
         return bpb
 
     # ------------------------------------------------------------------ loop
+    def _group_all_reduce(self, t: torch.Tensor, op) -> bool:
+        """All-reduce over the current group (the elastic ring's gloo group, else the default group);
+        False when a member of the elastic ring is gone."""
+        if self.egroup is not None:
+            ok = self.egroup.all_reduce(t, op)
+            self._comm_failed |= not ok
+            return ok
+        dist.all_reduce(t, op=op)
+        return True
+
     def _agreed_time(self, local_s: float) -> float:
         """The slowest rank's training time, so every rank stops on the same step and follows the
         same learning-rate schedule. Each browser peer of the reference keeps its own clock
         (src/distributed/trainer.ts:986-1005) and its ring tolerates a peer that stops early; here the
         ranks' collectives must stay matched, so the stop decision is collective."""
-        dev = self.device if self.is_cuda and dist.get_backend() == "nccl" else torch.device("cpu")
-        t = torch.tensor([local_s], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        nccl = self.egroup is None and self.is_cuda and dist.get_backend() == "nccl"
+        t = torch.tensor([local_s], dtype=torch.float64, device=self.device if nccl else torch.device("cpu"))
+        if not self._group_all_reduce(t, dist.ReduceOp.MAX):
+            return local_s
         return float(t.item())
+
+    # ------------------------------------------------------------------ elastic ring
+    def _init_elastic(self) -> None:
+        """Registers this rank in the job store's membership room, starts its heartbeat and builds the
+        first ring's gloo group (the reference's ring formation, server/signaling.ts:75-119)."""
+        from .parallel.membership import ElasticGroup, Membership, store_client
+        cfg = self.cfg
+        self._store = store_client()
+        self.membership = Membership(self._store, f"rank{self.rank:05d}", room="train", heartbeat_s=cfg.heartbeat_s,
+                                     dead_after_s=cfg.dead_after_s, heartbeat_store=store_client())
+        self.membership.register()
+        self.membership.start()
+        ring = self.membership.wait_for(self.world, cfg.reform_timeout_s)
+        self.egroup = ElasticGroup(self._store, ring, room="train", timeout_s=cfg.comm_timeout_s)
+
+    def _reform(self) -> None:
+        """After a step that lost a peer: wait until membership drops it, form the smaller ring with its
+        own gloo group and re-sync the state from the new position 0. The reference re-forms on the
+        server's ``peer-left`` (server/signaling.ts:264-295, trainer.ts:654-668); its ranks may keep
+        different weights when some completed the aborted step, which the re-sync removes."""
+        from .parallel.membership import ElasticGroup
+        cfg = self.cfg
+        old = self.egroup.ring.peers
+        self.log(f"peer lost at step {self.metrics.step}; re-forming the ring of {len(old)}")
+        ring = self.membership.wait_for_change(old, cfg.reform_timeout_s)
+        self.egroup = ElasticGroup(self._store, ring, room="train", timeout_s=cfg.comm_timeout_s)
+        self.comm = RingAllReduce(wire_dtype=cfg.wire_dtype, timeout_s=cfg.comm_timeout_s, log=self.log,
+                                  elastic=self.egroup)
+        self.rank, self.world = ring.position, ring.total
+        self._resync()
+        self._comm_failed = False
+        self.log(f"ring re-formed: version {ring.version}, {ring.total} peers {ring.peers}")
+
+    def _resync(self) -> None:
+        """Broadcasts weights, optimizer state and loss scale from ring position 0."""
+        g = self.egroup
+        if g.rank == 0:
+            tensors, meta = self.checkpoint_state()
+            buf = ckpt.to_bytes(tensors, meta)
+            n = torch.tensor([len(buf)], dtype=torch.int64)
+        else:
+            n = torch.zeros(1, dtype=torch.int64)
+        if not g.broadcast(n):
+            raise RuntimeError("state re-sync failed (size)")
+        data = (torch.frombuffer(bytearray(buf), dtype=torch.uint8) if g.rank == 0
+                else torch.empty(int(n.item()), dtype=torch.uint8))
+        if not g.broadcast(data):
+            raise RuntimeError("state re-sync failed (payload)")
+        if g.rank != 0:
+            tensors, meta = ckpt.from_bytes(data.numpy().tobytes())
+            info = ckpt.restore(self.model, tensors, meta, self.optimizer, log=self.log)
+            self.scaler.scale = float(info.get("lossScale", self.scaler.scale) or self.scaler.scale)
+            if self.engine is not None:
+                self.engine.refresh_shadows()
 
     def start_training(self) -> TrainerMetrics:
         cfg = self.cfg
@@ -383,8 +461,10 @@ class Trainer:
             dt = time.perf_counter() - t0
             if self.metrics.step > cfg.warmup_steps_excluded:
                 self.total_training_time += dt
-            if self.world > 1:
+            if self.world > 1 and not self._comm_failed:
                 self.total_training_time = self._agreed_time(self.total_training_time)
+            if self._comm_failed and self.egroup is not None:
+                self._reform()
             m = self.metrics
             if cfg.log_every and m.step % cfg.log_every == 0:
                 lrm = lr_multiplier(min(self.total_training_time / cfg.time_budget, 1), cfg.warmup_ratio,
@@ -426,6 +506,9 @@ class Trainer:
 
     def destroy(self) -> None:
         self.stop()
+        if self.membership is not None:
+            self.membership.leave()
+            self.membership = None
         if self.status_server is not None:
             self.status_server.stop()
             self.status_server = None

@@ -1,0 +1,55 @@
+"""Failure detection and elastic recovery on CPU gloo ranks (no GPU involved): a rank that crashes
+between steps stops its heartbeat; the survivors' next collective fails, the step's update is skipped,
+they wait until membership drops the lost peer, form a smaller ring with a new gloo group, re-sync the
+state from the new position 0 and finish the run with identical weights."""
+import numpy as np
+
+from dist_utils import run_world
+from bitresearch_b200.config import apply_overrides, preset
+from bitresearch_b200.train import Trainer
+
+
+class _Crash(Exception):
+    pass
+
+
+def _elastic(rank, world, crash_rank, crash_after):
+    cfg = apply_overrides(preset("tiny-cpu"), [
+        "model.n_layer=1", "model.n_embd=64", "model.n_head=1", "model.n_kv_head=1", "model.sequence_len=32",
+        "model.vocab_size=128", "device_batch=2", f"total_batch_tokens={64 * world}", "eval_tokens=128",
+        "log_every=0", "results_tsv=", "max_steps=8", "time_budget=1e9", "comm=ring", "elastic=true",
+        "heartbeat_s=0.2", "dead_after_s=1.5", "comm_timeout_s=4", "reform_timeout_s=60"])
+    logs = []
+    tr = Trainer(cfg, device="cpu", log=logs.append)
+    tr.initialize()
+    if rank == crash_rank:
+        step = tr.train_step
+
+        def crashing(*a, **k):
+            if tr.metrics.step >= crash_after:
+                raise _Crash()
+            return step(*a, **k)
+
+        tr.train_step = crashing
+        try:
+            tr.start_training()
+        except _Crash:
+            tr.membership.stop()  # no graceful leave: the heartbeat just stops
+            tr.egroup.pg.abort()
+            return {"crashed_at": tr.metrics.step}
+    m = tr.start_training()
+    params = np.concatenate([v.detach().numpy().ravel() for v in tr.model.named().values()])
+    tr.destroy()
+    return {"step": m.step, "world": tr.world, "rank": tr.rank, "skipped": m.skipped_steps, "params": params,
+            "logs": logs, "val_bpb": m.val_bpb}
+
+
+def test_survivors_reform_the_ring_and_finish_in_lockstep():
+    r0, r1, r2 = run_world(_elastic, 3, 2, 3, timeout=180)
+    assert r2 == {"crashed_at": 3}
+    for r in (r0, r1):
+        assert r["step"] == 8 and r["world"] == 2 and r["skipped"] == 1, {k: r[k] for k in ("step", "world", "skipped")}
+        assert np.isfinite(r["val_bpb"]) and r["val_bpb"] > 0
+    assert (r0["rank"], r1["rank"]) == (0, 1)
+    assert np.array_equal(r0["params"], r1["params"])
+    assert any("ring re-formed: version 2, 2 peers" in line for line in r0["logs"]), r0["logs"]
