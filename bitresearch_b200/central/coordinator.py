@@ -128,8 +128,10 @@ class Coordinator:
                     rng.integers(0, V, size=(B, T), dtype=np.int32))
         src = self._sources.get(slot)
         if src is None:
+            import copy
+
             from ..data.pipeline import make_batch_source
-            tc = self.train_cfg
+            tc = copy.deepcopy(self.train_cfg)
             tc.data = self.cfg.data
             src = self._sources[slot] = make_batch_source(tc, "train", slot, 1)
         x, y = src.next(B, T)

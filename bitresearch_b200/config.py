@@ -188,7 +188,8 @@ class TrainConfig:
     eval_tokens: int = 40 * 524288
     val_fraction: float = 0.1
     # data: "zipf" (BOS-packed Zipf docs), "markov" (Zipf docs whose tokens follow hashed order-1 /
-    # order-2 successor tables), "uniform" (uniform + BOS every 64), "tokens" (a .bin file)
+    # order-2 successor tables), "uniform" (uniform + BOS every 64), "tokens" (.bin shards, a manifest,
+    # or a .json token list), "documents" (a .json list of token arrays, best-fit BOS packed)
     data: str = "zipf"
     data_path: str = ""
     token_bytes_path: str = ""
@@ -200,6 +201,8 @@ class TrainConfig:
     token_bytes_max: int = 16
     bos_every: int = 64
     document_buffer_size: int = 1000
+    documents_bos_prefixed: bool = False  # data=documents: the documents already start with BOS
+    bos_token_id: int = -1  # data=documents: -1 = vocab_size - 1
     # compute
     impl: str = "cuda"  # "cuda" (sm_100a kernels) or "torch" (eager oracle path)
     dtype: str = "bf16"

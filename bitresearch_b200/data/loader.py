@@ -43,13 +43,20 @@ def load_token_bytes(path: str, vocab_size: int) -> np.ndarray:
 TOKEN_BYTES_NAMES = ("token_bytes.bin", "token-bytes.bin", "token_bytes.json")
 
 
+def is_manifest(path: str) -> bool:
+    """A parity manifest is a JSON object with a ``files`` entry; a token or document payload is not."""
+    with open(path, "rb") as f:
+        head = f.read(1 << 16).decode("utf-8", "ignore")
+    return head.lstrip().startswith("{") and '"files"' in head
+
+
 def find_manifest(path: str) -> str | None:
     """A manifest.json: ``path`` itself, or ``path/manifest.json``, or ``path/parity/manifest.json``."""
     import os
     if not path:
         return None
     if os.path.isfile(path) and path.endswith(".json"):
-        return path
+        return path if is_manifest(path) else None
     if os.path.isdir(path):
         for rel in ("manifest.json", os.path.join("parity", "manifest.json")):
             cand = os.path.join(path, rel)
@@ -107,6 +114,27 @@ def load_token_data(path: str) -> np.ndarray:
             return load_tokens_bin(cand)
         raise FileNotFoundError(f"{path}: no manifest.json, parity/manifest.json or tokens.bin")
     return load_tokens_bin(path)
+
+
+def load_json_payload(path: str) -> tuple[str, object]:
+    """A JSON data file as ``("tokens", int32 array)`` or ``("documents", [int32 arrays])``: a flat list
+    of ids is a token stream, a list of lists is documents, ``{"documents": [...]}`` or ``{"tokens": [...]}``
+    name their shape (the reference's 'auto' format detection, src/data/dataloader.ts:40-61, 140-170)."""
+    import json
+    with open(path) as f:
+        payload = json.load(f)
+    if isinstance(payload, dict):
+        if isinstance(payload.get("documents"), list):
+            payload = payload["documents"]
+        elif isinstance(payload.get("tokens"), list):
+            return "tokens", np.asarray(payload["tokens"], dtype=np.int32)
+        else:
+            raise ValueError(f"{path}: unsupported JSON data shape; expected tokens or documents")
+    if not isinstance(payload, list):
+        raise ValueError(f"{path}: unsupported JSON data shape; expected tokens or documents")
+    if payload and all(isinstance(d, list) for d in payload):
+        return "documents", [np.asarray(d, dtype=np.int32) for d in payload]
+    return "tokens", np.asarray(payload, dtype=np.int32)
 
 
 def discover_token_bytes(path: str) -> str:

@@ -20,7 +20,7 @@ import numpy as np
 import torch
 
 from ..config import TrainConfig
-from .loader import BestFitDocumentBatcher, TokenDataLoader, load_token_data
+from .loader import BestFitDocumentBatcher, TokenDataLoader, find_manifest, load_json_payload, load_token_data
 from .synthetic import UniformBOSStream, ZipfDocumentSource, bos_id
 
 
@@ -93,6 +93,37 @@ class _Uniform:
         return rows[:, :seq].copy(), rows[:, 1:].copy()
 
 
+class _Documents:
+    """A finite document list, best-fit BOS packed (natively when the data module is built), cycled with
+    an epoch counter like the reference's document loader (src/data/dataloader.ts:194-206)."""
+
+    def __init__(self, docs: list, bos: int, buffer_size: int, prefixed: bool):
+        if not docs:
+            raise ValueError("no documents in this split")
+        mod = _native()
+        self.mod = mod
+        if mod is not None:
+            flat = np.concatenate(docs).astype(np.int32) if docs else np.zeros(0, np.int32)
+            offs = np.zeros(len(docs) + 1, dtype=np.int64)
+            np.cumsum([len(d) for d in docs], out=offs[1:])
+            self.p = mod.corpus_packer(bos, buffer_size, flat, offs, prefixed)
+            self.b = None
+        else:
+            self.b = BestFitDocumentBatcher(docs, bos, buffer_size, documents_are_bos_prefixed=prefixed)
+
+    @property
+    def epoch(self):
+        return self.p.epoch if self.b is None else self.b.epoch
+
+    def next(self, batch: int, seq: int):
+        if self.b is not None:
+            x, y, _ = self.b.next_batch(batch, seq)
+            return x, y
+        rows = np.empty((batch, seq + 1), np.int32)
+        self.mod.pack_rows(self.p, rows, batch, seq)
+        return rows[:, :seq], rows[:, 1:]
+
+
 class _Tokens:
     def __init__(self, tokens: np.ndarray):
         self.l = TokenDataLoader(tokens)
@@ -117,8 +148,22 @@ def make_batch_source(cfg: TrainConfig, split: str = "train", rank: int = 0, wor
         return _ZipfNative(cfg, seed)
     if cfg.data == "uniform":
         return _Uniform(cfg, seed)
-    if cfg.data == "tokens":
-        toks = load_token_data(cfg.data_path)
+    if cfg.data in ("tokens", "documents"):
+        json_payload = cfg.data_path.endswith(".json") and find_manifest(cfg.data_path) is None
+        kind, payload = (load_json_payload(cfg.data_path) if json_payload
+                         else ("tokens", load_token_data(cfg.data_path)))
+        if cfg.data == "documents" and kind != "documents":
+            raise ValueError(f"{cfg.data_path}: data=documents needs a list of token arrays")
+        if kind == "documents":  # split by document count (src/data/dataloader.ts:269-278)
+            docs = payload
+            split_at = int(len(docs) * (1 - cfg.val_fraction))
+            part = docs[:split_at] if split == "train" else docs[split_at:]
+            if split == "train" and world > 1:
+                n = len(part) // world
+                part = part[rank * n:(rank + 1) * n]
+            bos = cfg.bos_token_id if cfg.bos_token_id >= 0 else cfg.model.vocab_size - 1
+            return _Documents(part, bos, cfg.document_buffer_size, cfg.documents_bos_prefixed)
+        toks = payload
         split_at = int(len(toks) * (1 - cfg.val_fraction))
         part = toks[:split_at] if split == "train" else toks[split_at:]
         if split == "train" and world > 1:  # contiguous per-rank shards of the training stream

@@ -181,7 +181,7 @@ class Trainer:
             self.engine.attach_optimizer(self.optimizer)
         # data
         self.train_source = make_batch_source(cfg, "train", self.rank, self.world)
-        if cfg.data == "tokens":
+        if cfg.data in ("tokens", "documents"):
             # explicit table, else the one the manifest / data directory provides, else all ones (the
             # reference's avgBytesPerToken = 1 fallback)
             tb_path = cfg.token_bytes_path or discover_token_bytes(cfg.data_path)

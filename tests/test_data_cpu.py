@@ -155,3 +155,39 @@ def test_markov_nll_matches_sampled_frequencies():
             checked += 1
         assert abs(sum(q[sel & (nxt == x)][0] for x in np.unique(nxt[sel])) - 1.0) < 1e-9
     assert checked > 10
+
+
+def test_json_documents_and_tokens_payloads(tmp_path):
+    import json
+    from bitresearch_b200.config import apply_overrides
+    from bitresearch_b200.data.loader import find_manifest, load_json_payload
+    rng = np.random.default_rng(0)
+    docs = [rng.integers(0, 100, size=int(rng.integers(3, 40))).tolist() for _ in range(50)]
+    p = tmp_path / "docs.json"
+    p.write_text(json.dumps({"documents": docs}))
+    kind, got = load_json_payload(str(p))
+    assert kind == "documents" and len(got) == 50 and got[3].tolist() == docs[3]
+    assert find_manifest(str(p)) is None  # a payload is not a manifest
+    t = tmp_path / "toks.json"
+    t.write_text(json.dumps(list(range(300))))
+    assert load_json_payload(str(t))[0] == "tokens"
+    for prefixed in (False, True):
+        d = [[127] + x for x in docs] if prefixed else docs
+        p.write_text(json.dumps(d))
+        cfg = apply_overrides(preset("tiny-cpu"), ["data=documents", f"data_path={p}", "model.vocab_size=128",
+                                                   f"documents_bos_prefixed={str(prefixed).lower()}"])
+        src = make_batch_source(cfg, "train", 0, 1)
+        x, y = src.next(4, 32)
+        assert (x[:, 0] == 127).all()  # every row starts with BOS
+        assert np.array_equal(x[:, 1:], y[:, :-1])
+        # rows are made of whole (or cropped) training documents: the first one follows the first BOS
+        train = docs[:45]
+        first = x[0, 1:1 + len(train[0])].tolist()
+        assert any(first == dd[:len(first)] for dd in train)
+        val = make_batch_source(cfg, "val", 0, 1)
+        vx, _ = val.next(1, 16)
+        assert vx[0, 0] == 127
+    # data=tokens with a .json token list
+    cfg = apply_overrides(preset("tiny-cpu"), ["data=tokens", f"data_path={t}"])
+    x, y = make_batch_source(cfg, "train", 0, 1).next(2, 8)
+    assert x[0].tolist() == list(range(8)) and y[0].tolist() == list(range(1, 9))
