@@ -580,13 +580,46 @@ class _Skip:
         return self.src.next(B, T)
 
 
+def _launch_peers(n: int, argv: list[str]) -> int:
+    """Re-runs this CLI as ``n`` local ranks through torch.distributed.run on 127.0.0.1 (the reference's
+    launcher opens N browser tabs, scripts/launch.ts:83-182)."""
+    import socket
+    import subprocess
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr=127.0.0.1", f"--master-port={port}", "-m", "bitresearch_b200.train", *argv]
+    return subprocess.call(cmd)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description="bitresearch-b200 data-parallel GPT trainer")
     ap.add_argument("--preset", default="d512")
     ap.add_argument("--resume", default="")
+    # the reference launcher's flags (scripts/launch.ts:13-23); the same settings as key=value work too
+    ap.add_argument("--peers", type=int, default=0, help="launch N local ranks (one per GPU) and train on all")
+    ap.add_argument("--max-steps", type=int, default=0)
+    ap.add_argument("--max-seconds", "--timeout", dest="max_seconds", type=float, default=0.0,
+                    help="training time budget in seconds")
     ap.add_argument("overrides", nargs="*", help="key=value config overrides (e.g. max_steps=100 model.n_layer=4)")
-    args = ap.parse_args(argv)
-    cfg = apply_overrides(preset(args.preset), args.overrides)
+    raw = list(sys.argv[1:] if argv is None else argv)
+    args = ap.parse_args(raw)
+    if args.peers > 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        rest, skip = [], False
+        for a in raw:  # drop --peers N / --peers=N, keep everything else for the ranks
+            if skip:
+                skip = False
+                continue
+            if a == "--peers":
+                skip = True
+                continue
+            if not a.startswith("--peers="):
+                rest.append(a)
+        return _launch_peers(args.peers, rest)
+    extra = ([f"max_steps={args.max_steps}"] if args.max_steps else []) + (
+        [f"time_budget={args.max_seconds}"] if args.max_seconds else [])
+    cfg = apply_overrides(preset(args.preset), list(args.overrides) + extra)
     rank, world, local = init_distributed("nccl" if torch.cuda.is_available() and cfg.impl != "cpu" else "gloo")
     if not torch.cuda.is_available():
         cfg.impl = "torch"

@@ -107,3 +107,15 @@ def test_checkpoint_resume_reproduces_trajectory(tmp_path):
     np.testing.assert_allclose(la, lb, rtol=0, atol=0)
     for n, p in a.model.named().items():
         assert torch.equal(p, b.model.named()[n]), n
+
+
+def test_cli_peers_launches_ranks(tmp_path):
+    import os
+    import subprocess
+    import sys
+    out = subprocess.run([sys.executable, "-m", "bitresearch_b200.train", "--preset", "tiny-cpu", "--peers", "2",
+                          "--max-steps", "2", "comm=ring", "eval_tokens=512", "results_tsv=", "log_every=1",
+                          "model.n_layer=1"], capture_output=True, text=True, timeout=240,
+                         cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert "world=2" in out.stdout and "num_steps:        2" in out.stdout and "peers=2" in out.stdout
