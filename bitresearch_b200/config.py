@@ -224,6 +224,9 @@ class TrainConfig:
     results_tsv: str = "results.tsv"
     metrics_jsonl: str = ""
     status_port: int = -1  # >= 0: rank 0 serves GET /status and GET /metrics on this port (0 picks one)
+    trace_phases: bool = False  # CUDA-event + NVTX phases (data, forward, backward, sync, optimizer) per step
+    profile_steps: str = ""  # "a:b": torch.profiler over steps [a, b), Chrome trace into profile_dir
+    profile_dir: str = "traces"
     log_every: int = 5
 
     def to_dict(self) -> dict[str, Any]:

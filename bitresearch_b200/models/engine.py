@@ -31,6 +31,7 @@ import torch
 from ..config import effective_window, has_value_embedding
 from ..ops import gemm
 from ..ops._ext import check_status, ext
+from ..utils.timing import traced
 
 
 class FusedGPTEngine:
@@ -49,6 +50,7 @@ class FusedGPTEngine:
         why = self.unsupported(cfg)
         if why is not None:
             raise ValueError(f"impl=cuda cannot run this model: {why}; use impl=torch")
+        self.timer = None  # a PhaseTimer: forward / backward as CUDA-event phases with NVTX ranges
         self.grads = grad_views
         self.flat_grad = flat_grad
         self.dev = next(model.parameters()).device
@@ -249,10 +251,13 @@ class FusedGPTEngine:
             else:
                 for g in self.grads.values():
                     g.zero_()
-        self._forward(idx, b, B)
-        b["loss"].zero_()
-        self.E.softcap_ce(b["logits"], targets.reshape(-1), 15.0, loss_scale / (B * self.T), b["nats"], b["loss"], True)
-        self._backward(idx, b, B)
+        with traced(self.timer, "forward"):
+            self._forward(idx, b, B)
+            b["loss"].zero_()
+            self.E.softcap_ce(b["logits"], targets.reshape(-1), 15.0, loss_scale / (B * self.T), b["nats"], b["loss"],
+                              True)
+        with traced(self.timer, "backward"):  # includes the bucket hooks that launch the gradient reduce
+            self._backward(idx, b, B)
         return b["loss"][0] / loss_scale
 
     @torch.no_grad()

@@ -46,6 +46,7 @@ from .optim.muon_adamw import MuonAdamW, lr_multiplier, muon_momentum, weight_de
 from .parallel.comm import flat_layout
 from .parallel.ring import RingAllReduce
 from .parallel.sparsify import GradientSparsifier
+from .utils.timing import traced
 from .utils.logging import MetricsLog, ResultsLogger, TrainerMetrics, summary_block
 
 B200_BF16_PEAK_FLOPS = 1630e12  # measured cuBLAS bf16 burst on this hardware (H100: 989.5e12, trainer.ts:102)
@@ -104,6 +105,9 @@ class Trainer:
         self.start_time = 0.0
         self.status_server = None
         self.membership = None
+        self.timer = None  # PhaseTimer when trace_phases is on
+        self.phase_ms: dict[str, float] = {}
+        self._profiler = None
         self.egroup = None  # ElasticGroup of the current ring (elastic ring path)
         self._comm_failed = False
         self.running = False
@@ -179,6 +183,11 @@ class Trainer:
             shadows=self.engine.shadows if self.engine is not None else None)
         if self.engine is not None:
             self.engine.attach_optimizer(self.optimizer)
+        if cfg.trace_phases and self.is_cuda:
+            from .utils.timing import PhaseTimer
+            self.timer = PhaseTimer()
+            if self.engine is not None:
+                self.engine.timer = self.timer
         # data
         self.train_source = make_batch_source(cfg, "train", self.rank, self.world)
         if cfg.data in ("tokens", "documents"):
@@ -228,20 +237,28 @@ class Trainer:
         if self.comm is not None and hasattr(self.comm, "begin_step"):
             self.comm.begin_step()
         for self._micro in range(self.grad_accum):
-            if batch is None:
-                x, y = self.next_batch()
-            elif isinstance(batch, list):
-                x, y = batch[self._micro]
+            with traced(self.timer, "data"):
+                if batch is None:
+                    x, y = self.next_batch()
+                elif isinstance(batch, list):
+                    x, y = batch[self._micro]
+                else:
+                    x, y = batch
+            if self.engine is None:
+                with traced(self.timer, "forward_backward"):
+                    losses.append(self._forward_backward(x, y, scale))
             else:
-                x, y = batch
-            losses.append(self._forward_backward(x, y, scale))
+                losses.append(self._forward_backward(x, y, scale))
         loss_t = losses[0].float() if len(losses) == 1 else torch.stack(losses).float().mean()
         t_compute = time.perf_counter()
-        ok = self._sync_and_update(progress, scale)
+        with traced(self.timer, "sync_update"):  # gradient sync tail, optimizer, parameter exchange
+            ok = self._sync_and_update(progress, scale)
         if not sync:
             self.metrics.step += 1
             return loss_t
         loss = float(loss_t)  # device -> host read of the step result
+        if self.timer is not None:
+            self.phase_ms = self.timer.collect()
         if self.engine is not None:
             st = self.engine.status()
             if st:
@@ -365,6 +382,27 @@ class Trainer:
         return bpb
 
     # ------------------------------------------------------------------ loop
+    def _profile_tick(self) -> None:
+        """torch.profiler over steps [a, b) of ``profile_steps="a:b"``; writes a Chrome trace per rank.
+        Timings read under the profiler are not benchmark numbers."""
+        spec = self.cfg.profile_steps
+        if not spec:
+            return
+        a, b = (int(v) for v in spec.split(":"))
+        step = self.metrics.step
+        if step == a and self._profiler is None:
+            acts = [torch.profiler.ProfilerActivity.CPU] + (
+                [torch.profiler.ProfilerActivity.CUDA] if self.is_cuda else [])
+            self._profiler = torch.profiler.profile(activities=acts, record_shapes=False)
+            self._profiler.__enter__()
+        elif step == b and self._profiler is not None:
+            self._profiler.__exit__(None, None, None)
+            os.makedirs(self.cfg.profile_dir, exist_ok=True)
+            path = os.path.join(self.cfg.profile_dir, f"trace_rank{self.rank}_steps{a}-{b}.json")
+            self._profiler.export_chrome_trace(path)
+            self._profiler = None
+            self.log(f"profiler trace: {path}")
+
     def _group_all_reduce(self, t: torch.Tensor, op) -> bool:
         """All-reduce over the current group (the elastic ring's gloo group, else the default group);
         False when a member of the elastic ring is gone."""
@@ -472,8 +510,14 @@ class Trainer:
                 self.log(f"Step {m.step} | loss={loss:.6f} | smooth={m.smooth_loss:.6f} | grad={m.grad_norm:.4f} | "
                          f"lrm={lrm:.2f} | {m.tokens_per_sec:.0f} tok/s | peers={m.peers_connected} | "
                          f"{m.elapsed_seconds:.0f}s")
-            jl.write({"step": m.step, "loss": loss, "smooth_loss": m.smooth_loss, "tokens_per_sec": m.tokens_per_sec,
-                      "step_ms": m.step_time_ms, "all_reduce_ms": m.all_reduce_time_ms, "mfu": m.mfu_percent})
+            rec = {"step": m.step, "loss": loss, "smooth_loss": m.smooth_loss, "tokens_per_sec": m.tokens_per_sec,
+                   "step_ms": m.step_time_ms, "all_reduce_ms": m.all_reduce_time_ms, "mfu": m.mfu_percent}
+            if self.phase_ms:
+                rec["phases_ms"] = self.phase_ms
+                if cfg.log_every and m.step % cfg.log_every == 0:
+                    self.log("phases: " + " | ".join(f"{k} {v:.2f} ms" for k, v in self.phase_ms.items()))
+            jl.write(rec)
+            self._profile_tick()
             if cfg.checkpoint_interval > 0 and m.step % cfg.checkpoint_interval == 0:
                 self.save_checkpoint()
         self.log("running final BPB evaluation")

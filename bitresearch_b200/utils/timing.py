@@ -47,6 +47,21 @@ class PhaseTimer:
 
 
 @contextlib.contextmanager
+def traced(timer: "PhaseTimer | None", name: str):
+    """One phase: an NVTX range (seen by Nsight / torch.profiler) and, with a timer, CUDA events on the
+    current stream. A no-op without a timer."""
+    if timer is None or not timer.enabled:
+        yield
+        return
+    torch.cuda.nvtx.range_push(name)
+    try:
+        with timer.phase(name):
+            yield
+    finally:
+        torch.cuda.nvtx.range_pop()
+
+
+@contextlib.contextmanager
 def nvtx(name: str):
     if torch.cuda.is_available():
         torch.cuda.nvtx.range_push(name)

@@ -119,3 +119,24 @@ def test_cli_peers_launches_ranks(tmp_path):
                          cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     assert out.returncode == 0, out.stderr[-2000:]
     assert "world=2" in out.stdout and "num_steps:        2" in out.stdout and "peers=2" in out.stdout
+
+
+def test_profiler_hook_writes_a_chrome_trace(tmp_path):
+    import json
+    cfg = _cfg(max_steps=4, time_budget=1e9, profile_steps="1:3", profile_dir=str(tmp_path))
+    tr = Trainer(cfg, device="cpu", log=lambda m: None)
+    tr.initialize()
+    tr.start_training()
+    path = tmp_path / "trace_rank0_steps1-3.json"
+    assert path.exists()
+    ev = json.loads(path.read_text())
+    assert len(ev["traceEvents"]) > 10
+
+
+def test_same_seed_replays_bitwise_on_cpu():
+    def run():
+        tr = Trainer(_cfg(max_steps=5), device="cpu", log=lambda m: None)
+        tr.initialize()
+        return [float(tr.train_step()) for _ in range(5)]
+
+    assert run() == run()
