@@ -13,7 +13,7 @@
 from __future__ import annotations
 
 from collections import deque
-from typing import Callable, Iterable, Sequence
+from typing import Callable, Sequence
 
 import numpy as np
 

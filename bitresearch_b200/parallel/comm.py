@@ -23,7 +23,6 @@ NVSwitch node with a direct algorithm:
 """
 from __future__ import annotations
 
-import math
 from collections import OrderedDict
 
 import numpy as np

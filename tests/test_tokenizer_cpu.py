@@ -6,7 +6,6 @@ import os
 import random
 
 import numpy as np
-import pytest
 
 from bitresearch_b200.data.loader import discover_token_bytes, find_manifest, load_token_data, manifest_artifacts
 from bitresearch_b200.data.tokenizer import SPECIAL_TOKENS, BPETokenizer
