@@ -65,3 +65,38 @@ def test_per_token_reduction_and_mask():
     mean = m.forward_torch(idx, tgt)
     valid = (tgt != -1).float()
     assert torch.allclose((nats * valid).sum() / nats.numel(), mean, atol=1e-6)
+
+
+def test_oracle_gradients_match_finite_differences():
+    """Central differences of the fp64 oracle's loss against its autograd gradients, for sampled entries of
+    every parameter (GQA, a short-window layer, a value-embedding layer, masked targets). The oracle's
+    gradients are the ones the eager path is held to above, and the eager path is what the fused engine's
+    hand-written backward is compared with on the GPU."""
+    cfg = GPTConfig(sequence_len=8, vocab_size=48, n_layer=2, n_head=2, n_kv_head=1, n_embd=32, window_pattern="SL")
+    m = _model(cfg, seed=3)
+    P = {n: p.detach().double().clone().requires_grad_(True) for n, p in m.named().items()}
+    g = torch.Generator().manual_seed(5)
+    idx = torch.randint(0, cfg.vocab_size, (2, 8), generator=g)
+    tgt = torch.randint(0, cfg.vocab_size, (2, 8), generator=g)
+    tgt[1, :2] = -1
+    _, loss = reference_forward(P, cfg, idx, tgt)
+    loss.backward()
+    eps, checked = 1e-6, 0
+    with torch.no_grad():
+        for n, p in P.items():
+            flat = p.view(-1)
+            grad = p.grad.view(-1)
+            picks = torch.randperm(flat.numel(), generator=g)[:4].tolist()
+            if n in ("wte", "lmHead") or n.startswith("ve_"):  # rows the batch touches carry the gradient
+                picks += torch.nonzero(grad).view(-1)[:3].tolist()
+            for j in picks:
+                old = flat[j].item()
+                flat[j] = old + eps
+                lp = reference_forward(P, cfg, idx, tgt)[1].item()
+                flat[j] = old - eps
+                lm = reference_forward(P, cfg, idx, tgt)[1].item()
+                flat[j] = old
+                fd = (lp - lm) / (2 * eps)
+                assert abs(fd - grad[j].item()) <= 1e-7 + 1e-5 * abs(fd), (n, j, fd, grad[j].item())
+                checked += 1
+    assert checked >= 4 * len(P)
