@@ -47,3 +47,57 @@ def evaluate_bpb(per_token_nats_fn, batch_source, token_bytes: np.ndarray, batch
         total_bytes += nbytes.sum().double()
     n, b = float(total_nats), float(total_bytes)
     return bpb_from_sums(n, b), n, b
+
+
+def _config_from_checkpoint(path: str):
+    """The TrainConfig stored in a checkpoint's ``trainConfig`` metadata, or None (reference checkpoints
+    store only the model config)."""
+    import json
+
+    from . import checkpoint as ckpt
+    from .config import TrainConfig
+    _, meta = ckpt.load(path)
+    raw = meta.get("trainConfig")
+    if not raw:
+        return None
+    d = json.loads(raw)
+    if isinstance(d, str):
+        d = json.loads(d)
+    return TrainConfig.from_dict(d)
+
+
+def main(argv=None) -> int:
+    """``python -m bitresearch_b200.eval --checkpoint PATH [--preset P] [key=value ...]``: loads a checkpoint
+    and prints its ``val_bpb`` on the configured validation split (the reference's load-checkpoint then
+    evaluate path, src/distributed/trainer.ts:1225-1289 and :897-976). The training config comes from the
+    checkpoint's metadata when it has one, else from ``--preset``; overrides apply on top (e.g. ``data=...
+    data_path=... eval_tokens=...``)."""
+    import argparse
+    import sys
+
+    from .config import apply_overrides, preset
+    from .train import Trainer
+    ap = argparse.ArgumentParser(description="evaluate a checkpoint's bits per byte")
+    ap.add_argument("--checkpoint", required=True)
+    ap.add_argument("--preset", default="d512")
+    ap.add_argument("--device", default=None)
+    ap.add_argument("overrides", nargs="*")
+    args = ap.parse_args(argv)
+    cfg = _config_from_checkpoint(args.checkpoint) or preset(args.preset)
+    cfg = apply_overrides(cfg, list(args.overrides) + ["results_tsv=", "log_every=0", "status_port=-1"])
+    if args.device is None and not torch.cuda.is_available():
+        cfg.impl, cfg.dtype = "torch", "fp32"
+    tr = Trainer(cfg, device=args.device, log=lambda m: print(m, file=sys.stderr))
+    tr.initialize()
+    info = tr.load_checkpoint(args.checkpoint)
+    bpb = tr.evaluate_bpb()
+    tr.destroy()
+    print(f"val_bpb:          {bpb:.6f}")
+    print(f"step:             {info.get('step', 0)}")
+    if "val_bpb_floor" in tr.metrics.extra:
+        print(f"val_bpb_floor:    {tr.metrics.extra['val_bpb_floor']:.6f}")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

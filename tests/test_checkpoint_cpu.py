@@ -64,3 +64,25 @@ def test_safetensors_library_reads_our_files(tmp_path):
     ckpt.save(str(tmp_path / "a.safetensors"), t, meta)
     loaded = st.load_file(str(tmp_path / "a.safetensors"))
     assert torch.equal(loaded["wte"], m.named()["wte"])
+
+
+def test_eval_cli_scores_a_saved_checkpoint(tmp_path, capsys):
+    from bitresearch_b200.config import apply_overrides, preset
+    from bitresearch_b200.eval import main
+    from bitresearch_b200.train import Trainer
+    cfg = apply_overrides(preset("tiny-cpu"), ["model.n_layer=1", "model.n_embd=64", "model.n_head=1",
+                                               "model.n_kv_head=1", "model.sequence_len=32", "model.vocab_size=128",
+                                               "device_batch=2", "total_batch_tokens=64", "eval_tokens=256",
+                                               "log_every=0", "results_tsv=", "data=markov", "doc_mean_len=16"])
+    tr = Trainer(cfg, device="cpu", log=lambda m: None)
+    tr.initialize()
+    for _ in range(3):
+        tr.train_step()
+    want = tr.evaluate_bpb()
+    path = tr.save_checkpoint(str(tmp_path / "c.safetensors"))
+    tr.destroy()
+    capsys.readouterr()
+    assert main(["--checkpoint", path]) == 0  # the config comes from the checkpoint's metadata
+    out = capsys.readouterr().out
+    got = float(out.split("val_bpb:")[1].split()[0])
+    assert abs(got - want) < 1e-6 and "step:             3" in out and "val_bpb_floor:" in out
