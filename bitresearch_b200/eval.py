@@ -49,29 +49,30 @@ def evaluate_bpb(per_token_nats_fn, batch_source, token_bytes: np.ndarray, batch
     return bpb_from_sums(n, b), n, b
 
 
-def _config_from_checkpoint(path: str):
-    """The TrainConfig stored in a checkpoint's ``trainConfig`` metadata, or None (reference checkpoints
-    store only the model config)."""
+def _config_from_checkpoint(path: str, fallback):
+    """The TrainConfig stored in a checkpoint's ``trainConfig`` metadata; for a checkpoint written by the
+    reference, which stores only the model config (``config``, src/distributed/trainer.ts:1132-1137),
+    ``fallback`` with that model."""
     import json
 
     from . import checkpoint as ckpt
-    from .config import TrainConfig
+    from .config import GPTConfig, TrainConfig
     _, meta = ckpt.load(path)
     raw = meta.get("trainConfig")
-    if not raw:
-        return None
-    d = json.loads(raw)
-    if isinstance(d, str):
-        d = json.loads(d)
-    return TrainConfig.from_dict(d)
+    if raw:
+        d = json.loads(raw)
+        return TrainConfig.from_dict(json.loads(d) if isinstance(d, str) else d)
+    if meta.get("config"):
+        fallback.model = GPTConfig.from_reference_dict(json.loads(meta["config"]))
+    return fallback
 
 
 def main(argv=None) -> int:
     """``python -m bitresearch_b200.eval --checkpoint PATH [--preset P] [key=value ...]``: loads a checkpoint
     and prints its ``val_bpb`` on the configured validation split (the reference's load-checkpoint then
     evaluate path, src/distributed/trainer.ts:1225-1289 and :897-976). The training config comes from the
-    checkpoint's metadata when it has one, else from ``--preset``; overrides apply on top (e.g. ``data=...
-    data_path=... eval_tokens=...``)."""
+    checkpoint's metadata when it has one, else from ``--preset`` with the checkpoint's model config;
+    overrides apply on top (e.g. ``data=... data_path=... eval_tokens=...``)."""
     import argparse
     import sys
 
@@ -83,7 +84,7 @@ def main(argv=None) -> int:
     ap.add_argument("--device", default=None)
     ap.add_argument("overrides", nargs="*")
     args = ap.parse_args(argv)
-    cfg = _config_from_checkpoint(args.checkpoint) or preset(args.preset)
+    cfg = _config_from_checkpoint(args.checkpoint, preset(args.preset))
     cfg = apply_overrides(cfg, list(args.overrides) + ["results_tsv=", "log_every=0", "status_port=-1"])
     if args.device is None and not torch.cuda.is_available():
         cfg.impl, cfg.dtype = "torch", "fp32"

@@ -86,3 +86,17 @@ def test_eval_cli_scores_a_saved_checkpoint(tmp_path, capsys):
     out = capsys.readouterr().out
     got = float(out.split("val_bpb:")[1].split()[0])
     assert abs(got - want) < 1e-6 and "step:             3" in out and "val_bpb_floor:" in out
+
+
+def test_eval_cli_takes_the_model_from_a_reference_style_checkpoint(tmp_path, capsys):
+    """A checkpoint with only the reference's metadata (step, lossScale, totalTokens, model config)."""
+    from bitresearch_b200.eval import main
+    cfg = _cfg()
+    m = GPT(cfg, seed=4)
+    t, meta = ckpt.build_state(m, None, step=11)
+    assert "trainConfig" not in meta
+    path = ckpt.save(str(tmp_path / "ref.safetensors"), t, meta)
+    assert main(["--checkpoint", path, "--preset", "tiny-cpu", "eval_tokens=64", "data=uniform", "bos_every=8",
+                 "device_batch=2"]) == 0
+    out = capsys.readouterr().out
+    assert float(out.split("val_bpb:")[1].split()[0]) > 0 and "step:             11" in out
