@@ -131,7 +131,7 @@ async def _fake_worker(port, on_batch):
 def test_straggler_timeout_and_stale_pushes():
     logs = []
     coord = Coordinator(CoordinatorConfig(port=0, start_delay_s=0.2, max_steps=2, min_workers=2,
-                                          straggler_timeout_s=1.0), _tiny(), log=logs.append)
+                                          straggler_timeout_s=3.0), _tiny(), log=logs.append)
     th = CoordinatorThread(coord)
     port = th.start()
 

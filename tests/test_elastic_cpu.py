@@ -18,7 +18,7 @@ def _elastic(rank, world, crash_rank, crash_after):
         "model.n_layer=1", "model.n_embd=64", "model.n_head=1", "model.n_kv_head=1", "model.sequence_len=32",
         "model.vocab_size=128", "device_batch=2", f"total_batch_tokens={64 * world}", "eval_tokens=128",
         "log_every=0", "results_tsv=", "max_steps=8", "time_budget=1e9", "comm=ring", "elastic=true",
-        "heartbeat_s=0.2", "dead_after_s=1.5", "comm_timeout_s=4", "reform_timeout_s=60"])
+        "heartbeat_s=0.2", "dead_after_s=3", "comm_timeout_s=4", "reform_timeout_s=60"])
     logs = []
     tr = Trainer(cfg, device="cpu", log=logs.append)
     tr.initialize()
