@@ -66,8 +66,11 @@ def collect_training_corpus(text_dir: str, files: list[str], max_chars: int, doc
     return docs, chars
 
 
-def tokenize_shard(tok: BPETokenizer, src: str, dst: str, batch: int = 2048) -> tuple[int, int]:
-    """Writes BOS-prefixed int32 ids of every non-empty line of ``src`` to ``dst`` (atomically)."""
+def tokenize_shard(tok: BPETokenizer, src: str, dst: str, batch: int = 2048, pool=None) -> tuple[int, int]:
+    """Writes BOS-prefixed int32 ids of every non-empty line of ``src`` to ``dst`` (atomically); with a
+    ``pool`` (``tok.pool(n)``) each batch of lines is encoded across its worker processes, in order."""
+    if pool is not None:
+        batch = max(batch, 16384)  # enough 256-line tasks per flush to keep every worker busy
     tmp = dst + ".tmp"
     docs = toks = 0
     bos = np.array([tok.bos_id], dtype=np.int32)
@@ -77,7 +80,7 @@ def tokenize_shard(tok: BPETokenizer, src: str, dst: str, batch: int = 2048) -> 
 
             def flush():
                 nonlocal docs, toks
-                for ids in tok.batch_encode(pending):
+                for ids in tok.batch_encode(pending, pool=pool):
                     bos.tofile(out)
                     np.asarray(ids, dtype=np.int32).tofile(out)
                     toks += 1 + len(ids)
@@ -162,6 +165,7 @@ def main(argv=None) -> int:
     ap.add_argument("--train-doc-cap", type=int, default=_env_int("PREPARE_WASM_TRAIN_DOC_CAP", 10_000, 1))
     ap.add_argument("--tokenize-shards", type=int, default=_env_int("PREPARE_WASM_TOKENIZE_SHARDS", 0, 0))
     ap.add_argument("--no-parity", action="store_true", help="skip the parity mirror and manifest")
+    ap.add_argument("--workers", type=int, default=os.cpu_count() or 1, help="encoding processes")
     args = ap.parse_args(argv)
     text_dir = args.text_dir or os.path.join(args.cache_dir, "text")
     bin_dir = args.bin_dir or os.path.join(args.cache_dir, "bin")
@@ -179,7 +183,12 @@ def main(argv=None) -> int:
         raise SystemExit("no training documents collected")
     print(f"training on {len(docs):,} documents ({chars:,} characters)")
     t0 = time.time()
-    tok = BPETokenizer().train(docs, args.vocab_size - len(SPECIAL_TOKENS))
+    tok = BPETokenizer()
+    if args.workers > 1:  # the chunk split of the training corpus runs in worker processes
+        with tok.pool(args.workers) as count_pool:
+            tok.train(docs, args.vocab_size - len(SPECIAL_TOKENS), pool=count_pool)
+    else:
+        tok.train(docs, args.vocab_size - len(SPECIAL_TOKENS))
     print(f"tokenizer trained in {time.time() - t0:.1f}s (vocab={tok.vocab_size()}, merges={tok.num_merges()})")
     sample = "Hello world! Numbers: 123. Unicode: 你好"
     ids = tok.encode(sample)
@@ -187,9 +196,17 @@ def main(argv=None) -> int:
     tok.save(tok_dir)
     print(f"tokenizer bundle saved to {tok_dir}")
     os.makedirs(bin_dir, exist_ok=True)
-    for name in files[:args.tokenize_shards] if args.tokenize_shards > 0 else files:
-        nd, nt = tokenize_shard(tok, os.path.join(text_dir, name), os.path.join(bin_dir, name[:-4] + ".bin"))
-        print(f"  {name}: {nd:,} docs / {nt:,} tokens")
+    pool = tok.pool(args.workers) if args.workers > 1 else None
+    try:
+        for name in files[:args.tokenize_shards] if args.tokenize_shards > 0 else files:
+            t1 = time.time()
+            nd, nt = tokenize_shard(tok, os.path.join(text_dir, name), os.path.join(bin_dir, name[:-4] + ".bin"),
+                                    pool=pool)
+            print(f"  {name}: {nd:,} docs / {nt:,} tokens in {time.time() - t1:.1f}s")
+    finally:
+        if pool is not None:
+            pool.close()
+            pool.join()
     if not args.no_parity:
         os.makedirs(args.public_data_dir, exist_ok=True)
         m = sync_parity_artifacts(args.cache_dir, bin_dir, tok_dir, args.public_data_dir)

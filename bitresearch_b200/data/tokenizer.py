@@ -39,6 +39,25 @@ def _native():
     return _native_data
 
 
+_POOL_TOK: "BPETokenizer | None" = None
+
+
+def _pool_init(merges, pattern) -> None:
+    global _POOL_TOK
+    _POOL_TOK = BPETokenizer(merges, pattern)
+
+
+def _pool_encode(texts: list[str]) -> list[np.ndarray]:
+    return [_POOL_TOK.encode(t) for t in texts]
+
+
+def _pool_count(texts: list[str]) -> collections.Counter:
+    c: collections.Counter = collections.Counter()
+    for t in texts:
+        c.update(_POOL_TOK._re.findall(t))
+    return c
+
+
 class BPETokenizer:
     def __init__(self, merges: Sequence[tuple[int, int]] = (), pattern: str = SPLIT_PATTERN):
         import regex
@@ -49,15 +68,22 @@ class BPETokenizer:
         self._vocab_bytes: list[bytes] | None = None
 
     # ------------------------------------------------------------------ training
-    def chunk_counts(self, texts: Iterable[str]) -> collections.Counter:
+    def chunk_counts(self, texts: Iterable[str], pool=None, chunk: int = 2048) -> collections.Counter:
+        """Occurrences of every pre-tokenized chunk; with a ``pool`` the split runs in its workers (parts
+        merged in order, so the result, insertion order included, is the serial one)."""
         counts: collections.Counter = collections.Counter()
-        for t in texts:
-            counts.update(self._re.findall(t))
+        if pool is None:
+            for t in texts:
+                counts.update(self._re.findall(t))
+            return counts
+        texts = list(texts)
+        for part in pool.imap(_pool_count, [texts[i:i + chunk] for i in range(0, len(texts), chunk)]):
+            counts.update(part)
         return counts
 
-    def train(self, texts: Iterable[str], vocab_size_no_special: int) -> "BPETokenizer":
+    def train(self, texts: Iterable[str], vocab_size_no_special: int, pool=None) -> "BPETokenizer":
         """Learns ``vocab_size_no_special - 256`` merges over the texts' chunks."""
-        counts = self.chunk_counts(texts)
+        counts = self.chunk_counts(texts, pool=pool)
         chunks = [c.encode("utf-8") for c in counts]
         merges = _native().bpe_train(chunks, list(counts.values()), int(vocab_size_no_special))
         self.merges = [tuple(m) for m in merges]
@@ -104,10 +130,22 @@ class BPETokenizer:
     def encode(self, text: str) -> np.ndarray:
         if self._enc is None:
             raise RuntimeError("tokenizer has no merges: train or load it first")
-        return self._enc.encode_chunks([c.encode("utf-8") for c in self._re.findall(text)])
+        return self._enc.encode_chunks(self._re.findall(text))  # str chunks reach C++ as UTF-8 bytes
 
-    def batch_encode(self, texts: Sequence[str]) -> list[np.ndarray]:
-        return [self.encode(t) for t in texts]
+    def batch_encode(self, texts: Sequence[str], pool=None, chunk: int = 256) -> list[np.ndarray]:
+        """Encodes ``texts`` in order; with a ``pool`` from :meth:`pool`, split over its worker processes
+        (the regex pre-split is Python-level work, so threads would serialise on the GIL)."""
+        if pool is None or len(texts) <= chunk:
+            return [self.encode(t) for t in texts]
+        parts = [list(texts[i:i + chunk]) for i in range(0, len(texts), chunk)]
+        return [ids for part in pool.imap(_pool_encode, parts) for ids in part]
+
+    def pool(self, workers: int):
+        """A process pool whose workers each hold this tokenizer. Workers start from a fork server (a clean
+        single-threaded process) rather than by forking the caller, which may run threads (torch's)."""
+        import multiprocessing as mp
+        ctx = mp.get_context("forkserver" if "forkserver" in mp.get_all_start_methods() else "spawn")
+        return ctx.Pool(workers, initializer=_pool_init, initargs=(self.merges, self.pattern))
 
     def decode(self, ids: Iterable[int]) -> str:
         vb = self.vocab_bytes()

@@ -134,3 +134,36 @@ def test_prepare_manifest_and_trainer(tmp_path):
     loss = float(tr.train_step())
     assert np.isfinite(loss)
     tr.destroy()
+
+
+def test_pooled_encoding_matches_serial(tmp_path):
+    docs = _corpus(400, seed=2)
+    tok = BPETokenizer().train(docs, 256 + 150)
+    with tok.pool(2) as pool:
+        pooled = tok.batch_encode(docs, pool=pool, chunk=16)
+    serial = tok.batch_encode(docs)
+    assert len(pooled) == len(serial) and all(np.array_equal(a, b) for a, b in zip(pooled, serial))
+
+
+def test_prepare_with_worker_pool_writes_the_same_shards(tmp_path):
+    from bitresearch_b200.data import prepare
+    outs = []
+    for workers in (1, 2):
+        cache = tmp_path / f"cache{workers}"
+        (cache / "text").mkdir(parents=True)
+        docs = _corpus(300, seed=4)
+        (cache / "text" / "shard_00000.txt").write_text("\n".join(docs[:250]) + "\n")
+        (cache / "text" / "shard_06542.txt").write_text("\n".join(docs[250:]) + "\n")
+        assert prepare.main(["--cache-dir", str(cache), "--vocab-size", "400", "--no-parity",
+                             "--workers", str(workers)]) == 0
+        outs.append([np.fromfile(cache / "bin" / n, dtype=np.int32) for n in ("shard_00000.bin", "shard_06542.bin")])
+    assert all(np.array_equal(a, b) for a, b in zip(*outs))
+
+
+def test_pooled_chunk_counts_match_serial():
+    docs = _corpus(500, seed=6)
+    tok = BPETokenizer()
+    with tok.pool(2) as pool:
+        pooled = tok.chunk_counts(docs, pool=pool, chunk=64)
+    serial = tok.chunk_counts(docs)
+    assert pooled == serial and list(pooled) == list(serial)
