@@ -75,3 +75,40 @@ def test_swarm_runs_all_variants_on_two_workers():
         m = r["metrics"]
         assert m["sharpe_ci_low"] <= m["mc_mean_sharpe"] <= m["sharpe_ci_high"]
         assert {r["peerId"] for r in res} <= {"worker-0", "worker-1"}
+
+
+def test_prepare_splits_csv_bars_and_feeds_the_runner(tmp_path, capsys):
+    import json
+    from bitresearch_b200.swarm import prepare, runner
+    csv_dir = tmp_path / "csv"
+    csv_dir.mkdir()
+    days = prepare.synthetic_bars("2020-06-01", "2021-12-31")["SPY"]["dates"]
+    for t in ("SPY", "QQQ", "IWM"):
+        rows = ["Date,Open,Close"] + [f"{d},1,{100 + i * 0.1 + (3 if t == 'QQQ' else 0)}" for i, d in enumerate(days)]
+        rows.insert(5, f"{days[3]},1,null")  # a missing bar is skipped
+        (csv_dir / f"{t.lower()}.csv").write_text("\n".join(rows) + "\n")
+    out = tmp_path / "data"
+    assert prepare.main(["--csv-dir", str(csv_dir), "--out", str(out), "--val-end", "2021-12-31"]) == 0
+    train = json.loads((out / "train.json").read_text())
+    val = json.loads((out / "val.json").read_text())
+    assert set(train) == {"SPY", "QQQ", "IWM"}
+    assert all(d <= "2020-12-31" for d in train["SPY"]["dates"]) and all(d > "2020-12-31" for d in val["SPY"]["dates"])
+    assert len(train["SPY"]["dates"]) + len(val["SPY"]["dates"]) == len(days)
+    cfg = json.loads((out / "config.json").read_text())
+    assert cfg["chunkSize"] == 5 and len(cfg["variants"]) == 1120
+    capsys.readouterr()
+    res_path = tmp_path / "res.json"
+    assert runner.main(["--variants", str(out / "config.json"), "--data", str(out / "val.json"), "--limit", "3",
+                        "--paths", "500", "--workers", "1", "--out", str(res_path)]) == 0
+    res = json.loads(res_path.read_text())
+    assert len(res) == 3 and all("sharpe_ci_low" in r["metrics"] for r in res)
+
+
+def test_prepare_without_input_writes_synthetic_business_days(tmp_path):
+    import datetime
+    import json
+    from bitresearch_b200.swarm import prepare
+    assert prepare.main(["--out", str(tmp_path)]) == 0
+    a = json.loads((tmp_path / "all.json").read_text())
+    assert set(a) == set(prepare.TICKERS)
+    assert all(datetime.date.fromisoformat(d).weekday() < 5 for d in a["SPY"]["dates"][:50])
