@@ -101,9 +101,11 @@ def _worker(name: str, device: str | None, data: dict, n_paths: int, seed: int, 
 
 def run_swarm(variants: list[dict], data: dict, workers: int = 1, n_paths: int = 50_000, seed: int = 0,
               devices: list[str] | None = None, chunk_size: int = 5, log=print, timeout_s: float = 3600.0,
-              status_port: int = -1) -> list[dict]:
+              status_port: int = -1, on_event=None) -> list[dict]:
     """Runs every variant on ``workers`` processes; returns the results sorted by Sharpe (best first).
-    ``status_port >= 0`` serves the progress at ``GET /status`` and ``GET /metrics`` meanwhile."""
+    ``status_port >= 0`` serves the progress at ``GET /status`` and ``GET /metrics`` meanwhile and pushes
+    ``swarm-progress`` / ``swarm-complete`` to ``/ws`` observers (server/signaling.ts:380-400); ``on_event``
+    receives the same messages in-process."""
     ctx = mp.get_context("spawn")
     q = SwarmQueue(variants, chunk_size)
     server = None
@@ -119,7 +121,14 @@ def run_swarm(variants: list[dict], data: dict, workers: int = 1, n_paths: int =
 
         server = StatusServer(status, q.status, port=status_port, prefix="bitresearch_swarm")
         server.start()
-        log(f"[swarm] status: {server.url}/status")
+        log(f"[swarm] status: {server.url}/status, observers: {server.url.replace('http', 'ws')}/ws")
+
+    def emit(msg: dict) -> None:
+        if server is not None:
+            server.publish(msg)
+        if on_event is not None:
+            on_event(msg)
+
     req_q, res_q = ctx.Queue(), ctx.Queue()
     work_qs, procs = {}, {}
     devices = devices or [None] * workers
@@ -139,6 +148,7 @@ def run_swarm(variants: list[dict], data: dict, workers: int = 1, n_paths: int =
                 prog = q.record(rest[0])
                 log(f"[swarm] {prog['totalCompleted']}/{prog['totalVariants']} best sharpe {prog['bestScore']:.4f} "
                     f"({prog['bestVariant']})")
+                emit({"type": "swarm-progress", **prog, "result": rest[0], "peerId": name})
             except queue.Empty:
                 pass
             while True:
@@ -165,6 +175,8 @@ def run_swarm(variants: list[dict], data: dict, workers: int = 1, n_paths: int =
                         idle.discard(name)
             if not procs:
                 raise RuntimeError("all swarm workers exited")
+        if q.done:
+            emit({"type": "swarm-complete", "results": q.results[:20]})
     finally:
         for name, wq in work_qs.items():
             wq.put(None)

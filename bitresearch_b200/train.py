@@ -516,6 +516,8 @@ class Trainer:
                 rec["phases_ms"] = self.phase_ms
                 if cfg.log_every and m.step % cfg.log_every == 0:
                     self.log("phases: " + " | ".join(f"{k} {v:.2f} ms" for k, v in self.phase_ms.items()))
+            if self.status_server is not None and cfg.log_every and m.step % cfg.log_every == 0:
+                self.status_server.publish({"type": "metrics", **rec, "grad_norm": m.grad_norm})
             jl.write(rec)
             self._profile_tick()
             if cfg.checkpoint_interval > 0 and m.step % cfg.checkpoint_interval == 0:
@@ -524,6 +526,10 @@ class Trainer:
         self.evaluate_bpb()
         total = time.perf_counter() - self.start_time
         peak = torch.cuda.max_memory_allocated(self.device) / 2 ** 20 if self.is_cuda else 0.0
+        if self.status_server is not None:
+            self.status_server.publish({"type": "training-complete", "val_bpb": self.metrics.val_bpb,
+                                        "num_steps": self.metrics.step, "training_seconds": self.total_training_time,
+                                        "total_seconds": total, **self.metrics.extra})
         if self.rank == 0:
             print(summary_block(self.metrics, self.total_training_time, total, peak, cfg.model.n_layer), flush=True)
             if cfg.results_tsv:

@@ -7,6 +7,10 @@ static ring: torch.distributed does not re-form the group), plus the trainer's m
 swarm serves its progress under ``swarms``. ``/metrics`` exposes the numeric fields as gauges for a
 Prometheus scrape.
 
+``/ws`` is a push feed for observers (the reference's observer page joins the swarm room and receives
+``swarm-progress`` / ``swarm-complete`` messages, observer.html:50-80): every message given to
+``publish`` goes to each connected client as JSON.
+
 The server runs on its own event loop in a daemon thread and only reads what the providers return, so
 the training loop never waits for it.
 """
@@ -48,6 +52,9 @@ class StatusServer:
         self._ready = threading.Event()
         self._stop: asyncio.Event | None = None
         self._error: BaseException | None = None
+        self._subs: set = set()
+        self._pending: set = set()
+        self.published = 0
         self.thread = threading.Thread(target=self._run, daemon=True)
 
     def _app(self):
@@ -61,10 +68,52 @@ class StatusServer:
             return web.Response(text=prometheus_text(self.prefix, self.metrics_fn()),
                                 content_type="text/plain")
 
+        async def feed(request):
+            ws = web.WebSocketResponse()
+            await ws.prepare(request)
+            self._subs.add(ws)
+            try:
+                async for _ in ws:
+                    pass
+            finally:
+                self._subs.discard(ws)
+            return ws
+
         app = web.Application()
         app.router.add_get("/status", status)
         app.router.add_get("/metrics", metrics)
+        app.router.add_get("/ws", feed)
         return app
+
+    async def _broadcast(self, text: str) -> None:
+        for ws in list(self._subs):
+            try:
+                await ws.send_str(text)
+            except (ConnectionError, RuntimeError):
+                self._subs.discard(ws)
+
+    def publish(self, msg: dict) -> None:
+        """Sends ``msg`` to every ``/ws`` client; callable from any thread, never blocks."""
+        if self._stop is None or not self.thread.is_alive():
+            return
+        text = json.dumps(msg, default=str)
+        self.published += 1
+
+        def start():
+            task = asyncio.ensure_future(self._broadcast(text))
+            self._pending.add(task)
+            task.add_done_callback(self._pending.discard)
+
+        self.loop.call_soon_threadsafe(start)
+
+    async def _drain_and_stop(self) -> None:
+        if self._pending:
+            await asyncio.wait(list(self._pending), timeout=5)
+        self._stop.set()
+
+    @property
+    def subscribers(self) -> int:
+        return len(self._subs)
 
     def _run(self):
         from aiohttp import web
@@ -99,6 +148,7 @@ class StatusServer:
         return self.port
 
     def stop(self) -> None:
+        """Delivers what was published, then shuts the server down."""
         if self._stop is not None and self.thread.is_alive():
-            self.loop.call_soon_threadsafe(self._stop.set)
+            self.loop.call_soon_threadsafe(lambda: asyncio.ensure_future(self._drain_and_stop()))
             self.thread.join(10)

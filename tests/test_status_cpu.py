@@ -28,7 +28,7 @@ def test_trainer_serves_status_and_metrics():
     cfg = apply_overrides(preset("tiny-cpu"), ["model.n_layer=1", "model.n_embd=64", "model.n_head=1",
                                                "model.n_kv_head=1", "model.sequence_len=32", "model.vocab_size=128",
                                                "device_batch=2", "total_batch_tokens=64", "eval_tokens=128",
-                                               "log_every=0", "results_tsv=", "max_steps=3", "status_port=0"])
+                                               "log_every=1", "results_tsv=", "max_steps=3", "status_port=0"])
     tr = Trainer(cfg, device="cpu", log=lambda m: None)
     tr.initialize()
     tr.start_training()
@@ -38,6 +38,7 @@ def test_trainer_serves_status_and_metrics():
     assert st["peers"][0]["position"] == 0 and st["training"]["step"] == 3 and st["training"]["val_bpb"] > 0
     m = _get(base + "/metrics")
     assert "bitresearch_step 3" in m and "bitresearch_val_bpb" in m
+    assert tr.status_server.published == 3 + 1  # metrics on every logging step (log_every=1) + completion
     tr.destroy()
     assert tr.status_server is None
 
@@ -57,3 +58,45 @@ def test_swarm_queue_status_and_server():
         assert "sw_bestScore 1.2" in _get(srv.url + "/metrics")
     finally:
         srv.stop()
+
+
+def test_observer_feed_receives_published_messages():
+    import asyncio
+    import threading
+    import time
+
+    import aiohttp
+    srv = StatusServer(lambda: {})
+    srv.start()
+    got = []
+
+    async def observe():
+        async with aiohttp.ClientSession() as s, s.ws_connect(srv.url.replace("http", "ws") + "/ws") as ws:
+            async for m in ws:
+                got.append(json.loads(m.data))
+
+    t = threading.Thread(target=lambda: asyncio.run(observe()), daemon=True)
+    t.start()
+    deadline = time.time() + 10
+    while srv.subscribers < 1:
+        assert time.time() < deadline
+        time.sleep(0.02)
+    for i in range(3):
+        srv.publish({"type": "swarm-progress", "totalCompleted": i + 1, "totalVariants": 3})
+    srv.publish({"type": "swarm-complete", "results": []})
+    srv.stop()  # delivers what was published first
+    t.join(10)
+    assert [m["type"] for m in got] == ["swarm-progress"] * 3 + ["swarm-complete"]
+    assert got[2]["totalCompleted"] == 3
+
+
+def test_swarm_emits_progress_and_completion_events():
+    from bitresearch_b200.swarm.runner import run_swarm
+    from bitresearch_b200.swarm.strategy import synthetic_market, variant_grid
+    events = []
+    res = run_swarm(variant_grid()[:4], synthetic_market(), workers=1, n_paths=300, log=lambda m: None,
+                    on_event=events.append)
+    prog = [e for e in events if e["type"] == "swarm-progress"]
+    assert len(res) == 4 and len(prog) == 4 and prog[-1]["totalCompleted"] == 4 and prog[-1]["totalVariants"] == 4
+    assert all(e["result"]["params"]["id"] in range(4) and e["peerId"] == "worker-0" for e in prog)
+    assert events[-1]["type"] == "swarm-complete" and len(events[-1]["results"]) == 4
