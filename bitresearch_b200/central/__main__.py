@@ -41,11 +41,6 @@ def _serve_args(ap):
     ap.add_argument("overrides", nargs="*")
 
 
-def _worker_main(url, device, max_steps, push_gradients):
-    from .worker import CentralWorker
-    w = CentralWorker(url, device=device, push_gradients=push_gradients)
-    res = asyncio.run(w.run(max_steps=max_steps))
-    print(f"[worker] {res}", flush=True)
 
 
 def main(argv=None) -> int:
@@ -65,7 +60,8 @@ def main(argv=None) -> int:
         asyncio.run(_coordinator(args).serve())
         return 0
     if args.cmd == "worker":
-        _worker_main(args.url, args.device, args.max_steps, args.push_gradients)
+        from .worker import run_worker_process
+        run_worker_process(args.url, args.device, args.max_steps, args.push_gradients)
         return 0
     import torch
     from .coordinator import CoordinatorThread
@@ -75,19 +71,28 @@ def main(argv=None) -> int:
     args.port = args.port if args.port else 0
     th = CoordinatorThread(_coordinator(args))
     port = th.start()
+    from .worker import run_worker_process
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_worker_main, args=(f"ws://{args.host}:{port}/ws",
-                                                     f"cuda:{i % n_gpu}" if n_gpu else "cpu", 0, False))
+    cpu_threads = 0 if n_gpu else max(1, (os.cpu_count() or 1) // n)
+    procs = [ctx.Process(target=run_worker_process, args=(f"ws://{args.host}:{port}/ws",
+                                                          f"cuda:{i % n_gpu}" if n_gpu else "cpu", 0, False,
+                                                          cpu_threads))
              for i in range(n)]
     for p in procs:
         p.start()
+    rc = 0
     try:
-        th.thread.join()
+        while th.thread.is_alive():
+            th.thread.join(1.0)
+            if th.thread.is_alive() and not any(p.is_alive() for p in procs):
+                print("[central] every worker process exited before the run finished", file=sys.stderr)
+                th.stop()
+                rc = 1
     except KeyboardInterrupt:
         th.stop()
     for p in procs:
         p.join(timeout=60)
-    return 0
+    return rc
 
 
 if __name__ == "__main__":

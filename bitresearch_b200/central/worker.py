@@ -152,3 +152,15 @@ class CentralWorker:
             await loop.run_in_executor(self._pool, self.trainer.destroy)
         self._pool.shutdown(wait=True)
         return {"workerId": self.worker_id, "steps": self.steps, "loss": self.last_loss, "kicked": self.kicked}
+
+
+def run_worker_process(url: str, device: str | None, max_steps: int = 0, push_gradients: bool = False,
+                       cpu_threads: int = 0) -> None:
+    """Entry point of one worker process (an importable target for ``multiprocessing``). ``cpu_threads``
+    caps torch's intra-op threads, so CPU workers sharing a host do not oversubscribe its cores."""
+    if cpu_threads > 0:
+        import torch
+        torch.set_num_threads(cpu_threads)
+    w = CentralWorker(url, device=device, push_gradients=push_gradients)
+    res = asyncio.run(w.run(max_steps=max_steps))
+    print(f"[worker] {res}", flush=True)

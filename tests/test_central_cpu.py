@@ -185,3 +185,17 @@ def test_worker_config_follows_welcome_and_engine_support():
     assert train_config_from_welcome(welcome, "cuda:0").impl == "torch"  # eager path on the GPU for 64-wide heads
     d = preset("d512")
     assert train_config_from_welcome({"config": model_config_message(d.model), "batchSize": 2}, "cuda:0").impl == "cuda"
+
+
+def test_local_mode_spawns_workers_and_finishes():
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, "-m", "bitresearch_b200.central", "local", "--preset", "tiny-cpu",
+                          "--max-steps", "2", "--start-delay", "0.3", "--port", "0", "--workers", "2"],
+                         capture_output=True, text=True, timeout=240, cwd=root,
+                         env={**os.environ, "PYTHONUNBUFFERED": "1"})
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert "step 2 complete" in out.stdout and "2 workers" in out.stdout
+    assert out.stdout.count("'kicked': True") == 2
