@@ -212,7 +212,7 @@ class TrainConfig:
     bucket_mb: float = 32.0
     overlap: bool = True
     sparsify: SparsifyConfig = field(default_factory=SparsifyConfig)
-    comm_timeout_s: float = 10.0
+    comm_timeout_s: float = 10.0  # elastic ring: 0 = the membership's dynamic timeout max(10, 3 rtt + 5) s
     # ring path only: re-form the ring without a lost rank (store heartbeats + a new gloo group)
     elastic: bool = False
     heartbeat_s: float = 2.0  # the reference pings every 2 s (webrtc-mesh.ts:173-196)

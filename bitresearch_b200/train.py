@@ -166,7 +166,7 @@ class Trainer:
         if self.world > 1 and cfg.comm == "ring":
             if cfg.elastic:
                 self._init_elastic()
-            self.comm = RingAllReduce(wire_dtype=cfg.wire_dtype, timeout_s=cfg.comm_timeout_s, log=self.log,
+            self.comm = RingAllReduce(wire_dtype=cfg.wire_dtype, timeout_s=self._ring_timeout(), log=self.log,
                                       elastic=self.egroup)
         fused_comm = cfg.impl == "cuda" and cfg.comm == "p2p" and self.world > 1
         if cfg.sparsify.enabled and not fused_comm:
@@ -436,7 +436,14 @@ class Trainer:
         self.membership.register()
         self.membership.start()
         ring = self.membership.wait_for(self.world, cfg.reform_timeout_s)
-        self.egroup = ElasticGroup(self._store, ring, room="train", timeout_s=cfg.comm_timeout_s)
+        self.egroup = ElasticGroup(self._store, ring, room="train", timeout_s=self._ring_timeout())
+
+    def _ring_timeout(self) -> float:
+        """``comm_timeout_s``, or with 0 the membership's dynamic timeout max(10, 3 * rtt + 5) s, read at ring
+        formation as the reference does (webrtc-mesh.ts:99-109, trainer.ts:656-659)."""
+        if self.cfg.comm_timeout_s > 0 or self.membership is None:
+            return self.cfg.comm_timeout_s if self.cfg.comm_timeout_s > 0 else 10.0
+        return self.membership.dynamic_timeout_s
 
     def _reform(self) -> None:
         """After a step that lost a peer: wait until membership drops it, form the smaller ring with its
@@ -448,8 +455,8 @@ class Trainer:
         old = self.egroup.ring.peers
         self.log(f"peer lost at step {self.metrics.step}; re-forming the ring of {len(old)}")
         ring = self.membership.wait_for_change(old, cfg.reform_timeout_s)
-        self.egroup = ElasticGroup(self._store, ring, room="train", timeout_s=cfg.comm_timeout_s)
-        self.comm = RingAllReduce(wire_dtype=cfg.wire_dtype, timeout_s=cfg.comm_timeout_s, log=self.log,
+        self.egroup = ElasticGroup(self._store, ring, room="train", timeout_s=self._ring_timeout())
+        self.comm = RingAllReduce(wire_dtype=cfg.wire_dtype, timeout_s=self._ring_timeout(), log=self.log,
                                   elastic=self.egroup)
         self.rank, self.world = ring.position, ring.total
         self._resync()

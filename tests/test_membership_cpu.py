@@ -26,3 +26,17 @@ def test_ring_formation_and_dead_peer_dropped():
     assert r.peers == ["peer-a", "peer-b"] and r.version > v0
     assert peers[1].form_ring() is None  # the silent peer is no longer a member
     assert 10.0 <= peers[0].dynamic_timeout_s < 11.0
+
+
+def test_ring_timeout_follows_config_or_membership_rtt():
+    from types import SimpleNamespace
+
+    from bitresearch_b200.train import Trainer
+    tr = Trainer.__new__(Trainer)
+    tr.cfg = SimpleNamespace(comm_timeout_s=4.0)
+    tr.membership = SimpleNamespace(dynamic_timeout_s=17.0)
+    assert tr._ring_timeout() == 4.0
+    tr.cfg.comm_timeout_s = 0
+    assert tr._ring_timeout() == 17.0
+    tr.membership = None
+    assert tr._ring_timeout() == 10.0
