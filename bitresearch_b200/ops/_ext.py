@@ -44,9 +44,9 @@ class _Counting:
             raw = getattr(self._mod, name)
             k = _KERNELS_PER_CALL.get(name, 1)
 
-            def fn(*a, _raw=raw, _k=k, _n=name):
+            def fn(*a, _raw=raw, _k=k, _n=name, **kw):
                 _COUNTS[_n] = _COUNTS.get(_n, 0) + _k
-                return _raw(*a)
+                return _raw(*a, **kw)
             self._cache[name] = fn
         return fn
 
