@@ -277,11 +277,13 @@ def _d512_topk() -> TrainConfig:
 
 
 def _ref_default() -> TrainConfig:
-    # the reference trainer's own DEFAULT_CONFIG (config.ts:14-22), batch 4 (trainer.ts:71)
+    # the reference trainer's own DEFAULT_CONFIG (config.ts:14-22), batch 4 (trainer.ts:71). Its heads are
+    # 64 wide and the sm_100a engine is built for 128-wide heads, so it trains on the eager path (bf16 on
+    # the GPU); multi-GPU runs then all-reduce with NCCL.
     return TrainConfig(
         model=GPTConfig(sequence_len=512, vocab_size=8192, n_layer=4, n_head=4, n_kv_head=4, n_embd=256,
                         window_pattern="L"),
-        device_batch=4, total_batch_tokens=4 * 512,
+        device_batch=4, total_batch_tokens=4 * 512, impl="torch",
     )
 
 

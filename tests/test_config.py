@@ -44,3 +44,12 @@ def test_presets_and_overrides():
     assert c.model.n_layer == 4 and c.matrix_lr == 0.02 and c.overlap is False
     m = GPT(GPTConfig(n_layer=2, n_embd=64, n_head=2, n_kv_head=2, vocab_size=64, sequence_len=16))
     assert m.num_params() == estimate_params(m.cfg)
+
+
+def test_every_preset_runs_on_a_path_that_supports_its_model():
+    from bitresearch_b200.config import PRESETS
+    from bitresearch_b200.models.engine import FusedGPTEngine
+    for name in PRESETS:
+        cfg = preset(name)
+        if cfg.impl == "cuda":
+            assert FusedGPTEngine.unsupported(cfg.model) is None, name
