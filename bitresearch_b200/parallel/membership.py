@@ -168,9 +168,13 @@ class ElasticGroup:
 
     def __init__(self, store, ring: RingTopology, room: str = "default", timeout_s: float = 30.0,
                  host: str = "127.0.0.1"):
+        import os
         opts = dist.ProcessGroupGloo._Options()
         opts._timeout = datetime.timedelta(seconds=timeout_s)
-        opts._devices = [dist.ProcessGroupGloo.create_device(hostname=host)]
+        iface = os.environ.get("GLOO_SOCKET_IFNAME", "").split(",")[0]
+        # loopback by default (one node); GLOO_SOCKET_IFNAME, gloo's own switch, names the interface otherwise
+        opts._devices = [dist.ProcessGroupGloo.create_device(interface=iface) if iface
+                         else dist.ProcessGroupGloo.create_device(hostname=host)]
         self.pg = dist.ProcessGroupGloo(dist.PrefixStore(f"{room}/pg/v{ring.version}", store), ring.position,
                                         ring.total, opts)
         self.ring = ring
