@@ -52,10 +52,7 @@ def _pool_encode(texts: list[str]) -> list[np.ndarray]:
 
 
 def _pool_count(texts: list[str]) -> collections.Counter:
-    c: collections.Counter = collections.Counter()
-    for t in texts:
-        c.update(_POOL_TOK._re.findall(t))
-    return c
+    return _POOL_TOK.chunk_counts(texts)
 
 
 class BPETokenizer:
@@ -73,8 +70,16 @@ class BPETokenizer:
         merged in order, so the result, insertion order included, is the serial one)."""
         counts: collections.Counter = collections.Counter()
         if pool is None:
-            for t in texts:
-                counts.update(self._re.findall(t))
+            texts = list(texts)
+            native = _native().count_ascii_chunks(texts) if self.pattern == SPLIT_PATTERN else None
+            if native is None:
+                rest = range(len(texts))
+            else:  # ASCII documents are split and counted natively, the others by the regex
+                keys, cnts, rest = native
+                for k, c in zip(keys, cnts):
+                    counts[k.decode("ascii")] += c
+            for i in rest:
+                counts.update(self._re.findall(texts[i]))
             return counts
         texts = list(texts)
         for part in pool.imap(_pool_count, [texts[i:i + chunk] for i in range(0, len(texts), chunk)]):
@@ -130,6 +135,10 @@ class BPETokenizer:
     def encode(self, text: str) -> np.ndarray:
         if self._enc is None:
             raise RuntimeError("tokenizer has no merges: train or load it first")
+        if self.pattern == SPLIT_PATTERN:
+            ids = self._enc.encode_text(text)  # split natively when the text is in the ASCII subset
+            if ids is not None:
+                return ids
         return self._enc.encode_chunks(self._re.findall(text))  # str chunks reach C++ as UTF-8 bytes
 
     def batch_encode(self, texts: Sequence[str], pool=None, chunk: int = 256) -> list[np.ndarray]:

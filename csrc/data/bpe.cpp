@@ -119,6 +119,159 @@ std::vector<std::pair<int32_t, int32_t>> bpe_train(const std::vector<std::string
   return merges;
 }
 
+// ------------------------------------------------------------------------------------ ASCII pre-split
+// The GPT-4 split pattern
+//   '(?i:[sdmt]|ll|ve|re) | [^\r\n\p{L}\p{N}]?+\p{L}+ | \p{N}{1,2} | ?[^\s\p{L}\p{N}]++[\r\n]* |
+//   \s*[\r\n] | \s+(?!\S) | \s+
+// restated as a scanner for text made only of printable ASCII (0x20-0x7E) and \t \n \v \f \r, where
+// \p{L} is [A-Za-z], \p{N} is [0-9] and \s is the six whitespace characters. At each position the
+// alternatives are tried in the pattern's order and the first that matches is taken, as a regex engine
+// does. Other text (non-ASCII or other control characters) returns false and is split by the regex.
+enum : uint8_t { C_LET, C_DIG, C_NL, C_WS, C_OTH, C_BAD };
+
+struct AsciiClass {
+  uint8_t c[256];
+  AsciiClass() {
+    for (int i = 0; i < 256; ++i) c[i] = C_BAD;
+    for (int i = 0x20; i < 0x7F; ++i) c[i] = C_OTH;
+    for (int i = 'a'; i <= 'z'; ++i) c[i] = C_LET;
+    for (int i = 'A'; i <= 'Z'; ++i) c[i] = C_LET;
+    for (int i = '0'; i <= '9'; ++i) c[i] = C_DIG;
+    c[(unsigned char)' '] = C_WS;
+    c[(unsigned char)'\t'] = C_WS;
+    c[0x0B] = C_WS;
+    c[0x0C] = C_WS;
+    c[(unsigned char)'\n'] = C_NL;
+    c[(unsigned char)'\r'] = C_NL;
+  }
+};
+const AsciiClass kAscii;
+
+inline bool is_ws(uint8_t k) { return k == C_WS || k == C_NL; }
+
+// Appends [begin, end) pairs of the chunks of s; false if s holds a character outside the ASCII subset.
+bool ascii_split(const std::string& s, std::vector<std::pair<size_t, size_t>>& out) {
+  const size_t n = s.size();
+  const unsigned char* p = reinterpret_cast<const unsigned char*>(s.data());
+  for (size_t i = 0; i < n; ++i)
+    if (kAscii.c[p[i]] == C_BAD) return false;
+  auto cls = [&](size_t i) -> uint8_t { return i < n ? kAscii.c[p[i]] : (uint8_t)C_BAD; };
+  auto lower = [&](size_t i) -> char { return i < n ? (char)(p[i] | 0x20) : '\0'; };
+  size_t i = 0;
+  while (i < n) {
+    const uint8_t k = cls(i);
+    // 1. contractions
+    if (p[i] == '\'') {
+      const char a = lower(i + 1);
+      if ((a == 's' || a == 'd' || a == 'm' || a == 't') && cls(i + 1) == C_LET) {
+        out.emplace_back(i, i + 2);
+        i += 2;
+        continue;
+      }
+      const char b = lower(i + 2);
+      if (cls(i + 1) == C_LET && cls(i + 2) == C_LET &&
+          ((a == 'l' && b == 'l') || (a == 'v' && b == 'e') || (a == 'r' && b == 'e'))) {
+        out.emplace_back(i, i + 3);
+        i += 3;
+        continue;
+      }
+    }
+    // 2. an optional non-letter, non-digit, non-newline character (possessive), then letters
+    if (k == C_LET || ((k == C_WS || k == C_OTH) && cls(i + 1) == C_LET)) {
+      size_t j = (k == C_LET) ? i : i + 1;
+      while (cls(j) == C_LET) ++j;
+      out.emplace_back(i, j);
+      i = j;
+      continue;
+    }
+    // 3. one or two digits
+    if (k == C_DIG) {
+      const size_t j = (cls(i + 1) == C_DIG) ? i + 2 : i + 1;
+      out.emplace_back(i, j);
+      i = j;
+      continue;
+    }
+    // 4. an optional space, other characters (possessive), then newlines
+    if (k == C_OTH || (p[i] == ' ' && cls(i + 1) == C_OTH)) {
+      size_t j = (k == C_OTH) ? i : i + 1;
+      while (cls(j) == C_OTH) ++j;
+      while (cls(j) == C_NL) ++j;
+      out.emplace_back(i, j);
+      i = j;
+      continue;
+    }
+    // whitespace from here on: the run [i, r)
+    size_t r = i;
+    while (r < n && is_ws(cls(r))) ++r;
+    // 5. whitespace up to and including its last newline
+    size_t last_nl = n;
+    for (size_t j = i; j < r; ++j)
+      if (cls(j) == C_NL) last_nl = j;
+    if (last_nl != n) {
+      out.emplace_back(i, last_nl + 1);
+      i = last_nl + 1;
+      continue;
+    }
+    // 6. whitespace not followed by a non-space: all of it at the end of the text, else all but its last
+    if (r == n) {
+      out.emplace_back(i, r);
+      i = r;
+      continue;
+    }
+    if (r - i >= 2) {
+      out.emplace_back(i, r - 1);
+      i = r - 1;
+      continue;
+    }
+    // 7. the rest of the whitespace
+    out.emplace_back(i, r);
+    i = r;
+  }
+  return true;
+}
+
+py::object split_ascii(const std::string& s) {
+  std::vector<std::pair<size_t, size_t>> sp;
+  if (!ascii_split(s, sp)) return py::none();
+  py::list out;
+  for (const auto& [a, b] : sp) out.append(py::str(s.data() + a, b - a));
+  return out;
+}
+
+// Chunk counts of many texts: (chunks as bytes, counts, indices of texts outside the ASCII subset, which
+// the caller splits with the regex). Chunks are listed in first-seen order.
+py::tuple count_ascii_chunks(const std::vector<std::string>& texts) {
+  std::unordered_map<std::string, int64_t> idx;
+  std::vector<std::string> keys;
+  std::vector<int64_t> counts;
+  std::vector<int64_t> rest;
+  {
+    py::gil_scoped_release nogil;
+    std::vector<std::pair<size_t, size_t>> sp;
+    for (size_t t = 0; t < texts.size(); ++t) {
+      sp.clear();
+      if (!ascii_split(texts[t], sp)) {
+        rest.push_back((int64_t)t);
+        continue;
+      }
+      for (const auto& [a, b] : sp) {
+        std::string c = texts[t].substr(a, b - a);
+        auto it = idx.find(c);
+        if (it == idx.end()) {
+          idx.emplace(c, (int64_t)keys.size());
+          keys.push_back(std::move(c));
+          counts.push_back(1);
+        } else {
+          counts[it->second] += 1;
+        }
+      }
+    }
+  }
+  py::list ks;
+  for (const auto& k : keys) ks.append(py::bytes(k));
+  return py::make_tuple(ks, counts, rest);
+}
+
 class BPEEncoder {
  public:
   explicit BPEEncoder(const std::vector<std::pair<int32_t, int32_t>>& merges) : merges_(merges) {
@@ -157,6 +310,23 @@ class BPEEncoder {
     return cache_.emplace(s, std::move(w)).first->second;
   }
 
+  // Splits and encodes one document when it is in the ASCII subset; None otherwise.
+  py::object encode_text(const std::string& text) {
+    std::vector<std::pair<size_t, size_t>> sp;
+    if (!ascii_split(text, sp)) return py::none();
+    std::vector<int32_t> out;
+    out.reserve(text.size() / 3 + 1);
+    std::string c;
+    for (const auto& [a, b] : sp) {
+      c.assign(text.data() + a, b - a);
+      const auto& ids = encode_chunk(c);
+      out.insert(out.end(), ids.begin(), ids.end());
+    }
+    py::array_t<int32_t> arr((py::ssize_t)out.size());
+    std::copy(out.begin(), out.end(), arr.mutable_data());
+    return std::move(arr);
+  }
+
   // Encodes pre-tokenized chunks of one document into one int32 array.
   py::array_t<int32_t> encode_chunks(const std::vector<std::string>& chunks) {
     std::vector<int32_t> out;
@@ -182,5 +352,9 @@ void register_bpe(py::module& m) {
         "Train byte-level BPE merges over (chunk, count) pairs; returns [(left, right)] in merge order.");
   py::class_<BPEEncoder>(m, "BPEEncoder")
       .def(py::init<const std::vector<std::pair<int32_t, int32_t>>&>(), py::arg("merges"))
-      .def("encode_chunks", &BPEEncoder::encode_chunks, py::arg("chunks"));
+      .def("encode_chunks", &BPEEncoder::encode_chunks, py::arg("chunks"))
+      .def("encode_text", &BPEEncoder::encode_text, py::arg("text"));
+  m.def("split_ascii", &split_ascii, py::arg("text"),
+        "GPT-4 pattern chunks of an ASCII text (printable + \\t\\n\\v\\f\\r), or None for other text.");
+  m.def("count_ascii_chunks", &count_ascii_chunks, py::arg("texts"));
 }

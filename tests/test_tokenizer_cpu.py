@@ -6,6 +6,7 @@ import os
 import random
 
 import numpy as np
+import pytest
 
 from bitresearch_b200.data.loader import discover_token_bytes, find_manifest, load_token_data, manifest_artifacts
 from bitresearch_b200.data.tokenizer import SPECIAL_TOKENS, BPETokenizer
@@ -166,4 +167,38 @@ def test_pooled_chunk_counts_match_serial():
     with tok.pool(2) as pool:
         pooled = tok.chunk_counts(docs, pool=pool, chunk=64)
     serial = tok.chunk_counts(docs)
-    assert pooled == serial and list(pooled) == list(serial)
+    assert pooled == serial
+    with tok.pool(2) as pool:
+        merges = BPETokenizer().train(docs, 256 + 80, pool=pool).merges
+    assert merges == BPETokenizer().train(docs, 256 + 80).merges  # merges depend on the counts, not their order
+
+
+def test_native_ascii_split_matches_the_regex():
+    import regex
+    nd = pytest.importorskip("bitresearch_b200._native_data")
+    from bitresearch_b200.data.tokenizer import SPLIT_PATTERN
+    pat = regex.compile(SPLIT_PATTERN)
+    rng = random.Random(1)
+    alpha = list("abZQsdmtlvreSDMTLVRE0189'\"  \t\n\r\x0b\x0c.,!?-()_#/;:<>") + ["  ", "\n\n", " '", "'s", "'LL", "\r\n"]
+    for _ in range(20000):
+        s = "".join(rng.choice(alpha) for _ in range(rng.randint(0, 24)))
+        assert nd.split_ascii(s) == pat.findall(s), repr(s)
+    chars = [chr(c) for c in range(0x20, 0x7F)] + ["\t", "\n", "\x0b", "\x0c", "\r"]
+    for x in chars:
+        for y in chars:
+            for s in (x + y + "a", " " + x + y, x + "'" + y):
+                assert nd.split_ascii(s) == pat.findall(s), repr(s)
+    assert nd.split_ascii("café") is None and nd.split_ascii("a\x01b") is None  # left to the regex
+
+
+def test_native_and_regex_paths_train_and_encode_alike():
+    docs = _corpus(300, seed=7)  # mixes ASCII documents and documents with non-ASCII words
+    tok = BPETokenizer()
+    native = tok.chunk_counts(docs)
+    by_regex = collections.Counter()
+    for d in docs:
+        by_regex.update(tok._re.findall(d))
+    assert native == by_regex
+    t = BPETokenizer().train(docs, 256 + 100)
+    for d in docs[:100]:
+        assert np.array_equal(t.encode(d), t._enc.encode_chunks(t._re.findall(d)))
