@@ -36,11 +36,17 @@ def bpe(n_docs: int, workers: int) -> None:
     from bitresearch_b200.data.tokenizer import BPETokenizer
     rng = random.Random(0)
     words = ["".join(rng.choice("abcdefghijklmnopqrstuvwxyz") for _ in range(rng.randint(1, 10))) for _ in range(5000)]
+    # web text is mostly ASCII with curly quotes, dashes, accents and some other scripts mixed in
+    words += ["\u201cquote\u201d", "caf\u00e9", "na\u00efve", "\u2014", "\u4f60\u597d", "it\u2019s", "\u00bd"] * 40
     docs = [" ".join(rng.choice(words) for _ in range(rng.randint(20, 400))) + "." for _ in range(n_docs)]
     mb = sum(map(len, docs)) / 1e6
     t = time.perf_counter()
     tok = BPETokenizer().train(docs[:5000], 4096)
     print(f"bpe train: {time.perf_counter() - t:.2f} s (5000 docs, 4096 tokens)")
+    t = time.perf_counter()
+    for d in docs:
+        tok._enc.encode_chunks(tok._re.findall(d))
+    with_regex = mb / (time.perf_counter() - t)
     t = time.perf_counter()
     tok.batch_encode(docs)
     serial = mb / (time.perf_counter() - t)
@@ -49,7 +55,8 @@ def bpe(n_docs: int, workers: int) -> None:
         t = time.perf_counter()
         tok.batch_encode(docs, pool=pool)
         pooled = mb / (time.perf_counter() - t)
-    print(f"bpe encode: {serial:.1f} MB/s on one process, {pooled:.1f} MB/s on {workers} workers ({mb:.1f} MB)")
+    print(f"bpe encode: {serial:.1f} MB/s on one process (regex split: {with_regex:.1f}), {pooled:.1f} MB/s on "
+          f"{workers} workers ({mb:.1f} MB)")
 
 
 def main() -> int:

@@ -119,128 +119,174 @@ std::vector<std::pair<int32_t, int32_t>> bpe_train(const std::vector<std::string
   return merges;
 }
 
-// ------------------------------------------------------------------------------------ ASCII pre-split
+// ---------------------------------------------------------------------------------------- native pre-split
 // The GPT-4 split pattern
 //   '(?i:[sdmt]|ll|ve|re) | [^\r\n\p{L}\p{N}]?+\p{L}+ | \p{N}{1,2} | ?[^\s\p{L}\p{N}]++[\r\n]* |
 //   \s*[\r\n] | \s+(?!\S) | \s+
-// restated as a scanner for text made only of printable ASCII (0x20-0x7E) and \t \n \v \f \r, where
-// \p{L} is [A-Za-z], \p{N} is [0-9] and \s is the six whitespace characters. At each position the
-// alternatives are tried in the pattern's order and the first that matches is taken, as a regex engine
-// does. Other text (non-ASCII or other control characters) returns false and is split by the regex.
+// restated as a scanner over code points. A class table gives each code point one of: letter (\p{L}),
+// number (\p{N}), newline (\r \n), other whitespace (\s), other, or "bad" (not handled here: the caller
+// uses the regex); its high bits name the contraction letter (s d m t l v e r) that the code point matches
+// case-insensitively. By default the table covers printable ASCII plus the ASCII whitespace; the Python
+// side installs a full table computed with the regex engine itself (set_split_table). At each position
+// the alternatives are tried in the pattern's order and the first match is taken, as a regex engine does.
 enum : uint8_t { C_LET, C_DIG, C_NL, C_WS, C_OTH, C_BAD };
+constexpr uint32_t kMaxCp = 0x110000;
 
-struct AsciiClass {
-  uint8_t c[256];
-  AsciiClass() {
-    for (int i = 0; i < 256; ++i) c[i] = C_BAD;
-    for (int i = 0x20; i < 0x7F; ++i) c[i] = C_OTH;
-    for (int i = 'a'; i <= 'z'; ++i) c[i] = C_LET;
-    for (int i = 'A'; i <= 'Z'; ++i) c[i] = C_LET;
-    for (int i = '0'; i <= '9'; ++i) c[i] = C_DIG;
-    c[(unsigned char)' '] = C_WS;
-    c[(unsigned char)'\t'] = C_WS;
-    c[0x0B] = C_WS;
-    c[0x0C] = C_WS;
-    c[(unsigned char)'\n'] = C_NL;
-    c[(unsigned char)'\r'] = C_NL;
-  }
-};
-const AsciiClass kAscii;
+std::vector<uint8_t>& split_table() {
+  static std::vector<uint8_t> t = [] {
+    std::vector<uint8_t> v(128, C_BAD);
+    for (int i = 0x20; i < 0x7F; ++i) v[i] = C_OTH;
+    for (int i = '0'; i <= '9'; ++i) v[i] = C_DIG;
+    const char* fold = "sdmtlver";
+    for (int i = 0; i < 26; ++i) {
+      uint8_t id = 0;
+      for (int k = 0; k < 8; ++k)
+        if ('a' + i == fold[k]) id = (uint8_t)(k + 1);
+      v['a' + i] = v['A' + i] = (uint8_t)(C_LET | (id << 3));
+    }
+    v[' '] = v['\t'] = v[0x0B] = v[0x0C] = C_WS;
+    v['\n'] = v['\r'] = C_NL;
+    return v;
+  }();
+  return t;
+}
 
-inline bool is_ws(uint8_t k) { return k == C_WS || k == C_NL; }
+void set_split_table(py::array_t<uint8_t, py::array::c_style> table) {
+  if (table.ndim() != 1 || table.shape(0) != (py::ssize_t)kMaxCp)
+    throw std::invalid_argument("split table must be uint8[0x110000]");
+  auto& t = split_table();
+  t.assign(table.data(), table.data() + kMaxCp);
+}
 
-// Appends [begin, end) pairs of the chunks of s; false if s holds a character outside the ASCII subset.
-bool ascii_split(const std::string& s, std::vector<std::pair<size_t, size_t>>& out) {
-  const size_t n = s.size();
+// UTF-8 -> per-code-point table entries and byte offsets (offs has one extra entry: the end).
+bool decode_classes(const std::string& s, std::vector<uint8_t>& cls, std::vector<size_t>& offs) {
+  const auto& t = split_table();
   const unsigned char* p = reinterpret_cast<const unsigned char*>(s.data());
-  for (size_t i = 0; i < n; ++i)
-    if (kAscii.c[p[i]] == C_BAD) return false;
-  auto cls = [&](size_t i) -> uint8_t { return i < n ? kAscii.c[p[i]] : (uint8_t)C_BAD; };
-  auto lower = [&](size_t i) -> char { return i < n ? (char)(p[i] | 0x20) : '\0'; };
+  const size_t n = s.size();
+  cls.clear();
+  offs.clear();
+  for (size_t i = 0; i < n;) {
+    uint32_t cp;
+    size_t len;
+    const unsigned char c = p[i];
+    if (c < 0x80) {
+      cp = c;
+      len = 1;
+    } else if ((c >> 5) == 6 && i + 1 < n) {
+      cp = ((c & 0x1F) << 6) | (p[i + 1] & 0x3F);
+      len = 2;
+    } else if ((c >> 4) == 14 && i + 2 < n) {
+      cp = ((c & 0x0F) << 12) | ((p[i + 1] & 0x3F) << 6) | (p[i + 2] & 0x3F);
+      len = 3;
+    } else if ((c >> 3) == 30 && i + 3 < n) {
+      cp = ((c & 0x07) << 18) | ((p[i + 1] & 0x3F) << 12) | ((p[i + 2] & 0x3F) << 6) | (p[i + 3] & 0x3F);
+      len = 4;
+    } else {
+      return false;
+    }
+    const uint8_t k = cp < t.size() ? t[cp] : (uint8_t)C_BAD;
+    if ((k & 7) == C_BAD) return false;
+    cls.push_back(k);
+    offs.push_back(i);
+    i += len;
+  }
+  offs.push_back(n);
+  return true;
+}
+
+// Appends [begin, end) byte ranges of the chunks of s; false if s holds a code point the table leaves out.
+bool native_split(const std::string& s, std::vector<std::pair<size_t, size_t>>& out) {
+  thread_local std::vector<uint8_t> kl;
+  thread_local std::vector<size_t> off;
+  if (!decode_classes(s, kl, off)) return false;
+  const size_t n = kl.size();
+  auto cls = [&](size_t i) -> uint8_t { return i < n ? (uint8_t)(kl[i] & 7) : (uint8_t)C_BAD; };
+  auto letter = [&](size_t i) -> uint8_t { return i < n ? (uint8_t)(kl[i] >> 3) : (uint8_t)0; };
+  auto is_ws = [&](size_t i) { const uint8_t k = cls(i); return k == C_WS || k == C_NL; };
+  auto emit = [&](size_t a, size_t b) { out.emplace_back(off[a], off[b]); };
+  enum : uint8_t { L_S = 1, L_D, L_M, L_T, L_L, L_V, L_E, L_R };
   size_t i = 0;
   while (i < n) {
     const uint8_t k = cls(i);
-    // 1. contractions
-    if (p[i] == '\'') {
-      const char a = lower(i + 1);
-      if ((a == 's' || a == 'd' || a == 'm' || a == 't') && cls(i + 1) == C_LET) {
-        out.emplace_back(i, i + 2);
+    // 1. contractions (the apostrophe is U+0027 only)
+    if (s[off[i]] == '\'' && off[i + 1] - off[i] == 1) {
+      const uint8_t a = letter(i + 1), b = letter(i + 2);
+      if (a == L_S || a == L_D || a == L_M || a == L_T) {
+        emit(i, i + 2);
         i += 2;
         continue;
       }
-      const char b = lower(i + 2);
-      if (cls(i + 1) == C_LET && cls(i + 2) == C_LET &&
-          ((a == 'l' && b == 'l') || (a == 'v' && b == 'e') || (a == 'r' && b == 'e'))) {
-        out.emplace_back(i, i + 3);
+      if ((a == L_L && b == L_L) || (a == L_V && b == L_E) || (a == L_R && b == L_E)) {
+        emit(i, i + 3);
         i += 3;
         continue;
       }
     }
-    // 2. an optional non-letter, non-digit, non-newline character (possessive), then letters
+    // 2. an optional non-letter, non-number, non-newline code point (possessive), then letters
     if (k == C_LET || ((k == C_WS || k == C_OTH) && cls(i + 1) == C_LET)) {
       size_t j = (k == C_LET) ? i : i + 1;
       while (cls(j) == C_LET) ++j;
-      out.emplace_back(i, j);
+      emit(i, j);
       i = j;
       continue;
     }
-    // 3. one or two digits
+    // 3. one or two numbers
     if (k == C_DIG) {
       const size_t j = (cls(i + 1) == C_DIG) ? i + 2 : i + 1;
-      out.emplace_back(i, j);
+      emit(i, j);
       i = j;
       continue;
     }
-    // 4. an optional space, other characters (possessive), then newlines
-    if (k == C_OTH || (p[i] == ' ' && cls(i + 1) == C_OTH)) {
+    // 4. an optional space (U+0020), others (possessive), then newlines
+    if (k == C_OTH || (s[off[i]] == ' ' && cls(i + 1) == C_OTH)) {
       size_t j = (k == C_OTH) ? i : i + 1;
       while (cls(j) == C_OTH) ++j;
       while (cls(j) == C_NL) ++j;
-      out.emplace_back(i, j);
+      emit(i, j);
       i = j;
       continue;
     }
     // whitespace from here on: the run [i, r)
     size_t r = i;
-    while (r < n && is_ws(cls(r))) ++r;
+    while (r < n && is_ws(r)) ++r;
     // 5. whitespace up to and including its last newline
     size_t last_nl = n;
     for (size_t j = i; j < r; ++j)
       if (cls(j) == C_NL) last_nl = j;
     if (last_nl != n) {
-      out.emplace_back(i, last_nl + 1);
+      emit(i, last_nl + 1);
       i = last_nl + 1;
       continue;
     }
     // 6. whitespace not followed by a non-space: all of it at the end of the text, else all but its last
     if (r == n) {
-      out.emplace_back(i, r);
+      emit(i, r);
       i = r;
       continue;
     }
     if (r - i >= 2) {
-      out.emplace_back(i, r - 1);
+      emit(i, r - 1);
       i = r - 1;
       continue;
     }
     // 7. the rest of the whitespace
-    out.emplace_back(i, r);
+    emit(i, r);
     i = r;
   }
   return true;
 }
 
-py::object split_ascii(const std::string& s) {
+py::object split_text(const std::string& s) {
   std::vector<std::pair<size_t, size_t>> sp;
-  if (!ascii_split(s, sp)) return py::none();
+  if (!native_split(s, sp)) return py::none();
   py::list out;
   for (const auto& [a, b] : sp) out.append(py::str(s.data() + a, b - a));
   return out;
 }
 
-// Chunk counts of many texts: (chunks as bytes, counts, indices of texts outside the ASCII subset, which
-// the caller splits with the regex). Chunks are listed in first-seen order.
-py::tuple count_ascii_chunks(const std::vector<std::string>& texts) {
+// Chunk counts of many texts: (chunks as UTF-8 bytes, counts, indices of texts the table cannot split,
+// which the caller splits with the regex). Chunks are listed in first-seen order.
+py::tuple count_chunks_native(const std::vector<std::string>& texts) {
   std::unordered_map<std::string, int64_t> idx;
   std::vector<std::string> keys;
   std::vector<int64_t> counts;
@@ -250,7 +296,7 @@ py::tuple count_ascii_chunks(const std::vector<std::string>& texts) {
     std::vector<std::pair<size_t, size_t>> sp;
     for (size_t t = 0; t < texts.size(); ++t) {
       sp.clear();
-      if (!ascii_split(texts[t], sp)) {
+      if (!native_split(texts[t], sp)) {
         rest.push_back((int64_t)t);
         continue;
       }
@@ -310,10 +356,10 @@ class BPEEncoder {
     return cache_.emplace(s, std::move(w)).first->second;
   }
 
-  // Splits and encodes one document when it is in the ASCII subset; None otherwise.
+  // Splits and encodes one document when the split table covers it; None otherwise.
   py::object encode_text(const std::string& text) {
     std::vector<std::pair<size_t, size_t>> sp;
-    if (!ascii_split(text, sp)) return py::none();
+    if (!native_split(text, sp)) return py::none();
     std::vector<int32_t> out;
     out.reserve(text.size() / 3 + 1);
     std::string c;
@@ -354,7 +400,9 @@ void register_bpe(py::module& m) {
       .def(py::init<const std::vector<std::pair<int32_t, int32_t>>&>(), py::arg("merges"))
       .def("encode_chunks", &BPEEncoder::encode_chunks, py::arg("chunks"))
       .def("encode_text", &BPEEncoder::encode_text, py::arg("text"));
-  m.def("split_ascii", &split_ascii, py::arg("text"),
-        "GPT-4 pattern chunks of an ASCII text (printable + \\t\\n\\v\\f\\r), or None for other text.");
-  m.def("count_ascii_chunks", &count_ascii_chunks, py::arg("texts"));
+  m.def("split_text", &split_text, py::arg("text"),
+        "GPT-4 pattern chunks of a text, or None when the split table does not cover it.");
+  m.def("count_chunks_native", &count_chunks_native, py::arg("texts"));
+  m.def("set_split_table", &set_split_table, py::arg("table"),
+        "Installs the per-code-point class table (uint8[0x110000]: class | contraction letter << 3).");
 }

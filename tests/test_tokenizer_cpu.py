@@ -173,22 +173,24 @@ def test_pooled_chunk_counts_match_serial():
     assert merges == BPETokenizer().train(docs, 256 + 80).merges  # merges depend on the counts, not their order
 
 
-def test_native_ascii_split_matches_the_regex():
+def test_native_split_matches_the_regex():
     import regex
     nd = pytest.importorskip("bitresearch_b200._native_data")
     from bitresearch_b200.data.tokenizer import SPLIT_PATTERN
+    BPETokenizer()  # installs the code-point table
     pat = regex.compile(SPLIT_PATTERN)
     rng = random.Random(1)
-    alpha = list("abZQsdmtlvreSDMTLVRE0189'\"  \t\n\r\x0b\x0c.,!?-()_#/;:<>") + ["  ", "\n\n", " '", "'s", "'LL", "\r\n"]
+    alpha = list("abZQsdmtlvreSDMTLVRE0189'\"  \t\n\r\x0b\x0c.,!?-()_#/;:<>") + [
+        "  ", "\n\n", " '", "'s", "'LL", "\r\n", "é", "ß", "\u017f", "你", "²", "½", "\u0663", "\u216b", "\xa0", "\x85",
+        "\u3000", "\x1c", "\u200b", "\u201c", "\u2014", "\U0001f600", "\u0301", "\u212a", "\x00", "\x7f"]
     for _ in range(20000):
         s = "".join(rng.choice(alpha) for _ in range(rng.randint(0, 24)))
-        assert nd.split_ascii(s) == pat.findall(s), repr(s)
-    chars = [chr(c) for c in range(0x20, 0x7F)] + ["\t", "\n", "\x0b", "\x0c", "\r"]
+        assert nd.split_text(s) == pat.findall(s), repr(s)
+    chars = [chr(c) for c in range(0x20, 0x7F)] + ["\t", "\n", "\x0b", "\x0c", "\r", "\xa0", "\u017f", "\u2028"]
     for x in chars:
         for y in chars:
             for s in (x + y + "a", " " + x + y, x + "'" + y):
-                assert nd.split_ascii(s) == pat.findall(s), repr(s)
-    assert nd.split_ascii("café") is None and nd.split_ascii("a\x01b") is None  # left to the regex
+                assert nd.split_text(s) == pat.findall(s), repr(s)
 
 
 def test_native_and_regex_paths_train_and_encode_alike():
