@@ -24,6 +24,7 @@ import base64
 import collections
 import json
 import os
+import threading
 from typing import Iterable, Sequence
 
 import numpy as np
@@ -40,6 +41,7 @@ def _native():
 
 
 _SPLIT_TABLE = False
+_SPLIT_LOCK = threading.Lock()
 
 
 def _install_split_table() -> None:
@@ -47,8 +49,13 @@ def _install_split_table() -> None:
     (``\p{L}``, ``\p{N}``, ``\s``, and which code points match the contraction letters case-insensitively),
     so the native and regex splits agree by construction. Once per process, about 0.3 s."""
     global _SPLIT_TABLE
-    if _SPLIT_TABLE:
-        return
+    with _SPLIT_LOCK:
+        if not _SPLIT_TABLE:
+            _build_split_table()
+            _SPLIT_TABLE = True
+
+
+def _build_split_table() -> None:
     import regex
     let, dig, nl, ws, oth, bad = range(6)
     allc = "".join(map(chr, range(0xD800))) + "".join(map(chr, range(0xE000, 0x110000)))
@@ -60,7 +67,6 @@ def _install_split_table() -> None:
     for k, ch in enumerate("sdmtlver"):
         t[np.fromiter(map(ord, regex.findall(f"(?i:{ch})", allc)), dtype=np.int64)] |= (k + 1) << 3
     _native().set_split_table(t)
-    _SPLIT_TABLE = True
 
 
 _POOL_TOK: "BPETokenizer | None" = None

@@ -155,6 +155,7 @@ void set_split_table(py::array_t<uint8_t, py::array::c_style> table) {
   if (table.ndim() != 1 || table.shape(0) != (py::ssize_t)kMaxCp)
     throw std::invalid_argument("split table must be uint8[0x110000]");
   auto& t = split_table();
+  if (t.size() == kMaxCp) return;  // installed once; readers may run without the GIL, so never replaced
   t.assign(table.data(), table.data() + kMaxCp);
 }
 
