@@ -1,5 +1,5 @@
 """Host data-path throughput: the native packer per synthetic source, and BPE encoding of a synthetic
-text corpus on one process and on a worker pool.
+web-like text corpus on one thread and on a thread pool.
 
   python benchmarks/data_path.py [--docs 20000] [--workers 8]
 
@@ -55,8 +55,8 @@ def bpe(n_docs: int, workers: int) -> None:
         t = time.perf_counter()
         tok.batch_encode(docs, pool=pool)
         pooled = mb / (time.perf_counter() - t)
-    print(f"bpe encode: {serial:.1f} MB/s on one process (regex split: {with_regex:.1f}), {pooled:.1f} MB/s on "
-          f"{workers} workers ({mb:.1f} MB)")
+    print(f"bpe encode: {serial:.1f} MB/s on one thread (regex split: {with_regex:.1f}), {pooled:.1f} MB/s on "
+          f"{workers} threads ({mb:.1f} MB)")
 
 
 def main() -> int:

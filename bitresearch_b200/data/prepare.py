@@ -68,7 +68,7 @@ def collect_training_corpus(text_dir: str, files: list[str], max_chars: int, doc
 
 def tokenize_shard(tok: BPETokenizer, src: str, dst: str, batch: int = 2048, pool=None) -> tuple[int, int]:
     """Writes BOS-prefixed int32 ids of every non-empty line of ``src`` to ``dst`` (atomically); with a
-    ``pool`` (``tok.pool(n)``) each batch of lines is encoded across its worker processes, in order."""
+    ``pool`` (``tok.pool(n)``) each batch of lines is encoded across its threads, in order."""
     if pool is not None:
         batch = max(batch, 16384)  # enough 256-line tasks per flush to keep every worker busy
     tmp = dst + ".tmp"
@@ -165,7 +165,7 @@ def main(argv=None) -> int:
     ap.add_argument("--train-doc-cap", type=int, default=_env_int("PREPARE_WASM_TRAIN_DOC_CAP", 10_000, 1))
     ap.add_argument("--tokenize-shards", type=int, default=_env_int("PREPARE_WASM_TOKENIZE_SHARDS", 0, 0))
     ap.add_argument("--no-parity", action="store_true", help="skip the parity mirror and manifest")
-    ap.add_argument("--workers", type=int, default=os.cpu_count() or 1, help="encoding processes")
+    ap.add_argument("--workers", type=int, default=os.cpu_count() or 1, help="encoding threads")
     args = ap.parse_args(argv)
     text_dir = args.text_dir or os.path.join(args.cache_dir, "text")
     bin_dir = args.bin_dir or os.path.join(args.cache_dir, "bin")
@@ -184,7 +184,7 @@ def main(argv=None) -> int:
     print(f"training on {len(docs):,} documents ({chars:,} characters)")
     t0 = time.time()
     tok = BPETokenizer()
-    if args.workers > 1:  # the chunk split of the training corpus runs in worker processes
+    if args.workers > 1:  # the chunk split of the training corpus runs on threads
         with tok.pool(args.workers) as count_pool:
             tok.train(docs, args.vocab_size - len(SPECIAL_TOKENS), pool=count_pool)
     else:
@@ -205,8 +205,7 @@ def main(argv=None) -> int:
             print(f"  {name}: {nd:,} docs / {nt:,} tokens in {time.time() - t1:.1f}s")
     finally:
         if pool is not None:
-            pool.close()
-            pool.join()
+            pool.shutdown()
     if not args.no_parity:
         os.makedirs(args.public_data_dir, exist_ok=True)
         m = sync_parity_artifacts(args.cache_dir, bin_dir, tok_dir, args.public_data_dir)

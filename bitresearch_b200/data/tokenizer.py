@@ -69,22 +69,6 @@ def _build_split_table() -> None:
     _native().set_split_table(t)
 
 
-_POOL_TOK: "BPETokenizer | None" = None
-
-
-def _pool_init(merges, pattern) -> None:
-    global _POOL_TOK
-    _POOL_TOK = BPETokenizer(merges, pattern)
-
-
-def _pool_encode(texts: list[str]) -> list[np.ndarray]:
-    return [_POOL_TOK.encode(t) for t in texts]
-
-
-def _pool_count(texts: list[str]) -> collections.Counter:
-    return _POOL_TOK.chunk_counts(texts)
-
-
 class BPETokenizer:
     def __init__(self, merges: Sequence[tuple[int, int]] = (), pattern: str = SPLIT_PATTERN):
         import regex
@@ -95,12 +79,13 @@ class BPETokenizer:
         if self.native_split:
             _install_split_table()
         self._enc = _native().BPEEncoder(self.merges) if self.merges else None
+        self._tls = threading.local()  # one encoder per pool thread (an encoder's chunk cache is not shared)
         self._vocab_bytes: list[bytes] | None = None
 
     # ------------------------------------------------------------------ training
     def chunk_counts(self, texts: Iterable[str], pool=None, chunk: int = 2048) -> collections.Counter:
-        """Occurrences of every pre-tokenized chunk; with a ``pool`` the split runs in its workers (parts
-        merged in order, so the result, insertion order included, is the serial one)."""
+        """Occurrences of every pre-tokenized chunk; with a ``pool`` from :meth:`pool` the parts are split
+        and counted on its threads (natively, without the GIL) and merged in order."""
         counts: collections.Counter = collections.Counter()
         if pool is None:
             texts = list(texts)
@@ -115,7 +100,7 @@ class BPETokenizer:
                 counts.update(self._re.findall(texts[i]))
             return counts
         texts = list(texts)
-        for part in pool.imap(_pool_count, [texts[i:i + chunk] for i in range(0, len(texts), chunk)]):
+        for part in pool.map(self.chunk_counts, [texts[i:i + chunk] for i in range(0, len(texts), chunk)]):
             counts.update(part)
         return counts
 
@@ -126,6 +111,7 @@ class BPETokenizer:
         merges = _native().bpe_train(chunks, list(counts.values()), int(vocab_size_no_special))
         self.merges = [tuple(m) for m in merges]
         self._enc = _native().BPEEncoder(self.merges)
+        self._tls = threading.local()
         self._vocab_bytes = None
         return self
 
@@ -165,29 +151,34 @@ class BPETokenizer:
         return tb
 
     # ------------------------------------------------------------------ encode / decode
-    def encode(self, text: str) -> np.ndarray:
-        if self._enc is None:
+    def encode(self, text: str, _enc=None) -> np.ndarray:
+        enc = _enc or self._enc
+        if enc is None:
             raise RuntimeError("tokenizer has no merges: train or load it first")
         if self.native_split:
-            ids = self._enc.encode_text(text)  # split natively unless the text holds a lone surrogate
+            ids = enc.encode_text(text)  # split natively unless the text holds a lone surrogate
             if ids is not None:
                 return ids
-        return self._enc.encode_chunks(self._re.findall(text))  # str chunks reach C++ as UTF-8 bytes
+        return enc.encode_chunks(self._re.findall(text))  # str chunks reach C++ as UTF-8 bytes
+
+    def _encode_part(self, texts: list[str]) -> list[np.ndarray]:
+        enc = getattr(self._tls, "enc", None)
+        if enc is None:
+            enc = self._tls.enc = _native().BPEEncoder(self.merges)
+        return [self.encode(t, enc) for t in texts]
 
     def batch_encode(self, texts: Sequence[str], pool=None, chunk: int = 256) -> list[np.ndarray]:
-        """Encodes ``texts`` in order; with a ``pool`` from :meth:`pool`, split over its worker processes
-        (the regex pre-split is Python-level work, so threads would serialise on the GIL)."""
+        """Encodes ``texts`` in order; with a ``pool`` from :meth:`pool` the parts run on its threads, each
+        with its own encoder (the native split and merge loop release the GIL)."""
         if pool is None or len(texts) <= chunk:
             return [self.encode(t) for t in texts]
         parts = [list(texts[i:i + chunk]) for i in range(0, len(texts), chunk)]
-        return [ids for part in pool.imap(_pool_encode, parts) for ids in part]
+        return [ids for part in pool.map(self._encode_part, parts) for ids in part]
 
     def pool(self, workers: int):
-        """A process pool whose workers each hold this tokenizer. Workers start from a fork server (a clean
-        single-threaded process) rather than by forking the caller, which may run threads (torch's)."""
-        import multiprocessing as mp
-        ctx = mp.get_context("forkserver" if "forkserver" in mp.get_all_start_methods() else "spawn")
-        return ctx.Pool(workers, initializer=_pool_init, initargs=(self.merges, self.pattern))
+        """A thread pool for :meth:`batch_encode` and :meth:`chunk_counts` (use it as a context manager)."""
+        from concurrent.futures import ThreadPoolExecutor
+        return ThreadPoolExecutor(max_workers=max(1, workers), thread_name_prefix="bpe")
 
     def decode(self, ids: Iterable[int]) -> str:
         vb = self.vocab_bytes()

@@ -357,18 +357,27 @@ class BPEEncoder {
     return cache_.emplace(s, std::move(w)).first->second;
   }
 
-  // Splits and encodes one document when the split table covers it; None otherwise.
+  // Splits and encodes one document when the split table covers it; None otherwise. The work runs
+  // without the GIL, so threads with an encoder each encode in parallel (one encoder is not thread-safe:
+  // its chunk cache is shared by its calls).
   py::object encode_text(const std::string& text) {
-    std::vector<std::pair<size_t, size_t>> sp;
-    if (!native_split(text, sp)) return py::none();
     std::vector<int32_t> out;
-    out.reserve(text.size() / 3 + 1);
-    std::string c;
-    for (const auto& [a, b] : sp) {
-      c.assign(text.data() + a, b - a);
-      const auto& ids = encode_chunk(c);
-      out.insert(out.end(), ids.begin(), ids.end());
+    bool ok;
+    {
+      py::gil_scoped_release nogil;
+      std::vector<std::pair<size_t, size_t>> sp;
+      ok = native_split(text, sp);
+      if (ok) {
+        out.reserve(text.size() / 3 + 1);
+        std::string c;
+        for (const auto& [a, b] : sp) {
+          c.assign(text.data() + a, b - a);
+          const auto& ids = encode_chunk(c);
+          out.insert(out.end(), ids.begin(), ids.end());
+        }
+      }
     }
+    if (!ok) return py::none();
     py::array_t<int32_t> arr((py::ssize_t)out.size());
     std::copy(out.begin(), out.end(), arr.mutable_data());
     return std::move(arr);
