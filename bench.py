@@ -25,6 +25,7 @@ import os
 import sys
 import time
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -33,6 +34,22 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "tokens/s (device-timed, max over ranks)"
+def _resident_batches(cfg, rank, world, B, T, accum, device, dtype):
+    """Two steps' worth of micro-batches from the configured seeded data stream (the same for both
+    arms), kept on the device and alternated in the timed loop."""
+    from bitresearch_b200.data.pipeline import make_batch_source
+    src = make_batch_source(cfg, "train", rank, world)
+    out = []
+    for _ in range(2):
+        step = []
+        for _ in range(accum):
+            x, y = src.next(B, T)
+            step.append((torch.from_numpy(np.ascontiguousarray(x)).to(device=device, dtype=dtype),
+                         torch.from_numpy(np.ascontiguousarray(y)).to(device=device, dtype=dtype)))
+        out.append(step)
+    return out
+
+
 def model_desc(m) -> str:
     """e.g. 'autoresearch GPT d512 depth-8 (4x128 heads, vocab 8192, SSSL windows 1024/2048, VE, ReLU^2, QK-norm)'."""
     hd = m.n_embd // m.n_head
@@ -120,10 +137,7 @@ def main():
         tr.initialize()
         accum = tr.grad_accum
         B = tr.device_batch
-        gen = torch.Generator(device="cpu").manual_seed(1234 + rank)
-        batches = [[(torch.randint(0, cfg.model.vocab_size, (B, T), generator=gen, dtype=torch.int32).to(device),
-                     torch.randint(0, cfg.model.vocab_size, (B, T), generator=gen, dtype=torch.int32).to(device))
-                    for _ in range(accum)] for _ in range(2)]
+        batches = _resident_batches(cfg, rank, world, B, T, accum, device, torch.int32)
         it = [0]
 
         def step():
@@ -137,10 +151,7 @@ def main():
         cfg.impl = "torch"
         tr = DDPBaseline(cfg, device)
         accum, B = tr.grad_accum, tr.device_batch
-        gen = torch.Generator(device="cpu").manual_seed(1234 + rank)
-        batches = [[(torch.randint(0, cfg.model.vocab_size, (B, T), generator=gen).to(device),
-                     torch.randint(0, cfg.model.vocab_size, (B, T), generator=gen).to(device))
-                    for _ in range(accum)] for _ in range(2)]
+        batches = _resident_batches(cfg, rank, world, B, T, accum, device, torch.int64)
         it = [0]
 
         def step():
@@ -177,7 +188,9 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic: seeded random token ids; random-init weights",
+            "dtype": "bf16", "data": (f"synthetic: seeded {cfg.data} stream ({'Zipf(1.1) tokens BOS-packed into geometric-length documents' if cfg.data == 'zipf' else cfg.data}), "
+                     "device-timed steps on resident batches, the e2e field through the trainer's pinned pipeline; "
+                     "random-init weights"),
             "config": {"model": model_desc(cfg.model), "global_batch": global_tokens, "global_batch_unit": "tokens",
                        "seq_len": T, "device_batch": B, "grad_accum": accum, "parallelism": f"dp{world}",
                        "comm": (args.comm if args.impl == "ours" else "nccl-ddp") if world > 1 else "none",
