@@ -56,6 +56,13 @@ def test_gloo_dp_ring_ranks_identical():
         assert np.array_equal(r0[n], r1[n]), n
 
 
+def test_gloo_dp_process_group_all_reduce_ranks_identical():
+    # comm=nccl: one all-reduce of the flat gradient over the default group (gloo here), replicated optimizer
+    r0, r1 = run_world(_dp, 2, "nccl", False)
+    for n in r0:
+        assert np.array_equal(r0[n], r1[n]), n
+
+
 def test_gloo_dp_topk_sparsified_ring():
     r0, r1 = run_world(_dp, 2, "ring", True)
     for n in r0:
