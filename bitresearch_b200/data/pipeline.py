@@ -217,26 +217,33 @@ class PinnedPrefetcher:
             self.free.put(i)
         self.h2d_bytes = 2 * batch * seq * 4
         self._stop = False
+        self._error: BaseException | None = None
         self.thread = threading.Thread(target=self._fill, daemon=True)
         self.thread.start()
         self._inflight: list[int] = []
 
     def _fill(self):
-        while not self._stop:
-            i = self.free.get()
-            if i is None:
-                return
-            hx, hy = self.host[i]
-            if hasattr(self.source, "next_into"):
-                self.source.next_into(hx, hy, self.batch, self.seq)
-            else:
-                x, y = self.source.next(self.batch, self.seq)
-                hx.numpy()[...] = x
-                hy.numpy()[...] = y
-            self.ready.put(i)
+        try:
+            while not self._stop:
+                i = self.free.get()
+                if i is None:
+                    return
+                hx, hy = self.host[i]
+                if hasattr(self.source, "next_into"):
+                    self.source.next_into(hx, hy, self.batch, self.seq)
+                else:
+                    x, y = self.source.next(self.batch, self.seq)
+                    hx.numpy()[...] = x
+                    hy.numpy()[...] = y
+                self.ready.put(i)
+        except BaseException as e:  # handed to the consumer, which would otherwise wait forever
+            self._error = e
+            self.ready.put(-1)
 
     def get(self):
         i = self.ready.get()
+        if i < 0:
+            raise RuntimeError(f"the data thread failed: {self._error!r}") from self._error
         hx, hy = self.host[i]
         dx, dy = self.dev[i]
         cur = torch.cuda.current_stream(self.device)

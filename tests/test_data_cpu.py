@@ -191,3 +191,24 @@ def test_json_documents_and_tokens_payloads(tmp_path):
     cfg = apply_overrides(preset("tiny-cpu"), ["data=tokens", f"data_path={t}"])
     x, y = make_batch_source(cfg, "train", 0, 1).next(2, 8)
     assert x[0].tolist() == list(range(8)) and y[0].tolist() == list(range(1, 9))
+
+
+def test_prefetcher_hands_a_data_error_to_the_consumer():
+    """A failing source must surface in get() instead of leaving the training loop waiting."""
+    from queue import Queue
+
+    import torch
+    from bitresearch_b200.data.pipeline import PinnedPrefetcher
+
+    class Broken:
+        def next(self, b, t):
+            raise ValueError("corrupt shard")
+
+    p = PinnedPrefetcher.__new__(PinnedPrefetcher)  # no CUDA here: only the host side is exercised
+    p.source, p.batch, p.seq = Broken(), 2, 4
+    p.host = [(torch.zeros(2, 4, dtype=torch.int32), torch.zeros(2, 4, dtype=torch.int32))]
+    p.free, p.ready, p._stop, p._error = Queue(), Queue(), False, None
+    p.free.put(0)
+    p._fill()
+    with pytest.raises(RuntimeError, match="corrupt shard"):
+        p.get()
