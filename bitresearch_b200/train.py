@@ -595,7 +595,12 @@ class Trainer:
             d = path or os.path.join(self.cfg.checkpoint_dir, f"step{self.metrics.step:06d}")
             ckpt.save_sharded(d, self.rank, self.world, t_local if self.rank == 0 else
                               OrderedDict((k, v) for k, v in t_local.items() if k.startswith(("adam_", "muon_"))), meta)
-            dist.barrier()
+            # every shard is on disk before position 0 merges (a blocking gloo all-reduce over the live ring
+            # in elastic mode, where the default group may contain a lost rank)
+            if self.egroup is None:
+                dist.barrier()
+            elif not self.egroup.all_reduce(torch.zeros(1), dist.ReduceOp.SUM):
+                raise RuntimeError("a peer was lost while saving a checkpoint")
             if self.rank == 0:
                 out = d + ".safetensors"
                 ckpt.merge_shards(d, out, order=[n for n, _, _ in self.specs])

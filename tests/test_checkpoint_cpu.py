@@ -1,4 +1,5 @@
 import json
+import os
 import struct
 
 import torch
@@ -100,3 +101,40 @@ def test_eval_cli_takes_the_model_from_a_reference_style_checkpoint(tmp_path, ca
                  "device_batch=2"]) == 0
     out = capsys.readouterr().out
     assert float(out.split("val_bpb:")[1].split()[0]) > 0 and "step:             11" in out
+
+
+def _sharded_save(rank, world, out_dir):
+    import numpy as np
+    from bitresearch_b200.config import apply_overrides, preset
+    from bitresearch_b200.train import Trainer
+    cfg = apply_overrides(preset("tiny-cpu"), ["model.n_layer=1", "model.n_embd=64", "model.n_head=1",
+                                               "model.n_kv_head=1", "model.sequence_len=32", "model.vocab_size=128",
+                                               "device_batch=2", f"total_batch_tokens={64 * world}",
+                                               "eval_tokens=128", "log_every=0", "results_tsv=", "comm=ring"])
+    tr = Trainer(cfg, device="cpu", log=lambda m: None)
+    tr.initialize()
+    for _ in range(2):
+        tr.train_step()
+    path = tr.save_checkpoint(os.path.join(out_dir, "ck"))
+    return path, {n: p.detach().numpy().copy() for n, p in tr.model.named().items()}
+
+
+def test_multi_rank_checkpoint_merges_and_reloads(tmp_path):
+    import numpy as np
+    from dist_utils import run_world
+    from bitresearch_b200.config import apply_overrides, preset
+    from bitresearch_b200.train import Trainer
+    (p0, w0), (p1, _) = run_world(_sharded_save, 2, str(tmp_path))
+    assert p0.endswith(".safetensors") and os.path.isfile(p0)
+    t, meta = ckpt.load(p0)
+    assert "shard" not in meta and any(k.startswith("adam_") for k in t) and any(k.startswith("muon_") for k in t)
+    cfg = apply_overrides(preset("tiny-cpu"), ["model.n_layer=1", "model.n_embd=64", "model.n_head=1",
+                                               "model.n_kv_head=1", "model.sequence_len=32", "model.vocab_size=128",
+                                               "device_batch=2", "total_batch_tokens=64", "eval_tokens=128",
+                                               "log_every=0", "results_tsv="])
+    tr = Trainer(cfg, device="cpu", log=lambda m: None)
+    tr.initialize()
+    info = tr.load_checkpoint(p0)
+    assert info["step"] == 2 and info["optimizer_loaded"]
+    for n, p in tr.model.named().items():
+        assert np.array_equal(p.detach().numpy(), w0[n]), n
