@@ -7,7 +7,7 @@
 import glob
 import os
 
-from setuptools import setup
+from setuptools import find_packages, setup
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
@@ -55,7 +55,7 @@ os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")  # the explicit -gencode 
 setup(
     name="bitresearch_b200",
     version="0.1.0",
-    packages=["bitresearch_b200"],
+    packages=find_packages(include=["bitresearch_b200", "bitresearch_b200.*"]),
     ext_modules=_ext_modules(),
     cmdclass=_cmdclass(),
 )
