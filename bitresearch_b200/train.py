@@ -657,7 +657,7 @@ def _launch_peers(n: int, argv: list[str]) -> int:
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description="bitresearch-b200 data-parallel GPT trainer")
-    ap.add_argument("--preset", default="d512")
+    ap.add_argument("--preset", default=None, help="default d512; with --resume, the checkpoint's own config")
     ap.add_argument("--resume", default="")
     # the reference launcher's flags (scripts/launch.ts:13-23); the same settings as key=value work too
     ap.add_argument("--peers", type=int, default=0, help="launch N local ranks (one per GPU) and train on all")
@@ -681,7 +681,12 @@ def main(argv=None):
         return _launch_peers(args.peers, rest)
     extra = ([f"max_steps={args.max_steps}"] if args.max_steps else []) + (
         [f"time_budget={args.max_seconds}"] if args.max_seconds else [])
-    cfg = apply_overrides(preset(args.preset), list(args.overrides) + extra)
+    if args.resume and args.preset is None:  # continue with the configuration the checkpoint was trained with
+        from .eval import _config_from_checkpoint
+        base = _config_from_checkpoint(args.resume, preset("d512"))
+    else:
+        base = preset(args.preset or "d512")
+    cfg = apply_overrides(base, list(args.overrides) + extra)
     rank, world, local = init_distributed("nccl" if torch.cuda.is_available() and cfg.impl != "cpu" else "gloo")
     if not torch.cuda.is_available():
         cfg.impl = "torch"

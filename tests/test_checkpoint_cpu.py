@@ -138,3 +138,17 @@ def test_multi_rank_checkpoint_merges_and_reloads(tmp_path):
     assert info["step"] == 2 and info["optimizer_loaded"]
     for n, p in tr.model.named().items():
         assert np.array_equal(p.detach().numpy(), w0[n]), n
+
+
+def test_resume_takes_the_checkpoint_config(tmp_path, capsys):
+    from bitresearch_b200.train import main
+    common = ["results_tsv=", "log_every=0", "eval_tokens=256", "model.n_layer=1", "model.n_embd=64",
+              "model.n_head=1", "model.n_kv_head=1", "model.sequence_len=32", "model.vocab_size=128",
+              "device_batch=2", "total_batch_tokens=64", f"checkpoint_dir={tmp_path}", "checkpoint_interval=3"]
+    main(["--preset", "tiny-cpu", "--max-steps", "3"] + common)
+    saved = sorted(p for p in os.listdir(tmp_path) if p.endswith(".safetensors"))
+    assert len(saved) == 1
+    capsys.readouterr()
+    main(["--resume", str(tmp_path / saved[0]), "--max-steps", "5", "checkpoint_interval=0"])
+    out = capsys.readouterr().out
+    assert "num_steps:        5" in out and "depth:            1" in out  # the tiny model, not the d512 default
