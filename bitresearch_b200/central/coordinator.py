@@ -405,10 +405,13 @@ class CoordinatorThread:
 
     def _run(self):
         asyncio.set_event_loop(self.loop)
-        self.loop.run_until_complete(self.coord.start())
-        self._ready.set()
-        self.loop.run_until_complete(self.coord.finished.wait())
-        self.loop.run_until_complete(self.coord.shutdown())
+        try:
+            self.loop.run_until_complete(self.coord.start())
+            self._ready.set()
+            self.loop.run_until_complete(self.coord.finished.wait())
+            self.loop.run_until_complete(self.coord.shutdown())
+        finally:
+            self.loop.close()
 
     def start(self) -> int:
         self.thread.start()

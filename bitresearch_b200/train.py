@@ -393,7 +393,7 @@ class Trainer:
         if step == a and self._profiler is None:
             acts = [torch.profiler.ProfilerActivity.CPU] + (
                 [torch.profiler.ProfilerActivity.CUDA] if self.is_cuda else [])
-            self._profiler = torch.profiler.profile(activities=acts, record_shapes=False)
+            self._profiler = torch.profiler.profile(activities=acts, record_shapes=False, acc_events=True)
             self._profiler.__enter__()
         elif step == b and self._profiler is not None:
             self._profiler.__exit__(None, None, None)

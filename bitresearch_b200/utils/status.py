@@ -94,7 +94,7 @@ class StatusServer:
 
     def publish(self, msg: dict) -> None:
         """Sends ``msg`` to every ``/ws`` client; callable from any thread, never blocks."""
-        if self._stop is None or not self.thread.is_alive():
+        if self._stop is None or not self.thread.is_alive() or self.loop.is_closed():
             return
         text = json.dumps(msg, default=str)
         self.published += 1
@@ -135,6 +135,8 @@ class StatusServer:
         except BaseException as e:  # surfaced by start()
             self._error = e
             self._ready.set()
+        finally:
+            self.loop.close()
 
     @property
     def url(self) -> str:
