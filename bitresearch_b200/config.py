@@ -218,6 +218,8 @@ class TrainConfig:
     heartbeat_s: float = 2.0  # the reference pings every 2 s (webrtc-mesh.ts:173-196)
     dead_after_s: float = 10.0  # a peer silent this long is dropped at the next re-formation
     reform_timeout_s: float = 60.0
+    # elastic ring: pause while fewer peers are alive (trainer.ts minRingSize), stop after reform_timeout_s
+    min_ring_size: int = 1
     # checkpoints / logging
     checkpoint_interval: int = 0
     checkpoint_dir: str = "checkpoints"

@@ -455,6 +455,14 @@ class Trainer:
         old = self.egroup.ring.peers
         self.log(f"peer lost at step {self.metrics.step}; re-forming the ring of {len(old)}")
         ring = self.membership.wait_for_change(old, cfg.reform_timeout_s)
+        if ring.total < cfg.min_ring_size:
+            # the reference pauses while the ring is smaller than minRingSize, polling every 2 s
+            # (src/distributed/trainer.ts:992-999); peers that rejoin the store's room are taken in
+            self.log(f"ring too small ({ring.total}/{cfg.min_ring_size}), waiting up to {cfg.reform_timeout_s:.0f} s")
+            try:
+                ring = self.membership.wait_for(cfg.min_ring_size, cfg.reform_timeout_s)
+            except TimeoutError as e:
+                raise RuntimeError(f"ring stayed below min_ring_size={cfg.min_ring_size}: {e}") from e
         self.egroup = ElasticGroup(self._store, ring, room="train", timeout_s=self._ring_timeout())
         self.comm = RingAllReduce(wire_dtype=cfg.wire_dtype, timeout_s=self._ring_timeout(), log=self.log,
                                   elastic=self.egroup)

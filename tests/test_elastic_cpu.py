@@ -13,12 +13,12 @@ class _Crash(Exception):
     pass
 
 
-def _elastic(rank, world, crash_rank, crash_after):
+def _elastic(rank, world, crash_rank, crash_after, extra=()):
     cfg = apply_overrides(preset("tiny-cpu"), [
         "model.n_layer=1", "model.n_embd=64", "model.n_head=1", "model.n_kv_head=1", "model.sequence_len=32",
         "model.vocab_size=128", "device_batch=2", f"total_batch_tokens={64 * world}", "eval_tokens=128",
         "log_every=0", "results_tsv=", "max_steps=8", "time_budget=1e9", "comm=ring", "elastic=true",
-        "heartbeat_s=0.2", "dead_after_s=3", "comm_timeout_s=4", "reform_timeout_s=60"])
+        "heartbeat_s=0.2", "dead_after_s=3", "comm_timeout_s=4", "reform_timeout_s=60", *extra])
     logs = []
     tr = Trainer(cfg, device="cpu", log=logs.append)
     tr.initialize()
@@ -37,7 +37,11 @@ def _elastic(rank, world, crash_rank, crash_after):
             tr.membership.stop()  # no graceful leave: the heartbeat just stops
             tr.egroup.pg.abort()
             return {"crashed_at": tr.metrics.step}
-    m = tr.start_training()
+    try:
+        m = tr.start_training()
+    except RuntimeError as e:
+        tr.destroy()
+        return {"error": str(e), "logs": logs}
     params = np.concatenate([v.detach().numpy().ravel() for v in tr.model.named().values()])
     tr.destroy()
     return {"step": m.step, "world": tr.world, "rank": tr.rank, "skipped": m.skipped_steps, "params": params,
@@ -53,3 +57,11 @@ def test_survivors_reform_the_ring_and_finish_in_lockstep():
     assert (r0["rank"], r1["rank"]) == (0, 1)
     assert np.array_equal(r0["params"], r1["params"])
     assert any("ring re-formed: version 2, 2 peers" in line for line in r0["logs"]), r0["logs"]
+
+
+def test_ring_below_min_size_stops_instead_of_training_on():
+    r0, r1, r2 = run_world(_elastic, 3, 2, 3, ("min_ring_size=3", "reform_timeout_s=8"), timeout=180)
+    assert r2 == {"crashed_at": 3}
+    for r in (r0, r1):
+        assert "ring stayed below min_ring_size=3" in r.get("error", ""), r
+    assert any("ring too small (2/3)" in line for line in r0["logs"])
