@@ -220,6 +220,12 @@ class TrainConfig:
     reform_timeout_s: float = 60.0
     # elastic ring: pause while fewer peers are alive (trainer.ts minRingSize), stop after reform_timeout_s
     min_ring_size: int = 1
+    # elastic ring: this process joins a running job's ring instead of forming the first one (it takes
+    # part in the next re-formation and receives the state from a member)
+    elastic_join: bool = False
+    # elastic ring: every this many steps the members take in peers that joined the room (0 = never;
+    # a ring paused below min_ring_size always takes them in)
+    join_check_steps: int = 10
     # checkpoints / logging
     checkpoint_interval: int = 0
     checkpoint_dir: str = "checkpoints"

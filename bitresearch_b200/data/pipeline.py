@@ -241,8 +241,11 @@ class PinnedPrefetcher:
             self.ready.put(-1)
 
     def get(self):
+        if self._error is not None:  # every later call raises too, instead of waiting on an empty queue
+            raise RuntimeError(f"the data thread failed: {self._error!r}") from self._error
         i = self.ready.get()
         if i < 0:
+            self.ready.put(-1)
             raise RuntimeError(f"the data thread failed: {self._error!r}") from self._error
         hx, hy = self.host[i]
         dx, dy = self.dev[i]

@@ -14,9 +14,11 @@ NVSwitch node with a direct algorithm:
   ``signal`` (flags[bucket] = step, release) -> ``reduce`` (every owner reads its owned elements from
   all peers' send buffers, sums in fp32, scales by 1/N). The 1/N scale is the mean, fixing the
   reference's ring, which returns the sum (ring-allreduce.ts:161-165).
-* **After backward:** the sharded MuonAdamW step on owned parameters, ``signal`` (flags[params]),
-  then ``gather``: each rank pulls the parameters it does not own from their owners, refreshing the
-  bf16 GEMM shadows in the same pass.
+* **After backward:** the sharded MuonAdamW step on owned parameters, then ``push``: each owner
+  stores its updated parameters into every peer's symmetric parameter buffer with posted NVLink stores
+  and flags each peer; each rank waits (bounded) for the other owners' flags and refreshes the bf16
+  GEMM shadows of the parameters it does not own from its local copy. (``comm_gather`` is the pull
+  form of the same exchange, kept for the collective sweep.)
 * **Failure handling:** every device-side wait is bounded (``comm_timeout_s``); a timeout sets the
   device status word, the host sees it and reports the step as aborted (the reference's
   ``allReduce() -> null``). Non-finite gradients on any rank skip the update on all ranks.

@@ -9,7 +9,11 @@ This replaces the reference's WebSocket signalling server and WebRTC keep-alive:
   (webrtc-mesh.ts:514-528);
 * ``dynamic_timeout_s = max(10, 3 * max_rtt + 5)`` seconds (webrtc-mesh.ts:99-109);
 * a peer whose heartbeat is older than ``dead_after_s`` is dropped at the next ``form_ring``, the
-  equivalent of the server's ``peer-left`` + re-formation (server/signaling.ts:264-295).
+  equivalent of the server's ``peer-left`` + re-formation (server/signaling.ts:264-295);
+* a re-formation that must include newcomers (the server re-forms on join too, :210-213) is decided by
+  one member, which publishes the new peer list under a sequence number (``publish_ring``); every
+  member and every joining peer forms its ring from that list (``wait_published``), so all of them
+  build the same group even when they read the heartbeats at different times.
 
 ``ElasticGroup`` is a gloo process group over the members of one ring version, built from the job's
 store under a per-version prefix. Forming it needs no collective over the old group, so the survivors
@@ -105,11 +109,16 @@ class Membership:
 
     def alive_peers(self, now: float | None = None) -> list[str]:
         now = time.time() if now is None else now
-        return sorted(pid for pid, ptype in self.registered_peers()
-                      if ptype == "compute" and now - self.last_seen(pid) <= self.dead_after_s)
+        # a peer id registered twice (a process that re-registered) counts once
+        return sorted({pid for pid, ptype in self.registered_peers()
+                       if ptype == "compute" and now - self.last_seen(pid) <= self.dead_after_s})
 
     def form_ring(self) -> RingTopology | None:
-        peers = self.alive_peers()
+        return self.ring_from(self.alive_peers())
+
+    def ring_from(self, peers: list[str]) -> RingTopology | None:
+        """This peer's place in the ring over ``peers`` (None if it is not one of them)."""
+        peers = sorted(set(peers))
         if self.peer_id not in peers:
             return None
         N = len(peers)
@@ -137,6 +146,33 @@ class Membership:
                     return ring
             if time.time() > deadline:
                 raise TimeoutError(f"only {len(self.alive_peers())} of {n} peers joined room {self.room!r}")
+            time.sleep(min(0.05, self.heartbeat_s))
+
+    def latest_published(self) -> int:
+        return int(self.store.add(self._k("ring_seq"), 0))
+
+    def publish_ring(self, peers: list[str]) -> int:
+        """Makes ``peers`` the next ring (called by one member); returns its sequence number."""
+        seq = int(self.store.add(self._k("ring_seq"), 1))
+        self.store.set(self._k("ring_list", str(seq)), ",".join(sorted(set(peers))))
+        return seq
+
+    def wait_published(self, after: int, timeout_s: float = 60.0) -> tuple[int, RingTopology]:
+        """Waits for a ring list published after sequence number ``after`` that includes this peer;
+        returns (its sequence number, this peer's place in it)."""
+        deadline = time.time() + timeout_s
+        seen = after
+        while True:
+            latest = self.latest_published()
+            for seq in range(seen + 1, latest + 1):
+                peers = self.store.get(self._k("ring_list", str(seq))).decode().split(",")
+                ring = self.ring_from(peers)
+                if ring is not None:
+                    return seq, ring
+            seen = max(seen, latest)
+            if time.time() > deadline:
+                raise TimeoutError(f"no ring including {self.peer_id} was published in room {self.room!r} "
+                                   f"within {timeout_s:.0f} s")
             time.sleep(min(0.05, self.heartbeat_s))
 
     def wait_for_change(self, peers: list[str], timeout_s: float = 60.0) -> RingTopology:

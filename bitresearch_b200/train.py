@@ -95,6 +95,10 @@ class Trainer:
         self.cfg = cfg
         self.rank = dist.get_rank() if dist.is_initialized() else 0
         self.world = dist.get_world_size() if dist.is_initialized() else 1
+        if cfg.elastic_join and not dist.is_initialized():
+            # a process joining a running elastic job: its launcher's RANK / WORLD_SIZE size the batch
+            self.rank = int(os.environ.get("RANK", "0"))
+            self.world = int(os.environ.get("WORLD_SIZE", "1"))
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
         self.device = torch.device(device)
@@ -163,8 +167,8 @@ class Trainer:
         else:
             for name, p in self.model.named().items():
                 p.grad = self.grad_views[name]
-        if self.world > 1 and cfg.comm == "ring":
-            if cfg.elastic:
+        if (self.world > 1 or cfg.elastic_join) and cfg.comm == "ring":
+            if cfg.elastic or cfg.elastic_join:
                 self._init_elastic()
             self.comm = RingAllReduce(wire_dtype=cfg.wire_dtype, timeout_s=self._ring_timeout(), log=self.log,
                                       elastic=self.egroup)
@@ -199,6 +203,10 @@ class Trainer:
             self.token_bytes = make_token_bytes(cfg.model.vocab_size, cfg.token_bytes_max)
         if self.is_cuda:
             self.prefetch = PinnedPrefetcher(self.train_source, self.device_batch, T, self.device)
+        if getattr(self, "_join_resync", False):  # a joining process takes the ring's state
+            self._join_resync = False
+            self._resync(member=False)
+            self.log(f"joined the ring at step {self.metrics.step}: {self.egroup.ring.peers}")
 
     # ------------------------------------------------------------------ batches
     def next_batch(self):
@@ -427,16 +435,28 @@ class Trainer:
     # ------------------------------------------------------------------ elastic ring
     def _init_elastic(self) -> None:
         """Registers this rank in the job store's membership room, starts its heartbeat and builds the
-        first ring's gloo group (the reference's ring formation, server/signaling.ts:75-119)."""
+        first ring's gloo group (the reference's ring formation, server/signaling.ts:75-119). With
+        ``elastic_join`` the process instead waits until the running ring takes it in (the server
+        re-forms the ring on join, server/signaling.ts:210-213); it receives the state once the
+        optimizer exists (end of ``initialize``)."""
         from .parallel.membership import ElasticGroup, Membership, store_client
         cfg = self.cfg
         self._store = store_client()
-        self.membership = Membership(self._store, f"rank{self.rank:05d}", room="train", heartbeat_s=cfg.heartbeat_s,
+        # a joining process gets an id of its own, so a restarted rank never collides with its old entry
+        pid = f"rank{self.rank:05d}" + (f"-join{os.getpid()}" if cfg.elastic_join else "")
+        self.membership = Membership(self._store, pid, room="train", heartbeat_s=cfg.heartbeat_s,
                                      dead_after_s=cfg.dead_after_s, heartbeat_store=store_client())
+        self._ring_seq = self.membership.latest_published()
         self.membership.register()
         self.membership.start()
-        ring = self.membership.wait_for(self.world, cfg.reform_timeout_s)
+        if cfg.elastic_join:
+            self.log(f"{pid} waiting to be taken into the ring")
+            self._ring_seq, ring = self.membership.wait_published(self._ring_seq, cfg.reform_timeout_s)
+            self._join_resync = True
+        else:
+            ring = self.membership.wait_for(self.world, cfg.reform_timeout_s)
         self.egroup = ElasticGroup(self._store, ring, room="train", timeout_s=self._ring_timeout())
+        self.rank, self.world = ring.position, ring.total
 
     def _ring_timeout(self) -> float:
         """``comm_timeout_s``, or with 0 the membership's dynamic timeout max(10, 3 * rtt + 5) s, read at ring
@@ -446,50 +466,99 @@ class Trainer:
         return self.membership.dynamic_timeout_s
 
     def _reform(self) -> None:
-        """After a step that lost a peer: wait until membership drops it, form the smaller ring with its
-        own gloo group and re-sync the state from the new position 0. The reference re-forms on the
-        server's ``peer-left`` (server/signaling.ts:264-295, trainer.ts:654-668); its ranks may keep
-        different weights when some completed the aborted step, which the re-sync removes."""
-        from .parallel.membership import ElasticGroup
+        """After a step that lost a peer: wait until membership drops it, form the new ring with its own
+        gloo group and re-sync the state from a surviving member. The reference re-forms on the server's
+        ``peer-left`` (server/signaling.ts:264-295, trainer.ts:654-668); its ranks may keep different
+        weights when some completed the aborted step, which the re-sync removes.
+
+        The first surviving member decides the new ring (survivors plus any peers that joined the room)
+        and publishes it; every member, and every joining process, forms its ring from that list, so
+        all of them build the same group whatever heartbeats each of them saw. While fewer than
+        ``min_ring_size`` peers are alive the ring pauses, as the reference does with minRingSize
+        (src/distributed/trainer.ts:992-999), and stops after ``reform_timeout_s``."""
         cfg = self.cfg
         old = self.egroup.ring.peers
+        me = self.membership.peer_id
         self.log(f"peer lost at step {self.metrics.step}; re-forming the ring of {len(old)}")
-        ring = self.membership.wait_for_change(old, cfg.reform_timeout_s)
-        if ring.total < cfg.min_ring_size:
-            # the reference pauses while the ring is smaller than minRingSize, polling every 2 s
-            # (src/distributed/trainer.ts:992-999); peers that rejoin the store's room are taken in
-            self.log(f"ring too small ({ring.total}/{cfg.min_ring_size}), waiting up to {cfg.reform_timeout_s:.0f} s")
-            try:
-                ring = self.membership.wait_for(cfg.min_ring_size, cfg.reform_timeout_s)
-            except TimeoutError as e:
+        changed = self.membership.wait_for_change(old, cfg.reform_timeout_s)
+        surv = sorted(set(changed.peers) & set(old))
+        small = len(surv) < cfg.min_ring_size
+        if small:
+            self.log(f"ring too small ({len(surv)}/{cfg.min_ring_size}), waiting up to {cfg.reform_timeout_s:.0f} s")
+        try:
+            if surv and surv[0] == me:
+                deadline = time.time() + cfg.reform_timeout_s
+                while len(alive := self.membership.alive_peers()) < cfg.min_ring_size:
+                    if time.time() > deadline:
+                        raise TimeoutError(f"only {len(alive)} peers alive")
+                    time.sleep(min(0.05, cfg.heartbeat_s))
+                self.membership.publish_ring(sorted((set(alive) - set(old)) | set(surv)))
+            self._ring_seq, ring = self.membership.wait_published(self._ring_seq, cfg.reform_timeout_s)
+        except TimeoutError as e:
+            if small:
                 raise RuntimeError(f"ring stayed below min_ring_size={cfg.min_ring_size}: {e}") from e
+            raise RuntimeError(f"ring re-formation failed: {e}") from e
+        self._switch_ring(ring, survivors=old)
+
+    def _take_in_joiners(self) -> None:
+        """Every ``join_check_steps`` steps: the ring's first member looks for peers that joined the room;
+        if there are any, all members agree (one all-reduce), it publishes the larger ring and everyone,
+        the newcomers included, switches to it and re-syncs the state."""
+        cfg = self.cfg
+        ring = self.egroup.ring
+        new = []
+        if ring.position == 0:
+            new = sorted(set(self.membership.alive_peers()) - set(ring.peers))
+        flag = torch.tensor([1.0 if new else 0.0])
+        if not self._group_all_reduce(flag, dist.ReduceOp.MAX) or flag.item() == 0:
+            return
+        if ring.position == 0:
+            self.log(f"taking in {new} at step {self.metrics.step}")
+            self.membership.publish_ring(sorted(set(ring.peers) | set(new)))
+        self._ring_seq, nring = self.membership.wait_published(self._ring_seq, cfg.reform_timeout_s)
+        self._switch_ring(nring, survivors=ring.peers)
+
+    def _switch_ring(self, ring, survivors: list[str]) -> None:
+        """Builds ``ring``'s gloo group and ring all-reduce, then re-syncs the state from the first
+        member that was already training (never from a process that just joined)."""
+        from .parallel.membership import ElasticGroup
+        cfg = self.cfg
         self.egroup = ElasticGroup(self._store, ring, room="train", timeout_s=self._ring_timeout())
         self.comm = RingAllReduce(wire_dtype=cfg.wire_dtype, timeout_s=self._ring_timeout(), log=self.log,
                                   elastic=self.egroup)
         self.rank, self.world = ring.position, ring.total
-        self._resync()
+        self._resync(member=self.membership.peer_id in survivors)
         self._comm_failed = False
         self.log(f"ring re-formed: version {ring.version}, {ring.total} peers {ring.peers}")
 
-    def _resync(self) -> None:
-        """Broadcasts weights, optimizer state and loss scale from ring position 0."""
+    def _resync(self, member: bool = True) -> None:
+        """Broadcasts weights, optimizer state, loss scale and schedule state from the lowest ring position
+        held by a member that was training before (``member``); a process that just joined receives."""
         g = self.egroup
-        if g.rank == 0:
+        pos = torch.tensor([float(g.rank if member else g.size)])
+        if not g.all_reduce(pos, dist.ReduceOp.MIN) or int(pos.item()) >= g.size:
+            raise RuntimeError("state re-sync failed (no member holds the training state)")
+        root = int(pos.item())
+        if g.rank == root:
             tensors, meta = self.checkpoint_state()
             buf = ckpt.to_bytes(tensors, meta)
             n = torch.tensor([len(buf)], dtype=torch.int64)
         else:
             n = torch.zeros(1, dtype=torch.int64)
-        if not g.broadcast(n):
+        if not g.broadcast(n, root):
             raise RuntimeError("state re-sync failed (size)")
-        data = (torch.frombuffer(bytearray(buf), dtype=torch.uint8) if g.rank == 0
+        data = (torch.frombuffer(bytearray(buf), dtype=torch.uint8) if g.rank == root
                 else torch.empty(int(n.item()), dtype=torch.uint8))
-        if not g.broadcast(data):
+        if not g.broadcast(data, root):
             raise RuntimeError("state re-sync failed (payload)")
-        if g.rank != 0:
+        if g.rank != root:
             tensors, meta = ckpt.from_bytes(data.numpy().tobytes())
             info = ckpt.restore(self.model, tensors, meta, self.optimizer, log=self.log)
             self.scaler.scale = float(info.get("lossScale", self.scaler.scale) or self.scaler.scale)
+            self.metrics.step = int(info.get("step", self.metrics.step) or 0)
+            self.metrics.total_tokens = int(info.get("totalTokens", self.metrics.total_tokens) or 0)
+            self.total_training_time = float(info.get("totalTrainingTime", self.total_training_time) or 0.0)
+            self.metrics.smooth_loss = float(info.get("smoothLoss", self.metrics.smooth_loss) or 0.0)
             if self.engine is not None:
                 self.engine.refresh_shadows()
 
@@ -518,6 +587,11 @@ class Trainer:
                 self.total_training_time = self._agreed_time(self.total_training_time)
             if self._comm_failed and self.egroup is not None:
                 self._reform()
+            elif (self.egroup is not None and cfg.join_check_steps > 0
+                  and self.metrics.step % cfg.join_check_steps == 0):
+                self._take_in_joiners()
+                if self._comm_failed:
+                    self._reform()
             m = self.metrics
             if cfg.log_every and m.step % cfg.log_every == 0:
                 lrm = lr_multiplier(min(self.total_training_time / cfg.time_budget, 1), cfg.warmup_ratio,

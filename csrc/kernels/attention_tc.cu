@@ -31,12 +31,6 @@
 #include "status.h"
 #include "tma_host.h"
 
-// Pipeline split for profiling only (benchmarks/attn_split.py): 1 removes the softmax arithmetic,
-// 2 decouples the MMA lane from the softmax warps. Both compute wrong values; 0 is the kernel.
-#ifndef ATTN_SPLIT_MODE
-#define ATTN_SPLIT_MODE 0
-#endif
-
 namespace br {
 namespace {
 
@@ -218,7 +212,7 @@ __global__ void __launch_bounds__(320, 1)
       auto issue_pv = [&](int x, int j) -> bool {
         const Band& bx = x ? bB : bA;
         const int t = bx.lo + j, i = t - u_lo, st = i % F2_VST;
-        if ((ATTN_SPLIT_MODE != 2 && !mbar_wait(&p_full[x], j & 1, kBudgetNs, abort_flag, p.status)) ||
+        if (!mbar_wait(&p_full[x], j & 1, kBudgetNs, abort_flag, p.status) ||
             !mbar_wait(&v_full[st], (i / F2_VST) & 1, kBudgetNs, abort_flag, p.status))
           return false;
         tc_fence_after();
@@ -258,7 +252,7 @@ __global__ void __launch_bounds__(320, 1)
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < bx.n; ++j) {
-      if (ATTN_SPLIT_MODE != 2 && !mbar_wait_warp(&s_full[x], j & 1, kBudgetNs, abort_flag, p.status)) {
+      if (!mbar_wait_warp(&s_full[x], j & 1, kBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
         break;
@@ -321,7 +315,7 @@ __global__ void __launch_bounds__(320, 1)
       const uint64_t sc2 = f32x2(p.scale_log2, p.scale_log2), nm2 = f32x2(-mref, -mref);
       uint64_t l2 = f32x2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < (ATTN_SPLIT_MODE == 1 ? 0 : 2); ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 64; i += 2) {
@@ -516,7 +510,7 @@ __global__ void __launch_bounds__(320, 1)
           ok = false;
           break;
         }
-        if (ATTN_SPLIT_MODE != 2 && !mbar_wait(&p_full[j & 1], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
           ok = false;
           break;
         }
@@ -601,7 +595,7 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int set = j & 1;
-      if (ATTN_SPLIT_MODE != 2 && !mbar_wait_warp(&s_full[set], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+      if (!mbar_wait_warp(&s_full[set], (j >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
         break;
@@ -634,8 +628,7 @@ __global__ void __launch_bounds__(320, 1)
           pk[i / 2] = pack_bf16(g.x, g.y);
         }
       };
-      if (ATTN_SPLIT_MODE == 1) {
-      } else if (interior) {
+      if (interior) {
         body(std::false_type{});
       } else {
         body(std::true_type{});
@@ -803,7 +796,7 @@ __global__ void __launch_bounds__(320, 1)
           ok = false;
           break;
         }
-        if (ATTN_SPLIT_MODE != 2 && !mbar_wait(&p_full[it & 1], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+        if (!mbar_wait(&p_full[it & 1], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
           ok = false;
           break;
         }
@@ -837,7 +830,7 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
     for (int it = 0; it < iters; ++it) {
       const int set = it & 1, st = it % DK_STAGES;
-      if (ATTN_SPLIT_MODE != 2 && !mbar_wait_warp(&s_full[set], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+      if (!mbar_wait_warp(&s_full[set], (it >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
         break;
@@ -882,8 +875,7 @@ __global__ void __launch_bounds__(320, 1)
           ss[i / 2 + 1] = pack_bf16(g1.x, g1.y);
         }
       };
-      if (ATTN_SPLIT_MODE == 1) {
-      } else if (interior) {
+      if (interior) {
         body(std::false_type{});
       } else {
         body(std::true_type{});

@@ -76,16 +76,32 @@ extern "C" __attribute__((visibility("default"))) cudaError_t br_muon_normalize_
   float* ss = nullptr;
   cudaError_t e = scratch_for_current_device(&ss);
   if (e != cudaSuccess) return e;
-  noalloc_clear_kernel<<<(S + 255) / 256, 256, 0, stream>>>(ss, S);
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int dev = 0, sms = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
   int64_t chunks = (n + 1023) / 1024;
   const int64_t cap = 4 * (int64_t)sms / S + 1;
   if (chunks > cap) chunks = cap;
   if (chunks < 1) chunks = 1;
   const dim3 grid((unsigned)chunks, (unsigned)S);
-  noalloc_momentum_kernel<<<grid, 256, 0, stream>>>(grad, mom, n, mu, ss);
-  noalloc_normalize_kernel<<<grid, 256, 0, stream>>>(grad, mom, n, mu, ss, x_out);
-  return cudaGetLastError();
+  // cudaLaunchKernel returns the status of this launch itself, so an error left on the thread by
+  // earlier, unrelated work is neither reported as this call's failure nor cleared
+  {
+    void* args[] = {&ss, &S};
+    if ((e = cudaLaunchKernel(reinterpret_cast<const void*>(noalloc_clear_kernel), dim3((S + 255) / 256), dim3(256),
+                              args, 0, stream)) != cudaSuccess)
+      return e;
+  }
+  {
+    void* args[] = {const_cast<float**>(&grad), &mom, &n, &mu, &ss};
+    if ((e = cudaLaunchKernel(reinterpret_cast<const void*>(noalloc_momentum_kernel), grid, dim3(256), args, 0,
+                              stream)) != cudaSuccess)
+      return e;
+  }
+  {
+    const float* ssc = ss;
+    void* args[] = {const_cast<float**>(&grad), &mom, &n, &mu, const_cast<float**>(&ssc), &x_out};
+    e = cudaLaunchKernel(reinterpret_cast<const void*>(noalloc_normalize_kernel), grid, dim3(256), args, 0, stream);
+  }
+  return e;
 }

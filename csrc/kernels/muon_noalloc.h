@@ -28,8 +28,10 @@ extern "C" {
 // null pointer), or the error of the set-up or launch.
 //
 // Scratch: a file-scope __device__ array that every GPU loading the library holds until exit. The first
-// call on each device looks up its address (cudaGetSymbolAddress) with that device current; make that
-// first call before any stream capture. Every call shares the array and clears the part it uses, so
+// call on each device looks up its address (cudaGetSymbolAddress) with that device current and keeps it
+// for the life of the process; make that first call before any stream capture. A caller that resets a
+// device (cudaDeviceReset) must not use this entry point on that device again in the same process: the
+// kept address belongs to the destroyed context. Every call shares the array and clears the part it uses, so
 // calls whose kernels overlap on the GPU (different streams, or different host threads, on one device)
 // race and must be ordered by the caller.
 cudaError_t br_muon_normalize_noalloc(const float* grad, float* mom, __nv_bfloat16* x_out, int S, int64_t n, float mu,

@@ -212,3 +212,9 @@ def test_prefetcher_hands_a_data_error_to_the_consumer():
     p._fill()
     with pytest.raises(RuntimeError, match="corrupt shard"):
         p.get()
+    # a later call (cleanup, eval) raises as well instead of blocking on the empty queue
+    with pytest.raises(RuntimeError, match="corrupt shard"):
+        p.get()
+    p._error = None  # the queue still holds the sentinel for a consumer that bypasses the flag
+    with pytest.raises(RuntimeError):
+        p.get()

@@ -1,7 +1,10 @@
 """Failure detection and elastic recovery on CPU gloo ranks (no GPU involved): a rank that crashes
 between steps stops its heartbeat; the survivors' next collective fails, the step's update is skipped,
 they wait until membership drops the lost peer, form a smaller ring with a new gloo group, re-sync the
-state from the new position 0 and finish the run with identical weights."""
+state from the new position 0 and finish the run with identical weights. A process that joins the room
+later (a restarted rank) is taken into the ring, receives the state and finishes in lock-step too."""
+import time
+
 import numpy as np
 
 from dist_utils import run_world
@@ -13,12 +16,16 @@ class _Crash(Exception):
     pass
 
 
-def _elastic(rank, world, crash_rank, crash_after, extra=()):
-    cfg = apply_overrides(preset("tiny-cpu"), [
+def _cfg(world, extra):
+    return apply_overrides(preset("tiny-cpu"), [
         "model.n_layer=1", "model.n_embd=64", "model.n_head=1", "model.n_kv_head=1", "model.sequence_len=32",
         "model.vocab_size=128", "device_batch=2", f"total_batch_tokens={64 * world}", "eval_tokens=128",
         "log_every=0", "results_tsv=", "max_steps=8", "time_budget=1e9", "comm=ring", "elastic=true",
         "heartbeat_s=0.2", "dead_after_s=3", "comm_timeout_s=4", "reform_timeout_s=60", *extra])
+
+
+def _elastic(rank, world, crash_rank, crash_after, extra=(), rejoin=False, join_delay_s=0.0):
+    cfg = _cfg(world, extra)
     logs = []
     tr = Trainer(cfg, device="cpu", log=logs.append)
     tr.initialize()
@@ -36,7 +43,15 @@ def _elastic(rank, world, crash_rank, crash_after, extra=()):
         except _Crash:
             tr.membership.stop()  # no graceful leave: the heartbeat just stops
             tr.egroup.pg.abort()
-            return {"crashed_at": tr.metrics.step}
+            crashed_at = tr.metrics.step
+            if not rejoin:
+                return {"crashed_at": crashed_at}
+        # the same rank restarts as a new process would: a fresh trainer that joins the running job,
+        # once its old entry has aged out of the room (later still when the ring should re-form first)
+        time.sleep(max(cfg.dead_after_s + 1, join_delay_s))
+        logs = []
+        tr = Trainer(apply_overrides(cfg, ["elastic_join=true"]), device="cpu", log=logs.append)
+        tr.initialize()
     try:
         m = tr.start_training()
     except RuntimeError as e:
@@ -65,3 +80,29 @@ def test_ring_below_min_size_stops_instead_of_training_on():
     for r in (r0, r1):
         assert "ring stayed below min_ring_size=3" in r.get("error", ""), r
     assert any("ring too small (2/3)" in line for line in r0["logs"])
+
+
+def test_restarted_rank_rejoins_a_paused_ring():
+    """min_ring_size=3: the two survivors pause; the crashed rank's restart joins the room, the ring of
+    three re-forms, the joiner receives the state from a survivor and all three finish identically."""
+    r0, r1, r2 = run_world(_elastic, 3, 2, 3, ("min_ring_size=3",), True, timeout=240)
+    for r in (r0, r1, r2):
+        assert "error" not in r, r.get("error")
+        assert r["step"] == 8 and r["world"] == 3, {k: r[k] for k in ("step", "world")}
+    assert np.array_equal(r0["params"], r1["params"]) and np.array_equal(r0["params"], r2["params"])
+    assert any(line.startswith("joined the ring at step") for line in r2["logs"]), r2["logs"]
+
+
+def test_running_ring_takes_in_a_joiner():
+    """min_ring_size=1: the survivors keep training as a ring of two; the restarted rank joins the room
+    after that ring formed, and the running ring takes it in at its next check, after which all three
+    train in lock-step."""
+    r0, r1, r2 = run_world(_elastic, 3, 2, 3, ("join_check_steps=1", "max_steps=24"), True, 14.0, timeout=300)
+    for r in (r0, r1, r2):
+        assert "error" not in r, r.get("error")
+        assert r["step"] == 24 and r["world"] == 3, {k: r[k] for k in ("step", "world")}
+    assert np.array_equal(r0["params"], r1["params"]) and np.array_equal(r0["params"], r2["params"])
+    assert any("ring re-formed: version 2, 2 peers" in line for line in r0["logs"]), r0["logs"]
+    assert any("taking in ['rank00002-join" in line for line in r0["logs"]), r0["logs"][-5:]
+    joined = [line for line in r2["logs"] if line.startswith("joined the ring at step")]
+    assert joined and 4 < int(joined[0].split()[5].rstrip(":")) < 24, joined
