@@ -92,6 +92,21 @@ def _time_steps(step_fn, K: int) -> float:
     return a.elapsed_time(b) / K
 
 
+def _replica_check(params) -> dict:
+    """Sum and sum of |x| of every parameter (fp64, per rank), reduced MAX and MIN over ranks: equal
+    extremes mean every rank holds bitwise the same values after the timed steps."""
+    v = torch.zeros(2, dtype=torch.float64, device="cuda")
+    for p in params:
+        d = p.detach().double()
+        v[0] += d.sum()
+        v[1] += d.abs().sum()
+    hi, lo = v.clone(), v.clone()
+    if dist.is_initialized():
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+    return {"replicas_identical": bool(torch.equal(hi, lo)), "param_sum": float(hi[0]), "param_abs_sum": float(hi[1])}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -140,12 +155,17 @@ def main():
         batches = _resident_batches(cfg, rank, world, B, T, accum, device, torch.int32)
         it = [0]
 
+        last = [None]
+
         def step():
-            tr.train_step(batches[it[0] % 2], sync=False)
+            last[0] = tr.train_step(batches[it[0] % 2], sync=False)
             it[0] += 1
 
         def e2e_step():
-            tr.train_step()
+            last[0] = tr.train_step()
+
+        def params():
+            return list(tr.model.named().values())
     else:
         from baseline.ddp_baseline import DDPBaseline
         cfg.impl = "torch"
@@ -154,15 +174,20 @@ def main():
         batches = _resident_batches(cfg, rank, world, B, T, accum, device, torch.int64)
         it = [0]
 
+        last = [None]
+
         def step():
-            tr.train_step(batches[it[0] % 2])
+            last[0] = tr.train_step(batches[it[0] % 2])
             it[0] += 1
         host = [[(x.cpu().pin_memory(), y.cpu().pin_memory()) for x, y in bb] for bb in batches]
 
         def e2e_step():
             bs = [(x.to(device, non_blocking=True), y.to(device, non_blocking=True)) for x, y in host[it[0] % 2]]
-            float(tr.train_step(bs))
+            last[0] = float(tr.train_step(bs))
             it[0] += 1
+
+        def params():
+            return list(tr.model.parameters())
 
     for _ in range(W):
         step()
@@ -184,6 +209,12 @@ def main():
                "h2d_bytes_per_step": 2 * 4 * B * T * accum, "d2h_bytes_per_step": 4,
                "api": "Trainer.train_step()" if args.impl == "ours" else "DDPBaseline.train_step() + loss.item()"}
 
+    # after the timed steps (outside the timed regions): do the ranks hold identical replicas, and the
+    # loss of the last step, max over ranks
+    check = _replica_check(params())
+    final_loss = torch.tensor([float(last[0])], dtype=torch.float64, device="cuda")
+    if dist.is_initialized():
+        dist.all_reduce(final_loss, op=dist.ReduceOp.MAX)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -195,7 +226,7 @@ def main():
                        "seq_len": T, "device_batch": B, "grad_accum": accum, "parallelism": f"dp{world}",
                        "comm": (args.comm if args.impl == "ours" else "nccl-ddp") if world > 1 else "none",
                        "l2": "inputs larger than L2 (activations tens of GB per step); no flush"},
-            "impl": args.impl, "clocks": clk, "e2e": e2e,
+            "impl": args.impl, "clocks": clk, "e2e": e2e, "final_loss": float(final_loss), **check,
             "gpu_launches": launches if args.impl == "ours" else 0,
             "launches_by_kernel": by_kernel if args.impl == "ours" else {},
         }

@@ -15,7 +15,9 @@ Per layer (forward):
   rms_fwd             xn2 = bf16(rms(mid))
   GEMM (RELU2 epi)    h = relu(xn2 @ Wfc)^2
   GEMM (F32 epi)      x_next = mid + h @ Wmlp_proj
-Head: rms_fwd -> GEMM with softcap epilogue -> fused CE (loss + dlogits in place).
+Head: rms_fwd -> lm_head GEMM whose epilogue computes the softcapped cross-entropy statistics and writes
+G = exp(z - cap) (1 - (z/cap)^2) instead of the logits -> ce_finalize (loss, per-token nats, per-row scale,
+the target column's fp32 gradient, the scaled activations for dW and the target scatter into dW).
 Backward mirrors it: dW via ``X^T @ dY`` split-K GEMMs (fp32 vector reductions), dX via ``dY @ W^T``
 GEMMs (the ReLU^2 derivative fused into the mlp_proj dX epilogue), rms/ladder backward kernels,
 attention backward, RoPE/QK-norm/VE backward and the embedding scatter.
@@ -129,7 +131,10 @@ class FusedGPTEngine:
             "lse": [torch.empty(B, H, T, **f32) for _ in range(L)],
             "h": [torch.empty(M, self.F, **bf) for _ in range(L)],
             "rstdf": torch.empty(M, **f32), "xf": torch.empty(M, D, **bf),
-            "logits": torch.empty(M, self.V, **bf), "nats": torch.empty(M, **f32),
+            # fused head: G (dlogits up to a per-row scale and the target column), CE statistics
+            "G": torch.empty(M, self.V, **bf), "ce_part": torch.empty((self.V + 255) // 256, M, **f32),
+            "zt": torch.empty(M, **f32), "rowscale": torch.empty(M, **f32), "coef": torch.empty(M, **f32),
+            "xs_head": torch.empty(M, D, **bf), "nats": torch.empty(M, **f32),
             "loss": torch.zeros(1, **f32),
             # backward scratch
             "dx": torch.empty(M, D, **f32), "dx_b": torch.empty(M, D, **bf),
@@ -175,20 +180,34 @@ class FusedGPTEngine:
                         beta=1.0)
             x = b["xs"][i]
         E.rms_fwd(x, b["xf"], b["rstdf"])
-        gemm.matmul(b["xf"], self.shadows["lmHead"].t(), out=b["logits"], epi=gemm.SOFTCAP, alpha=1 / 15.0, beta=15.0)
+
+    def _head(self, tg: torch.Tensor, b: dict, scale: float, grad: bool):
+        """lm_head + softcap 15 + cross-entropy (gpt.ts:296-313) without writing the logits: the GEMM epilogue
+        keeps per-row exp-sums and the target logit, ``ce_finalize`` adds ``scale * sum(nats)`` into the loss.
+        With ``grad`` it also prepares the backward: G, the per-row scale, the scaled activations for the
+        weight-gradient GEMM and the target column's contribution to the lm_head gradient."""
+        E = self.E
+        E.gemm_softcap_ce(b["xf"], self.shadows["lmHead"], b["G"], tg, b["ce_part"], b["zt"], 15.0, grad)
+        if grad:
+            E.ce_finalize(b["ce_part"], b["zt"], tg, self.V, 15.0, scale, nats=b["nats"], loss_sum=b["loss"],
+                          rowscale=b["rowscale"], coef=b["coef"], x=b["xf"], xs=b["xs_head"], dw=self.grads["lmHead"])
+        else:
+            E.ce_finalize(b["ce_part"], b["zt"], tg, self.V, 15.0, scale, nats=b["nats"])
 
     # ------------------------------------------------------------------ backward
-    def _backward(self, idx: torch.Tensor, b: dict, B: int):
+    def _backward(self, idx: torch.Tensor, tg: torch.Tensor, b: dict, B: int):
         E, P, G = self.E, self.P, self.grads
         T, D, H, KV, hd = self.T, self.D, self.H, self.KV, self.hd
         Dq, Dkv = self.Dq, self.Dkv
         idx = idx.reshape(-1)
         A = gemm.ATOMIC
-        # head: dlmHead += dz^T xf ; dxf = dz @ lmHead
-        gemm.matmul(b["logits"].t(), b["xf"], out=G["lmHead"], epi=A, k_splits=0)
-        gemm.matmul(b["logits"], self.shadows["lmHead"], out=b["dxn"])
+        # head: dlogits = rowscale * G + [target] coef, so dlmHead += G^T (rowscale xf) (the target scatter
+        # ran in ce_finalize) and dxf = rowscale (G lmHead) + coef lmHead[target], folded into rms_bwd
+        gemm.matmul(b["G"].t(), b["xs_head"], out=G["lmHead"], epi=A, k_splits=0)
+        gemm.matmul(b["G"], self.shadows["lmHead"], out=b["dmid"], epi=gemm.F32)
         self._ready(0)
-        E.rms_bwd(b["xs"][-1], b["rstdf"], b["dxn"], None, b["dx"], b["dx_b"])
+        E.rms_bwd(b["xs"][-1], b["rstdf"], b["dmid"], None, b["dx"], b["dx_b"], b["rowscale"], b["coef"], tg,
+                  P["lmHead"])
         b["dx0"].zero_()
         for i in reversed(range(self.L)):
             # MLP
@@ -251,13 +270,13 @@ class FusedGPTEngine:
             else:
                 for g in self.grads.values():
                     g.zero_()
+        tg = targets.reshape(-1).to(torch.int32).contiguous()
         with traced(self.timer, "forward"):
             self._forward(idx, b, B)
             b["loss"].zero_()
-            self.E.softcap_ce(b["logits"], targets.reshape(-1), 15.0, loss_scale / (B * self.T), b["nats"], b["loss"],
-                              True)
+            self._head(tg, b, loss_scale / (B * self.T), grad=True)
         with traced(self.timer, "backward"):  # includes the bucket hooks that launch the gradient reduce
-            self._backward(idx, b, B)
+            self._backward(idx, tg, b, B)
         return b["loss"][0] / loss_scale
 
     @torch.no_grad()
@@ -265,7 +284,7 @@ class FusedGPTEngine:
         B = idx.shape[0]
         b = self._buffers(B)
         self._forward(idx, b, B)
-        self.E.softcap_ce(b["logits"], targets.reshape(-1), 15.0, 1.0, b["nats"], None, False)
+        self._head(targets.reshape(-1).to(torch.int32).contiguous(), b, 1.0, grad=False)
         return b["nats"].view(B, self.T).clone()
 
     def status(self) -> int:

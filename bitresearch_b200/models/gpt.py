@@ -116,8 +116,8 @@ class GPT(nn.Module):
 
     def forward_torch(self, idx: torch.Tensor, targets: torch.Tensor | None = None, reduction: str = "mean",
                       exact_ce: bool = True, compute_dtype: torch.dtype | None = None):
-        """Eager forward. Returns the mean loss (``reduction='mean'``), per-token nats [B,T]
-        (``'none'``) or logits (``targets is None``).
+        """Eager forward. Returns the mean loss (``reduction='mean'``), per-token nats [B,T] with 0 at
+        ignored (-1) targets (``'none'``) or logits (``targets is None``).
 
         ``exact_ce`` uses the reference's ``-log(softmax + 1e-10)`` (gpt.ts:306-313); otherwise
         ``F.cross_entropy``. ``compute_dtype`` casts matmul operands (bf16 for the GPU baseline).
@@ -165,9 +165,9 @@ class GPT(nn.Module):
             nll = -logp.gather(1, flat_t.clamp(min=0).unsqueeze(1)).squeeze(1)
         else:
             nll = F.cross_entropy(logits, flat_t.clamp(min=0), reduction="none")
-        if reduction == "none":
-            return nll.view(B, T)
         valid = (flat_t != -1).to(nll.dtype)
+        if reduction == "none":  # the reference's masked per-token loss: 0 at ignored positions
+            return (nll * valid).view(B, T)
         return (nll * valid).sum() / nll.numel()
 
 

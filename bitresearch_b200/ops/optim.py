@@ -96,10 +96,9 @@ def step_muon(opt, grads) -> None:
             key = ("x", S, r, c)
             if key not in opt._ws:
                 dev = grads[chunk[0]].device
-                lines = r if r >= c else c
                 opt._ws[key] = (torch.empty(S, r, c, dtype=torch.bfloat16, device=dev),
-                                torch.empty(S, dtype=torch.float32, device=dev),
-                                torch.empty(2 * S + S * lines, dtype=torch.float32, device=dev))
+                                torch.empty(E.muon_prepare_scratch(S, r * c), dtype=torch.float32, device=dev),
+                                torch.empty(E.muon_finish_scratch(S, r, c), dtype=torch.float32, device=dev))
             X, ss, work = opt._ws[key]
             G = [grads[n].contiguous() for n in chunk]
             E.muon_prepare(G, [opt.state[n]["mom"] for n in chunk], mu, X, ss)

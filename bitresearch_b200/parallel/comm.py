@@ -32,6 +32,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops._ext import check_status, ext
+from ..utils.timing import traced
 
 WIRE_CODE = {"fp32": 0, "f32": 0, "bf16": 1, "fp16": 2, "f16": 2}
 WIRE_BYTES = {0: 4, 1: 2, 2: 2}
@@ -295,24 +296,29 @@ class P2PGradSync:
 
     # ------------------------------------------------------------------ step
     def step(self, step_idx: int, scale: float, opt) -> bool:
+        timer = self.tr.timer
         cur = torch.cuda.current_stream()
-        cur.wait_stream(self.comm_stream)
+        with traced(timer, "sync.comm_tail"):  # the compute stream waits for the last bucket's reduce
+            cur.wait_stream(self.comm_stream)
         epoch = self.epoch + 1
-        # agree on skipping: any non-finite gradient on any rank skips the update everywhere
-        flag = self.bad.clone().float()
-        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
-        status = check_status()
-        ok = status == 0 and float(flag.item()) == 0.0
+        with traced(timer, "sync.agree"):
+            # agree on skipping: any non-finite gradient on any rank skips the update everywhere
+            flag = self.bad.clone().float()
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+            status = check_status()
+            ok = status == 0 and float(flag.item()) == 0.0
         if ok:
-            opt.step({n: self.red_views[n] for n in self.owned_names})
+            with traced(timer, "sync.optimizer"):
+                opt.step({n: self.red_views[n] for n in self.owned_names})
         # push (possibly unchanged) owned parameters into every peer's buffer with posted NVLink stores,
         # flag each peer, then wait for the other owners' pushes and refresh the bf16 shadows locally.
         # Every rank finished its backward before the skip agreement above, so no peer still reads the
         # values being overwritten; pushes only touch a peer's non-owned regions.
-        self.E.comm_push(self.params_flat, self.param_buf.peers_dev, self.rank, self.push_chunks, 0)
-        self.E.comm_signal_peers(self.push_flags.peers_dev, self.rank, epoch)
-        self.E.comm_shadow_refresh(self.params_flat, self.push_flags.ptr, self.world, self.rank, epoch,
-                                   self.gather_segs, 0, self.budget)
+        with traced(timer, "sync.param_push"):
+            self.E.comm_push(self.params_flat, self.param_buf.peers_dev, self.rank, self.push_chunks, 0)
+            self.E.comm_signal_peers(self.push_flags.peers_dev, self.rank, epoch)
+            self.E.comm_shadow_refresh(self.params_flat, self.push_flags.ptr, self.world, self.rank, epoch,
+                                       self.gather_segs, 0, self.budget)
         self.epoch = epoch
         if status:
             self.tr.log(f"p2p collective timed out (status {status}); step {step_idx} skipped")

@@ -19,7 +19,15 @@ void ladder_rms_fwd(const torch::Tensor& x, const torch::Tensor& x0, const torch
                     torch::Tensor& rstd);
 void rms_fwd(const torch::Tensor& x, torch::Tensor& xn, c10::optional<torch::Tensor> rstd);
 void rms_bwd(const torch::Tensor& x, const torch::Tensor& rstd, const torch::Tensor& dy,
-             c10::optional<torch::Tensor> dres, c10::optional<torch::Tensor> dx, c10::optional<torch::Tensor> dxb);
+             c10::optional<torch::Tensor> dres, c10::optional<torch::Tensor> dx, c10::optional<torch::Tensor> dxb,
+             c10::optional<torch::Tensor> rowscale, c10::optional<torch::Tensor> coef,
+             c10::optional<torch::Tensor> targets, c10::optional<torch::Tensor> wtab);
+void gemm_softcap_ce(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& g, const torch::Tensor& targets,
+                     torch::Tensor& partial, torch::Tensor& zt, double cap, bool store);
+void ce_finalize(const torch::Tensor& partial, const torch::Tensor& zt, const torch::Tensor& targets, int64_t V,
+                 double cap, double scale, c10::optional<torch::Tensor> nats, c10::optional<torch::Tensor> loss_sum,
+                 c10::optional<torch::Tensor> rowscale, c10::optional<torch::Tensor> coef,
+                 c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> xs, c10::optional<torch::Tensor> dw);
 void ladder_bwd(const torch::Tensor& x, const torch::Tensor& x0, const torch::Tensor& lam_r,
                 const torch::Tensor& lam_0, int64_t layer, const torch::Tensor& rstd, const torch::Tensor& dxn,
                 const torch::Tensor& dres, c10::optional<torch::Tensor> dgate_in, torch::Tensor& dx,
@@ -43,6 +51,8 @@ void softcap_ce(torch::Tensor& logits, const torch::Tensor& targets, double cap,
 void adamw_multi(const std::vector<torch::Tensor>& params, const std::vector<torch::Tensor>& grads,
                  const std::vector<torch::Tensor>& ms, const std::vector<torch::Tensor>& vs,
                  const std::vector<torch::Tensor>& shadows, const std::vector<double>& hyper);
+int64_t muon_prepare_scratch(int64_t S, int64_t n);
+int64_t muon_finish_scratch(int64_t S, int64_t r, int64_t c);
 void muon_prepare(const std::vector<torch::Tensor>& grads, const std::vector<torch::Tensor>& moms, double mu,
                   torch::Tensor& X, torch::Tensor& ss);
 void muon_finish(const torch::Tensor& X, const std::vector<torch::Tensor>& grads,
@@ -99,7 +109,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_rms_fwd", &br::embed_rms_fwd);
   m.def("ladder_rms_fwd", &br::ladder_rms_fwd);
   m.def("rms_fwd", &br::rms_fwd);
-  m.def("rms_bwd", &br::rms_bwd);
+  m.def("rms_bwd", &br::rms_bwd, pybind11::arg("x"), pybind11::arg("rstd"), pybind11::arg("dy"),
+        pybind11::arg("dres"), pybind11::arg("dx"), pybind11::arg("dxb"), pybind11::arg("rowscale") = pybind11::none(),
+        pybind11::arg("coef") = pybind11::none(), pybind11::arg("targets") = pybind11::none(),
+        pybind11::arg("wtab") = pybind11::none());
+  m.def("gemm_softcap_ce", &br::gemm_softcap_ce);
+  m.def("ce_finalize", &br::ce_finalize, pybind11::arg("partial"), pybind11::arg("zt"), pybind11::arg("targets"),
+        pybind11::arg("V"), pybind11::arg("cap"), pybind11::arg("scale"), pybind11::arg("nats") = pybind11::none(),
+        pybind11::arg("loss_sum") = pybind11::none(), pybind11::arg("rowscale") = pybind11::none(),
+        pybind11::arg("coef") = pybind11::none(), pybind11::arg("x") = pybind11::none(),
+        pybind11::arg("xs") = pybind11::none(), pybind11::arg("dw") = pybind11::none());
   m.def("ladder_bwd", &br::ladder_bwd, pybind11::arg("x"), pybind11::arg("x0"), pybind11::arg("lam_r"),
         pybind11::arg("lam_0"), pybind11::arg("layer"), pybind11::arg("rstd"), pybind11::arg("dxn"),
         pybind11::arg("dres"), pybind11::arg("dgate_in"), pybind11::arg("dx"), pybind11::arg("dx0_acc"),
@@ -113,6 +132,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("softcap_ce", &br::softcap_ce);
   m.def("adamw_multi", &br::adamw_multi);
   m.def("muon_prepare", &br::muon_prepare);
+  m.def("muon_prepare_scratch", &br::muon_prepare_scratch);
+  m.def("muon_finish_scratch", &br::muon_finish_scratch);
   m.def("muon_finish", &br::muon_finish);
   m.def("attn_fwd", &br::attn_fwd);
   m.def("attn_bwd", &br::attn_bwd);

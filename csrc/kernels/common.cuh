@@ -20,7 +20,18 @@ enum : int {
   kErrTimeoutEpilogue = 3,
   kErrTimeoutPeer = 4,
   kErrBadArg = 5,
+  kErrBadIndex = 6,  // a token id or target outside its table: the access was skipped
 };
+
+// Every kernel that gathers or scatters rows of a table by a token id or target checks the id first:
+// one compare per row. An id outside [0, n) records kErrBadIndex in the device status word (the first
+// error wins) and the kernel skips that row's table access instead of reading or writing outside the
+// table; the host reads the status like a timeout's and reports the step as failed.
+__device__ __forceinline__ bool index_ok(int64_t i, int64_t n, int* status) {
+  if (i >= 0 && i < n) return true;
+  if (status) atomicCAS(status, 0, (int)kErrBadIndex);
+  return false;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

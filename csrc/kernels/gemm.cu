@@ -41,6 +41,7 @@ enum GemmEpi : int {
   EPI_ATOMIC_F32 = 4,  // C(f32) += alpha*acc                       (TMA reduce-add)
   EPI_SOFTCAP = 5,     // C(bf16) = beta*tanh(alpha*acc)             (alpha = 1/cap, beta = cap)
   EPI_QKV_ROPE = 6,    // fused QKV projection output (see QkvRope), BN = 256
+  EPI_SOFTCAP_CE = 7,  // lm_head + softcap + cross-entropy statistics (see CeHead), BN = 256
 };
 
 // The QKV projection's epilogue: the output columns are [q heads | k heads | v heads] of 128 columns
@@ -60,6 +61,22 @@ struct QkvRope {
   const float* wg;       // [32, KV]
   float* gate;           // [M, KV]
   int T, H, KV, ld_cur;
+  int V;                 // rows of the value-embedding table (token ids are checked against it)
+};
+
+// The lm_head epilogue fused with the softcapped cross-entropy (gpt.ts:296-313). With z = cap*tanh(acc/cap)
+// every logit lies in [-cap, cap], so e = exp(z - cap) lies in [exp(-2 cap), 1] and needs no running
+// maximum. Per element the epilogue writes (when `store`) the bf16 tile of
+//   G = e * (1 - (z/cap)^2)          (softmax numerator times the softcap derivative; 0 at the target),
+// which the backward GEMMs consume in place of dlogits, and per row and 256-column tile it writes the
+// partial sum of e into partial[n_tile][row] and, in the tile holding the row's target, z there.
+// `ce_finalize` (loss.cu) turns these into the loss, per-token nats, a per-row scale for G and the
+// target column's exact fp32 gradient; the logits themselves are never written.
+struct CeHead {
+  const int* targets;  // [M] (rows whose target is outside [0, N) are masked)
+  float* partial;      // [n_tiles][M]
+  float* zt;           // [M]
+  int store;           // 0: statistics only (evaluation)
 };
 
 struct GemmParams {
@@ -70,6 +87,7 @@ struct GemmParams {
   float alpha, beta;
   int* status;
   QkvRope rope;
+  CeHead ce;
 };
 
 constexpr int BM = 128;
@@ -409,7 +427,7 @@ __global__ void __launch_bounds__(192, 1)
               if (head < rp.H) rp.rq[(int64_t)mrow * rp.H + head] = r;
               else rp.rk[(int64_t)mrow * rp.KV + (head - rp.H)] = r;
             }
-          } else if (rp.ve != nullptr) {
+          } else if (rp.ve != nullptr && index_ok(__ldg(rp.idx + msafe), rp.V, valid ? p.status : nullptr)) {
             const int kvh = head - nqk;
             const float4* cz = reinterpret_cast<const float4*>(rp.cur + msafe * rp.ld_cur);
             float z = 0.f;
@@ -456,6 +474,13 @@ __global__ void __launch_bounds__(192, 1)
         }
         continue;
       }
+      // softcapped cross-entropy statistics of this thread's row over the tile (EPI_SOFTCAP_CE)
+      float ce_sum = 0.f, ce_zt = 0.f;
+      int ce_t = -1;
+      if constexpr (EPI == EPI_SOFTCAP_CE) {
+        const int mrow = row0 + lane;
+        ce_t = mrow < p.M ? __ldg(p.ce.targets + mrow) : -1;
+      }
 #pragma unroll 1
       for (int c = 0; c < CPT; ++c, ++nchunk) {
         const int slot = nchunk % NBUF;
@@ -482,7 +507,27 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int q = 0; q < 8; ++q) {  // eight 16-byte chunks per 128-byte row
           uint4* slotp = reinterpret_cast<uint4*>(myrow + swz_off(lane, q));
-          if constexpr (epi_f32(EPI)) {
+          if constexpr (EPI == EPI_SOFTCAP_CE) {
+            // z = cap tanh(acc/cap); e = exp(z - cap) = 2^((th - 1) cap log2(e)); G = e (1 - th^2)
+            const float k2 = p.beta * 1.4426950408889634f;
+            uint32_t os[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float g[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int col = col0 + 8 * q + 2 * j + h;
+                const float th = tanh_approx(__uint_as_float(r[8 * q + 2 * j + h]) * p.alpha);
+                const float e = col < p.N ? exp2f(fmaf(th, k2, -k2)) : 0.f;  // TMA zero-fills past N
+                ce_sum += e;
+                const bool at_t = col == ce_t;
+                ce_zt = at_t ? th * p.beta : ce_zt;
+                g[h] = at_t ? 0.f : e * fmaf(-th, th, 1.f);
+              }
+              os[j] = pack_bf16(g[0], g[1]);
+            }
+            *slotp = make_uint4(os[0], os[1], os[2], os[3]);
+          } else if constexpr (epi_f32(EPI)) {
             float4 x = AUX ? *reinterpret_cast<const float4*>(slotp) : make_float4(0.f, 0.f, 0.f, 0.f);
             float4 o;
             o.x = epi_op<EPI == EPI_ATOMIC_F32 ? EPI_BF16 : EPI>(__uint_as_float(r[4 * q + 0]), x.x, p);
@@ -510,12 +555,19 @@ __global__ void __launch_bounds__(192, 1)
           tc_fence_before();
           mbar_arrive(&tempty_bar[acc]);
         }
-        if (leader) {
+        if (leader && (EPI != EPI_SOFTCAP_CE || p.ce.store)) {
           if constexpr (EPI == EPI_ATOMIC_F32)
             tma_reduce_add_3d(&tmC, buf, col0, row0, b);
           else
             tma_store_3d(&tmC, buf, col0, row0, b);
           bulk_commit();
+        }
+      }
+      if constexpr (EPI == EPI_SOFTCAP_CE) {
+        const int mrow = row0 + lane;
+        if (ok && mrow < p.M) {
+          p.ce.partial[(int64_t)n * p.M + mrow] = ce_sum;
+          if (ce_t >= n * BN && ce_t < n * BN + BN) p.ce.zt[mrow] = ce_zt;
         }
       }
     }
@@ -684,6 +736,52 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
     dispatch_major<128>(a_mn, b_mn, (int)epi, mp, p, grid, st);
 }
 
+// The lm_head GEMM fused with the softcapped cross-entropy statistics (EPI_SOFTCAP_CE, see CeHead):
+// x [M, K] bf16 rows, w [N, K] bf16 rows (the [vocab, dim] table), g [M, N] bf16 (written when store),
+// targets int32 [M], partial fp32 [ceil(N/256), M], zt fp32 [M].
+void gemm_softcap_ce(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& g, const torch::Tensor& targets,
+                     torch::Tensor& partial, torch::Tensor& zt, double cap, bool store) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && g.scalar_type() == at::kBFloat16,
+              "gemm_softcap_ce: bf16 x, w, g");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && g.stride(1) == 1, "gemm_softcap_ce: contiguous rows");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && g.size(0) == M && g.size(1) == N, "gemm_softcap_ce: shapes");
+  TORCH_CHECK(targets.scalar_type() == at::kInt && targets.is_contiguous() && targets.numel() == M,
+              "gemm_softcap_ce: int32 targets [M]");
+  const int64_t n_tiles = (N + 255) / 256;
+  TORCH_CHECK(partial.scalar_type() == at::kFloat && partial.is_contiguous() && partial.numel() >= n_tiles * M,
+              "gemm_softcap_ce: partial fp32 [ceil(N/256), M]");
+  TORCH_CHECK(zt.scalar_type() == at::kFloat && zt.numel() >= M, "gemm_softcap_ce: zt fp32 [M]");
+  TORCH_CHECK(cap > 0, "gemm_softcap_ce: cap > 0");
+  c10::cuda::CUDAGuard guard(x.device());
+  Maps mp;
+  mp.a = bf16_map(x.data_ptr(), K, M, 1, x.stride(0), 0, BM);
+  mp.b = bf16_map(w.data_ptr(), K, N, 1, w.stride(0), 0, 256);
+  mp.c = out_map(g, M, N, 1, g.stride(0), 0);
+  mp.x = mp.c;
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.batch = 1;
+  p.m_tiles = (int)((M + BM - 1) / BM);
+  p.n_tiles = (int)n_tiles;
+  p.k_blocks = (int)((K + BK - 1) / BK);
+  p.k_splits = 1;
+  p.kb_per_split = p.k_blocks;
+  p.has_aux = 0;
+  p.alpha = (float)(1.0 / cap);
+  p.beta = (float)cap;
+  p.status = status_ptr(x.device().index());
+  p.ce.targets = targets.data_ptr<int>();
+  p.ce.partial = partial.data_ptr<float>();
+  p.ce.zt = zt.data_ptr<float>();
+  p.ce.store = store ? 1 : 0;
+  const int total = p.m_tiles * p.n_tiles;
+  launch_t<256, false, false, EPI_SOFTCAP_CE, false>(mp, p, std::min(total, num_sms()),
+                                                      at::cuda::getCurrentCUDAStream());
+}
+
 // out[M, (H+2KV)*128] = x[M, K] @ w[K, N] with the QKV epilogue (RoPE + QK-norm on q/k heads, the
 // value-embedding add on v heads when `ve` is given). x, w, out: bf16 with contiguous rows.
 void gemm_qkv_rope(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, const torch::Tensor& cosT,
@@ -742,6 +840,7 @@ void gemm_qkv_rope(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor
     r.ld_cur = (int)cur->stride(0);
     r.wg = wg->data_ptr<float>();
     r.gate = gate->data_ptr<float>();
+    r.V = (int)ve->size(0);
   }
   const int total = p.m_tiles * p.n_tiles;
   launch_t<256, false, true, EPI_QKV_ROPE, false>(mp, p, std::min(total, num_sms()), at::cuda::getCurrentCUDAStream());

@@ -12,6 +12,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "status.h"
 
 namespace br {
 namespace {
@@ -30,7 +31,8 @@ __device__ __forceinline__ void online(float& m, float& s, float x) {
 template <bool GRAD>
 __global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld,
                                                        const int* __restrict__ targets, int V, float cap, float scale,
-                                                       float* __restrict__ nats, float* __restrict__ loss_sum) {
+                                                       float* __restrict__ nats, float* __restrict__ loss_sum,
+                                                       int* status) {
   __shared__ float sm[kThreads / 32], ss[kThreads / 32];
   __shared__ float bcast[3];
   const int row = blockIdx.x;
@@ -68,7 +70,8 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict_
       S = S * __expf(M - mm) + ss[i] * __expf(sm[i] - mm);
       M = mm;
     }
-    const int t = targets[row];
+    int t = targets[row];
+    if (t != -1 && !index_ok(t, V, status)) t = -1;  // an id outside the vocabulary is ignored and reported
     const int tt = t < 0 ? 0 : t;
     const float pt = __expf(__bfloat162float(L[tt]) - M) / S;
     const float nll = -__logf(pt + 1e-10f);
@@ -83,7 +86,7 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict_
   __syncthreads();
   if constexpr (GRAD) {
     const float M = bcast[0], cs = bcast[1], coef = bcast[2];
-    const int t = targets[row];
+    const int t = targets[row] < V ? targets[row] : -1;
     const float ic = 1.f / cap;
     for (int i = threadIdx.x; i < nvec; i += kThreads) {
       const uint4 u = *reinterpret_cast<const uint4*>(L + i * 8);
@@ -108,7 +111,143 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict_
   }
 }
 
+// Finishes the cross-entropy of the fused lm_head epilogue (EPI_SOFTCAP_CE in gemm.cu), whose GEMM wrote
+// per (256-column tile, row) partial sums of e_j = exp(z_j - cap), the target's softcapped logit z_t and
+// G = e (1 - (z/cap)^2) with G_t = 0. Per row, with S = sum_j e_j:
+//   lse = cap + log S, p_t = exp(z_t - lse), nats = -log(p_t + 1e-10)      (the reference's eps form)
+//   dz_j = r (p_j - [j == t]) c'_j, r = scale p_t / (p_t + 1e-10), c' = 1 - (z/cap)^2
+//        = rowscale * G_j + [j == t] coef,  rowscale = r / S,  coef = r (p_t - 1) c'_t
+// so the backward consumes G with rowscale folded into its other operand and the target column added
+// exactly in fp32: dx = rowscale (G W) + coef W[t] (rms_bwd's head form), dW = G^T (rowscale x) plus
+// the scatter dW[t] += coef x done here, and xs = bf16(rowscale x) is written for the dW GEMM.
+// Rows whose target is -1 are masked (no loss, no gradient, nats 0); any other target outside [0, V) is
+// masked the same way and reported as kErrBadIndex.
+// Block: 256 rows. Phase 1 is one thread per row (coalesced [tile][row] partials); phase 2 one warp per
+// row for the 16-byte vector work on x.
+constexpr int kFinRows = 256;
+
+__global__ void __launch_bounds__(kFinRows) ce_finalize_kernel(
+    const float* __restrict__ partial, int n_tiles, const float* __restrict__ zt, const int* __restrict__ targets,
+    int M, int V, float cap, float scale, float* __restrict__ nats, float* __restrict__ loss_sum,
+    float* __restrict__ rowscale, float* __restrict__ coef, const __nv_bfloat16* __restrict__ x,
+    __nv_bfloat16* __restrict__ xs, float* __restrict__ dw, int D, int* status) {
+  __shared__ float s_rs[kFinRows], s_cf[kFinRows], s_red[kFinRows / 32];
+  __shared__ int s_t[kFinRows];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int base = blockIdx.x * kFinRows; base < M; base += gridDim.x * kFinRows) {
+    const int m = base + threadIdx.x;
+    float contrib = 0.f;
+    if (m < M) {
+      float S = 0.f;
+      for (int n = 0; n < n_tiles; ++n) S += __ldg(partial + (int64_t)n * M + m);
+      const int t = __ldg(targets + m);
+      const bool valid = t == -1 ? false : index_ok(t, V, status);  // -1: ignored position
+      const float z = valid ? __ldg(zt + m) : 0.f;
+      const float pt = __expf(z - cap - __logf(S));
+      const float nll = -__logf(pt + 1e-10f);
+      if (nats) nats[m] = valid ? nll : 0.f;
+      contrib = valid ? nll * scale : 0.f;
+      const float r = valid ? scale * (pt / (pt + 1e-10f)) : 0.f;
+      const float zc = z / cap;
+      const float rs = r / S, cf = r * (pt - 1.f) * (1.f - zc * zc);
+      if (rowscale) rowscale[m] = rs;
+      if (coef) coef[m] = cf;
+      s_rs[threadIdx.x] = rs;
+      s_cf[threadIdx.x] = cf;
+      s_t[threadIdx.x] = valid ? t : -1;
+    }
+    if (loss_sum) {
+      const float w = warp_sum(contrib);
+      if (lane == 0) s_red[warp] = w;
+    }
+    __syncthreads();
+    if (loss_sum && threadIdx.x == 0) {
+      float tot = 0.f;
+      for (int i = 0; i < kFinRows / 32; ++i) tot += s_red[i];
+      atomicAdd(loss_sum, tot);
+    }
+    if (x) {
+      for (int i = warp; i < kFinRows && base + i < M; i += kFinRows / 32) {
+        const int64_t row = base + i;
+        const float rs = s_rs[i], cf = s_cf[i];
+        const int t = s_t[i];
+        for (int c = lane * 8; c < D; c += 256) {
+          const uint4 u = *reinterpret_cast<const uint4*>(x + row * D + c);
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+          float v[8];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = unpack_bf16(w[k]);
+            v[2 * k] = f.x;
+            v[2 * k + 1] = f.y;
+          }
+          if (xs)
+            *reinterpret_cast<uint4*>(xs + row * D + c) =
+                make_uint4(pack_bf16(rs * v[0], rs * v[1]), pack_bf16(rs * v[2], rs * v[3]),
+                           pack_bf16(rs * v[4], rs * v[5]), pack_bf16(rs * v[6], rs * v[7]));
+          if (dw && t >= 0) {
+            float* d = dw + (int64_t)t * D + c;
+            red_add_v4_f32(d, cf * v[0], cf * v[1], cf * v[2], cf * v[3]);
+            red_add_v4_f32(d + 4, cf * v[4], cf * v[5], cf * v[6], cf * v[7]);
+          }
+        }
+      }
+    }
+    __syncthreads();  // the shared row data is rewritten by the next row block
+  }
+}
+
 }  // namespace
+
+void ce_finalize(const torch::Tensor& partial, const torch::Tensor& zt, const torch::Tensor& targets, int64_t V,
+                 double cap, double scale, c10::optional<torch::Tensor> nats, c10::optional<torch::Tensor> loss_sum,
+                 c10::optional<torch::Tensor> rowscale, c10::optional<torch::Tensor> coef,
+                 c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> xs, c10::optional<torch::Tensor> dw) {
+  const int64_t M = targets.numel();
+  const int64_t n_tiles = (V + 255) / 256;
+  TORCH_CHECK(targets.scalar_type() == at::kInt && targets.is_contiguous(), "ce_finalize: int32 targets");
+  TORCH_CHECK(partial.scalar_type() == at::kFloat && partial.is_contiguous() && partial.numel() >= n_tiles * M,
+              "ce_finalize: partial fp32 [ceil(V/256), M]");
+  TORCH_CHECK(zt.scalar_type() == at::kFloat && zt.numel() >= M, "ce_finalize: zt fp32 [M]");
+  auto f32 = [&](const c10::optional<torch::Tensor>& t, const char* name) -> float* {
+    if (!t.has_value() || !t->defined()) return nullptr;
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() >= M, "ce_finalize: ", name);
+    return t->data_ptr<float>();
+  };
+  int64_t D = 0;
+  const __nv_bfloat16* xp = nullptr;
+  __nv_bfloat16* xsp = nullptr;
+  float* dwp = nullptr;
+  if (x.has_value() && x->defined()) {
+    TORCH_CHECK(x->scalar_type() == at::kBFloat16 && x->is_contiguous() && x->dim() == 2 && x->size(0) == M,
+                "ce_finalize: x bf16 [M, D]");
+    D = x->size(1);
+    TORCH_CHECK(D % 8 == 0, "ce_finalize: D % 8");
+    xp = reinterpret_cast<const __nv_bfloat16*>(x->data_ptr());
+    if (xs.has_value() && xs->defined()) {
+      TORCH_CHECK(xs->scalar_type() == at::kBFloat16 && xs->is_contiguous() && xs->numel() == M * D, "ce_finalize: xs");
+      xsp = reinterpret_cast<__nv_bfloat16*>(xs->data_ptr());
+    }
+    if (dw.has_value() && dw->defined()) {
+      TORCH_CHECK(dw->scalar_type() == at::kFloat && dw->is_contiguous() && dw->numel() == V * D, "ce_finalize: dw");
+      dwp = dw->data_ptr<float>();
+    }
+  }
+  float* ls = nullptr;
+  if (loss_sum.has_value() && loss_sum->defined()) {
+    TORCH_CHECK(loss_sum->scalar_type() == at::kFloat, "ce_finalize: loss_sum fp32");
+    ls = loss_sum->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(targets.device());
+  int dev = targets.device().index(), sms = 0;
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t blocks = std::min<int64_t>((M + kFinRows - 1) / kFinRows, (int64_t)sms * 8);
+  ce_finalize_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), kFinRows, 0, at::cuda::getCurrentCUDAStream()>>>(
+      partial.data_ptr<float>(), (int)n_tiles, zt.data_ptr<float>(), targets.data_ptr<int>(), (int)M, (int)V,
+      (float)cap, (float)scale, f32(nats, "nats"), ls, f32(rowscale, "rowscale"), f32(coef, "coef"), xp, xsp, dwp,
+      (int)D, status_ptr(targets.device().index()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 // logits: bf16 [M, V] (row stride ld), softcapped; overwritten by dz when grad=true.
 void softcap_ce(torch::Tensor& logits, const torch::Tensor& targets, double cap, double scale,
@@ -124,10 +263,12 @@ void softcap_ce(torch::Tensor& logits, const torch::Tensor& targets, double cap,
   float* ls = loss_sum.has_value() ? loss_sum->data_ptr<float>() : nullptr;
   if (grad)
     ce_kernel<true><<<(unsigned)M, kThreads, 0, st>>>(L, logits.stride(0), targets.data_ptr<int>(), (int)V,
-                                                       (float)cap, (float)scale, n, ls);
+                                                       (float)cap, (float)scale, n, ls,
+                                                       status_ptr(logits.device().index()));
   else
     ce_kernel<false><<<(unsigned)M, kThreads, 0, st>>>(L, logits.stride(0), targets.data_ptr<int>(), (int)V,
-                                                        (float)cap, (float)scale, n, ls);
+                                                        (float)cap, (float)scale, n, ls,
+                                                       status_ptr(logits.device().index()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -16,6 +16,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "status.h"
 
 namespace br {
 namespace {
@@ -50,10 +51,16 @@ template <>
 __device__ __forceinline__ float4 load_any<__nv_bfloat16>(const __nv_bfloat16* p) { return ldb4(p); }
 
 __global__ void embed_rms_fwd_kernel(const int* __restrict__ idx, const float* __restrict__ wte, float* __restrict__ x0,
-                                     float* __restrict__ rstd, int M, int D) {
+                                     float* __restrict__ rstd, int M, int D, int V, int* status) {
   const int lane = threadIdx.x & 31;
   for (int row = blockIdx.x * kWarps + (threadIdx.x >> 5); row < M; row += gridDim.x * kWarps) {
-    const float* w = wte + (int64_t)idx[row] * D;
+    const int id = idx[row];
+    if (!index_ok(id, V, lane == 0 ? status : nullptr)) {  // a zero row with rstd 0: no gradient either
+      for (int c = lane * 4; c < D; c += 128) st4(x0 + (int64_t)row * D + c, make_float4(0.f, 0.f, 0.f, 0.f));
+      if (lane == 0) rstd[row] = 0.f;
+      continue;
+    }
+    const float* w = wte + (int64_t)id * D;
     float ss = 0.f;
     for (int c = lane * 4; c < D; c += 128) {
       float4 v = ld4(w + c);
@@ -102,20 +109,50 @@ __global__ void rms_fwd_kernel(const float* __restrict__ x, __nv_bfloat16* __res
   }
 }
 
+// The lm_head backward's row terms (the fused softcapped cross-entropy, loss.cu): the incoming gradient
+// is rowscale[row] * dy + coef[row] * w[targets[row]] (w: the [V, D] fp32 table; masked rows have
+// coef 0 and a target outside [0, V)).
+struct HeadGrad {
+  const float* rowscale;
+  const float* coef;
+  const int* targets;
+  const float* w;
+  int V;
+};
+
+template <typename TD, bool HEAD>
+__device__ __forceinline__ float4 head_dy(const TD* dy, int64_t off, int c, float rs, float cf, const float* wrow) {
+  float4 g = load_any<TD>(dy + off + c);
+  if constexpr (HEAD) {
+    g = scale4(g, rs);
+    if (wrow) g = axpby4(1.f, g, cf, ld4(wrow + c));
+  }
+  return g;
+}
+
 // dx = r * (dy - y * mean(dy*y)) + dres, y = x*r
-template <typename TD>
+template <typename TD, bool HEAD>
 __global__ void rms_bwd_kernel(const float* __restrict__ x, const float* __restrict__ rstd, const TD* __restrict__ dy,
                                const float* __restrict__ dres, float* __restrict__ dx, __nv_bfloat16* __restrict__ dxb,
-                               int M, int D) {
+                               int M, int D, HeadGrad hg) {
   const int lane = threadIdx.x & 31;
   for (int row = blockIdx.x * kWarps + (threadIdx.x >> 5); row < M; row += gridDim.x * kWarps) {
     const int64_t off = (int64_t)row * D;
     const float r = rstd[row];
+    float rs = 1.f, cf = 0.f;
+    const float* wrow = nullptr;
+    if constexpr (HEAD) {
+      rs = hg.rowscale[row];
+      cf = hg.coef[row];
+      const int t = hg.targets[row];
+      if (t >= 0 && t < hg.V) wrow = hg.w + (int64_t)t * D;
+    }
     float s = 0.f;
-    for (int c = lane * 4; c < D; c += 128) s += dot4(load_any<TD>(dy + off + c), scale4(ld4(x + off + c), r));
+    for (int c = lane * 4; c < D; c += 128)
+      s += dot4(head_dy<TD, HEAD>(dy, off, c, rs, cf, wrow), scale4(ld4(x + off + c), r));
     const float mean = warp_sum(s) / D;
     for (int c = lane * 4; c < D; c += 128) {
-      float4 g = load_any<TD>(dy + off + c);
+      float4 g = head_dy<TD, HEAD>(dy, off, c, rs, cf, wrow);
       float4 y = scale4(ld4(x + off + c), r);
       float4 o = make_float4(r * (g.x - y.x * mean), r * (g.y - y.y * mean), r * (g.z - y.z * mean),
                              r * (g.w - y.w * mean));
@@ -211,11 +248,13 @@ __global__ void ladder_bwd_kernel(const float* __restrict__ x, const float* __re
 
 __global__ void embed_bwd_kernel(const int* __restrict__ idx, const float* __restrict__ wte,
                                  const float* __restrict__ rstd, const float* __restrict__ dx0, float* __restrict__ dwte,
-                                 int M, int D) {
+                                 int M, int D, int V, int* status) {
   const int lane = threadIdx.x & 31;
   for (int row = blockIdx.x * kWarps + (threadIdx.x >> 5); row < M; row += gridDim.x * kWarps) {
     const int64_t off = (int64_t)row * D;
-    const int64_t woff = (int64_t)idx[row] * D;
+    const int id = idx[row];
+    if (!index_ok(id, V, lane == 0 ? status : nullptr)) continue;
+    const int64_t woff = (int64_t)id * D;
     const float r = rstd[row];
     float s = 0.f;
     for (int c = lane * 4; c < D; c += 128) s += dot4(ld4(dx0 + off + c), scale4(ld4(wte + woff + c), r));
@@ -256,7 +295,8 @@ void embed_rms_fwd(const torch::Tensor& idx, const torch::Tensor& wte, torch::Te
   check_rows(x0, M, D, at::kFloat, "x0");
   c10::cuda::CUDAGuard g(wte.device());
   embed_rms_fwd_kernel<<<rows_grid(M), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
-      idx.data_ptr<int>(), wte.data_ptr<float>(), x0.data_ptr<float>(), rstd.data_ptr<float>(), (int)M, (int)D);
+      idx.data_ptr<int>(), wte.data_ptr<float>(), x0.data_ptr<float>(), rstd.data_ptr<float>(), (int)M, (int)D,
+      (int)wte.size(0), status_ptr(wte.device().index()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -284,20 +324,42 @@ void rms_fwd(const torch::Tensor& x, torch::Tensor& xn, c10::optional<torch::Ten
 }
 
 void rms_bwd(const torch::Tensor& x, const torch::Tensor& rstd, const torch::Tensor& dy,
-             c10::optional<torch::Tensor> dres, c10::optional<torch::Tensor> dx, c10::optional<torch::Tensor> dxb) {
+             c10::optional<torch::Tensor> dres, c10::optional<torch::Tensor> dx, c10::optional<torch::Tensor> dxb,
+             c10::optional<torch::Tensor> rowscale, c10::optional<torch::Tensor> coef,
+             c10::optional<torch::Tensor> targets, c10::optional<torch::Tensor> wtab) {
   const int64_t D = x.size(-1), M = x.numel() / D;
+  TORCH_CHECK(D % 4 == 0, "rms_bwd: D % 4");
   c10::cuda::CUDAGuard g(x.device());
   auto st = at::cuda::getCurrentCUDAStream();
   const float* dr = dres.has_value() ? dres->data_ptr<float>() : nullptr;
   float* o = dx.has_value() ? dx->data_ptr<float>() : nullptr;
   __nv_bfloat16* ob = dxb.has_value() ? reinterpret_cast<__nv_bfloat16*>(dxb->data_ptr()) : nullptr;
-  if (dy.scalar_type() == at::kFloat)
-    rms_bwd_kernel<float><<<rows_grid(M), 32 * kWarps, 0, st>>>(x.data_ptr<float>(), rstd.data_ptr<float>(),
-                                                                dy.data_ptr<float>(), dr, o, ob, (int)M, (int)D);
-  else
-    rms_bwd_kernel<__nv_bfloat16><<<rows_grid(M), 32 * kWarps, 0, st>>>(
-        x.data_ptr<float>(), rstd.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), dr, o,
-        ob, (int)M, (int)D);
+  HeadGrad hg{};
+  const bool head = rowscale.has_value() && rowscale->defined();
+  if (head) {
+    TORCH_CHECK(coef.has_value() && targets.has_value() && wtab.has_value(), "rms_bwd: head form needs coef, targets, w");
+    check_rows(*rowscale, M, 1, at::kFloat, "rowscale");
+    check_rows(*coef, M, 1, at::kFloat, "coef");
+    check_rows(*targets, M, 1, at::kInt, "targets");
+    TORCH_CHECK(wtab->scalar_type() == at::kFloat && wtab->is_contiguous() && wtab->dim() == 2 && wtab->size(1) == D,
+                "rms_bwd: w fp32 [V, D]");
+    hg = HeadGrad{rowscale->data_ptr<float>(), coef->data_ptr<float>(), targets->data_ptr<int>(),
+                  wtab->data_ptr<float>(), (int)wtab->size(0)};
+  }
+  const float* xp = x.data_ptr<float>();
+  const float* rp = rstd.data_ptr<float>();
+  if (dy.scalar_type() == at::kFloat) {
+    if (head)
+      rms_bwd_kernel<float, true><<<rows_grid(M), 32 * kWarps, 0, st>>>(xp, rp, dy.data_ptr<float>(), dr, o, ob,
+                                                                      (int)M, (int)D, hg);
+    else
+      rms_bwd_kernel<float, false><<<rows_grid(M), 32 * kWarps, 0, st>>>(xp, rp, dy.data_ptr<float>(), dr, o, ob,
+                                                                       (int)M, (int)D, hg);
+  } else {
+    TORCH_CHECK(!head, "rms_bwd: the head form takes an fp32 dy");
+    rms_bwd_kernel<__nv_bfloat16, false><<<rows_grid(M), 32 * kWarps, 0, st>>>(
+        xp, rp, reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), dr, o, ob, (int)M, (int)D, hg);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -334,7 +396,7 @@ void embed_bwd(const torch::Tensor& idx, const torch::Tensor& wte, const torch::
   c10::cuda::CUDAGuard g(wte.device());
   embed_bwd_kernel<<<rows_grid(M), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
       idx.data_ptr<int>(), wte.data_ptr<float>(), rstd.data_ptr<float>(), dx0.data_ptr<float>(),
-      dwte.data_ptr<float>(), (int)M, (int)D);
+      dwte.data_ptr<float>(), (int)M, (int)D, (int)wte.size(0), status_ptr(wte.device().index()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

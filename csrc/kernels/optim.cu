@@ -70,8 +70,22 @@ struct MatPtrs {
   int64_t shadow_ld[64];
 };
 
-// grid: (chunks, S). ss[S] accumulates sum(g'^2).
-__global__ void muon_momentum_kernel(const __grid_constant__ MatPtrs P, int64_t n, float mu, float* __restrict__ ss) {
+// Block sum in a fixed order (warp tree, then the warps' sums in index order): the same inputs give the same
+// bits on every rank, so replicated optimizer steps keep replicas identical (float atomics would not).
+__device__ __forceinline__ float block_sum_fixed(float v) {
+  __shared__ float warps[32];
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) warps[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += warps[w];
+  __syncthreads();
+  return t;  // valid in thread 0
+}
+
+// grid: (chunks, S). part[s * chunks + chunk] = this block's sum(g'^2).
+__global__ void muon_momentum_kernel(const __grid_constant__ MatPtrs P, int64_t n, float mu, float* __restrict__ part) {
   const int s = blockIdx.y;
   const float* g = P.g[s];
   float* mom = P.mom[s];
@@ -83,23 +97,34 @@ __global__ void muon_momentum_kernel(const __grid_constant__ MatPtrs P, int64_t 
     const float gp = (1.f - mu) * gi + mu * mi;
     acc += gp * gp;
   }
-  acc = warp_sum(acc);
-  if ((threadIdx.x & 31) == 0) atomicAdd(ss + s, acc);
+  acc = block_sum_fixed(acc);
+  if (threadIdx.x == 0) part[(int64_t)s * gridDim.x + blockIdx.x] = acc;
 }
 
+// Every block sums the partials of its matrix in chunk order (the same result in every block and on
+// every rank); block 0 also stores the total in ss[s].
 __global__ void muon_normalize_kernel(const __grid_constant__ MatPtrs P, int64_t n, float mu,
-                                      const float* __restrict__ ss, __nv_bfloat16* __restrict__ X) {
+                                      const float* __restrict__ part, float* __restrict__ ss,
+                                      __nv_bfloat16* __restrict__ X) {
   const int s = blockIdx.y;
   const float* g = P.g[s];
   const float* mom = P.mom[s];
-  const float inv = 1.f / (sqrtf(ss[s]) * 1.02f + 1e-6f);
+  __shared__ float tot;
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int c = 0; c < (int)gridDim.x; ++c) t += part[(int64_t)s * gridDim.x + c];
+    tot = t;
+    if (blockIdx.x == 0) ss[s] = t;
+  }
+  __syncthreads();
+  const float inv = 1.f / (sqrtf(tot) * 1.02f + 1e-6f);
   __nv_bfloat16* x = X + (int64_t)s * n;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     x[i] = __float2bfloat16(((1.f - mu) * g[i] + mu * mom[i]) * inv);
 }
 
 // One thread per reduction line (row when r >= c, column otherwise); grid (ceil(lines/256), S).
-// sums[2*s] += sum(v_mean) * red, sums[2*s+1] += sum(v_mean * red * step^2).
+// Block partials: sums[2 * (s * nblk + blk)] = sum(v_mean * red), [.. + 1] = sum(v_mean * red * step^2).
 __global__ void normuon_stats_kernel(const __nv_bfloat16* __restrict__ X, const __grid_constant__ MatPtrs P, int r,
                                      int c, float beta2, float* __restrict__ vmean_out, float* __restrict__ sums) {
   const int s = blockIdx.y;
@@ -132,21 +157,32 @@ __global__ void normuon_stats_kernel(const __nv_bfloat16* __restrict__ X, const 
     a = vm * red;
     b = vm * red * st * st;
   }
-  a = warp_sum(a);
-  b = warp_sum(b);
-  if ((threadIdx.x & 31) == 0) {
-    atomicAdd(sums + 2 * s, a);
-    atomicAdd(sums + 2 * s + 1, b);
+  a = block_sum_fixed(a);
+  b = block_sum_fixed(b);
+  if (threadIdx.x == 0) {
+    const int64_t o = 2 * ((int64_t)s * gridDim.x + blockIdx.x);
+    sums[o] = a;
+    sums[o + 1] = b;
   }
 }
 
 __global__ void muon_apply_kernel(const __nv_bfloat16* __restrict__ X, const __grid_constant__ MatPtrs P, int r, int c,
-                                  const float* __restrict__ step_sz, const float* __restrict__ sums, float lr,
-                                  float wd) {
+                                  const float* __restrict__ step_sz, const float* __restrict__ sums, int nblk,
+                                  float lr, float wd) {
   const int s = blockIdx.y;
   const bool rows_major = r >= c;
   const int lines = rows_major ? r : c;
-  const float ratio = sqrtf(sums[2 * s]) / (sqrtf(sums[2 * s + 1]) + 1e-10f);
+  __shared__ float ratio_s;
+  if (threadIdx.x == 0) {  // the stats kernel's block partials, in block order
+    float a = 0.f, b = 0.f;
+    for (int k = 0; k < nblk; ++k) {
+      a += sums[2 * ((int64_t)s * nblk + k)];
+      b += sums[2 * ((int64_t)s * nblk + k) + 1];
+    }
+    ratio_s = sqrtf(a) / (sqrtf(b) + 1e-10f);
+  }
+  __syncthreads();
+  const float ratio = ratio_s;
   const int64_t n = (int64_t)r * c;
   const __nv_bfloat16* x = X + (int64_t)s * n;
   float* p = P.p[s];
@@ -192,6 +228,16 @@ MatPtrs make_ptrs(const std::vector<torch::Tensor>& g, const std::vector<torch::
 
 }  // namespace
 
+// Scratch sizes (floats) of the two Muon entry points, for callers that allocate it once.
+int64_t muon_prepare_scratch(int64_t S, int64_t n) {
+  const int64_t chunks = std::max<int64_t>(1, std::min<int64_t>((n + 1023) / 1024, 4 * sms() / std::max<int64_t>(S, 1) + 1));
+  return S + S * chunks;
+}
+int64_t muon_finish_scratch(int64_t S, int64_t r, int64_t c) {
+  const int64_t lines = r >= c ? r : c;
+  return 2 * S * ((lines + 255) / 256) + S * lines;
+}
+
 void adamw_multi(const std::vector<torch::Tensor>& params, const std::vector<torch::Tensor>& grads,
                  const std::vector<torch::Tensor>& ms, const std::vector<torch::Tensor>& vs,
                  const std::vector<torch::Tensor>& shadows, const std::vector<double>& hyper) {
@@ -234,11 +280,14 @@ void muon_prepare(const std::vector<torch::Tensor>& grads, const std::vector<tor
   c10::cuda::CUDAGuard guard(grads[0].device());
   auto st = at::cuda::getCurrentCUDAStream();
   MatPtrs P = make_ptrs(grads, moms, {}, {}, {});
-  ss.zero_();
   const int chunks = (int)std::max<int64_t>(1, std::min<int64_t>((n + 1023) / 1024, 4 * sms() / std::max(S, 1) + 1));
+  // ss: [S] totals followed by [S, chunks] block partials
+  TORCH_CHECK(ss.scalar_type() == at::kFloat && ss.numel() >= muon_prepare_scratch(S, n),
+              "muon_prepare: ss needs muon_prepare_scratch(S, n) floats");
+  float* part = ss.data_ptr<float>() + S;
   dim3 grid(chunks, S);
-  muon_momentum_kernel<<<grid, 256, 0, st>>>(P, n, (float)mu, ss.data_ptr<float>());
-  muon_normalize_kernel<<<grid, 256, 0, st>>>(P, n, (float)mu, ss.data_ptr<float>(),
+  muon_momentum_kernel<<<grid, 256, 0, st>>>(P, n, (float)mu, part);
+  muon_normalize_kernel<<<grid, 256, 0, st>>>(P, n, (float)mu, part, ss.data_ptr<float>(),
                                               reinterpret_cast<__nv_bfloat16*>(X.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -252,17 +301,17 @@ void muon_finish(const torch::Tensor& X, const std::vector<torch::Tensor>& grads
   auto st = at::cuda::getCurrentCUDAStream();
   MatPtrs P = make_ptrs(grads, {}, params, secs, shadows);
   const int lines = (int)(r >= c ? r : c);
-  // work: [2*S + S*lines] floats: sums then per-line step sizes
-  TORCH_CHECK(work.numel() >= 2 * S + (int64_t)S * lines, "muon_finish: work buffer too small");
+  const int nblk = (lines + 255) / 256;
+  // work: [2 * S * nblk] block partial sums, then [S * lines] per-line step sizes
+  TORCH_CHECK(work.numel() >= muon_finish_scratch(S, r, c), "muon_finish: work needs muon_finish_scratch(S, r, c) floats");
   float* sums = work.data_ptr<float>();
-  float* step_sz = sums + 2 * S;
-  cudaMemsetAsync(sums, 0, sizeof(float) * 2 * S, st);
-  normuon_stats_kernel<<<dim3((lines + 255) / 256, S), 256, 0, st>>>(
+  float* step_sz = sums + 2 * (int64_t)S * nblk;
+  normuon_stats_kernel<<<dim3(nblk, S), 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()), P, (int)r, (int)c, (float)beta2, step_sz, sums);
   const int64_t n = r * c;
   const int chunks = (int)std::max<int64_t>(1, std::min<int64_t>((n + 1023) / 1024, 4 * sms() / std::max(S, 1) + 1));
   muon_apply_kernel<<<dim3(chunks, S), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()), P, (int)r,
-                                                     (int)c, step_sz, sums, (float)lr, (float)wd);
+                                                     (int)c, step_sz, sums, nblk, (float)lr, (float)wd);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -15,6 +15,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "status.h"
 
 namespace br {
 namespace {
@@ -25,7 +26,9 @@ constexpr int kGateCh = 32;
 
 struct RopeArgs {
   int M, T, H, KV, hd;
-  int ld;  // row stride of qkv (elements)
+  int ld;      // row stride of qkv (elements)
+  int V;       // rows of the value-embedding table (token ids are checked against it)
+  int* status;
 };
 
 // One warp per token; lane l owns head elements {2l, 2l+1} and {h2+2l, h2+2l+1} (hd = 128), so every
@@ -94,7 +97,7 @@ __global__ void __launch_bounds__(256) rope_fwd_kernel(__nv_bfloat16* __restrict
         }
       }
     }
-    if (ve != nullptr) {
+    if (ve != nullptr && index_ok(idx[m], a.V, lane == 0 ? a.status : nullptr)) {
       const float cz = cur[(int64_t)m * D + lane];
       const float* e = ve + (int64_t)idx[m] * (a.KV * 128);
       for (int h = 0; h < a.KV; ++h) {
@@ -168,7 +171,9 @@ __global__ void __launch_bounds__(256) rope_bwd_kernel(__nv_bfloat16* __restrict
         }
       }
     }
-    if (ve != nullptr) {
+    if (ve != nullptr && !index_ok(idx[m], a.V, lane == 0 ? a.status : nullptr)) {
+      if (lane < a.KV) dz[(int64_t)m * a.KV + lane] = 0.f;  // the forward skipped this row's VE add
+    } else if (ve != nullptr) {
       const int64_t erow = (int64_t)idx[m] * (a.KV * 128);
       for (int h = 0; h < a.KV; ++h) {
         const int64_t off = base + (nqk + h) * 128 + 4 * lane;
@@ -239,8 +244,9 @@ void rope_fwd(torch::Tensor& qkv, int64_t T, int64_t H, int64_t KV, int64_t hd, 
   TORCH_CHECK(hd == 128, "rope_fwd: head_dim 128");
   TORCH_CHECK(qkv.stride(0) % 8 == 0, "rope_fwd: row stride must be a multiple of 8");
   const int64_t M = qkv.size(0);
-  RopeArgs a{(int)M, (int)T, (int)H, (int)KV, (int)hd, (int)qkv.stride(0)};
   const bool has_ve = ve.has_value() && ve->defined();
+  RopeArgs a{(int)M, (int)T, (int)H, (int)KV, (int)hd, (int)qkv.stride(0), has_ve ? (int)ve->size(0) : 0,
+             status_ptr(qkv.device().index())};
   c10::cuda::CUDAGuard g(qkv.device());
   TORCH_CHECK(H + KV <= 32, "rope_fwd: at most 32 q/k heads");
   rope_fwd_kernel<<<grid_for(M), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
@@ -257,8 +263,9 @@ void rope_bwd(torch::Tensor& dqkv, const torch::Tensor& qkv, int64_t T, int64_t 
               c10::optional<torch::Tensor> dve, c10::optional<torch::Tensor> dz) {
   const int64_t M = qkv.size(0);
   TORCH_CHECK(dqkv.stride(0) == qkv.stride(0), "rope_bwd: dqkv/qkv row strides differ");
-  RopeArgs a{(int)M, (int)T, (int)H, (int)KV, (int)hd, (int)qkv.stride(0)};
   const bool has_ve = ve.has_value() && ve->defined();
+  RopeArgs a{(int)M, (int)T, (int)H, (int)KV, (int)hd, (int)qkv.stride(0), has_ve ? (int)ve->size(0) : 0,
+             status_ptr(qkv.device().index())};
   c10::cuda::CUDAGuard g(qkv.device());
   TORCH_CHECK(hd == 128 && H + KV <= 32, "rope_bwd: head_dim 128, at most 32 q/k heads");
   rope_bwd_kernel<<<grid_for(M), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(

@@ -34,8 +34,6 @@ def _ext_modules():
         "-U__CUDA_NO_BFLOAT16_CONVERSIONS__", "-U__CUDA_NO_HALF2_OPERATORS__",
         "-Xptxas", "-v" if os.environ.get("BR_PTXAS_VERBOSE") else "-O3",
     ]
-    if os.environ.get("BR_DEBUG"):
-        nvcc += ["-DBR_DEBUG"]
     cuda = CUDAExtension(
         "bitresearch_b200._C",
         [os.path.relpath(p, ROOT) for p in cpp + cu],

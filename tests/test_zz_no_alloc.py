@@ -39,7 +39,7 @@ def test_noalloc_entry_matches_list_entry(cuda):
     mom_b = mom_a.clone()                             # state advanced by the list entry point
     xa = torch.empty(S, r, c, dtype=torch.bfloat16, device=cuda)
     xb = torch.empty_like(xa)
-    ss = torch.empty(S, device=cuda)
+    ss = torch.empty(ext().muon_prepare_scratch(S, n), device=cuda)  # the list entry point's scratch
     stream = torch.cuda.current_stream(cuda).cuda_stream
     for call in range(2):
         g = torch.randn(S, r, c, device=cuda) * (0.01 * (call + 1))
