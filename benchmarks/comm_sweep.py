@@ -7,9 +7,12 @@ Bucket sizes 1 KB .. 256 MB (powers of 4) of N(0,1) values from a seed, for ever
 
 * ``nccl_rs`` / ``nccl_ar``: ``reduce_scatter_tensor`` / ``all_reduce`` (ReduceOp.AVG) on a tensor of the
   wire dtype (fp32, bf16 or fp16).
-* ``p2p_rs``: the trainer's path for one bucket: ``comm_pack`` (fp32 -> wire dtype, 1/N scale and the
-  non-finite check fused), a release flag, and ``comm_reduce`` where each owner reads its slice from
-  every peer's buffer over NVLink and sums in fp32.
+* ``p2p_rs_push``: the trainer's path for one bucket: ``comm_pack_push`` (fp32 -> wire dtype and the
+  non-finite check fused; each owner's slice is stored into that owner's receive slot for this rank,
+  posted NVLink stores), ``comm_signal_all`` (one release flag per owner) and ``comm_reduce_local``
+  (each owner sums its N slots from local memory, fp32, 1/N).
+* ``p2p_rs``: the pull form: ``comm_pack`` into this rank's own buffer, a release flag, and
+  ``comm_reduce`` where each owner reads its slice from every peer's buffer over NVLink.
 * ``p2p_ar``: ``p2p_rs`` into a symmetric result buffer, then every owner pushes its reduced slice
   (fp32) into each peer's buffer with posted NVLink stores (``comm_push``), the pair the trainer runs
   per step (gradient reduce-scatter, parameter push).
@@ -52,6 +55,10 @@ class P2PBench:
         self.rank, self.world = rank, world
         self.budget = budget_s
         self.send = SymmetricBuffer(max_elems * 4)
+        self.recv = SymmetricBuffer(max_elems * 4 + 64 * world)
+        self.rflags = SymmetricBuffer(world * 8)
+        self.recv_peers = torch.tensor(self.recv.peer_ptrs, dtype=torch.int64, device="cuda")
+        self.rflag_peers = torch.tensor(self.rflags.peer_ptrs, dtype=torch.int64, device="cuda")
         self.res = SymmetricBuffer(max_elems * 4)
         self.flags = SymmetricBuffer(64 * 8)
         self.push_flags = SymmetricBuffer(world * 8)
@@ -78,6 +85,9 @@ class P2PBench:
         self.n, self.per = n, per
         rows = [(o, ln) for o, ln, _ in chunk_ranges(r * per, per, size=chunk)]
         self.chunks = torch.tensor(rows, dtype=torch.int64, device="cuda").view(-1, 2)
+        push = [(o * per + s, ln, o, s) for o in range(W) for _, ln, s in chunk_ranges(o * per, per, size=chunk)]
+        self.push_tab = torch.tensor(push, dtype=torch.int64, device="cuda").view(-1, 4)
+        self.own_tab = torch.tensor([t for t in push if t[2] == r], dtype=torch.int64, device="cuda").view(-1, 4)
         segs = []
         for o in range(W):
             if o != r:
@@ -118,6 +128,16 @@ class P2PBench:
         mark("reduce")
         self._signal(SLOT_READ, e)
 
+    def rs_push(self, src: torch.Tensor, wire: int, out: torch.Tensor):
+        e = self.epoch = self.epoch + 1
+        self._wait(SLOT_READ)  # every owner has summed last iteration's slots
+        self.E.comm_pack_push(src, self.recv_peers, self.rank, self.per, self.push_tab, wire, 1.0, self.bad,
+                              self.blocks)
+        self.E.comm_signal_all(self.rflag_peers, self.rank, 0, e, self.bad)
+        self.E.comm_reduce_local(self.recv.ptr, self.rflags.ptr, self.world, 0, e, self.per, self.own_tab, out, wire,
+                                 1.0 / self.world, self.blocks, self.budget)
+        self._signal(SLOT_READ, e)
+
     def ar(self, src: torch.Tensor, wire: int, mark=None):
         """Reduce-scatter, then each owner pushes its reduced slice into every peer's result buffer
         (posted NVLink stores) and flags them; a rank is done when all owners' flags arrived."""
@@ -148,7 +168,8 @@ class P2PBench:
         self._signal(SLOT_READ, e)
 
     def close(self):
-        for b in (self.send, self.res, self.flags, self.push_flags, self.idx, self.val, self.cnt):
+        for b in (self.send, self.recv, self.rflags, self.res, self.flags, self.push_flags, self.idx, self.val,
+                  self.cnt):
             b.close()
 
 
@@ -204,7 +225,7 @@ def main():
     ap.add_argument("--min-bytes", type=int, default=1 << 10)
     ap.add_argument("--max-bytes", type=int, default=256 << 20)
     ap.add_argument("--wires", default="fp32,bf16,fp16")
-    ap.add_argument("--variants", default="nccl_rs,p2p_rs,nccl_ar,p2p_ar,p2p_topk")
+    ap.add_argument("--variants", default="nccl_rs,p2p_rs_push,p2p_rs,nccl_ar,p2p_ar,p2p_topk")
     ap.add_argument("--topk", type=float, default=0.01)
     ap.add_argument("--json", default="")
     ap.add_argument("--breakdown", default="", help="comma-separated bucket sizes (bytes): per-phase us of p2p_ar")
@@ -252,6 +273,8 @@ def main():
                     fn = lambda: dist.all_reduce(buf, op=dist.ReduceOp.AVG)  # noqa: E731
                 elif v == "p2p_rs":
                     fn = lambda: bench.rs(src32, code, red)  # noqa: E731
+                elif v == "p2p_rs_push":
+                    fn = lambda: bench.rs_push(src32, code, red)  # noqa: E731
                 elif v == "p2p_ar":
                     fn = lambda: bench.ar(src32, code)  # noqa: E731
                 elif v == "p2p_topk":

@@ -19,7 +19,9 @@ from ._ext import ext
 _MAX_ADAM = 32
 
 
-def step_adamw(opt, grads) -> None:
+def step_adamw(opt, grads, skip: torch.Tensor | None = None) -> None:
+    """``skip``: optional int32 [1] device word; when it holds nonzero at run time the kernels leave
+    parameters and state unchanged (the device-side agreement of a data-parallel step)."""
     P, G, Ms, Vs, Sh, H = [], [], [], [], [], []
     for group, lr, (b1, b2) in opt.adam_groups:
         for n in opt.groups[group]:
@@ -39,7 +41,7 @@ def step_adamw(opt, grads) -> None:
     E = ext()
     for i in range(0, len(P), _MAX_ADAM):
         j = i + _MAX_ADAM
-        E.adamw_multi(P[i:j], G[i:j], Ms[i:j], Vs[i:j], Sh[i:j], H[7 * i:7 * j])
+        E.adamw_multi(P[i:j], G[i:j], Ms[i:j], Vs[i:j], Sh[i:j], H[7 * i:7 * j], skip)
     for k, n in enumerate([n for g, _, _ in opt.adam_groups for n in opt.groups[g] if n in grads]):
         sh = opt.shadows.get(n)
         if sh is not None and not sh.is_contiguous():
@@ -75,7 +77,7 @@ def polar_express_tc(X: torch.Tensor, steps: int, bufs: dict) -> torch.Tensor:
     return cur
 
 
-def step_muon(opt, grads) -> None:
+def step_muon(opt, grads, skip: torch.Tensor | None = None) -> None:
     mu = opt.muon_momentum
     wd = opt.muon_weight_decay
     E = ext()
@@ -88,7 +90,7 @@ def step_muon(opt, grads) -> None:
         r, c = shape
         lr = opt.matrix_lr * opt.lr_multiplier * max(1.0, math.sqrt(max(r / c, c / r)))
         if not _gemm_ok(r, c):
-            _muon_eager(opt, names, grads, mu, lr, wd)
+            _muon_eager(opt, names, grads, mu, lr, wd, skip)
             continue
         for i in range(0, len(names), 64):
             chunk = names[i:i + 64]
@@ -101,25 +103,29 @@ def step_muon(opt, grads) -> None:
                                 torch.empty(E.muon_finish_scratch(S, r, c), dtype=torch.float32, device=dev))
             X, ss, work = opt._ws[key]
             G = [grads[n].contiguous() for n in chunk]
-            E.muon_prepare(G, [opt.state[n]["mom"] for n in chunk], mu, X, ss)
+            E.muon_prepare(G, [opt.state[n]["mom"] for n in chunk], mu, X, ss, skip)
             Xo = polar_express_tc(X, opt.ns_steps, opt._ws)
             sh = [opt.shadows.get(n, torch.Tensor()) for n in chunk]
             E.muon_finish(Xo, G, [opt.params[n].data for n in chunk], [opt.state[n]["sec"] for n in chunk], sh,
-                          r, c, opt.beta2, lr, wd, work)
+                          r, c, opt.beta2, lr, wd, work, skip)
             for n in chunk:
                 opt.state[n]["step"] += 1
 
 
-def _muon_eager(opt, names, grads, mu, lr, wd) -> None:
+def _muon_eager(opt, names, grads, mu, lr, wd, skip=None) -> None:
     G = torch.stack([grads[n].float() for n in names])
     P = torch.stack([opt.params[n].float() for n in names])
     M = torch.stack([opt.state[n]["mom"] for n in names])
     Sc = torch.stack([opt.state[n]["sec"] for n in names])
+    P0, M0, Sc0 = P.clone(), M.clone(), Sc.clone()
     M.mul_(mu).add_(G, alpha=1 - mu)
     X = polar_express(G * (1 - mu) + M * mu, opt.ns_steps, torch.float32)
     X, Sc = normuon_scale(X, Sc, opt.beta2)
     mask = (G * P >= 0).to(P.dtype)
     P.sub_(lr * X + lr * wd * P * mask)
+    if skip is not None:  # device-side select: the old values where the step is skipped
+        keep = skip.bool()
+        P, M, Sc = torch.where(keep, P0, P), torch.where(keep, M0, M), torch.where(keep, Sc0, Sc)
     for j, n in enumerate(names):
         opt.params[n].data.copy_(P[j])
         opt.state[n]["mom"].copy_(M[j])

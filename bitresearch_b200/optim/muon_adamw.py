@@ -120,18 +120,29 @@ class MuonAdamW:
 
     # ------------------------------------------------------------------ step
     @torch.no_grad()
-    def step(self, grads: dict[str, torch.Tensor]) -> None:
+    def step(self, grads: dict[str, torch.Tensor], skip: torch.Tensor | None = None) -> None:
+        """``skip`` (fused path only): an int32 [1] device word; nonzero at run time leaves every parameter and
+        state tensor unchanged, so a data-parallel step can agree on skipping without a host round trip
+        (the host-side step counters still advance; ``undo_steps`` takes them back)."""
         if self.impl == "cuda":
             from ..ops import optim as fused
-            fused.step_adamw(self, grads)
-            fused.step_muon(self, grads)
+            fused.step_adamw(self, grads, skip)
+            fused.step_muon(self, grads, skip)
             return
+        assert skip is None, "a device-side skip needs the fused optimizer"
+
         for group, lr, (b1, b2) in self.adam_groups:
             for n in self.groups[group]:
                 if n not in grads or grads[n] is None:
                     continue
                 self._adamw(n, grads[n].float(), lr * self.lr_multiplier, b1, b2, 1e-10, 0.0)
         self._muon_torch(grads)
+
+    def undo_steps(self, names) -> None:
+        """Takes back the step counters of ``names`` after a step the device skipped."""
+        for n in names:
+            if n in self.state and self.state[n].get("step", 0) > 0:
+                self.state[n]["step"] -= 1
 
     def _adamw(self, n, g, lr, b1, b2, eps, wd):
         p = self.params[n]

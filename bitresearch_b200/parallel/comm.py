@@ -10,10 +10,16 @@ NVSwitch node with a direct algorithm:
 * **Ownership (sharded optimizer).** Every parameter tensor has one owner rank (greedy balance by
   size, Newton-Schulz work counted for matrices). Only the owner keeps optimizer state and updates it.
 * **Per bucket, overlapped with backward** (comm stream, after an event recorded when the engine
-  finishes the bucket): ``pack`` (fp32 -> wire dtype, 1/loss-scale, non-finite check) ->
-  ``signal`` (flags[bucket] = step, release) -> ``reduce`` (every owner reads its owned elements from
-  all peers' send buffers, sums in fp32, scales by 1/N). The 1/N scale is the mean, fixing the
-  reference's ring, which returns the sum (ring-allreduce.ts:161-165).
+  finishes the bucket), a push reduce-scatter: ``pack_push`` (fp32 -> wire dtype, 1/loss-scale,
+  non-finite check; each parameter's slice is stored straight into its owner's receive slot for this
+  rank, posted NVLink stores) -> ``signal_all`` (flags[bucket][me] = 2*step + non-finite bit on every
+  rank, release) -> ``reduce_local`` (each owner waits on its local flags and sums the N slots from
+  local memory in rank order, fp32, scaled by 1/N). No load crosses NVLink. The 1/N scale is the mean,
+  fixing the reference's ring, which returns the sum (ring-allreduce.ts:161-165).
+* **Skip agreement on the device:** after the last bucket, ``agree`` ORs the non-finite bits every rank
+  sent with that bucket's flag (and the status word) into a device skip word, which the optimizer
+  kernels read; the host never waits for the step. It learns the outcome one step later from a pinned
+  copy (the reference's ``allReduce() -> null`` skip, without a host round trip).
 * **After backward:** the sharded MuonAdamW step on owned parameters, then ``push``: each owner
   stores its updated parameters into every peer's symmetric parameter buffer with posted NVLink stores
   and flags each peer; each rank waits (bounded) for the other owners' flags and refreshes the bf16
@@ -155,8 +161,40 @@ class P2PGradSync:
         self.owner = assign_owners(specs, self.world)
         self.owned_names = {n for n, r in self.owner.items() if r == self.rank}
         dev = trainer.device
-        # symmetric buffers: send (wire dtype), params (fp32), flags (int64)
-        self.send = SymmetricBuffer(total * WIRE_BYTES[self.wire])
+        # push reduce-scatter: each owner's parameters get offsets in its owned space; its receive buffer
+        # holds one slot of that space per source rank (all slots the same size on every rank)
+        owned_tot = [0] * self.world
+        self.owned_off = {}
+        for n, (off, numel, _) in self.layout.items():
+            o = self.owner[n]
+            self.owned_off[n] = owned_tot[o]
+            owned_tot[o] += -(-numel // ALIGN) * ALIGN
+        self.slot_elems = max(max(owned_tot), ALIGN)
+        self.recv = SymmetricBuffer(self.world * self.slot_elems * WIRE_BYTES[self.wire])
+        self.rflags = SymmetricBuffer(len(self.ranges) * self.world * 8)
+        self.recv_peers = torch.tensor(self.recv.peer_ptrs, dtype=torch.int64, device=dev)
+        self.rflag_peers = torch.tensor(self.rflags.peer_ptrs, dtype=torch.int64, device=dev)
+        self.push_tables, self.own_tables = [], []
+        for grp in self.groups:
+            rows, mine = [], []
+            for n in grp:
+                off, numel, _ = self.layout[n]
+                for c_off, ln, start in chunk_ranges(off, numel):
+                    row = (c_off, ln, self.owner[n], self.owned_off[n] + start)
+                    rows.append(row)
+                    if self.owner[n] == self.rank:
+                        mine.append(row)
+            self.push_tables.append(torch.tensor(rows, dtype=torch.int64, device=dev).view(-1, 4))
+            self.own_tables.append(torch.tensor(mine, dtype=torch.int64, device=dev).view(-1, 4))
+        # device skip word (the optimizer kernels read it) and its pinned host copy, read one step late
+        # fp16 loss scaling needs the answer on the host, and the top-k path agrees on the host too
+        self.device_skip = not trainer.scaler.enabled and not cfg.sparsify.enabled
+        self.skip = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.snap = torch.zeros(2, dtype=torch.int32).pin_memory()
+        self.snap_event = torch.cuda.Event()
+        self.snap_pending = False
+        self.snap_step, self.snap_names = -1, ()
+        # symmetric buffers: params (fp32), flags (int64)
         self.param_buf = SymmetricBuffer(total * 4)
         self.nflags = len(self.ranges) + 2
         self.flags = SymmetricBuffer(self.nflags * 8)
@@ -173,15 +211,6 @@ class P2PGradSync:
                 p.data = v
         # the reduced gradients the sharded optimizer consumes (views of ``red``)
         self.red_views = OrderedDict((n, self.red[o:o + k].view(s)) for n, (o, k, s) in self.layout.items())
-        # per-bucket owned chunks (offset, len) for the reduce kernel
-        self.reduce_chunks = []
-        for grp in self.groups:
-            ch = []
-            for n in grp:
-                if self.owner[n] == self.rank:
-                    off, numel, _ = self.layout[n]
-                    ch += [(o, ln) for o, ln, _ in chunk_ranges(off, numel)]
-            self.reduce_chunks.append(torch.tensor(ch, dtype=torch.int64, device=dev).view(-1, 2))
         self.flag_ptrs = torch.tensor([p for p in self.flags.peer_ptrs], dtype=torch.int64, device=dev)
         # parameter push: the chunks this rank owns, and one flag slot per source rank on every rank
         rows = []
@@ -280,10 +309,14 @@ class P2PGradSync:
             if self.sparse and self.sp_step >= self.sp_cfg.warmup_steps:
                 self._sparse_bucket(b, loss_scale)
                 return
-            self.E.comm_pack(self.tr.flat_grad, self.send.ptr, self.wire, lo, hi, 1.0 / loss_scale, self.bad)
-            self.E.comm_signal(self.flags.ptr + 8 * b, self.epoch + 1)
-            self.E.comm_reduce(self.send.peers_dev, self.flag_ptrs, b, self.epoch + 1, self.reduce_chunks[b],
-                               self.red, self.wire, 1.0 / self.world, 32, self.budget)
+            ep = self.epoch + 1
+            self.E.comm_pack_push(self.tr.flat_grad, self.recv_peers, self.rank, self.slot_elems, self.push_tables[b],
+                                  self.wire, 1.0 / loss_scale, self.bad, 0)
+            self.E.comm_signal_all(self.rflag_peers, self.rank, b, ep, self.bad)
+            self.E.comm_reduce_local(self.recv.ptr, self.rflags.ptr, self.world, b, ep, self.slot_elems,
+                                     self.own_tables[b], self.red, self.wire, 1.0 / self.world, 0, self.budget)
+            if b == len(self.ranges) - 1:
+                self.E.comm_agree(self.rflags.ptr, self.world, b, ep, self.skip, self.budget)
 
     def begin_step(self) -> None:
         self.bad.zero_()
@@ -296,33 +329,64 @@ class P2PGradSync:
 
     # ------------------------------------------------------------------ step
     def step(self, step_idx: int, scale: float, opt) -> bool:
+        """The sharded optimizer step and the parameter push, queued without waiting for the device.
+
+        With ``device_skip`` the skip decision is the device word ``agree`` wrote; the host learns it (and
+        any status code) from a pinned copy one step later (``poll``), so this returns True before the
+        outcome is known. Otherwise (fp16 loss scaling, top-k) the ranks agree on the host first."""
         timer = self.tr.timer
         cur = torch.cuda.current_stream()
         with traced(timer, "sync.comm_tail"):  # the compute stream waits for the last bucket's reduce
             cur.wait_stream(self.comm_stream)
         epoch = self.epoch + 1
-        with traced(timer, "sync.agree"):
-            # agree on skipping: any non-finite gradient on any rank skips the update everywhere
-            flag = self.bad.clone().float()
-            dist.all_reduce(flag, op=dist.ReduceOp.MAX)
-            status = check_status()
-            ok = status == 0 and float(flag.item()) == 0.0
-        if ok:
+        self.poll()
+        if self.device_skip:
+            ok = True
             with traced(timer, "sync.optimizer"):
-                opt.step({n: self.red_views[n] for n in self.owned_names})
+                opt.step({n: self.red_views[n] for n in self.owned_names}, skip=self.skip)
+            self.E.status_snapshot(self.snap, self.skip)
+            self.snap_event.record()
+            self.snap_pending, self.snap_step = True, step_idx
+        else:
+            with traced(timer, "sync.agree"):
+                # any non-finite gradient on any rank skips the update everywhere
+                flag = self.bad.clone().float()
+                dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+                status = check_status()
+                ok = status == 0 and float(flag.item()) == 0.0
+            if status:
+                self.tr.log(f"p2p collective timed out (status {status}); step {step_idx} skipped")
+            if ok:
+                with traced(timer, "sync.optimizer"):
+                    opt.step({n: self.red_views[n] for n in self.owned_names})
         # push (possibly unchanged) owned parameters into every peer's buffer with posted NVLink stores,
         # flag each peer, then wait for the other owners' pushes and refresh the bf16 shadows locally.
-        # Every rank finished its backward before the skip agreement above, so no peer still reads the
-        # values being overwritten; pushes only touch a peer's non-owned regions.
+        # Every rank's reduce of the last bucket waited for all ranks' last packs, so no peer still
+        # reads the values being overwritten; pushes only touch a peer's non-owned regions.
         with traced(timer, "sync.param_push"):
             self.E.comm_push(self.params_flat, self.param_buf.peers_dev, self.rank, self.push_chunks, 0)
             self.E.comm_signal_peers(self.push_flags.peers_dev, self.rank, epoch)
             self.E.comm_shadow_refresh(self.params_flat, self.push_flags.ptr, self.world, self.rank, epoch,
                                        self.gather_segs, 0, self.budget)
         self.epoch = epoch
-        if status:
-            self.tr.log(f"p2p collective timed out (status {status}); step {step_idx} skipped")
         return ok
+
+    def poll(self, wait: bool = False) -> None:
+        """Reads the previous step's device outcome once its copy has landed (or waits for it): a skipped
+        step takes back the optimizer's step counters and counts as skipped; a status code is logged and
+        cleared."""
+        if not self.snap_pending or not (wait or self.snap_event.query()):
+            return
+        self.snap_event.synchronize()
+        self.snap_pending = False
+        status, skipped = int(self.snap[0]), int(self.snap[1])
+        if skipped:
+            self.tr.optimizer.undo_steps(self.owned_names)
+            self.tr.skipped += 1
+            self.tr.log(f"step {self.snap_step} skipped on the device (non-finite gradient or status {status})")
+        if status:
+            check_status()  # clears the word for the next steps
+            self.tr.log(f"p2p collective reported status {status} at step {self.snap_step}")
 
     def grad_norm(self) -> float:
         """L2 norm of the step's mean gradient: each rank sums the squares of the reduced gradients it
@@ -335,8 +399,9 @@ class P2PGradSync:
 
     def close(self):
         torch.cuda.synchronize()
+        self.poll(wait=True)
         dist.barrier()
-        bufs = [self.send, self.param_buf, self.flags, self.push_flags]
+        bufs = [self.recv, self.rflags, self.param_buf, self.flags, self.push_flags]
         if self.sparse:
             bufs += [self.sp_idx, self.sp_val, self.sp_cnt]
         for b in bufs:

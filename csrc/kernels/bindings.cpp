@@ -50,15 +50,16 @@ void softcap_ce(torch::Tensor& logits, const torch::Tensor& targets, double cap,
                 c10::optional<torch::Tensor> nats, c10::optional<torch::Tensor> loss_sum, bool grad);
 void adamw_multi(const std::vector<torch::Tensor>& params, const std::vector<torch::Tensor>& grads,
                  const std::vector<torch::Tensor>& ms, const std::vector<torch::Tensor>& vs,
-                 const std::vector<torch::Tensor>& shadows, const std::vector<double>& hyper);
+                 const std::vector<torch::Tensor>& shadows, const std::vector<double>& hyper,
+                 c10::optional<torch::Tensor> skip);
 int64_t muon_prepare_scratch(int64_t S, int64_t n);
 int64_t muon_finish_scratch(int64_t S, int64_t r, int64_t c);
 void muon_prepare(const std::vector<torch::Tensor>& grads, const std::vector<torch::Tensor>& moms, double mu,
-                  torch::Tensor& X, torch::Tensor& ss);
+                  torch::Tensor& X, torch::Tensor& ss, c10::optional<torch::Tensor> skip);
 void muon_finish(const torch::Tensor& X, const std::vector<torch::Tensor>& grads,
                  const std::vector<torch::Tensor>& params, const std::vector<torch::Tensor>& secs,
                  const std::vector<torch::Tensor>& shadows, int64_t r, int64_t c, double beta2, double lr, double wd,
-                 torch::Tensor& work);
+                 torch::Tensor& work, c10::optional<torch::Tensor> skip);
 void attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
               torch::Tensor& lse, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd, int64_t window);
 void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& o,
@@ -75,6 +76,14 @@ torch::Tensor mc_sharpe(int64_t n_paths, int64_t steps, double mu, double sigma,
 void comm_push(const torch::Tensor& params, const torch::Tensor& peers, int64_t me, const torch::Tensor& chunks,
                int64_t max_blocks);
 void comm_signal_peers(const torch::Tensor& flag_peers, int64_t me, int64_t epoch);
+void comm_pack_push(const torch::Tensor& grad, const torch::Tensor& recv_peers, int64_t me, int64_t slot_elems,
+                    const torch::Tensor& chunks, int64_t wire, double scale, torch::Tensor& bad, int64_t max_blocks);
+void comm_signal_all(const torch::Tensor& flag_peers, int64_t me, int64_t slot, int64_t epoch, const torch::Tensor& bad);
+void comm_reduce_local(int64_t recv_ptr, int64_t flags_ptr, int64_t npeers, int64_t slot, int64_t epoch,
+                       int64_t slot_elems, const torch::Tensor& chunks, torch::Tensor& out, int64_t wire, double scale,
+                       int64_t max_blocks, double budget_s);
+void comm_agree(int64_t flags_ptr, int64_t npeers, int64_t slot, int64_t epoch, torch::Tensor& skip, double budget_s);
+void status_snapshot(torch::Tensor& out, c10::optional<torch::Tensor> skip);
 void comm_shadow_refresh(const torch::Tensor& params, int64_t push_flags_ptr, int64_t npeers, int64_t me,
                          int64_t epoch, const torch::Tensor& segs, int64_t max_blocks, double budget_s);
 std::tuple<int64_t, torch::Tensor> sym_alloc(int64_t bytes);
@@ -130,11 +139,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_bwd", &br::rope_bwd);
   m.def("ve_gate_bwd", &br::ve_gate_bwd);
   m.def("softcap_ce", &br::softcap_ce);
-  m.def("adamw_multi", &br::adamw_multi);
-  m.def("muon_prepare", &br::muon_prepare);
+  m.def("adamw_multi", &br::adamw_multi, pybind11::arg("params"), pybind11::arg("grads"), pybind11::arg("ms"),
+        pybind11::arg("vs"), pybind11::arg("shadows"), pybind11::arg("hyper"), pybind11::arg("skip") = pybind11::none());
+  m.def("muon_prepare", &br::muon_prepare, pybind11::arg("grads"), pybind11::arg("moms"), pybind11::arg("mu"),
+        pybind11::arg("X"), pybind11::arg("ss"), pybind11::arg("skip") = pybind11::none());
   m.def("muon_prepare_scratch", &br::muon_prepare_scratch);
   m.def("muon_finish_scratch", &br::muon_finish_scratch);
-  m.def("muon_finish", &br::muon_finish);
+  m.def("muon_finish", &br::muon_finish, pybind11::arg("X"), pybind11::arg("grads"), pybind11::arg("params"),
+        pybind11::arg("secs"), pybind11::arg("shadows"), pybind11::arg("r"), pybind11::arg("c"), pybind11::arg("beta2"),
+        pybind11::arg("lr"), pybind11::arg("wd"), pybind11::arg("work"), pybind11::arg("skip") = pybind11::none());
   m.def("attn_fwd", &br::attn_fwd);
   m.def("attn_bwd", &br::attn_bwd);
   m.def("attn_fwd_tc", &br::attn_fwd_tc);
@@ -146,6 +159,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_push", &br::comm_push);
   m.def("comm_signal_peers", &br::comm_signal_peers);
   m.def("comm_shadow_refresh", &br::comm_shadow_refresh);
+  m.def("comm_pack_push", &br::comm_pack_push);
+  m.def("comm_signal_all", &br::comm_signal_all);
+  m.def("comm_reduce_local", &br::comm_reduce_local);
+  m.def("comm_agree", &br::comm_agree);
+  m.def("status_snapshot", &br::status_snapshot);
   m.def("sym_alloc", &br::sym_alloc);
   m.def("sym_open", &br::sym_open);
   m.def("sym_close", &br::sym_close);

@@ -372,6 +372,160 @@ __global__ void __launch_bounds__(256) shadow_refresh_kernel(const float* __rest
   }
 }
 
+// ------------------------------------------------------------------------------ push reduce-scatter
+// The gradient reduce-scatter the trainer runs. Every rank packs a finished bucket into the wire dtype and
+// stores each parameter's slice straight into its owner's receive buffer, in the slot of the sending rank
+// (posted NVLink stores for peers: no load ever crosses the link); a one-thread kernel then release-stores
+// (2 * epoch + this rank's non-finite bit) into flags[bucket][me] of every rank. Each owner waits on its
+// own (local) flags and sums the N slots from local memory in rank order (deterministic), scaled by 1/N.
+// Receive layout on rank o: [source rank][slot_elems] in the wire dtype, parameters at their offsets in
+// o's owned space. The non-finite bits of the last bucket's flags give every rank the same skip decision.
+
+struct PushChunk {
+  int64_t off;       // element offset in the flat gradient buffer
+  int64_t len;
+  int64_t owner;
+  int64_t slot_off;  // element offset inside the owner's per-source slot
+};
+
+template <int WIRE>
+__device__ __forceinline__ void store_wire8(void* base, int64_t i, const float (&x)[8]) {
+  if constexpr (WIRE == W_F32) {
+    float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + i);
+    d[0] = make_float4(x[0], x[1], x[2], x[3]);
+    d[1] = make_float4(x[4], x[5], x[6], x[7]);
+  } else if constexpr (WIRE == W_BF16) {
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + i) =
+        make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]), pack_bf16(x[6], x[7]));
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const __half2 h = __floats2half2_rn(x[2 * k], x[2 * k + 1]);
+      w[k] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(base) + i) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// grid-stride over the bucket's chunks: recv[owner][me * slot + slot_off + j] = wire(grad[off + j] * scale)
+template <int WIRE>
+__global__ void __launch_bounds__(128) pack_push_kernel(const float* __restrict__ grad, void* const* __restrict__ recv,
+                                                        int me, int64_t slot_elems,
+                                                        const PushChunk* __restrict__ chunks, int nchunks,
+                                                        float scale, int* __restrict__ bad) {
+  int nonfinite = 0;
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    const PushChunk ch = chunks[c];
+    const float* src = grad + ch.off;
+    void* dst = recv[ch.owner];
+    const int64_t base = (int64_t)me * slot_elems + ch.slot_off;
+    const int64_t n8 = ch.len & ~int64_t(7);
+    for (int64_t j = threadIdx.x * 8; j < n8; j += (int64_t)blockDim.x * 8) {
+      const float4 a = *reinterpret_cast<const float4*>(src + j);
+      const float4 b = *reinterpret_cast<const float4*>(src + j + 4);
+      float x[8] = {a.x * scale, a.y * scale, a.z * scale, a.w * scale,
+                    b.x * scale, b.y * scale, b.z * scale, b.w * scale};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) nonfinite |= !isfinite(x[k]);
+      store_wire8<WIRE>(dst, base + j, x);
+    }
+    for (int64_t j = n8 + threadIdx.x; j < ch.len; j += blockDim.x) {
+      const float x = src[j] * scale;
+      nonfinite |= !isfinite(x);
+      store_wire<WIRE>(dst, base + j, x);
+    }
+  }
+  if (__syncthreads_or(nonfinite) && threadIdx.x == 0) atomicOr(bad, 1);
+}
+
+// flags[p][slot * npeers + me] = 2 * epoch + (bad != 0) on every rank p (this one included), after all of
+// this GPU's earlier writes (release, system scope)
+__global__ void signal_all_kernel(int64_t* const* flags, int npeers, int me, int slot, int64_t epoch,
+                                  const int* bad) {
+  __threadfence_system();
+  const int64_t v = 2 * epoch + (*bad ? 1 : 0);
+  for (int p = 0; p < npeers; ++p) st_release_sys(flags[p] + (int64_t)slot * npeers + me, v);
+}
+
+// Waits (thread 0, bounded) until every source's flag of `slot` in this rank's (local) flag array has
+// reached 2 * epoch; returns false on timeout.
+__device__ bool wait_local_flags(const int64_t* flags, int npeers, int slot, int64_t epoch, uint64_t budget_ns,
+                                 int* status) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    const int64_t* f = flags + (int64_t)slot * npeers;
+    for (int p = 0; p < npeers && ok; ++p) {
+      uint32_t it = 0;
+      while (ld_acquire_sys(f + p) < 2 * epoch) {
+        if ((++it & 63u) == 0 && globaltimer_ns() - t0 > budget_ns) {
+          ok = 0;
+          if (status) atomicCAS(status, 0, kErrTimeoutPeer);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+// out[off + j] = scale * sum over sources (in rank order) of recv[src * slot + slot_off + j], for the chunks
+// of the bucket this rank owns; all reads are local.
+template <int WIRE>
+__global__ void __launch_bounds__(256) reduce_local_kernel(const void* __restrict__ recv, const int64_t* flags,
+                                                           int npeers, int slot, int64_t epoch, int64_t slot_elems,
+                                                           const PushChunk* __restrict__ chunks, int nchunks,
+                                                           float* __restrict__ out, float scale, uint64_t budget_ns,
+                                                           int* status) {
+  if (!wait_local_flags(flags, npeers, slot, epoch, budget_ns, status)) return;
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    const PushChunk ch = chunks[c];
+    const int64_t n8 = ch.len & ~int64_t(7);
+    for (int64_t j = threadIdx.x * 8; j < n8; j += (int64_t)blockDim.x * 8) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int p = 0; p < npeers; ++p) {
+        float v[8];
+        load8<WIRE>(recv, (int64_t)p * slot_elems + ch.slot_off + j, v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] += v[k];
+      }
+      float4* o = reinterpret_cast<float4*>(out + ch.off + j);
+      o[0] = make_float4(acc[0] * scale, acc[1] * scale, acc[2] * scale, acc[3] * scale);
+      o[1] = make_float4(acc[4] * scale, acc[5] * scale, acc[6] * scale, acc[7] * scale);
+    }
+    for (int64_t j = n8 + threadIdx.x; j < ch.len; j += blockDim.x) {
+      float acc = 0.f;
+      for (int p = 0; p < npeers; ++p) acc += load1<WIRE>(recv, (int64_t)p * slot_elems + ch.slot_off + j);
+      out[ch.off + j] = acc * scale;
+    }
+  }
+}
+
+// One thread: waits for every source's flag of `slot` (the step's last bucket), then
+// skip = OR of their non-finite bits, or 1 when a wait timed out or a kernel reported an error this step.
+__global__ void agree_kernel(const int64_t* flags, int npeers, int slot, int64_t epoch, int* skip,
+                             uint64_t budget_ns, int* status) {
+  const uint64_t t0 = globaltimer_ns();
+  const int64_t* f = flags + (int64_t)slot * npeers;
+  int any = 0;
+  for (int p = 0; p < npeers; ++p) {
+    uint32_t it = 0;
+    int64_t v;
+    while ((v = ld_acquire_sys(f + p)) < 2 * epoch) {
+      if ((++it & 63u) == 0 && globaltimer_ns() - t0 > budget_ns) {
+        atomicCAS(status, 0, kErrTimeoutPeer);
+        v = 2 * epoch + 1;
+        break;
+      }
+    }
+    any |= (int)(v & 1);
+  }
+  *skip = (any || *reinterpret_cast<volatile int*>(status) != 0) ? 1 : 0;
+}
+
 // ------------------------------------------------------------------------------ top-k + error feedback
 // Deep Gradient Compression as in the reference sparsifier (gradient-sparsifier.ts:82-144), per bucket:
 //   g = grad * scale + e (+ momentum correction v = mu*v + g, g = v); thr = the floor(S*(1-k))-th
@@ -632,6 +786,74 @@ void comm_signal_peers(const torch::Tensor& flag_peers, int64_t me, int64_t epoc
   c10::cuda::CUDAGuard g(flag_peers.device());
   signal_peers_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<int64_t* const*>(flag_peers.data_ptr<int64_t>()), (int)flag_peers.numel(), (int)me, epoch);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// chunks: int64 [n, 4] (off, len, owner, slot_off) of every parameter run of one bucket; recv_peers: int64 [N]
+// receive-buffer pointers (this rank's own included)
+void comm_pack_push(const torch::Tensor& grad, const torch::Tensor& recv_peers, int64_t me, int64_t slot_elems,
+                    const torch::Tensor& chunks, int64_t wire, double scale, torch::Tensor& bad, int64_t max_blocks) {
+  static_assert(sizeof(PushChunk) == 4 * 8, "PushChunk layout");
+  c10::cuda::CUDAGuard g(grad.device());
+  const int n = (int)chunks.size(0);
+  if (n == 0) return;
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int grid = (int)std::min<int64_t>(n, max_blocks > 0 ? max_blocks : sm_count());
+  auto R = reinterpret_cast<void* const*>(recv_peers.data_ptr<int64_t>());
+  auto C = reinterpret_cast<const PushChunk*>(chunks.data_ptr<int64_t>());
+  if (wire == W_F32)
+    pack_push_kernel<W_F32><<<grid, 128, 0, st>>>(grad.data_ptr<float>(), R, (int)me, slot_elems, C, n, (float)scale,
+                                                 bad.data_ptr<int>());
+  else if (wire == W_BF16)
+    pack_push_kernel<W_BF16><<<grid, 128, 0, st>>>(grad.data_ptr<float>(), R, (int)me, slot_elems, C, n, (float)scale,
+                                                  bad.data_ptr<int>());
+  else
+    pack_push_kernel<W_F16><<<grid, 128, 0, st>>>(grad.data_ptr<float>(), R, (int)me, slot_elems, C, n, (float)scale,
+                                                 bad.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void comm_signal_all(const torch::Tensor& flag_peers, int64_t me, int64_t slot, int64_t epoch, const torch::Tensor& bad) {
+  c10::cuda::CUDAGuard g(flag_peers.device());
+  signal_all_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<int64_t* const*>(flag_peers.data_ptr<int64_t>()), (int)flag_peers.numel(), (int)me, (int)slot,
+      epoch, bad.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// chunks: int64 [n, 4] of the runs this rank owns in the bucket; recv_ptr/flags_ptr: this rank's buffers
+void comm_reduce_local(int64_t recv_ptr, int64_t flags_ptr, int64_t npeers, int64_t slot, int64_t epoch,
+                       int64_t slot_elems, const torch::Tensor& chunks, torch::Tensor& out, int64_t wire, double scale,
+                       int64_t max_blocks, double budget_s) {
+  c10::cuda::CUDAGuard g(out.device());
+  const int n = (int)chunks.size(0);
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(n, max_blocks > 0 ? max_blocks : sm_count()));
+  const void* R = reinterpret_cast<const void*>(recv_ptr);
+  auto F = reinterpret_cast<const int64_t*>(flags_ptr);
+  auto C = reinterpret_cast<const PushChunk*>(chunks.data_ptr<int64_t>());
+  const uint64_t budget = (uint64_t)(budget_s * 1e9);
+  int* status = status_ptr(out.device().index());
+  if (wire == W_F32)
+    reduce_local_kernel<W_F32><<<grid, 256, 0, st>>>(R, F, (int)npeers, (int)slot, epoch, slot_elems, C, n,
+                                                    out.data_ptr<float>(), (float)scale, budget, status);
+  else if (wire == W_BF16)
+    reduce_local_kernel<W_BF16><<<grid, 256, 0, st>>>(R, F, (int)npeers, (int)slot, epoch, slot_elems, C, n,
+                                                     out.data_ptr<float>(), (float)scale, budget, status);
+  else
+    reduce_local_kernel<W_F16><<<grid, 256, 0, st>>>(R, F, (int)npeers, (int)slot, epoch, slot_elems, C, n,
+                                                    out.data_ptr<float>(), (float)scale, budget, status);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// skip (int32 [1]) = 1 if any rank flagged a non-finite gradient in the step (bit of `slot`'s flags), a wait
+// timed out or the device status word is set; 0 otherwise
+void comm_agree(int64_t flags_ptr, int64_t npeers, int64_t slot, int64_t epoch, torch::Tensor& skip, double budget_s) {
+  c10::cuda::CUDAGuard g(skip.device());
+  agree_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<const int64_t*>(flags_ptr),
+                                                              (int)npeers, (int)slot, epoch, skip.data_ptr<int>(),
+                                                              (uint64_t)(budget_s * 1e9),
+                                                              status_ptr(skip.device().index()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -35,11 +35,13 @@ struct AdamTensor {
 struct AdamBatch {
   AdamTensor t[kMaxT];
   int count;
+  const int* skip;  // nonzero: leave every tensor unchanged (the step's update is skipped on the device)
 };
 
 constexpr int kAdamPerBlock = 256 * 8;
 
 __global__ void adamw_kernel(const __grid_constant__ AdamBatch b) {
+  if (b.skip && *b.skip) return;
   int ti = 0;
   while (ti + 1 < b.count && blockIdx.x >= b.t[ti + 1].block0) ++ti;
   const AdamTensor& T = b.t[ti];
@@ -85,7 +87,9 @@ __device__ __forceinline__ float block_sum_fixed(float v) {
 }
 
 // grid: (chunks, S). part[s * chunks + chunk] = this block's sum(g'^2).
-__global__ void muon_momentum_kernel(const __grid_constant__ MatPtrs P, int64_t n, float mu, float* __restrict__ part) {
+__global__ void muon_momentum_kernel(const __grid_constant__ MatPtrs P, int64_t n, float mu, float* __restrict__ part,
+                                     const int* skip) {
+  if (skip && *skip) return;  // momentum unchanged; the NS iteration then runs on stale data, never applied
   const int s = blockIdx.y;
   const float* g = P.g[s];
   float* mom = P.mom[s];
@@ -126,7 +130,9 @@ __global__ void muon_normalize_kernel(const __grid_constant__ MatPtrs P, int64_t
 // One thread per reduction line (row when r >= c, column otherwise); grid (ceil(lines/256), S).
 // Block partials: sums[2 * (s * nblk + blk)] = sum(v_mean * red), [.. + 1] = sum(v_mean * red * step^2).
 __global__ void normuon_stats_kernel(const __nv_bfloat16* __restrict__ X, const __grid_constant__ MatPtrs P, int r,
-                                     int c, float beta2, float* __restrict__ vmean_out, float* __restrict__ sums) {
+                                     int c, float beta2, float* __restrict__ vmean_out, float* __restrict__ sums,
+                                     const int* skip) {
+  if (skip && *skip) return;
   const int s = blockIdx.y;
   const bool rows_major = r >= c;
   const int lines = rows_major ? r : c;
@@ -168,7 +174,8 @@ __global__ void normuon_stats_kernel(const __nv_bfloat16* __restrict__ X, const 
 
 __global__ void muon_apply_kernel(const __nv_bfloat16* __restrict__ X, const __grid_constant__ MatPtrs P, int r, int c,
                                   const float* __restrict__ step_sz, const float* __restrict__ sums, int nblk,
-                                  float lr, float wd) {
+                                  float lr, float wd, const int* skip) {
+  if (skip && *skip) return;
   const int s = blockIdx.y;
   const bool rows_major = r >= c;
   const int lines = rows_major ? r : c;
@@ -240,8 +247,9 @@ int64_t muon_finish_scratch(int64_t S, int64_t r, int64_t c) {
 
 void adamw_multi(const std::vector<torch::Tensor>& params, const std::vector<torch::Tensor>& grads,
                  const std::vector<torch::Tensor>& ms, const std::vector<torch::Tensor>& vs,
-                 const std::vector<torch::Tensor>& shadows, const std::vector<double>& hyper) {
-  // hyper: per tensor [lr, b1, b2, bias1, bias2, eps, wd]
+                 const std::vector<torch::Tensor>& shadows, const std::vector<double>& hyper,
+                 c10::optional<torch::Tensor> skip) {
+  // hyper: per tensor [lr, b1, b2, bias1, bias2, eps, wd]; skip: optional int32 [1] device word
   const size_t n = params.size();
   TORCH_CHECK(n <= (size_t)kMaxT && hyper.size() == 7 * n, "adamw_multi: bad arguments");
   if (n == 0) return;
@@ -268,13 +276,15 @@ void adamw_multi(const std::vector<torch::Tensor>& params, const std::vector<tor
     blocks += (t.n + kAdamPerBlock - 1) / kAdamPerBlock;
   }
   b.count = (int)n;
+  b.skip = skip.has_value() && skip->defined() ? skip->data_ptr<int>() : nullptr;
   adamw_kernel<<<(unsigned)blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(b);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // Returns X (bf16 [S, r, c]) normalised for Newton-Schulz; updates momentum buffers in place.
 void muon_prepare(const std::vector<torch::Tensor>& grads, const std::vector<torch::Tensor>& moms, double mu,
-                  torch::Tensor& X, torch::Tensor& ss) {
+                  torch::Tensor& X, torch::Tensor& ss, c10::optional<torch::Tensor> skip) {
+  const int* sk = skip.has_value() && skip->defined() ? skip->data_ptr<int>() : nullptr;
   const int S = (int)grads.size();
   const int64_t n = grads[0].numel();
   c10::cuda::CUDAGuard guard(grads[0].device());
@@ -286,7 +296,7 @@ void muon_prepare(const std::vector<torch::Tensor>& grads, const std::vector<tor
               "muon_prepare: ss needs muon_prepare_scratch(S, n) floats");
   float* part = ss.data_ptr<float>() + S;
   dim3 grid(chunks, S);
-  muon_momentum_kernel<<<grid, 256, 0, st>>>(P, n, (float)mu, part);
+  muon_momentum_kernel<<<grid, 256, 0, st>>>(P, n, (float)mu, part, sk);
   muon_normalize_kernel<<<grid, 256, 0, st>>>(P, n, (float)mu, part, ss.data_ptr<float>(),
                                               reinterpret_cast<__nv_bfloat16*>(X.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -295,7 +305,8 @@ void muon_prepare(const std::vector<torch::Tensor>& grads, const std::vector<tor
 void muon_finish(const torch::Tensor& X, const std::vector<torch::Tensor>& grads,
                  const std::vector<torch::Tensor>& params, const std::vector<torch::Tensor>& secs,
                  const std::vector<torch::Tensor>& shadows, int64_t r, int64_t c, double beta2, double lr, double wd,
-                 torch::Tensor& work) {
+                 torch::Tensor& work, c10::optional<torch::Tensor> skip) {
+  const int* sk = skip.has_value() && skip->defined() ? skip->data_ptr<int>() : nullptr;
   const int S = (int)grads.size();
   c10::cuda::CUDAGuard guard(X.device());
   auto st = at::cuda::getCurrentCUDAStream();
@@ -307,11 +318,11 @@ void muon_finish(const torch::Tensor& X, const std::vector<torch::Tensor>& grads
   float* sums = work.data_ptr<float>();
   float* step_sz = sums + 2 * (int64_t)S * nblk;
   normuon_stats_kernel<<<dim3(nblk, S), 256, 0, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()), P, (int)r, (int)c, (float)beta2, step_sz, sums);
+      reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()), P, (int)r, (int)c, (float)beta2, step_sz, sums, sk);
   const int64_t n = r * c;
   const int chunks = (int)std::max<int64_t>(1, std::min<int64_t>((n + 1023) / 1024, 4 * sms() / std::max(S, 1) + 1));
   muon_apply_kernel<<<dim3(chunks, S), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()), P, (int)r,
-                                                     (int)c, step_sz, sums, nblk, (float)lr, (float)wd);
+                                                     (int)c, step_sz, sums, nblk, (float)lr, (float)wd, sk);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

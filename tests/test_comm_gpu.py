@@ -1,7 +1,8 @@
 """NVLink collective kernels.
 
 * 1 GPU: a reduce whose peer flag is never set gives up after its budget, records the timeout in the
-  device status word and leaves the context usable.
+  device status word and leaves the context usable (pull reduce, push reduce and the skip agreement);
+  the push reduce-scatter's index arithmetic on a world of one.
 * 2 GPUs (one process each, NCCL only for rendezvous): packed bf16/fp32 gradients reduced by their
   owners equal the mean of the ranks' inputs; the parameter gather (pull) and the parameter push
   deliver the owners' values and refresh bf16 shadows; the fused top-k path reduces the kept entries;
@@ -41,12 +42,102 @@ def test_bounded_wait_times_out_and_context_survives(cuda):
         E.sym_free(ptr)
 
 
+def test_push_reduce_and_agree_time_out_and_context_survives(cuda):
+    from bitresearch_b200.ops._ext import check_status, ext
+    E = ext()
+    check_status()
+    ptr, _ = E.sym_alloc(1 << 20)
+    try:
+        chunks = torch.tensor([[0, 1024, 0, 0]], dtype=torch.int64, device=cuda)
+        out = torch.zeros(1024, device=cuda)
+        t0 = time.time()
+        E.comm_reduce_local(ptr, ptr + (1 << 19), 1, 0, 1, 1024, chunks, out, 0, 1.0, 4, 0.2)  # flag stays 0
+        torch.cuda.synchronize()
+        assert check_status() == 4 and 0.15 < time.time() - t0 < 5.0
+        skip = torch.zeros(1, dtype=torch.int32, device=cuda)
+        E.comm_agree(ptr + (1 << 19), 1, 0, 1, skip, 0.2)
+        torch.cuda.synchronize()
+        assert check_status() == 4 and int(skip.item()) == 1  # a timed-out step is skipped
+        x = torch.randn(1000, device=cuda)
+        assert torch.isfinite((x @ x).reshape(1)).all()
+    finally:
+        E.sym_free(ptr)
+
+
+@pytest.mark.parametrize("wire,code", [("fp32", 0), ("bf16", 1), ("fp16", 2)])
+def test_push_reduce_scatter_world_of_one(cuda, wire, code):
+    """pack_push -> signal_all -> reduce_local -> agree with this GPU as the only rank: two parameters
+    with odd lengths at scattered slot offsets come back as scale * value; a NaN sets the skip word."""
+    from bitresearch_b200.ops._ext import check_status, ext
+    E = ext()
+    check_status()
+    wb = {0: 4, 1: 2, 2: 2}[code]
+    slot = 4096
+    rptr, _ = E.sym_alloc(slot * wb)
+    fptr, _ = E.sym_alloc(2 * 8)
+    try:
+        grad = torch.randn(3000, device=cuda)
+        # parameter a: flat [0, 1237) -> slot 2048; parameter b: flat [1248, 2990) -> slot 0
+        chunks = torch.tensor([[0, 1237, 0, 2048], [1248, 1742, 0, 0]], dtype=torch.int64, device=cuda)
+        peers = torch.tensor([rptr], dtype=torch.int64, device=cuda)
+        fpeers = torch.tensor([fptr], dtype=torch.int64, device=cuda)
+        bad = torch.zeros(1, dtype=torch.int32, device=cuda)
+        out = torch.zeros(3000, device=cuda)
+        skip = torch.full((1,), 7, dtype=torch.int32, device=cuda)
+        E.comm_pack_push(grad, peers, 0, slot, chunks, code, 0.5, bad, 0)
+        E.comm_signal_all(fpeers, 0, 1, 1, bad)
+        E.comm_reduce_local(rptr, fptr, 1, 1, 1, slot, chunks, out, code, 2.0, 0, 5.0)
+        E.comm_agree(fptr, 1, 1, 1, skip, 5.0)
+        torch.cuda.synchronize()
+        assert check_status() == 0 and int(bad.item()) == 0 and int(skip.item()) == 0
+        ref = grad * 0.5
+        if code:
+            ref = ref.to(torch.bfloat16 if code == 1 else torch.float16).float()
+        ref = ref * 2.0
+        for lo, hi in ((0, 1237), (1248, 2990)):
+            torch.testing.assert_close(out[lo:hi], ref[lo:hi], rtol=0, atol=0)
+        assert out[1237:1248].abs().max().item() == 0 and out[2990:].abs().max().item() == 0
+        grad[5] = float("nan")  # next step: a non-finite gradient reaches the skip word
+        bad.zero_()
+        E.comm_pack_push(grad, peers, 0, slot, chunks, code, 0.5, bad, 0)
+        E.comm_signal_all(fpeers, 0, 1, 2, bad)
+        E.comm_agree(fptr, 1, 1, 2, skip, 5.0)
+        torch.cuda.synchronize()
+        assert int(bad.item()) == 1 and int(skip.item()) == 1 and check_status() == 0
+    finally:
+        E.sym_free(rptr)
+        E.sym_free(fptr)
+
+
 def _port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     p = s.getsockname()[1]
     s.close()
     return p
+
+
+def _to_numpy(x):
+    """Results cross the queue as numpy arrays: a torch CPU tensor would travel as a shared-memory file
+    descriptor that is gone once the child exits, which it may do before the parent reads it."""
+    if isinstance(x, torch.Tensor):
+        x = x.detach().cpu()
+        return ("__tensor__", (x.float() if x.dtype == torch.bfloat16 else x).numpy().copy(), str(x.dtype))
+    if isinstance(x, dict):
+        return {k: _to_numpy(v) for k, v in x.items()}
+    if isinstance(x, (list, tuple)):
+        return type(x)(_to_numpy(v) for v in x)
+    return x
+
+
+def _to_torch(x):
+    if isinstance(x, tuple) and len(x) == 3 and x[0] == "__tensor__":
+        return torch.from_numpy(x[1])
+    if isinstance(x, dict):
+        return {k: _to_torch(v) for k, v in x.items()}
+    if isinstance(x, (list, tuple)):
+        return type(x)(_to_torch(v) for v in x)
+    return x
 
 
 def _worker(rank, world, port, fn, q):
@@ -57,7 +148,7 @@ def _worker(rank, world, port, fn, q):
         torch.cuda.set_device(rank)
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                                 device_id=torch.device("cuda", rank))
-        q.put((rank, "ok", fn(rank, world)))
+        q.put((rank, "ok", _to_numpy(fn(rank, world))))
     except BaseException:
         import traceback
         q.put((rank, "err", traceback.format_exc()))
@@ -83,7 +174,7 @@ def _run(fn, world=2, timeout=300):
         for _ in range(world):
             r, st, v = q.get(timeout=timeout)
             assert st == "ok", f"rank {r}:\n{v}"
-            res[r] = v
+            res[r] = _to_torch(v)
     finally:
         for p in ps:
             p.join(timeout=60)
@@ -156,6 +247,61 @@ def test_p2p_reduce_and_gather_2gpu():
         assert torch.all(local[other * half:(other + 1) * half] == other + 1)
         assert torch.all(local[r * half:(r + 1) * half] == r + 1)
         assert torch.all(shadow == other + 1)
+
+
+def _push_rs(rank, world):
+    """Two parameters owned by rank 0 and one by rank 1 (uneven ownership), two steps; on the second, rank 1
+    has a NaN in a parameter rank 0 owns: rank 0's reduce sees it, and both ranks' skip words are set."""
+    from bitresearch_b200.ops._ext import check_status, ext
+    from bitresearch_b200.parallel.comm import SymmetricBuffer
+    E = ext()
+    out = {}
+    for wire, code, wb in (("fp32", 0, 4), ("bf16", 1, 2)):
+        slot = 3072  # rank 0 owns 1000 + 2000 (slots 0 and 1008), rank 1 owns 1500 (slot 0)
+        recv = SymmetricBuffer(world * slot * wb)
+        flags = SymmetricBuffer(2 * world * 8)
+        rp = torch.tensor(recv.peer_ptrs, dtype=torch.int64, device="cuda")
+        fp = torch.tensor(flags.peer_ptrs, dtype=torch.int64, device="cuda")
+        # flat: a [0, 1000) owner 0 slot 0 | b [1008, 3008) owner 0 slot 1008 | c [3008, 4508) owner 1 slot 0
+        table = [(0, 1000, 0, 0), (1008, 2000, 0, 1008), (3008, 1500, 1, 0)]
+        allc = torch.tensor(table, dtype=torch.int64, device="cuda")
+        mine = torch.tensor([t for t in table if t[2] == rank], dtype=torch.int64, device="cuda")
+        bad = torch.zeros(1, dtype=torch.int32, device="cuda")
+        skip = torch.zeros(1, dtype=torch.int32, device="cuda")
+        res = []
+        for epoch in (1, 2):
+            g = torch.randn(4508, generator=torch.Generator().manual_seed(10 * epoch + rank)).cuda()
+            if epoch == 2 and rank == 1:
+                g[1500] = float("nan")
+            bad.zero_()
+            red = torch.zeros(4508, device="cuda")
+            E.comm_pack_push(g, rp, rank, slot, allc, code, 1.0, bad, 0)
+            E.comm_signal_all(fp, rank, 1, epoch, bad)
+            E.comm_reduce_local(recv.ptr, flags.ptr, world, 1, epoch, slot, mine, red, code, 1.0 / world, 0, 10.0)
+            E.comm_agree(flags.ptr, world, 1, epoch, skip, 10.0)
+            torch.cuda.synchronize()
+            res.append((red.cpu(), int(skip.item()), check_status()))
+            torch.distributed.barrier()
+        out[wire] = res
+        recv.close()
+        flags.close()
+    return out
+
+
+def test_push_reduce_scatter_2gpu():
+    res = _run(_push_rs)
+    gs = {e: [torch.randn(4508, generator=torch.Generator().manual_seed(10 * e + r)) for r in range(2)] for e in (1, 2)}
+    mean = (gs[1][0] + gs[1][1]) / 2
+    own = {0: [(0, 1000), (1008, 3008)], 1: [(3008, 4508)]}
+    for wire, tol in (("fp32", 1e-6), ("bf16", 1e-2)):
+        for r in range(2):
+            red, skip, st = res[r][wire][0]
+            assert st == 0 and skip == 0
+            for lo, hi in own[r]:
+                torch.testing.assert_close(red[lo:hi], mean[lo:hi], rtol=tol, atol=tol)
+            red2, skip2, st2 = res[r][wire][1]
+            assert st2 == 0 and skip2 == 1  # both ranks agree to skip the step with rank 1's NaN
+        assert torch.isnan(res[0][wire][1][0][1500])
 
 
 def _push(rank, world):
@@ -254,6 +400,59 @@ def test_p2p_trainer_matches_nccl_2gpu():
             diff = (pn[n] - pp[n]).norm().item()
             adam = not n.startswith("layer")
             assert diff <= (0.25 if adam else 0.1) * moved, (r, n, diff, moved)
+
+
+def _device_skip(rank, world):
+    """p2p trainer, 2 ranks: on the second step rank 1's gradient gets a NaN just before the first bucket is
+    packed; both ranks must leave every parameter unchanged, learn of the skip one step later and keep
+    identical replicas."""
+    from bitresearch_b200.config import apply_overrides, preset
+    from bitresearch_b200.train import Trainer
+    cfg = apply_overrides(preset("d512"), ["model.n_layer=2", "model.sequence_len=256", "model.vocab_size=1024",
+                                           "device_batch=4", f"total_batch_tokens={4 * 256 * world}",
+                                           "log_every=0", "results_tsv=", "comm=p2p"])
+    tr = Trainer(cfg, device=torch.device("cuda", rank), log=lambda m: None)
+    tr.initialize()
+    hook = tr.engine.bucket_hook
+    state = {"poison": False}
+
+    def poisoned(b, scale):
+        if state["poison"] and b == 0:
+            tr.flat_grad[tr.bucket_ranges[0][0]] = float("nan")
+        hook(b, scale)
+
+    tr.engine.bucket_hook = poisoned
+    g = torch.Generator(device="cpu").manual_seed(100 + rank)
+    batches = [(torch.randint(0, 1024, (4, 256), generator=g, dtype=torch.int32).cuda(),
+                torch.randint(0, 1024, (4, 256), generator=g, dtype=torch.int32).cuda()) for _ in range(3)]
+    tr.train_step(batches[0])
+    torch.cuda.synchronize()
+    before = {n: p.detach().float().cpu().clone() for n, p in tr.model.named().items()}
+    state["poison"] = rank == 1
+    tr.train_step(batches[1])
+    torch.cuda.synchronize()
+    after = {n: p.detach().float().cpu().clone() for n, p in tr.model.named().items()}
+    skipped_late = tr.skipped
+    state["poison"] = False
+    tr.train_step(batches[2])  # polls the previous step's outcome
+    torch.cuda.synchronize()
+    tr.comm.poll(wait=True)
+    final = {n: p.detach().float().cpu() for n, p in tr.model.named().items()}
+    out = (before, after, skipped_late, tr.skipped, final)
+    tr.destroy()
+    return out
+
+
+def test_device_side_skip_keeps_replicas_2gpu():
+    res = _run(_device_skip)
+    for r in range(2):
+        before, after, skipped_late, skipped, _ = res[r]
+        for n in before:
+            assert torch.equal(before[n], after[n]), (r, n)  # the poisoned step changed nothing
+        assert skipped == 1
+    for n in res[0][4]:
+        assert torch.equal(res[0][4][n], res[1][4][n]), n  # replicas identical after the next step
+        assert torch.isfinite(res[0][4][n]).all(), n
 
 
 @pytest.mark.parametrize("masking", [False, True])
