@@ -79,14 +79,18 @@ def _barrier_sync():
     torch.cuda.synchronize()
 
 
-def _time_steps(step_fn, K: int) -> float:
-    """ms per step on this rank (CUDA events around K steps)."""
+def _time_steps(step_fn, K: int, join=None) -> float:
+    """ms per step on this rank (CUDA events around K steps). ``join`` makes the launching stream wait for
+    work the steps queued on side streams (the parameter exchange that overlaps the next forward), so the
+    end event covers all of it."""
     _barrier_sync()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(K):
         step_fn()
+    if join is not None:
+        join()
     b.record()
     _barrier_sync()
     return a.elapsed_time(b) / K
@@ -193,7 +197,8 @@ def main():
         step()
     clocks = ClockSampler(gpu_index=None).start()
     reset_launch_counts()
-    ms = _time_steps(step, K)
+    join = tr.join_streams if args.impl == "ours" else None
+    ms = _time_steps(step, K, join)
     by_kernel = launch_counts()
     launches = sum(by_kernel.values())
     clk = clocks.stop()
@@ -204,7 +209,7 @@ def main():
     if not args.no_e2e:
         for _ in range(1):
             e2e_step()
-        ms_e2e = _max_over_ranks(_time_steps(e2e_step, K))
+        ms_e2e = _max_over_ranks(_time_steps(e2e_step, K, join))
         e2e = {"value": global_tokens / (ms_e2e / 1e3), "unit": "tokens/s", "ms_per_step": ms_e2e,
                "h2d_bytes_per_step": 2 * 4 * B * T * accum, "d2h_bytes_per_step": 4,
                "api": "Trainer.train_step()" if args.impl == "ours" else "DDPBaseline.train_step() + loss.item()"}

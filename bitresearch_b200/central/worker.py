@@ -50,7 +50,7 @@ def train_config_from_welcome(msg: dict, device: str):
         cfg.impl, cfg.dtype, cfg.ns_dtype = "torch", "fp32", "fp32"
     else:
         from ..models.engine import FusedGPTEngine
-        # the sm_100a engine when it supports the model; e.g. the reference's 4 x 64 heads: eager path on the GPU
+        # the sm_100a engine when it supports the model (64- and 128-wide heads), else the eager path on the GPU
         cfg.impl = "cuda" if FusedGPTEngine.unsupported(m) is None else "torch"
     return cfg
 

@@ -291,7 +291,7 @@ def _ref_default() -> TrainConfig:
     return TrainConfig(
         model=GPTConfig(sequence_len=512, vocab_size=8192, n_layer=4, n_head=4, n_kv_head=4, n_embd=256,
                         window_pattern="L"),
-        device_batch=4, total_batch_tokens=4 * 512, impl="torch",
+        device_batch=4, total_batch_tokens=4 * 512, impl="cuda",
     )
 
 

@@ -39,11 +39,12 @@ from ..utils.timing import traced
 class FusedGPTEngine:
     @staticmethod
     def unsupported(cfg) -> str | None:
-        """Why the sm_100a engine cannot run this model config, or None. Its attention kernels and the
-        QKV epilogue are built for 128-wide heads (every benchmark config has them); other widths train
+        """Why the sm_100a engine cannot run this model config, or None. Heads are 128 wide (the tcgen05
+        attention and the QKV epilogue with RoPE + QK-norm fused) or 64 wide (the reference's default
+        model: register-tiled attention and the separate RoPE/QK-norm/VE kernels); other widths train
         through the eager path (``impl=torch``) on the same GPU."""
-        if cfg.head_dim != 128:
-            return f"head_dim {cfg.head_dim} (n_embd {cfg.n_embd} / n_head {cfg.n_head}); the kernels need 128"
+        if cfg.head_dim not in (64, 128):
+            return f"head_dim {cfg.head_dim} (n_embd {cfg.n_embd} / n_head {cfg.n_head}); the kernels need 64 or 128"
         return None
 
     def __init__(self, model, grad_views: dict, batch: int, seq: int, flat_grad: torch.Tensor | None = None):
@@ -72,12 +73,16 @@ class FusedGPTEngine:
         # bucket_hook(b, grad_scale) is called on the compute stream when bucket b's gradients are
         # final (b = 0: lm_head, 1..L: layers L-1..0, L+1: embeddings and scalars)
         self.bucket_hook = None
-        # tcgen05 attention needs whole 128-row tiles; other lengths use the register-tiled kernels
-        self.tc_attention = seq % 128 == 0
+        # tcgen05 attention needs 128-wide heads and whole 128-row tiles; otherwise the register-tiled kernels
+        self.tc_attention = seq % 128 == 0 and self.hd == 128
         # the QKV GEMM applies RoPE/QK-norm/VE in its epilogue when each 256-column tile holds two heads
         self.fused_rope = self.hd == 128 and self.H % 2 == 0 and self.KV % 2 == 0
         self._hook_on = False
         self._grad_scale = 1.0
+        # param_ready(g) is called on the compute stream before the first kernel that reads parameter
+        # group g (0: embeddings and scalars, 1..L: layer g-1 with its value embedding, L+1: lm_head), so
+        # a data-parallel parameter exchange still in flight can overlap the forward
+        self.param_ready = None
 
     # ------------------------------------------------------------------ weights
     def _alloc_shadows(self):
@@ -153,9 +158,12 @@ class FusedGPTEngine:
         T, D, H, KV, hd = self.T, self.D, self.H, self.KV, self.hd
         Dq, Dkv = self.Dq, self.Dkv
         idx = idx.reshape(-1)
+        ready = self.param_ready or (lambda g: None)
+        ready(0)
         E.embed_rms_fwd(idx, P["wte"], b["x0"], b["rstd0"])
         x = b["x0"]
         for i in range(self.L):
+            ready(i + 1)
             cur, xn = b["cur"][i], b["xn"][i]
             E.ladder_rms_fwd(x, b["x0"], P["residLambdas"], P["x0Lambdas"], i, cur, xn, b["rstd1"][i])
             qkv = b["qkv"][i]
@@ -180,6 +188,7 @@ class FusedGPTEngine:
                         beta=1.0)
             x = b["xs"][i]
         E.rms_fwd(x, b["xf"], b["rstdf"])
+        ready(self.L + 1)
 
     def _head(self, tg: torch.Tensor, b: dict, scale: float, grad: bool):
         """lm_head + softcap 15 + cross-entropy (gpt.ts:296-313) without writing the logits: the GEMM epilogue

@@ -59,6 +59,22 @@ def bucket_order(specs, n_layer: int) -> list[list[str]]:
     return buckets
 
 
+def forward_groups(specs, n_layer: int) -> list[list[str]]:
+    """Parameter names grouped by the point in the forward that first reads them: embeddings and the
+    residual scalars, then each layer with its value embedding, then the lm_head. The parameter exchange
+    after the sharded optimizer runs group by group in this order, so the next forward can start on
+    the first groups while the later ones are still crossing NVLink."""
+    names = [n for n, _, _ in specs]
+    groups = [[n for n in ("wte", "residLambdas", "x0Lambdas") if n in names]]
+    for i in range(n_layer):
+        g = [n for n in names if n.startswith(f"layer{i}_")]
+        if f"ve_{i}" in names:
+            g.append(f"ve_{i}")
+        groups.append(g)
+    groups.append(["lmHead"])
+    return groups
+
+
 def flat_layout(specs, n_layer: int):
     """(OrderedDict name -> (offset, numel, shape), bucket ranges [(lo, hi)], bucket names, total)."""
     shapes = {n: s for n, s, _ in specs}
@@ -212,37 +228,54 @@ class P2PGradSync:
         # the reduced gradients the sharded optimizer consumes (views of ``red``)
         self.red_views = OrderedDict((n, self.red[o:o + k].view(s)) for n, (o, k, s) in self.layout.items())
         self.flag_ptrs = torch.tensor([p for p in self.flags.peer_ptrs], dtype=torch.int64, device=dev)
-        # parameter push: the chunks this rank owns, and one flag slot per source rank on every rank
-        rows = []
-        for n in self.owned_names:
-            off, numel, _ = self.layout[n]
-            rows += [(o, ln) for o, ln, _ in chunk_ranges(off, numel)]
-        self.push_chunks = torch.tensor(sorted(rows), dtype=torch.int64, device=dev).view(-1, 2)
-        self.push_flags = SymmetricBuffer(self.world * 8)
+        # parameter exchange, group by group in forward order: the chunks of each group this rank owns,
+        # and one flag slot per (group, source rank) on every rank
+        self.fgroups = forward_groups(specs, trainer.model.cfg.n_layer)
+        assert sorted(n for g in self.fgroups for n in g) == sorted(self.layout), "forward groups cover every parameter"
+        self.push_chunks = []
+        for grp in self.fgroups:
+            rows = []
+            for n in grp:
+                if self.owner[n] == self.rank:
+                    off, numel, _ = self.layout[n]
+                    rows += [(o, ln) for o, ln, _ in chunk_ranges(off, numel)]
+            self.push_chunks.append(torch.tensor(sorted(rows), dtype=torch.int64, device=dev).view(-1, 2))
+        G = len(self.fgroups)
+        self.push_flags = SymmetricBuffer(G * self.world * 8)
+        self.group_flag_peers = [torch.tensor([p + 8 * g * self.world for p in self.push_flags.peer_ptrs],
+                                              dtype=torch.int64, device=dev) for g in range(G)]
         self._build_gather_table(trainer)
+        self.group_events = [torch.cuda.Event() for _ in range(G)]
+        self.opt_done = torch.cuda.Event()
         self.sparse = cfg.sparsify.enabled
         if self.sparse:
             self._init_sparse(trainer, cfg)
-        self.comm_stream = torch.cuda.Stream(device=dev)
+        # high priority: when a compute kernel's CTA retires, the block scheduler hands the SM to a waiting
+        # bucket kernel first, so reduces do not queue behind the rest of the backward
+        self.comm_stream = torch.cuda.Stream(device=dev, priority=-1)
         self.events = [torch.cuda.Event() for _ in self.ranges]
         self.done = torch.cuda.Event()
         self.epoch = 0
         dist.barrier()
 
     def _build_gather_table(self, trainer):
+        """Per forward group: the segments of parameters other ranks own, with their bf16 shadows."""
         shadows = trainer.engine.shadows if trainer.engine is not None else {}
-        rows = []
-        for n, (off, numel, shape) in self.layout.items():
-            o = self.owner[n]
-            if o == self.rank:
-                continue
-            sh = shadows.get(n)
-            cols = int(shape[-1]) if sh is not None else 0
-            ld = int(sh.stride(0)) if sh is not None else 0
-            ptr = int(sh.data_ptr()) if sh is not None else 0
-            for c_off, ln, start in chunk_ranges(off, numel):
-                rows.append((c_off, ln, o, cols, ld, ptr, start))
-        self.gather_segs = torch.tensor(rows, dtype=torch.int64, device=trainer.device).view(-1, 7)
+        self.gather_segs = []
+        for grp in self.fgroups:
+            rows = []
+            for n in grp:
+                off, numel, shape = self.layout[n]
+                o = self.owner[n]
+                if o == self.rank:
+                    continue
+                sh = shadows.get(n)
+                cols = int(shape[-1]) if sh is not None else 0
+                ld = int(sh.stride(0)) if sh is not None else 0
+                ptr = int(sh.data_ptr()) if sh is not None else 0
+                for c_off, ln, start in chunk_ranges(off, numel):
+                    rows.append((c_off, ln, o, cols, ld, ptr, start))
+            self.gather_segs.append(torch.tensor(rows, dtype=torch.int64, device=trainer.device).view(-1, 7))
 
     # ------------------------------------------------------------------ top-k + error feedback
     def _init_sparse(self, trainer, cfg):
@@ -359,17 +392,35 @@ class P2PGradSync:
             if ok:
                 with traced(timer, "sync.optimizer"):
                     opt.step({n: self.red_views[n] for n in self.owned_names})
-        # push (possibly unchanged) owned parameters into every peer's buffer with posted NVLink stores,
-        # flag each peer, then wait for the other owners' pushes and refresh the bf16 shadows locally.
-        # Every rank's reduce of the last bucket waited for all ranks' last packs, so no peer still
-        # reads the values being overwritten; pushes only touch a peer's non-owned regions.
-        with traced(timer, "sync.param_push"):
-            self.E.comm_push(self.params_flat, self.param_buf.peers_dev, self.rank, self.push_chunks, 0)
-            self.E.comm_signal_peers(self.push_flags.peers_dev, self.rank, epoch)
-            self.E.comm_shadow_refresh(self.params_flat, self.push_flags.ptr, self.world, self.rank, epoch,
-                                       self.gather_segs, 0, self.budget)
+        # The parameter exchange runs on the comm stream, overlapped with the next forward: per forward group,
+        # push the (possibly unchanged) owned parameters into every peer's buffer with posted NVLink stores,
+        # flag each peer, wait for the other owners' flags of the group and refresh its bf16 shadows locally,
+        # then record the group's event; the engine's forward waits for group g's event just before its
+        # first kernel that reads group g. Every rank's reduce of the last bucket waited for all ranks'
+        # last packs, so no peer still reads the values being overwritten; pushes only touch a peer's
+        # non-owned regions.
+        self.opt_done.record()
+        s = self.comm_stream
+        s.wait_event(self.opt_done)
+        with torch.cuda.stream(s), traced(timer, "sync.param_exchange"):
+            for g in range(len(self.fgroups)):
+                self.E.comm_push(self.params_flat, self.param_buf.peers_dev, self.rank, self.push_chunks[g], 0)
+                self.E.comm_signal_peers(self.group_flag_peers[g], self.rank, epoch)
+                self.E.comm_shadow_refresh(self.params_flat, self.push_flags.ptr + 8 * g * self.world, self.world,
+                                           self.rank, epoch, self.gather_segs[g], 0, self.budget)
+                self.group_events[g].record(s)
+        if self.tr.engine is not None:
+            self.tr.engine.param_ready = self.param_ready
         self.epoch = epoch
         return ok
+
+    def param_ready(self, g: int) -> None:
+        """Makes the current stream wait until forward group ``g`` of the last exchange has arrived."""
+        torch.cuda.current_stream().wait_event(self.group_events[g])
+
+    def wait_exchange(self) -> None:
+        """Makes the current stream wait for the whole last exchange (before reading every parameter)."""
+        torch.cuda.current_stream().wait_event(self.group_events[-1])
 
     def poll(self, wait: bool = False) -> None:
         """Reads the previous step's device outcome once its copy has landed (or waits for it): a skipped

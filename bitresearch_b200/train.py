@@ -657,7 +657,15 @@ class Trainer:
             self.comm.close()
 
     # ------------------------------------------------------------------ checkpoints
+    def join_streams(self) -> None:
+        """Makes the current stream wait for the work this trainer queued on side streams (the data-parallel
+        parameter exchange that overlaps the next forward): an event recorded after this call covers every
+        step so far."""
+        if self.comm is not None and hasattr(self.comm, "comm_stream"):
+            torch.cuda.current_stream().wait_stream(self.comm.comm_stream)
+
     def checkpoint_state(self):
+        self.join_streams() if self.is_cuda else None
         if self.engine is not None:
             self.engine.sync_params_to_model()
         return ckpt.build_state(

@@ -1,4 +1,4 @@
-// Causal sliding-window flash attention (head_dim 128, bf16 in, fp32 softmax), forward and backward.
+// Causal sliding-window flash attention (head_dim 64 or 128, bf16 in, fp32 softmax), forward and backward.
 //
 // Semantics (src/model/gpt.ts:252-277): query i attends to keys j with i - w + 1 <= j <= i, where
 // w is the layer's window (w >= T is plain causal); scores are scaled by 1/sqrt(hd). Key blocks
@@ -25,7 +25,6 @@
 namespace br {
 namespace {
 
-constexpr int HD = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct AttnArgs {
@@ -47,22 +46,25 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// byte offset of element (row, col) in a [rows][128] bf16 tile with 16-byte chunks XOR-swizzled by row
+// byte offset of element (row, col) in a [rows][HD] bf16 tile with 16-byte chunks XOR-swizzled by row
+// (HD / 8 >= 8 chunks per row, so the XOR with row & 7 stays inside the row)
+template <int HD>
 __device__ __forceinline__ uint32_t swz(int row, int col) {
-  return (uint32_t)(row * 256 + ((((col >> 3) ^ (row & 7))) << 4) + ((col & 7) << 1));
+  return (uint32_t)(row * (2 * HD) + ((((col >> 3) ^ (row & 7))) << 4) + ((col & 7) << 1));
 }
 
 // Load `rows` rows (token index t0 + r of batch b) of a head slice into a swizzled tile.
-template <int ROWS, int NTHREADS>
+template <int ROWS, int NTHREADS, int HD>
 __device__ __forceinline__ void load_tile(uint32_t tile, const __nv_bfloat16* base, int64_t ld, int b, int T, int t0,
                                           int col0) {
+  constexpr int CH = HD / 8;  // 16-byte chunks per row
 #pragma unroll
-  for (int i = threadIdx.x; i < ROWS * 16; i += NTHREADS) {
-    const int r = i >> 4, c = i & 15;
+  for (int i = threadIdx.x; i < ROWS * CH; i += NTHREADS) {
+    const int r = i / CH, c = i % CH;
     const int t = t0 + r;
     const bool ok = t < T && t >= 0;
     const __nv_bfloat16* g = base + ((int64_t)b * T + (ok ? t : 0)) * ld + col0 + c * 8;
-    cp_async16(tile + swz(r, c * 8), g, ok);
+    cp_async16(tile + swz<HD>(r, c * 8), g, ok);
   }
 }
 
@@ -85,19 +87,22 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
 }
 
 // A fragment (16 rows x 16 k) at (r0, k0) of a swizzled tile, rows = M dim, cols = K dim.
+template <int HD>
 __device__ __forceinline__ void frag_a(uint32_t (&a)[4], uint32_t tile, int r0, int k0) {
   const int l = threadIdx.x & 31;
-  ldsm_x4(a, tile + swz(r0 + (l & 15), k0 + ((l >> 4) << 3)));
+  ldsm_x4(a, tile + swz<HD>(r0 + (l & 15), k0 + ((l >> 4) << 3)));
 }
 // B fragments for two n-tiles (16 n) x 16 k where the tile stores [n][k] (k contiguous).
+template <int HD>
 __device__ __forceinline__ void frag_b_nk(uint32_t (&b)[4], uint32_t tile, int n0, int k0) {
   const int l = threadIdx.x & 31;
-  ldsm_x4(b, tile + swz(n0 + (l & 7) + ((l >> 4) << 3), k0 + (((l >> 3) & 1) << 3)));
+  ldsm_x4(b, tile + swz<HD>(n0 + (l & 7) + ((l >> 4) << 3), k0 + (((l >> 3) & 1) << 3)));
 }
 // B fragments for two n-tiles (16 n) x 16 k where the tile stores [k][n] (n contiguous).
+template <int HD>
 __device__ __forceinline__ void frag_b_kn(uint32_t (&b)[4], uint32_t tile, int k0, int n0) {
   const int l = threadIdx.x & 31;
-  ldsm_x4_t(b, tile + swz(k0 + (l & 7) + (((l >> 3) & 1) << 3), n0 + ((l >> 4) << 3)));
+  ldsm_x4_t(b, tile + swz<HD>(k0 + (l & 7) + (((l >> 3) & 1) << 3), n0 + ((l >> 4) << 3)));
 }
 // Pack two accumulator n-tiles (16 rows x 16 cols) into an A fragment.
 __device__ __forceinline__ void pack_a(uint32_t (&a)[4], const float (&c0)[4], const float (&c1)[4]) {
@@ -111,14 +116,15 @@ __device__ __forceinline__ bool visible(int qi, int kj, int T, int w) { return k
 
 // ---------------------------------------------------------------------------------- forward
 constexpr int F_BM = 128, F_BN = 64, F_THREADS = 256;
-constexpr int F_SMEM = F_BM * 256 + 2 * 2 * F_BN * 256;  // Q + double-buffered K, V
+constexpr int f_smem(int HD) { return (F_BM + 2 * 2 * F_BN) * 2 * HD; }  // Q + double-buffered K, V
 
+template <int HD>
 __global__ void __launch_bounds__(F_THREADS, 2)
     attn_fwd_kernel(AttnArgs a, __nv_bfloat16* __restrict__ out, int64_t ldo, float* __restrict__ lse) {
   extern __shared__ __align__(128) uint8_t sm[];
   const uint32_t sQ = smem_u32(sm);
-  const uint32_t sK = sQ + F_BM * 256;
-  const uint32_t sV = sK + 2 * F_BN * 256;
+  const uint32_t sK = sQ + F_BM * 2 * HD;
+  const uint32_t sV = sK + 2 * F_BN * 2 * HD;
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (a.H / a.KV);
   const int q0 = qb * F_BM;
@@ -129,14 +135,14 @@ __global__ void __launch_bounds__(F_THREADS, 2)
   const int kb_lo = max(0, q0 - w + 1) / F_BN;
   const int kb_hi = min(q0 + F_BM - 1, a.T - 1) / F_BN;
 
-  load_tile<F_BM, F_THREADS>(sQ, a.q, a.ldq, b, a.T, q0, h * HD);
-  load_tile<F_BN, F_THREADS>(sK, a.k, a.ldk, b, a.T, kb_lo * F_BN, kvh * HD);
-  load_tile<F_BN, F_THREADS>(sV, a.v, a.ldv, b, a.T, kb_lo * F_BN, kvh * HD);
+  load_tile<F_BM, F_THREADS, HD>(sQ, a.q, a.ldq, b, a.T, q0, h * HD);
+  load_tile<F_BN, F_THREADS, HD>(sK, a.k, a.ldk, b, a.T, kb_lo * F_BN, kvh * HD);
+  load_tile<F_BN, F_THREADS, HD>(sV, a.v, a.ldv, b, a.T, kb_lo * F_BN, kvh * HD);
   cp_async_commit();
 
-  float o[16][4];
+  float o[HD / 8][4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
   const int r0 = warp * 16;
   const int qrow[2] = {q0 + r0 + g, q0 + r0 + g + 8};
@@ -144,24 +150,24 @@ __global__ void __launch_bounds__(F_THREADS, 2)
   for (int kb = kb_lo; kb <= kb_hi; ++kb) {
     const int buf = (kb - kb_lo) & 1;
     if (kb < kb_hi) {
-      load_tile<F_BN, F_THREADS>(sK + (buf ^ 1) * F_BN * 256, a.k, a.ldk, b, a.T, (kb + 1) * F_BN, kvh * HD);
-      load_tile<F_BN, F_THREADS>(sV + (buf ^ 1) * F_BN * 256, a.v, a.ldv, b, a.T, (kb + 1) * F_BN, kvh * HD);
+      load_tile<F_BN, F_THREADS, HD>(sK + (buf ^ 1) * F_BN * 2 * HD, a.k, a.ldk, b, a.T, (kb + 1) * F_BN, kvh * HD);
+      load_tile<F_BN, F_THREADS, HD>(sV + (buf ^ 1) * F_BN * 2 * HD, a.v, a.ldv, b, a.T, (kb + 1) * F_BN, kvh * HD);
     }
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    const uint32_t tK = sK + buf * F_BN * 256, tV = sV + buf * F_BN * 256;
+    const uint32_t tK = sK + buf * F_BN * 2 * HD, tV = sV + buf * F_BN * 2 * HD;
     float s[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < HD / 16; ++kk) {
       uint32_t af[4];
-      frag_a(af, sQ, r0, kk * 16);
+      frag_a<HD>(af, sQ, r0, kk * 16);
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
         uint32_t bf[4];
-        frag_b_nk(bf, tK, np * 16, kk * 16);
+        frag_b_nk<HD>(bf, tK, np * 16, kk * 16);
         mma16816(s[2 * np], af, bf[0], bf[1]);
         mma16816(s[2 * np + 1], af, bf[2], bf[3]);
       }
@@ -188,7 +194,7 @@ __global__ void __launch_bounds__(F_THREADS, 2)
       mrow[ri] = mn;
       lrow[ri] *= alpha;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < HD / 8; ++i) {
         o[i][2 * ri] *= alpha;
         o[i][2 * ri + 1] *= alpha;
       }
@@ -209,7 +215,7 @@ __global__ void __launch_bounds__(F_THREADS, 2)
 #pragma unroll
       for (int nd = 0; nd < HD / 16; ++nd) {
         uint32_t bf[4];
-        frag_b_kn(bf, tV, kk * 16, nd * 16);
+        frag_b_kn<HD>(bf, tV, kk * 16, nd * 16);
         mma16816(o[2 * nd], af, bf[0], bf[1]);
         mma16816(o[2 * nd + 1], af, bf[2], bf[3]);
       }
@@ -228,13 +234,14 @@ __global__ void __launch_bounds__(F_THREADS, 2)
     const float inv = lrow[ri] > 0.f ? 1.f / lrow[ri] : 0.f;
     __nv_bfloat16* orow = out + ((int64_t)b * a.T + qi) * ldo + h * HD;
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
+    for (int nt = 0; nt < HD / 8; ++nt)
       *reinterpret_cast<uint32_t*>(orow + nt * 8 + 2 * tq) = pack_bf16(o[nt][2 * ri] * inv, o[nt][2 * ri + 1] * inv);
     if (tq == 0) lse[((int64_t)b * a.H + h) * a.T + qi] = (mrow[ri] + __log2f(lrow[ri])) / kLog2e;
   }
 }
 
 // ---------------------------------------------------------------------------------- delta
+template <int HD>
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo, const __nv_bfloat16* __restrict__ dout,
                                   int64_t ldd, float* __restrict__ delta, int B, int T, int H) {
   const int lane = threadIdx.x & 31;
@@ -242,10 +249,17 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int64_t l
   for (int64_t task = blockIdx.x * 8ll + (threadIdx.x >> 5); task < total; task += (int64_t)gridDim.x * 8) {
     const int h = (int)(task % H);
     const int64_t m = task / H;
-    const uint2 ou = *reinterpret_cast<const uint2*>(o + m * ldo + h * HD + lane * 4);
-    const uint2 du = *reinterpret_cast<const uint2*>(dout + m * ldd + h * HD + lane * 4);
-    const float2 o0 = unpack_bf16(ou.x), o1 = unpack_bf16(ou.y), d0 = unpack_bf16(du.x), d1 = unpack_bf16(du.y);
-    float s = o0.x * d0.x + o0.y * d0.y + o1.x * d1.x + o1.y * d1.y;
+    float s;
+    if constexpr (HD == 128) {
+      const uint2 ou = *reinterpret_cast<const uint2*>(o + m * ldo + h * HD + lane * 4);
+      const uint2 du = *reinterpret_cast<const uint2*>(dout + m * ldd + h * HD + lane * 4);
+      const float2 o0 = unpack_bf16(ou.x), o1 = unpack_bf16(ou.y), d0 = unpack_bf16(du.x), d1 = unpack_bf16(du.y);
+      s = o0.x * d0.x + o0.y * d0.y + o1.x * d1.x + o1.y * d1.y;
+    } else {
+      const float2 o0 = unpack_bf16(*reinterpret_cast<const uint32_t*>(o + m * ldo + h * HD + lane * 2));
+      const float2 d0 = unpack_bf16(*reinterpret_cast<const uint32_t*>(dout + m * ldd + h * HD + lane * 2));
+      s = o0.x * d0.x + o0.y * d0.y;
+    }
     s = warp_sum(s);
     const int b = (int)(m / T), t = (int)(m % T);
     if (lane == 0) delta[((int64_t)b * H + h) * T + t] = s;
@@ -254,16 +268,17 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int64_t l
 
 // ---------------------------------------------------------------------------------- dQ
 constexpr int Q_BM = 64, Q_BN = 64, Q_THREADS = 128;
-constexpr int Q_SMEM = 2 * Q_BM * 256 + 2 * 2 * Q_BN * 256;  // Q, dO + double-buffered K, V
+constexpr int q_smem(int HD) { return (2 * Q_BM + 2 * 2 * Q_BN) * 2 * HD; }  // Q, dO + double-buffered K, V
 
+template <int HD>
 __global__ void __launch_bounds__(Q_THREADS, 2)
     attn_dq_kernel(AttnArgs a, const __nv_bfloat16* __restrict__ dout, int64_t ldd, const float* __restrict__ lse,
                    const float* __restrict__ delta, __nv_bfloat16* __restrict__ dq, int64_t lddq) {
   extern __shared__ __align__(128) uint8_t sm[];
   const uint32_t sQ = smem_u32(sm);
-  const uint32_t sdO = sQ + Q_BM * 256;
-  const uint32_t sK = sdO + Q_BM * 256;
-  const uint32_t sV = sK + 2 * Q_BN * 256;
+  const uint32_t sdO = sQ + Q_BM * 2 * HD;
+  const uint32_t sK = sdO + Q_BM * 2 * HD;
+  const uint32_t sV = sK + 2 * Q_BN * 2 * HD;
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (a.H / a.KV);
   const int q0 = qb * Q_BM;
@@ -273,10 +288,10 @@ __global__ void __launch_bounds__(Q_THREADS, 2)
   const int kb_lo = max(0, q0 - w + 1) / Q_BN;
   const int kb_hi = min(q0 + Q_BM - 1, a.T - 1) / Q_BN;
 
-  load_tile<Q_BM, Q_THREADS>(sQ, a.q, a.ldq, b, a.T, q0, h * HD);
-  load_tile<Q_BM, Q_THREADS>(sdO, dout, ldd, b, a.T, q0, h * HD);
-  load_tile<Q_BN, Q_THREADS>(sK, a.k, a.ldk, b, a.T, kb_lo * Q_BN, kvh * HD);
-  load_tile<Q_BN, Q_THREADS>(sV, a.v, a.ldv, b, a.T, kb_lo * Q_BN, kvh * HD);
+  load_tile<Q_BM, Q_THREADS, HD>(sQ, a.q, a.ldq, b, a.T, q0, h * HD);
+  load_tile<Q_BM, Q_THREADS, HD>(sdO, dout, ldd, b, a.T, q0, h * HD);
+  load_tile<Q_BN, Q_THREADS, HD>(sK, a.k, a.ldk, b, a.T, kb_lo * Q_BN, kvh * HD);
+  load_tile<Q_BN, Q_THREADS, HD>(sV, a.v, a.ldv, b, a.T, kb_lo * Q_BN, kvh * HD);
   cp_async_commit();
 
   const int r0 = warp * 16;
@@ -288,33 +303,33 @@ __global__ void __launch_bounds__(Q_THREADS, 2)
     lse2[ri] = lse[((int64_t)b * a.H + h) * a.T + qi] * kLog2e;
     dl[ri] = delta[((int64_t)b * a.H + h) * a.T + qi];
   }
-  float acc[16][4];
+  float acc[HD / 8][4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int i = 0; i < HD / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 
   for (int kb = kb_lo; kb <= kb_hi; ++kb) {
     const int buf = (kb - kb_lo) & 1;
     if (kb < kb_hi) {
-      load_tile<Q_BN, Q_THREADS>(sK + (buf ^ 1) * Q_BN * 256, a.k, a.ldk, b, a.T, (kb + 1) * Q_BN, kvh * HD);
-      load_tile<Q_BN, Q_THREADS>(sV + (buf ^ 1) * Q_BN * 256, a.v, a.ldv, b, a.T, (kb + 1) * Q_BN, kvh * HD);
+      load_tile<Q_BN, Q_THREADS, HD>(sK + (buf ^ 1) * Q_BN * 2 * HD, a.k, a.ldk, b, a.T, (kb + 1) * Q_BN, kvh * HD);
+      load_tile<Q_BN, Q_THREADS, HD>(sV + (buf ^ 1) * Q_BN * 2 * HD, a.v, a.ldv, b, a.T, (kb + 1) * Q_BN, kvh * HD);
     }
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    const uint32_t tK = sK + buf * Q_BN * 256, tV = sV + buf * Q_BN * 256;
+    const uint32_t tK = sK + buf * Q_BN * 2 * HD, tV = sV + buf * Q_BN * 2 * HD;
     float s[8][4], dp[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = dp[i][0] = dp[i][1] = dp[i][2] = dp[i][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < HD / 16; ++kk) {
       uint32_t aq[4], ad[4];
-      frag_a(aq, sQ, r0, kk * 16);
-      frag_a(ad, sdO, r0, kk * 16);
+      frag_a<HD>(aq, sQ, r0, kk * 16);
+      frag_a<HD>(ad, sdO, r0, kk * 16);
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
         uint32_t bk[4], bv[4];
-        frag_b_nk(bk, tK, np * 16, kk * 16);
-        frag_b_nk(bv, tV, np * 16, kk * 16);
+        frag_b_nk<HD>(bk, tK, np * 16, kk * 16);
+        frag_b_nk<HD>(bv, tV, np * 16, kk * 16);
         mma16816(s[2 * np], aq, bk[0], bk[1]);
         mma16816(s[2 * np + 1], aq, bk[2], bk[3]);
         mma16816(dp[2 * np], ad, bv[0], bv[1]);
@@ -338,7 +353,7 @@ __global__ void __launch_bounds__(Q_THREADS, 2)
 #pragma unroll
       for (int nd = 0; nd < HD / 16; ++nd) {
         uint32_t bf[4];
-        frag_b_kn(bf, tK, kk * 16, nd * 16);
+        frag_b_kn<HD>(bf, tK, kk * 16, nd * 16);
         mma16816(acc[2 * nd], af, bf[0], bf[1]);
         mma16816(acc[2 * nd + 1], af, bf[2], bf[3]);
       }
@@ -352,24 +367,25 @@ __global__ void __launch_bounds__(Q_THREADS, 2)
     if (qi >= a.T) continue;
     __nv_bfloat16* row = dq + ((int64_t)b * a.T + qi) * lddq + h * HD;
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
+    for (int nt = 0; nt < HD / 8; ++nt)
       *reinterpret_cast<uint32_t*>(row + nt * 8 + 2 * tq) = pack_bf16(acc[nt][2 * ri] * sc, acc[nt][2 * ri + 1] * sc);
   }
 }
 
 // ---------------------------------------------------------------------------------- dK, dV
 constexpr int K_BN = 64, K_BM = 64, K_THREADS = 128;
-constexpr int K_SMEM = 2 * K_BN * 256 + 2 * 2 * K_BM * 256;  // K, V + double-buffered Q, dO
+constexpr int k_smem(int HD) { return (2 * K_BN + 2 * 2 * K_BM) * 2 * HD; }  // K, V + double-buffered Q, dO
 
+template <int HD>
 __global__ void __launch_bounds__(K_THREADS, 2)
     attn_dkdv_kernel(AttnArgs a, const __nv_bfloat16* __restrict__ dout, int64_t ldd, const float* __restrict__ lse,
                      const float* __restrict__ delta, __nv_bfloat16* __restrict__ dk, int64_t lddk,
                      __nv_bfloat16* __restrict__ dv, int64_t lddv) {
   extern __shared__ __align__(128) uint8_t sm[];
   const uint32_t sK = smem_u32(sm);
-  const uint32_t sV = sK + K_BN * 256;
-  const uint32_t sQ = sV + K_BN * 256;
-  const uint32_t sdO = sQ + 2 * K_BM * 256;
+  const uint32_t sV = sK + K_BN * 2 * HD;
+  const uint32_t sQ = sV + K_BN * 2 * HD;
+  const uint32_t sdO = sQ + 2 * K_BM * 2 * HD;
   const int kb = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int group = a.H / a.KV;
   const int k0 = kb * K_BN;
@@ -380,19 +396,19 @@ __global__ void __launch_bounds__(K_THREADS, 2)
   const int qb_hi = min(a.T - 1, k0 + K_BN - 1 + w - 1) / K_BM;
   const int nq = qb_hi - qb_lo + 1;
 
-  load_tile<K_BN, K_THREADS>(sK, a.k, a.ldk, b, a.T, k0, kvh * HD);
-  load_tile<K_BN, K_THREADS>(sV, a.v, a.ldv, b, a.T, k0, kvh * HD);
+  load_tile<K_BN, K_THREADS, HD>(sK, a.k, a.ldk, b, a.T, k0, kvh * HD);
+  load_tile<K_BN, K_THREADS, HD>(sV, a.v, a.ldv, b, a.T, k0, kvh * HD);
   const int r0 = warp * 16;
   const int krow[2] = {k0 + r0 + g, k0 + r0 + g + 8};
-  float dka[16][4], dva[16][4];
+  float dka[HD / 8][4], dva[HD / 8][4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) dka[i][0] = dka[i][1] = dka[i][2] = dka[i][3] = dva[i][0] = dva[i][1] = dva[i][2] = dva[i][3] = 0.f;
+  for (int i = 0; i < HD / 8; ++i) dka[i][0] = dka[i][1] = dka[i][2] = dka[i][3] = dva[i][0] = dva[i][1] = dva[i][2] = dva[i][3] = 0.f;
 
   const int iters = nq * group;
   {
     const int h = kvh * group;
-    load_tile<K_BM, K_THREADS>(sQ, a.q, a.ldq, b, a.T, qb_lo * K_BM, h * HD);
-    load_tile<K_BM, K_THREADS>(sdO, dout, ldd, b, a.T, qb_lo * K_BM, h * HD);
+    load_tile<K_BM, K_THREADS, HD>(sQ, a.q, a.ldq, b, a.T, qb_lo * K_BM, h * HD);
+    load_tile<K_BM, K_THREADS, HD>(sdO, dout, ldd, b, a.T, qb_lo * K_BM, h * HD);
     cp_async_commit();
   }
   for (int it = 0; it < iters; ++it) {
@@ -401,13 +417,13 @@ __global__ void __launch_bounds__(K_THREADS, 2)
     const int qb = qb_lo + it % nq;
     if (it + 1 < iters) {
       const int h2 = kvh * group + (it + 1) / nq, qb2 = qb_lo + (it + 1) % nq;
-      load_tile<K_BM, K_THREADS>(sQ + (buf ^ 1) * K_BM * 256, a.q, a.ldq, b, a.T, qb2 * K_BM, h2 * HD);
-      load_tile<K_BM, K_THREADS>(sdO + (buf ^ 1) * K_BM * 256, dout, ldd, b, a.T, qb2 * K_BM, h2 * HD);
+      load_tile<K_BM, K_THREADS, HD>(sQ + (buf ^ 1) * K_BM * 2 * HD, a.q, a.ldq, b, a.T, qb2 * K_BM, h2 * HD);
+      load_tile<K_BM, K_THREADS, HD>(sdO + (buf ^ 1) * K_BM * 2 * HD, dout, ldd, b, a.T, qb2 * K_BM, h2 * HD);
     }
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    const uint32_t tQ = sQ + buf * K_BM * 256, tD = sdO + buf * K_BM * 256;
+    const uint32_t tQ = sQ + buf * K_BM * 2 * HD, tD = sdO + buf * K_BM * 2 * HD;
     const int q0 = qb * K_BM;
     float st[8][4], dpt[8][4];
 #pragma unroll
@@ -415,13 +431,13 @@ __global__ void __launch_bounds__(K_THREADS, 2)
 #pragma unroll
     for (int kk = 0; kk < HD / 16; ++kk) {
       uint32_t ak[4], av[4];
-      frag_a(ak, sK, r0, kk * 16);
-      frag_a(av, sV, r0, kk * 16);
+      frag_a<HD>(ak, sK, r0, kk * 16);
+      frag_a<HD>(av, sV, r0, kk * 16);
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
         uint32_t bq[4], bd[4];
-        frag_b_nk(bq, tQ, np * 16, kk * 16);
-        frag_b_nk(bd, tD, np * 16, kk * 16);
+        frag_b_nk<HD>(bq, tQ, np * 16, kk * 16);
+        frag_b_nk<HD>(bd, tD, np * 16, kk * 16);
         mma16816(st[2 * np], ak, bq[0], bq[1]);
         mma16816(st[2 * np + 1], ak, bq[2], bq[3]);
         mma16816(dpt[2 * np], av, bd[0], bd[1]);
@@ -453,8 +469,8 @@ __global__ void __launch_bounds__(K_THREADS, 2)
 #pragma unroll
       for (int nd = 0; nd < HD / 16; ++nd) {
         uint32_t bo[4], bq[4];
-        frag_b_kn(bo, tD, kk * 16, nd * 16);
-        frag_b_kn(bq, tQ, kk * 16, nd * 16);
+        frag_b_kn<HD>(bo, tD, kk * 16, nd * 16);
+        frag_b_kn<HD>(bq, tQ, kk * 16, nd * 16);
         mma16816(dva[2 * nd], ap, bo[0], bo[1]);
         mma16816(dva[2 * nd + 1], ap, bo[2], bo[3]);
         mma16816(dka[2 * nd], as, bq[0], bq[1]);
@@ -471,7 +487,7 @@ __global__ void __launch_bounds__(K_THREADS, 2)
     __nv_bfloat16* rk = dk + ((int64_t)b * a.T + kj) * lddk + kvh * HD;
     __nv_bfloat16* rv = dv + ((int64_t)b * a.T + kj) * lddv + kvh * HD;
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
+    for (int nt = 0; nt < HD / 8; ++nt) {
       *reinterpret_cast<uint32_t*>(rk + nt * 8 + 2 * tq) = pack_bf16(dka[nt][2 * ri] * sc, dka[nt][2 * ri + 1] * sc);
       *reinterpret_cast<uint32_t*>(rv + nt * 8 + 2 * tq) = pack_bf16(dva[nt][2 * ri], dva[nt][2 * ri + 1]);
     }
@@ -480,7 +496,7 @@ __global__ void __launch_bounds__(K_THREADS, 2)
 
 AttnArgs make_args(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, int64_t B, int64_t T,
                    int64_t H, int64_t KV, int64_t hd, int64_t window) {
-  TORCH_CHECK(hd == HD, "attention kernels are built for head_dim 128");
+  TORCH_CHECK(hd == 64 || hd == 128, "attention kernels are built for head_dim 64 and 128");
   TORCH_CHECK(H % KV == 0, "H must be a multiple of KV");
   TORCH_CHECK(q.stride(1) == 1 && k.stride(1) == 1 && v.stride(1) == 1, "q/k/v rows must be contiguous");
   TORCH_CHECK(q.stride(0) % 8 == 0 && k.stride(0) % 8 == 0 && v.stride(0) % 8 == 0, "row strides must be multiples of 8");
@@ -500,33 +516,64 @@ AttnArgs make_args(const torch::Tensor& q, const torch::Tensor& k, const torch::
   return a;
 }
 
-}  // namespace
-
-// q, k, v: [B*T, *] column slices (head h at h*hd); o: [B*T, H*hd]; lse: fp32 [B, H, T].
-void attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
-              torch::Tensor& lse, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd, int64_t window) {
-  AttnArgs a = make_args(q, k, v, B, T, H, KV, hd, window);
-  c10::cuda::CUDAGuard guard(q.device());
+template <int HD>
+void launch_fwd(const AttnArgs& a, torch::Tensor& o, torch::Tensor& lse) {
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, F_SMEM));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, f_smem(HD)));
     attr = true;
   }
-  dim3 grid((unsigned)((T + F_BM - 1) / F_BM), (unsigned)H, (unsigned)B);
-  attn_fwd_kernel<<<grid, F_THREADS, F_SMEM, at::cuda::getCurrentCUDAStream()>>>(
+  dim3 grid((unsigned)((a.T + F_BM - 1) / F_BM), (unsigned)a.H, (unsigned)a.B);
+  attn_fwd_kernel<HD><<<grid, F_THREADS, f_smem(HD), at::cuda::getCurrentCUDAStream()>>>(
       a, reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), o.stride(0), lse.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void attn_delta(const torch::Tensor& o, const torch::Tensor& dout, torch::Tensor& delta, int64_t B, int64_t T,
-                int64_t H) {
+template <int HD>
+void launch_delta(const torch::Tensor& o, const torch::Tensor& dout, torch::Tensor& delta, int64_t B, int64_t T,
+                  int64_t H, cudaStream_t st) {
   const int64_t tasks = B * T * H;
-  attn_delta_kernel<<<(unsigned)std::min<int64_t>((tasks + 7) / 8, 148 * 16), 256, 0,
-                      at::cuda::getCurrentCUDAStream()>>>(
+  attn_delta_kernel<HD><<<(unsigned)std::min<int64_t>((tasks + 7) / 8, 148 * 16), 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), o.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0), delta.data_ptr<float>(), (int)B, (int)T,
       (int)H);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <int HD>
+void launch_bwd(const AttnArgs& a, const torch::Tensor& o, const torch::Tensor& dout, const torch::Tensor& lse,
+                torch::Tensor& dq, torch::Tensor& dk, torch::Tensor& dv, torch::Tensor& delta) {
+  auto st = at::cuda::getCurrentCUDAStream();
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_dq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, q_smem(HD)));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_dkdv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, k_smem(HD)));
+    attr = true;
+  }
+  launch_delta<HD>(o, dout, delta, a.B, a.T, a.H, st);
+  attn_dq_kernel<HD><<<dim3((unsigned)((a.T + Q_BM - 1) / Q_BM), (unsigned)a.H, (unsigned)a.B), Q_THREADS, q_smem(HD),
+                       st>>>(a, reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
+                             lse.data_ptr<float>(), delta.data_ptr<float>(),
+                             reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), dq.stride(0));
+  attn_dkdv_kernel<HD><<<dim3((unsigned)((a.T + K_BN - 1) / K_BN), (unsigned)a.KV, (unsigned)a.B), K_THREADS,
+                         k_smem(HD), st>>>(a, reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
+                                           lse.data_ptr<float>(), delta.data_ptr<float>(),
+                                           reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), dk.stride(0),
+                                           reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()), dv.stride(0));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+// q, k, v: [B*T, *] column slices (head h at h*hd); o: [B*T, H*hd]; lse: fp32 [B, H, T]. hd: 64 or 128.
+void attn_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
+              torch::Tensor& lse, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd, int64_t window) {
+  AttnArgs a = make_args(q, k, v, B, T, H, KV, hd, window);
+  c10::cuda::CUDAGuard guard(q.device());
+  if (hd == 128)
+    launch_fwd<128>(a, o, lse);
+  else
+    launch_fwd<64>(a, o, lse);
 }
 
 // dq, dk, dv: column slices like q, k, v (may live in one fused [B*T, 3D] buffer).
@@ -537,26 +584,10 @@ void attn_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tenso
   (void)dq_acc;
   AttnArgs a = make_args(q, k, v, B, T, H, KV, hd, window);
   c10::cuda::CUDAGuard guard(q.device());
-  auto st = at::cuda::getCurrentCUDAStream();
-  static bool attr = false;
-  if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Q_SMEM));
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, K_SMEM));
-    attr = true;
-  }
-  const int64_t tasks = B * T * H;
-  attn_delta_kernel<<<(unsigned)std::min<int64_t>((tasks + 7) / 8, 148 * 16), 256, 0, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), o.stride(0),
-      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0), delta.data_ptr<float>(), (int)B, (int)T,
-      (int)H);
-  attn_dq_kernel<<<dim3((unsigned)((T + Q_BM - 1) / Q_BM), (unsigned)H, (unsigned)B), Q_THREADS, Q_SMEM, st>>>(
-      a, reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0), lse.data_ptr<float>(),
-      delta.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), dq.stride(0));
-  attn_dkdv_kernel<<<dim3((unsigned)((T + K_BN - 1) / K_BN), (unsigned)KV, (unsigned)B), K_THREADS, K_SMEM, st>>>(
-      a, reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0), lse.data_ptr<float>(),
-      delta.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), dk.stride(0),
-      reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()), dv.stride(0));
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (hd == 128)
+    launch_bwd<128>(a, o, dout, lse, dq, dk, dv, delta);
+  else
+    launch_bwd<64>(a, o, dout, lse, dq, dk, dv, delta);
 }
 
 }  // namespace br

@@ -408,9 +408,11 @@ __device__ __forceinline__ void store_wire8(void* base, int64_t i, const float (
   }
 }
 
+constexpr int kPushUnroll = 4;
+
 // grid-stride over the bucket's chunks: recv[owner][me * slot + slot_off + j] = wire(grad[off + j] * scale)
 template <int WIRE>
-__global__ void __launch_bounds__(128) pack_push_kernel(const float* __restrict__ grad, void* const* __restrict__ recv,
+__global__ void __launch_bounds__(256) pack_push_kernel(const float* __restrict__ grad, void* const* __restrict__ recv,
                                                         int me, int64_t slot_elems,
                                                         const PushChunk* __restrict__ chunks, int nchunks,
                                                         float scale, int* __restrict__ bad) {
@@ -421,14 +423,29 @@ __global__ void __launch_bounds__(128) pack_push_kernel(const float* __restrict_
     void* dst = recv[ch.owner];
     const int64_t base = (int64_t)me * slot_elems + ch.slot_off;
     const int64_t n8 = ch.len & ~int64_t(7);
-    for (int64_t j = threadIdx.x * 8; j < n8; j += (int64_t)blockDim.x * 8) {
-      const float4 a = *reinterpret_cast<const float4*>(src + j);
-      const float4 b = *reinterpret_cast<const float4*>(src + j + 4);
-      float x[8] = {a.x * scale, a.y * scale, a.z * scale, a.w * scale,
-                    b.x * scale, b.y * scale, b.z * scale, b.w * scale};
+    const int64_t step = (int64_t)blockDim.x * 8;
+    // kPushUnroll independent 32-byte loads per thread in flight (the kernel is latency-bound otherwise)
+    for (int64_t j0 = threadIdx.x * 8; j0 < n8; j0 += kPushUnroll * step) {
+      float4 a[kPushUnroll], b[kPushUnroll];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) nonfinite |= !isfinite(x[k]);
-      store_wire8<WIRE>(dst, base + j, x);
+      for (int u = 0; u < kPushUnroll; ++u) {
+        const int64_t j = j0 + u * step;
+        if (j < n8) {
+          a[u] = __ldcs(reinterpret_cast<const float4*>(src + j));
+          b[u] = __ldcs(reinterpret_cast<const float4*>(src + j + 4));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kPushUnroll; ++u) {
+        const int64_t j = j0 + u * step;
+        if (j < n8) {
+          float x[8] = {a[u].x * scale, a[u].y * scale, a[u].z * scale, a[u].w * scale,
+                        b[u].x * scale, b[u].y * scale, b[u].z * scale, b[u].w * scale};
+#pragma unroll
+          for (int k = 0; k < 8; ++k) nonfinite |= !isfinite(x[k]);
+          store_wire8<WIRE>(dst, base + j, x);
+        }
+      }
     }
     for (int64_t j = n8 + threadIdx.x; j < ch.len; j += blockDim.x) {
       const float x = src[j] * scale;
@@ -449,12 +466,12 @@ __global__ void signal_all_kernel(int64_t* const* flags, int npeers, int me, int
 }
 
 // Waits (thread 0, bounded) until every source's flag of `slot` in this rank's (local) flag array has
-// reached 2 * epoch; returns false on timeout.
+// reached 2 * epoch; returns false on timeout. The result reaches the block through __syncthreads_and, so
+// the kernel needs no shared memory and can share an SM with a kernel that fills it.
 __device__ bool wait_local_flags(const int64_t* flags, int npeers, int slot, int64_t epoch, uint64_t budget_ns,
                                  int* status) {
-  __shared__ int ok;
+  int ok = 1;
   if (threadIdx.x == 0) {
-    ok = 1;
     const uint64_t t0 = globaltimer_ns();
     const int64_t* f = flags + (int64_t)slot * npeers;
     for (int p = 0; p < npeers && ok; ++p) {
@@ -468,8 +485,7 @@ __device__ bool wait_local_flags(const int64_t* flags, int npeers, int slot, int
       }
     }
   }
-  __syncthreads();
-  return ok != 0;
+  return __syncthreads_and(ok) != 0;
 }
 
 // out[off + j] = scale * sum over sources (in rank order) of recv[src * slot + slot_off + j], for the chunks
@@ -481,20 +497,36 @@ __global__ void __launch_bounds__(256) reduce_local_kernel(const void* __restric
                                                            float* __restrict__ out, float scale, uint64_t budget_ns,
                                                            int* status) {
   if (!wait_local_flags(flags, npeers, slot, epoch, budget_ns, status)) return;
+  const int64_t step = (int64_t)blockDim.x * 8;
   for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
     const PushChunk ch = chunks[c];
     const int64_t n8 = ch.len & ~int64_t(7);
-    for (int64_t j = threadIdx.x * 8; j < n8; j += (int64_t)blockDim.x * 8) {
-      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int p = 0; p < npeers; ++p) {
-        float v[8];
-        load8<WIRE>(recv, (int64_t)p * slot_elems + ch.slot_off + j, v);
+    // kRedUnroll independent 16-byte loads per source in flight per thread
+    for (int64_t j0 = threadIdx.x * 8; j0 < n8; j0 += kRedUnroll * step) {
+      float acc[kRedUnroll][8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc[k] += v[k];
+      for (int u = 0; u < kRedUnroll; ++u)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[u][k] = 0.f;
+      for (int p = 0; p < npeers; ++p) {
+        float v[kRedUnroll][8];
+#pragma unroll
+        for (int u = 0; u < kRedUnroll; ++u)
+          if (j0 + u * step < n8) load8<WIRE>(recv, (int64_t)p * slot_elems + ch.slot_off + j0 + u * step, v[u]);
+#pragma unroll
+        for (int u = 0; u < kRedUnroll; ++u)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[u][k] += v[u][k];
       }
-      float4* o = reinterpret_cast<float4*>(out + ch.off + j);
-      o[0] = make_float4(acc[0] * scale, acc[1] * scale, acc[2] * scale, acc[3] * scale);
-      o[1] = make_float4(acc[4] * scale, acc[5] * scale, acc[6] * scale, acc[7] * scale);
+#pragma unroll
+      for (int u = 0; u < kRedUnroll; ++u) {
+        const int64_t j = j0 + u * step;
+        if (j < n8) {
+          float4* o = reinterpret_cast<float4*>(out + ch.off + j);
+          o[0] = make_float4(acc[u][0] * scale, acc[u][1] * scale, acc[u][2] * scale, acc[u][3] * scale);
+          o[1] = make_float4(acc[u][4] * scale, acc[u][5] * scale, acc[u][6] * scale, acc[u][7] * scale);
+        }
+      }
     }
     for (int64_t j = n8 + threadIdx.x; j < ch.len; j += blockDim.x) {
       float acc = 0.f;
@@ -802,13 +834,13 @@ void comm_pack_push(const torch::Tensor& grad, const torch::Tensor& recv_peers, 
   auto R = reinterpret_cast<void* const*>(recv_peers.data_ptr<int64_t>());
   auto C = reinterpret_cast<const PushChunk*>(chunks.data_ptr<int64_t>());
   if (wire == W_F32)
-    pack_push_kernel<W_F32><<<grid, 128, 0, st>>>(grad.data_ptr<float>(), R, (int)me, slot_elems, C, n, (float)scale,
+    pack_push_kernel<W_F32><<<grid, 256, 0, st>>>(grad.data_ptr<float>(), R, (int)me, slot_elems, C, n, (float)scale,
                                                  bad.data_ptr<int>());
   else if (wire == W_BF16)
-    pack_push_kernel<W_BF16><<<grid, 128, 0, st>>>(grad.data_ptr<float>(), R, (int)me, slot_elems, C, n, (float)scale,
+    pack_push_kernel<W_BF16><<<grid, 256, 0, st>>>(grad.data_ptr<float>(), R, (int)me, slot_elems, C, n, (float)scale,
                                                   bad.data_ptr<int>());
   else
-    pack_push_kernel<W_F16><<<grid, 128, 0, st>>>(grad.data_ptr<float>(), R, (int)me, slot_elems, C, n, (float)scale,
+    pack_push_kernel<W_F16><<<grid, 256, 0, st>>>(grad.data_ptr<float>(), R, (int)me, slot_elems, C, n, (float)scale,
                                                  bad.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -189,6 +189,96 @@ __global__ void __launch_bounds__(256) rope_bwd_kernel(__nv_bfloat16* __restrict
   }
 }
 
+// 64-wide heads: one warp per token, one head at a time. Lane l < 16 holds elements 2l, 2l+1 of the first
+// half of the head and lane l + 16 the same elements of the second half, so RoPE's partner values are one
+// shuffle away (xor 16); the cos/sin tables are [T, 32].
+__global__ void __launch_bounds__(256) rope64_fwd_kernel(__nv_bfloat16* __restrict__ qkv, RopeArgs a,
+                                                         const float* __restrict__ cosT, const float* __restrict__ sinT,
+                                                         float* __restrict__ rq, float* __restrict__ rk,
+                                                         const int* __restrict__ idx, const float* __restrict__ ve,
+                                                         const float* __restrict__ cur, const float* __restrict__ wg,
+                                                         float* __restrict__ gate, int D) {
+  const int lane = threadIdx.x & 31;
+  const bool first = lane < 16;
+  const int nqk = a.H + a.KV;
+  for (int m = blockIdx.x * kWarps + (threadIdx.x >> 5); m < a.M; m += gridDim.x * kWarps) {
+    __nv_bfloat16* row = qkv + (int64_t)m * a.ld;
+    const int t = m % a.T;
+    const float2 c = *reinterpret_cast<const float2*>(cosT + t * 32 + 2 * (lane & 15));
+    const float2 sn = *reinterpret_cast<const float2*>(sinT + t * 32 + 2 * (lane & 15));
+    for (int hs = 0; hs < nqk; ++hs) {
+      __nv_bfloat16* hp = row + hs * 64 + 2 * lane;
+      const float2 x = ldb2(hp);
+      const float2 q = make_float2(__shfl_xor_sync(0xffffffffu, x.x, 16), __shfl_xor_sync(0xffffffffu, x.y, 16));
+      // first half: y1 = x1 c + x2 s; second half: y2 = x2 c - x1 s
+      const float sg = first ? 1.f : -1.f;
+      const float ya = x.x * c.x + sg * q.x * sn.x, yb = x.y * c.y + sg * q.y * sn.y;
+      const float r = rsqrtf(warp_sum(ya * ya + yb * yb) / 64.f + kEps);
+      stb2(hp, ya * r, yb * r);
+      if (lane == 0) (hs < a.H ? rq[(int64_t)m * a.H + hs] : rk[(int64_t)m * a.KV + (hs - a.H)]) = r;
+    }
+    if (ve != nullptr && index_ok(idx[m], a.V, lane == 0 ? a.status : nullptr)) {
+      const float cz = cur[(int64_t)m * D + lane];
+      const float* e = ve + (int64_t)idx[m] * (a.KV * 64);
+      for (int h = 0; h < a.KV; ++h) {
+        const float z = warp_sum(cz * wg[lane * a.KV + h]);
+        const float g = 2.f / (1.f + __expf(-z));
+        __nv_bfloat16* pv = row + (nqk + h) * 64 + 2 * lane;
+        const float2 ev = *reinterpret_cast<const float2*>(e + h * 64 + 2 * lane);
+        const float2 v = ldb2(pv);
+        stb2(pv, v.x + ev.x * g, v.y + ev.y * g);
+        if (lane == 0) gate[(int64_t)m * a.KV + h] = g;
+      }
+    }
+  }
+}
+
+// Backward of rope64_fwd_kernel, in place on dqkv (qkv holds the forward's normalised outputs).
+__global__ void __launch_bounds__(256) rope64_bwd_kernel(__nv_bfloat16* __restrict__ dqkv,
+                                                         const __nv_bfloat16* __restrict__ qkv, RopeArgs a,
+                                                         const float* __restrict__ cosT, const float* __restrict__ sinT,
+                                                         const float* __restrict__ rq, const float* __restrict__ rk,
+                                                         const int* __restrict__ idx, const float* __restrict__ ve,
+                                                         const float* __restrict__ gate, float* __restrict__ dve,
+                                                         float* __restrict__ dz) {
+  const int lane = threadIdx.x & 31;
+  const bool first = lane < 16;
+  const int nqk = a.H + a.KV;
+  for (int m = blockIdx.x * kWarps + (threadIdx.x >> 5); m < a.M; m += gridDim.x * kWarps) {
+    const int64_t base = (int64_t)m * a.ld;
+    const int t = m % a.T;
+    const float2 c = *reinterpret_cast<const float2*>(cosT + t * 32 + 2 * (lane & 15));
+    const float2 sn = *reinterpret_cast<const float2*>(sinT + t * 32 + 2 * (lane & 15));
+    for (int hs = 0; hs < nqk; ++hs) {
+      const int64_t off = base + hs * 64 + 2 * lane;
+      const float r = hs < a.H ? rq[(int64_t)m * a.H + hs] : rk[(int64_t)m * a.KV + (hs - a.H)];
+      const float2 g = ldb2(dqkv + off), u = ldb2(qkv + off);
+      const float mean = warp_sum(g.x * u.x + g.y * u.y) / 64.f;
+      // gradient of the rotated (pre-norm) values, then the inverse rotation:
+      // dx1 = dy1 c - dy2 s (first half), dx2 = dy2 c + dy1 s (second half)
+      const float da = r * (g.x - u.x * mean), db = r * (g.y - u.y * mean);
+      const float pa = __shfl_xor_sync(0xffffffffu, da, 16), pb = __shfl_xor_sync(0xffffffffu, db, 16);
+      const float sg = first ? -1.f : 1.f;
+      stb2(dqkv + off, da * c.x + sg * pa * sn.x, db * c.y + sg * pb * sn.y);
+    }
+    if (ve != nullptr && !index_ok(idx[m], a.V, lane == 0 ? a.status : nullptr)) {
+      if (lane < a.KV) dz[(int64_t)m * a.KV + lane] = 0.f;  // the forward skipped this row's VE add
+    } else if (ve != nullptr) {
+      const int64_t erow = (int64_t)idx[m] * (a.KV * 64);
+      for (int h = 0; h < a.KV; ++h) {
+        const int64_t off = base + (nqk + h) * 64 + 2 * lane;
+        const float g = gate[(int64_t)m * a.KV + h];
+        const float2 e = *reinterpret_cast<const float2*>(ve + erow + h * 64 + 2 * lane);
+        const float2 d = ldb2(dqkv + off);
+        const float dg = warp_sum(d.x * e.x + d.y * e.y);
+        atomicAdd(dve + erow + h * 64 + 2 * lane, d.x * g);
+        atomicAdd(dve + erow + h * 64 + 2 * lane + 1, d.y * g);
+        if (lane == 0) dz[(int64_t)m * a.KV + h] = dg * g * (1.f - 0.5f * g);
+      }
+    }
+  }
+}
+
 // dWg[c,h] += sum_m cur[m,c] dz[m,h];  dgate_in[m,c] = sum_h dz[m,h] Wg[c,h]
 template <int KVMAX>
 __global__ void ve_gate_bwd_kernel(const float* __restrict__ cur, const float* __restrict__ dz,
@@ -241,7 +331,7 @@ void rope_fwd(torch::Tensor& qkv, int64_t T, int64_t H, int64_t KV, int64_t hd, 
               const torch::Tensor& sinT, torch::Tensor& rq, torch::Tensor& rk, const torch::Tensor& idx,
               c10::optional<torch::Tensor> ve, c10::optional<torch::Tensor> cur, c10::optional<torch::Tensor> wg,
               c10::optional<torch::Tensor> gate) {
-  TORCH_CHECK(hd == 128, "rope_fwd: head_dim 128");
+  TORCH_CHECK(hd == 128 || hd == 64, "rope_fwd: head_dim 64 or 128");
   TORCH_CHECK(qkv.stride(0) % 8 == 0, "rope_fwd: row stride must be a multiple of 8");
   const int64_t M = qkv.size(0);
   const bool has_ve = ve.has_value() && ve->defined();
@@ -249,7 +339,8 @@ void rope_fwd(torch::Tensor& qkv, int64_t T, int64_t H, int64_t KV, int64_t hd, 
              status_ptr(qkv.device().index())};
   c10::cuda::CUDAGuard g(qkv.device());
   TORCH_CHECK(H + KV <= 32, "rope_fwd: at most 32 q/k heads");
-  rope_fwd_kernel<<<grid_for(M), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
+  auto kern = hd == 128 ? rope_fwd_kernel : rope64_fwd_kernel;
+  kern<<<grid_for(M), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), a, cosT.data_ptr<float>(), sinT.data_ptr<float>(),
       rq.data_ptr<float>(), rk.data_ptr<float>(), idx.data_ptr<int>(), has_ve ? ve->data_ptr<float>() : nullptr,
       has_ve ? cur->data_ptr<float>() : nullptr, has_ve ? wg->data_ptr<float>() : nullptr,
@@ -267,8 +358,9 @@ void rope_bwd(torch::Tensor& dqkv, const torch::Tensor& qkv, int64_t T, int64_t 
   RopeArgs a{(int)M, (int)T, (int)H, (int)KV, (int)hd, (int)qkv.stride(0), has_ve ? (int)ve->size(0) : 0,
              status_ptr(qkv.device().index())};
   c10::cuda::CUDAGuard g(qkv.device());
-  TORCH_CHECK(hd == 128 && H + KV <= 32, "rope_bwd: head_dim 128, at most 32 q/k heads");
-  rope_bwd_kernel<<<grid_for(M), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
+  TORCH_CHECK((hd == 128 || hd == 64) && H + KV <= 32, "rope_bwd: head_dim 64 or 128, at most 32 q/k heads");
+  auto kern = hd == 128 ? rope_bwd_kernel : rope64_bwd_kernel;
+  kern<<<grid_for(M), 32 * kWarps, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), a,
       cosT.data_ptr<float>(), sinT.data_ptr<float>(), rq.data_ptr<float>(), rk.data_ptr<float>(), idx.data_ptr<int>(),
       has_ve ? ve->data_ptr<float>() : nullptr, has_ve ? gate->data_ptr<float>() : nullptr,

@@ -176,13 +176,16 @@ def test_worker_config_follows_welcome_and_engine_support():
     from bitresearch_b200.central.coordinator import model_config_message
     from bitresearch_b200.models.engine import FusedGPTEngine
     ref = preset("ref-default")
-    assert FusedGPTEngine.unsupported(ref.model) is not None  # 4 x 64 heads
+    assert FusedGPTEngine.unsupported(ref.model) is None  # 4 x 64 heads run on the engine too
     assert FusedGPTEngine.unsupported(preset("d512").model) is None
+    odd = preset("ref-default").model
+    odd.n_head, odd.n_kv_head = 8, 8  # 32-wide heads: eager path
+    assert FusedGPTEngine.unsupported(odd) is not None
     welcome = {"config": model_config_message(ref.model), "batchSize": 3}
     c = train_config_from_welcome(welcome, "cpu")
     assert (c.model.n_layer, c.model.n_embd, c.model.n_head, c.model.sequence_len) == (4, 256, 4, 512)
     assert c.device_batch == 3 and c.total_batch_tokens == 3 * 512 and c.impl == "torch" and c.dtype == "fp32"
-    assert train_config_from_welcome(welcome, "cuda:0").impl == "torch"  # eager path on the GPU for 64-wide heads
+    assert train_config_from_welcome(welcome, "cuda:0").impl == "cuda"  # the engine runs 64-wide heads
     d = preset("d512")
     assert train_config_from_welcome({"config": model_config_message(d.model), "batchSize": 2}, "cuda:0").impl == "cuda"
 

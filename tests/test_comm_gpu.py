@@ -371,6 +371,7 @@ def _train(rank, world):
                     grads = {n: v.detach().float().cpu().clone() for n, v in tr.grad_views.items()}
                 else:
                     grads = {n: tr.comm.red_views[n].detach().float().cpu().clone() for n in tr.comm.owned_names}
+        torch.cuda.synchronize()  # the last parameter exchange runs on the comm stream
         out[comm] = (losses, {n: p.detach().float().cpu() for n, p in tr.model.named().items()}, grads, init)
         tr.destroy()
     return out
@@ -453,6 +454,40 @@ def test_device_side_skip_keeps_replicas_2gpu():
     for n in res[0][4]:
         assert torch.equal(res[0][4][n], res[1][4][n]), n  # replicas identical after the next step
         assert torch.isfinite(res[0][4][n]).all(), n
+
+
+def _overlap_forward(rank, world):
+    """p2p trainer, 2 ranks: the forward queued right after a step (it waits per layer for the parameter
+    exchange still running on the comm stream) gives bitwise the same per-token losses as the same forward
+    run after a device synchronisation and a barrier."""
+    from bitresearch_b200.config import apply_overrides, preset
+    from bitresearch_b200.train import Trainer
+    cfg = apply_overrides(preset("d512"), ["model.n_layer=4", "model.sequence_len=256", "model.vocab_size=1024",
+                                           "device_batch=4", f"total_batch_tokens={4 * 256 * world}",
+                                           "log_every=0", "results_tsv=", "comm=p2p"])
+    tr = Trainer(cfg, device=torch.device("cuda", rank), log=lambda m: None)
+    tr.initialize()
+    g = torch.Generator(device="cpu").manual_seed(7 + rank)
+    x = torch.randint(0, 1024, (4, 256), generator=g, dtype=torch.int32).cuda()
+    y = torch.randint(0, 1024, (4, 256), generator=g, dtype=torch.int32).cuda()
+    out = []
+    for _ in range(2):
+        tr.train_step((x, y), sync=False)
+        early = tr.engine.per_token_nats(x, y)  # queued behind the exchange, layer by layer
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        late = tr.engine.per_token_nats(x, y)
+        torch.cuda.synchronize()
+        out.append((early.cpu(), late.cpu()))
+    tr.destroy()
+    return out
+
+
+def test_forward_overlapping_the_parameter_exchange_2gpu():
+    res = _run(_overlap_forward)
+    for r in range(2):
+        for early, late in res[r]:
+            assert torch.equal(early, late), (r, (early - late).abs().max().item())
 
 
 @pytest.mark.parametrize("masking", [False, True])

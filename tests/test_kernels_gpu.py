@@ -101,10 +101,11 @@ def _rope_ref(qkv, T, H, KV, hd, cos, sin, idx, ve, cur, wg):
     return torch.cat([q.reshape(M, -1), k.reshape(M, -1), v.reshape(M, -1)], 1), gate
 
 
-def test_rope_qknorm_ve(cuda):
+@pytest.mark.parametrize("hd", [128, 64])
+def test_rope_qknorm_ve(cuda, hd):
     E = _ext()
     torch.manual_seed(1)
-    B, T, H, KV, hd, V = 2, 64, 4, 2, 128, 50
+    B, T, H, KV, V = 2, 64, 4, 2, 50
     M = B * T
     D = H * hd
     qkv = torch.randn(M, (H + 2 * KV) * hd, device=cuda)
@@ -187,13 +188,16 @@ def _attn_ref(q, k, v, window):
     return torch.einsum("bhqk,bkhd->bqhd", p, v), torch.logsumexp(s, -1)
 
 
-@pytest.mark.parametrize("B,T,H,KV,window", [(2, 256, 4, 4, 256), (1, 300, 4, 2, 100), (2, 512, 2, 2, 128),
-                                             (1, 193, 2, 1, 1000), (2, 1024, 2, 1, 300), (1, 2048, 2, 2, 1024),
-                                             (1, 640, 4, 2, 200), (2, 384, 2, 2, 384)])
-def test_attention_fwd_bwd(cuda, B, T, H, KV, window):
+@pytest.mark.parametrize("B,T,H,KV,window,hd", [(2, 256, 4, 4, 256, 128), (1, 300, 4, 2, 100, 128),
+                                                (2, 512, 2, 2, 128, 128), (1, 193, 2, 1, 1000, 128),
+                                                (2, 1024, 2, 1, 300, 128), (1, 2048, 2, 2, 1024, 128),
+                                                (1, 640, 4, 2, 200, 128), (2, 384, 2, 2, 384, 128),
+                                                (2, 512, 4, 4, 256, 64), (1, 300, 4, 2, 100, 64),
+                                                (1, 193, 2, 1, 1000, 64)])
+def test_attention_fwd_bwd(cuda, B, T, H, KV, window, hd):
     E = _ext()
     torch.manual_seed(3)
-    hd = 128
+    tc = T % 128 == 0 and hd == 128  # the tcgen05 kernels: 128-wide heads, whole 128-row tiles
     D, Dkv = H * hd, KV * hd
     M = B * T
     qkv = (torch.randn(M, D + 2 * Dkv, device=cuda)).to(torch.bfloat16)
@@ -201,7 +205,7 @@ def test_attention_fwd_bwd(cuda, B, T, H, KV, window):
     o = torch.empty(M, D, device=cuda, dtype=torch.bfloat16)
     lse = torch.empty(B, H, T, device=cuda)
     E.attn_fwd(q, k, v, o, lse, B, T, H, KV, hd, window)
-    if T % 128 == 0:
+    if tc:
         o_tc = torch.empty_like(o)
         lse_tc = torch.empty_like(lse)
         E.attn_fwd_tc(qkv, o_tc, lse_tc, B, T, H, KV, hd, window)
@@ -214,7 +218,7 @@ def test_attention_fwd_bwd(cuda, B, T, H, KV, window):
     ref, lse_ref = _attn_ref(qr, kr, vr, min(window, T))
     _assert(o, ref.reshape(M, D), 2e-2)
     _assert(lse, lse_ref, 1e-3)
-    if T % 128 == 0:
+    if tc:
         _assert(o_tc, ref.reshape(M, D), 2e-2)
         _assert(lse_tc * math.log(2.0), lse_ref, 1e-3)  # the tcgen05 kernel reports lse in log2 units
     do = torch.randn(M, D, device=cuda).to(torch.bfloat16)
@@ -226,7 +230,7 @@ def test_attention_fwd_bwd(cuda, B, T, H, KV, window):
     _assert(dqkv[:, :D], qr.grad.reshape(M, D), 3e-2)
     _assert(dqkv[:, D:D + Dkv], kr.grad.reshape(M, Dkv), 3e-2)
     _assert(dqkv[:, D + Dkv:], vr.grad.reshape(M, Dkv), 3e-2)
-    if T % 128 == 0:
+    if tc:
         dqkv_tc = torch.empty_like(qkv)
         delta_tc = torch.empty(B, H, T, device=cuda)
         E.attn_bwd_tc(qkv, o_tc, do, lse_tc, dqkv_tc, delta_tc, B, T, H, KV, hd, window)
