@@ -6,6 +6,7 @@
 Arms:
   ours       the sm_100a engine (tcgen05 GEMMs, fused kernels, flash attention, fused optimizer)
   ddp        plain PyTorch DistributedDataParallel + cuBLAS + SDPA of the same model and optimizer
+  ddp-compile  the same under torch.compile, with flex attention (fused sliding window) on every layer
   reference  the upstream project (a TypeScript/TF.js browser trainer; it has no Python package)
 
 Measurement: W untimed warm-up steps, then K timed full training steps (forward, backward, gradient
@@ -116,7 +117,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "ddp", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "ddp", "ddp-compile", "reference"])
     ap.add_argument("--preset", default="d512")
     ap.add_argument("--device-batch", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
@@ -173,7 +174,7 @@ def main():
     else:
         from baseline.ddp_baseline import DDPBaseline
         cfg.impl = "torch"
-        tr = DDPBaseline(cfg, device)
+        tr = DDPBaseline(cfg, device, compile=args.impl == "ddp-compile")
         accum, B = tr.grad_accum, tr.device_batch
         batches = _resident_batches(cfg, rank, world, B, T, accum, device, torch.int64)
         it = [0]

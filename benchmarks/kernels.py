@@ -182,6 +182,33 @@ def main():
             report(f"qkv+rope{tag}: gemm then rope_fwd", ms_sep, flops=2.0 * M * D * 3 * D)
             report(f"qkv+rope{tag}: fused epilogue", ms_fused, flops=2.0 * M * D * 3 * D)
 
+    # ------------------------------------------------------------------ lm_head + softcap + CE
+    if want("head"):
+        # the fused form (the logits never reach memory) against the two-pass form it replaced
+        # (softcapped bf16 logits written by the GEMM, read and overwritten by softcap_ce)
+        xf = torch.randn(M, D, **bf)
+        w = (torch.randn(V, D, device=dev) * 0.05)
+        wb = w.to(torch.bfloat16)
+        tgt = torch.randint(0, V, (M,), device=dev, dtype=torch.int32)
+        G = torch.empty(M, V, **bf)
+        part = torch.empty((V + 255) // 256, M, device=dev)
+        zt, rs, cf = (torch.empty(M, device=dev) for _ in range(3))
+        nats = torch.empty(M, device=dev)
+        ls = torch.zeros(1, device=dev)
+        xs = torch.empty(M, D, **bf)
+        dw = torch.zeros(V, D, device=dev)
+        f_head = 2.0 * M * D * V
+        ms = timeit(lambda: E.gemm_softcap_ce(xf, wb, G, tgt, part, zt, 15.0, True))
+        report(f"head: gemm_softcap_ce {M}x{D}x{V}", ms, flops=f_head)
+        ms_fin = timeit(lambda: E.ce_finalize(part, zt, tgt, V, 15.0, 1.0 / M, nats=nats, loss_sum=ls, rowscale=rs,
+                                              coef=cf, x=xf, xs=xs, dw=dw))
+        report("head: ce_finalize", ms_fin, nbytes=M * (4 * (V // 256) + 2 * D * 2))
+        ms_old = timeit(lambda: (gemm.matmul(xf, wb.t(), out=G, epi=gemm.SOFTCAP, alpha=1 / 15, beta=15.0),
+                                 E.softcap_ce(G, tgt, 15.0, 1.0 / M, nats, ls, True)))
+        report("head: two-pass (softcap GEMM + softcap_ce)", ms_old, flops=f_head)
+        ms_eval = timeit(lambda: E.gemm_softcap_ce(xf, wb, G, tgt, part, zt, 15.0, False))
+        report("head: gemm_softcap_ce, statistics only (eval)", ms_eval, flops=f_head)
+
     # ------------------------------------------------------------------ row kernels
     if want("rows"):
         x = torch.randn(M, D, device=dev)

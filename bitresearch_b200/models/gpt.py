@@ -60,6 +60,7 @@ class GPT(nn.Module):
             self.params[name] = nn.Parameter(torch.empty(shape, dtype=torch.float32, device=device))
         self.init_weights(init, seed)
         self.compute_dtype: torch.dtype | None = None  # matmul operand dtype of the eager path
+        self.attn_impl = "sdpa"  # eager attention: "sdpa" or "flex" (fused sliding window, under torch.compile)
         cos, sin = _rope(cfg.sequence_len, cfg.head_dim, device)
         self.register_buffer("rope_cos", cos, persistent=False)
         self.register_buffer("rope_sin", sin, persistent=False)
@@ -150,7 +151,7 @@ class GPT(nn.Module):
                 v = v + P[f"ve_{i}"][idx].view(B, T, KV, hd) * gate
             q = _rms(_rotary(q, cos, sin))
             k = _rms(_rotary(k, cos, sin))
-            o = _attention(q, k, v, effective_window(self.window_sizes[i][0], T), cd)
+            o = _attention(q, k, v, effective_window(self.window_sizes[i][0], T), cd, self.attn_impl)
             cur = cur + mm(o.reshape(B * T, D), P[f"layer{i}_proj"]).view(B, T, D)
             h = F.relu(mm(_rms(cur).reshape(B * T, D), P[f"layer{i}_fc"])).square()
             cur = cur + mm(h, P[f"layer{i}_mlp_proj"]).view(B, T, D)
@@ -190,10 +191,32 @@ def _rotary(x, cos, sin):
     return torch.cat([x1 * c + x2 * s, x2 * c - x1 * s], dim=-1)
 
 
-def _attention(q, k, v, window: int, cd):
-    """q,k,v [B,T,H|KV,hd]; causal with a ``window``-key band (keys i-window+1..i)."""
+_FLEX_MASKS: dict = {}
+
+
+def _flex_attention(q, k, v, window: int):
+    """Sliding-window causal attention through PyTorch's flex attention (a fused kernel that skips blocks
+    outside the band), for the baselines; q, k, v [B, H, T, hd]."""
+    from torch.nn.attention.flex_attention import create_block_mask, flex_attention
+    T = q.shape[2]
+    key = (T, window, q.device)
+    if key not in _FLEX_MASKS:
+        def band(b, h, qi, kj):
+            return (kj <= qi) & (kj > qi - window)
+        _FLEX_MASKS[key] = create_block_mask(band, B=None, H=None, Q_LEN=T, KV_LEN=T, device=q.device)
+    return flex_attention(q, k, v, block_mask=_FLEX_MASKS[key], enable_gqa=k.shape[1] != q.shape[1])
+
+
+def _attention(q, k, v, window: int, cd, impl: str = "sdpa"):
+    """q,k,v [B,T,H|KV,hd]; causal with a ``window``-key band (keys i-window+1..i). ``impl='flex'`` runs
+    flex attention (meant to be used under ``torch.compile``) instead of SDPA with a boolean band mask."""
     B, T, H, hd = q.shape
     KV = k.shape[2]
+    if impl == "flex":
+        q, k, v = (t.transpose(1, 2) for t in (q, k, v))
+        if cd is not None:
+            q, k, v = q.to(cd), k.to(cd), v.to(cd)
+        return _flex_attention(q, k, v, window).float().transpose(1, 2)
     if KV != H:
         k = k.repeat_interleave(H // KV, dim=2)
         v = v.repeat_interleave(H // KV, dim=2)
