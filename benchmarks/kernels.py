@@ -1,6 +1,6 @@
 """Per-kernel timings at the d512 depth-8 production shapes, against library baselines.
 
-  python benchmarks/kernels.py [--tokens 262144] [--json out.json]
+  python benchmarks/kernels.py [--tokens 262144] [--json out.json] [--only tags] [--pair on|off]
 
 Each kernel is timed with CUDA events on the launching stream after warm-up (median of R repeats);
 inputs of the large shapes exceed the 126 MB L2. FLOP/s and bytes/s are reported as fractions of the
@@ -53,10 +53,13 @@ def main():
     ap.add_argument("--tokens", type=int, default=262144)
     ap.add_argument("--json", default="")
     ap.add_argument("--only", default="")
+    ap.add_argument("--pair", default="on", choices=["on", "off"],
+                    help="256-column GEMM tiles on CTA pairs (cta_group::2) or on single CTAs")
     args = ap.parse_args()
     from bitresearch_b200.ops import gemm
     from bitresearch_b200.ops._ext import check_status, ext
     E = ext()
+    E.gemm_set_pair(args.pair == "on")
     dev = torch.device("cuda", 0)
     FLOPS, BW, src = peaks()
     M, D, F4, V, T, H = args.tokens, 512, 2048, 8192, 2048, 4

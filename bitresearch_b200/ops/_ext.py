@@ -15,7 +15,8 @@ _EXT = None
 _ERR: Exception | None = None
 # kernels launched by one call of a multi-kernel entry point
 _KERNELS_PER_CALL = {"attn_bwd": 3, "attn_bwd_tc": 2, "muon_prepare": 2, "muon_finish": 2, "read_status": 0,
-                     "reset_status": 0, "muon_prepare_scratch": 0, "muon_finish_scratch": 0}
+                     "reset_status": 0, "muon_prepare_scratch": 0, "muon_finish_scratch": 0, "gemm_set_pair": 0,
+                     "gemm_pair": 0, "status_snapshot": 0}
 _COUNTS: dict[str, int] = {}
 
 

@@ -13,6 +13,8 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
                  int64_t ldb, int64_t bsb, torch::Tensor& c, int64_t ldc, int64_t bsc, int64_t M, int64_t N,
                  int64_t K, int64_t batch, int64_t epi, c10::optional<torch::Tensor> aux, int64_t ld_aux,
                  int64_t bs_aux, double alpha, double beta, int64_t k_splits, int64_t block_n);
+void gemm_set_pair(bool on);
+bool gemm_pair();
 void embed_rms_fwd(const torch::Tensor& idx, const torch::Tensor& wte, torch::Tensor& x0, torch::Tensor& rstd);
 void ladder_rms_fwd(const torch::Tensor& x, const torch::Tensor& x0, const torch::Tensor& lam_r,
                     const torch::Tensor& lam_0, int64_t layer, torch::Tensor& cur, torch::Tensor& xn,
@@ -115,6 +117,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("reset_status", &br::reset_status);
   m.def("gemm", &br::gemm_launch);
   m.def("gemm_qkv_rope", &br::gemm_qkv_rope);
+  m.def("gemm_set_pair", &br::gemm_set_pair);
+  m.def("gemm_pair", &br::gemm_pair);
   m.def("embed_rms_fwd", &br::embed_rms_fwd);
   m.def("ladder_rms_fwd", &br::ladder_rms_fwd);
   m.def("rms_fwd", &br::rms_fwd);

@@ -99,12 +99,15 @@ constexpr uint64_t kWaitBudgetNs = 2000000000ull;
 // epilogue warp, issued up to three chunks (across tile boundaries) ahead of the chunk being
 // processed, so the DRAM latency of the aux tile overlaps the epilogue math; the main loop gives up
 // one stage to make room.
-template <int BN, bool AUX>
+// CG = 2: a CTA pair runs one 256-row tile (cta_group::2); each CTA loads its 128 rows of A and half of
+// B's BN columns, so a stage is 32 KB instead of 48 and the pair reads a third less operand data per
+// output than two single CTAs.
+template <int BN, bool AUX, int CG = 1>
 struct GemmCfg {
-  static constexpr int STAGES = AUX ? (BN == 256 ? 3 : 5) : (BN == 256 ? 4 : 6);
+  static constexpr int STAGES = CG == 2 ? (AUX ? 5 : 6) : (AUX ? (BN == 256 ? 3 : 5) : (BN == 256 ? 4 : 6));
   static constexpr int NBUF = AUX ? 4 : 2;  // staging buffers per epilogue warp
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = (BN / CG) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int EPI_BYTES = 4 * NBUF * CHUNK_BYTES;
@@ -175,12 +178,13 @@ __device__ __forceinline__ float epi_op(float acc, float aux, const GemmParams& 
   return v;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool AUX>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool AUX, int CG>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, GemmParams p) {
   static_assert(!AUX || epi_reads_aux(EPI), "aux ring for an epilogue without aux");
-  using Cfg = GemmCfg<BN, AUX>;
+  static_assert(CG == 1 || (CG == 2 && BN == 256), "CTA pairs run 256-column tiles");
+  using Cfg = GemmCfg<BN, AUX, CG>;
   constexpr int NBUF = Cfg::NBUF;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -200,8 +204,17 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = warp_id();
   const int total = p.m_tiles * p.n_tiles * p.batch * p.k_splits;
+  // CTA pairs: the pair shares one work unit (m counts 256-row tiles); rank 0 leads (issues the MMAs)
+  const uint32_t crank = CG == 2 ? cluster_rank() : 0u;
+  const bool lead = crank == 0;
+  const int unit0 = CG == 2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ustride = CG == 2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  auto row_base = [&](int m) { return (CG == 2 ? 2 * m + (int)crank : m) * BM; };
 
-  if (device_failed(p.status)) return;
+  // an early return is for single CTAs only: a pair must reach its cluster barriers together
+  if constexpr (CG == 1) {
+    if (device_failed(p.status)) return;
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -209,16 +222,24 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], 128 * CG);  // every epilogue thread of the pair releases the leader's
     }
     mbar_init(drain_bar, 1);
     for (int w = 0; w < 4 * NBUF; ++w) mbar_init(&aux_bar[w], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (CG == 2)
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    else
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2)
+    cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA arrive or load
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -235,30 +256,39 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+      // a pair's loads of one stage all count on the leader's full barrier, which expects both halves
+      auto load = [&](const CUtensorMap* m, void* dst, int c0, int c1, int c2) {
+        if constexpr (CG == 2)
+          tma_load_3d_pair(m, &full_bar[stage], dst, c0, c1, c2);
+        else
+          tma_load_3d(m, &full_bar[stage], dst, c0, c1, c2);
+      };
+      constexpr int BNC = BN / CG;  // B columns this CTA loads
+      for (int u = unit0; u < total && ok; u += ustride) {
         int m, n, b, kb0, kb1;
         decode_unit(p, u, m, n, b, kb0, kb1);
+        const int arow = row_base(m);
+        const int bcol = n * BN + (int)crank * BNC;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, kWaitBudgetNs, abort_flag, p.status)) {
             fail(kErrTimeoutProducer);
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          if (CG == 1 || lead) mbar_arrive_expect_tx(&full_bar[stage], CG * Cfg::STAGE_BYTES);
           uint8_t* a_dst = sA + stage * Cfg::A_BYTES;
           uint8_t* b_dst = sB + stage * Cfg::B_BYTES;
           if constexpr (!A_MN) {
-            tma_load_3d(&tmA, &full_bar[stage], a_dst, kb * BK, m * BM, b);
+            load(&tmA, a_dst, kb * BK, arow, b);
           } else {
-            tma_load_3d(&tmA, &full_bar[stage], a_dst, m * BM, kb * BK, b);
-            tma_load_3d(&tmA, &full_bar[stage], a_dst + 8192, m * BM + 64, kb * BK, b);
+            load(&tmA, a_dst, arow, kb * BK, b);
+            load(&tmA, a_dst + 8192, arow + 64, kb * BK, b);
           }
           if constexpr (!B_MN) {
-            tma_load_3d(&tmB, &full_bar[stage], b_dst, kb * BK, n * BN, b);
+            load(&tmB, b_dst, kb * BK, bcol, b);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_3d(&tmB, &full_bar[stage], b_dst + j * 8192, n * BN + j * 64, kb * BK, b);
+            for (int j = 0; j < BNC / 64; ++j) load(&tmB, b_dst + j * 8192, bcol + j * 64, kb * BK, b);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -267,7 +297,9 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      if (!ok || *abort_flag) {
+      // on an early exit, let the issued loads land (a pair's follower cannot see its loads complete: they
+      // count on the leader's barrier, whose drain covers them before the final cluster barrier)
+      if ((!ok || *abort_flag) && (CG == 1 || lead)) {
         int n_inflight = issued < STAGES ? issued : STAGES;
         int s = stage;
         uint32_t ph = phase;
@@ -281,13 +313,25 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else if (warp == 1) {
-    if (elect_one()) {
-      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+    if (elect_one() && (CG == 1 || lead)) {  // a pair's follower issues no MMA
+      constexpr uint32_t idesc = umma_idesc_bf16(CG * BM, BN, A_MN, B_MN);
+      auto mma = [&](uint32_t d, uint64_t ad, uint64_t bd, uint32_t acc) {
+        if constexpr (CG == 2)
+          umma_bf16_ss_pair(d, ad, bd, idesc, acc);
+        else
+          umma_bf16_ss(d, ad, bd, idesc, acc);
+      };
+      auto commit = [&](uint64_t* bar) {
+        if constexpr (CG == 2)
+          umma_commit_pair(bar);  // the same barrier in both CTAs
+        else
+          umma_commit(bar);
+      };
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++local) {
+      for (int u = unit0; u < total && ok; u += ustride, ++local) {
         int m, n, b, kb0, kb1;
         decode_unit(p, u, m, n, b, kb0, kb1);
         const int acc = local & 1;
@@ -313,17 +357,17 @@ __global__ void __launch_bounds__(192, 1)
                                      : umma_desc_sw128(a_base + k * 32, 16, 1024);
             const uint64_t bd = B_MN ? umma_desc_sw128(b_base + k * 2048, 8192, 1024)
                                      : umma_desc_sw128(b_base + k * 32, 16, 1024);
-            umma_bf16_ss(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            mma(d_tmem, ad, bd, (kb > kb0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&empty_bar[stage]);
+          commit(&empty_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
-        if (ok) umma_commit(&tfull_bar[acc]);
+        if (ok) commit(&tfull_bar[acc]);
       }
-      umma_commit(drain_bar);
+      commit(drain_bar);
       mbar_wait(drain_bar, 0, 100000000ull, nullptr);
     }
   } else {
@@ -337,7 +381,7 @@ __global__ void __launch_bounds__(192, 1)
     constexpr int CPT = BN / COLS;                 // chunks per tile
     int nchunk = 0;                                // chunks this warp has processed (ring position)
     // aux prefetch cursor (AUX only): next chunk to load, its work unit and chunk within the tile
-    int pchunk = 0, pu = blockIdx.x, pc = 0;
+    int pchunk = 0, pu = unit0, pc = 0;
     auto prefetch = [&](int upto) {
       while (pchunk < upto && pu < total) {
         if (pchunk >= NBUF) {
@@ -351,12 +395,12 @@ __global__ void __launch_bounds__(192, 1)
           decode_unit(p, pu, m, n, b, kb0, kb1);
           const int slot = pchunk % NBUF;
           mbar_arrive_expect_tx(&xbar[slot], CHUNK_BYTES);
-          tma_load_3d(&tmX, &xbar[slot], ebuf + slot * CHUNK_BYTES, n * BN + pc * COLS, m * BM + wq * 32, b);
+          tma_load_3d(&tmX, &xbar[slot], ebuf + slot * CHUNK_BYTES, n * BN + pc * COLS, row_base(m) + wq * 32, b);
         }
         ++pchunk;
         if (++pc == CPT) {
           pc = 0;
-          pu += gridDim.x;
+          pu += ustride;
         }
       }
     };
@@ -366,7 +410,18 @@ __global__ void __launch_bounds__(192, 1)
       if constexpr (AUX) tma_prefetch_desc(&tmX);
     }
     bool ok = true;
-    for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++local) {
+    // hands the accumulator back to the MMA warp (in a pair: on the leader's barrier)
+    auto release_acc = [&](int acc) {
+      if constexpr (CG == 2) {
+        if (lead)
+          mbar_arrive(&tempty_bar[acc]);
+        else
+          mbar_arrive_cluster(cluster_map(&tempty_bar[acc], 0));
+      } else {
+        mbar_arrive(&tempty_bar[acc]);
+      }
+    };
+    for (int u = unit0; u < total && ok; u += ustride, ++local) {
       int m, n, b, kb0, kb1;
       decode_unit(p, u, m, n, b, kb0, kb1);
       const int acc = local & 1;
@@ -378,7 +433,7 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      const int row0 = m * BM + wq * 32;
+      const int row0 = row_base(m) + wq * 32;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * BN;
       if constexpr (EPI == EPI_QKV_ROPE) {
         // two heads per tile; thread = row. Each head: 128 accumulator columns -> RoPE + QK-norm
@@ -397,7 +452,7 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld_wait();
           if (hh == 1) {  // accumulator fully read: hand it back to the MMA warp
             tc_fence_before();
-            mbar_arrive(&tempty_bar[acc]);
+            release_acc(acc);
           }
           float x[128];
 #pragma unroll
@@ -553,7 +608,7 @@ __global__ void __launch_bounds__(192, 1)
         if (c == CPT - 1) {
           // accumulator fully read: hand it back to the MMA warp
           tc_fence_before();
-          mbar_arrive(&tempty_bar[acc]);
+          release_acc(acc);
         }
         if (leader && (EPI != EPI_SOFTCAP_CE || p.ce.store)) {
           if constexpr (EPI == EPI_ATOMIC_F32)
@@ -579,10 +634,16 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2)
+    cluster_sync_all();  // the leader's MMAs and both CTAs' epilogues are done with TMEM and shared memory
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (CG == 2)
+      tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
@@ -603,37 +664,81 @@ struct Maps {
   CUtensorMap a, b, c, x;
 };
 
-template <int BN, bool AMN, bool BMN, int EPI, bool AUX>
-void launch_t(const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
-  auto k = gemm_kernel<BN, AMN, BMN, EPI, AUX>;
-  using Cfg = GemmCfg<BN, AUX>;
+// 256-column GEMMs with more than one 128-row tile run as CTA pairs unless switched off
+// (gemm_set_pair, for A/B measurements).
+bool g_pair = true;
+
+int pair_mode(int BN, int64_t M) { return g_pair && BN == 256 && M > BM ? 2 : 1; }
+
+// Persistent grid: one CTA (or one CTA pair) per SM (pair), no more than there are work units.
+int persistent_grid(int64_t units, int cg) {
+  const int slots = num_sms() / cg;
+  return cg * (int)std::min<int64_t>(units, slots);
+}
+
+template <int BN, bool AMN, bool BMN, int EPI, bool AUX, int CG>
+void launch_cg(const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
+  auto k = gemm_kernel<BN, AMN, BMN, EPI, AUX, CG>;
+  using Cfg = GemmCfg<BN, AUX, CG>;
   static bool attr = false;
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     attr = true;
   }
-  k<<<grid, 192, Cfg::SMEM, st>>>(mp.a, mp.b, mp.c, mp.x, p);
+  if constexpr (CG == 1) {
+    k<<<grid, 192, Cfg::SMEM, st>>>(mp.a, mp.b, mp.c, mp.x, p);
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    // a persistent pair grid no larger than the pairs that can be resident at once (SM pairs of a GPC)
+    static int max_pairs = 0;
+    if (!max_pairs) {
+      cfg.gridDim = dim3((unsigned)grid);
+      C10_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&max_pairs, k, &cfg));
+      if (max_pairs < 1) max_pairs = 1;
+    }
+    cfg.gridDim = dim3((unsigned)std::min(grid, 2 * max_pairs));
+    C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, mp.a, mp.b, mp.c, mp.x, p));
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+template <int BN, bool AMN, bool BMN, int EPI, bool AUX>
+void launch_t(const Maps& mp, const GemmParams& p, int grid, cudaStream_t st, int cg) {
+  if constexpr (BN == 256) {
+    if (cg == 2) return launch_cg<BN, AMN, BMN, EPI, AUX, 2>(mp, p, grid, st);
+  }
+  TORCH_CHECK(cg == 1, "gemm: CTA pairs need 256-column tiles");
+  launch_cg<BN, AMN, BMN, EPI, AUX, 1>(mp, p, grid, st);
+}
+
 template <int BN, bool AMN, bool BMN>
-void dispatch_epi(int epi, const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
+void dispatch_epi(int epi, const Maps& mp, const GemmParams& p, int grid, cudaStream_t st, int cg) {
   const bool aux = p.has_aux != 0;
   switch (epi) {
     case EPI_BF16:
-      return aux ? launch_t<BN, AMN, BMN, EPI_BF16, true>(mp, p, grid, st)
-                 : launch_t<BN, AMN, BMN, EPI_BF16, false>(mp, p, grid, st);
+      return aux ? launch_t<BN, AMN, BMN, EPI_BF16, true>(mp, p, grid, st, cg)
+                 : launch_t<BN, AMN, BMN, EPI_BF16, false>(mp, p, grid, st, cg);
     case EPI_F32:
-      return aux ? launch_t<BN, AMN, BMN, EPI_F32, true>(mp, p, grid, st)
-                 : launch_t<BN, AMN, BMN, EPI_F32, false>(mp, p, grid, st);
-    case EPI_ATOMIC_F32: return launch_t<BN, AMN, BMN, EPI_ATOMIC_F32, false>(mp, p, grid, st);
+      return aux ? launch_t<BN, AMN, BMN, EPI_F32, true>(mp, p, grid, st, cg)
+                 : launch_t<BN, AMN, BMN, EPI_F32, false>(mp, p, grid, st, cg);
+    case EPI_ATOMIC_F32: return launch_t<BN, AMN, BMN, EPI_ATOMIC_F32, false>(mp, p, grid, st, cg);
     default: break;
   }
   if constexpr (BN == 256) {
     switch (epi) {
-      case EPI_RELU2: return launch_t<BN, AMN, BMN, EPI_RELU2, false>(mp, p, grid, st);
-      case EPI_RELU2_BWD: return launch_t<BN, AMN, BMN, EPI_RELU2_BWD, true>(mp, p, grid, st);
-      case EPI_SOFTCAP: return launch_t<BN, AMN, BMN, EPI_SOFTCAP, false>(mp, p, grid, st);
+      case EPI_RELU2: return launch_t<BN, AMN, BMN, EPI_RELU2, false>(mp, p, grid, st, cg);
+      case EPI_RELU2_BWD: return launch_t<BN, AMN, BMN, EPI_RELU2_BWD, true>(mp, p, grid, st, cg);
+      case EPI_SOFTCAP: return launch_t<BN, AMN, BMN, EPI_SOFTCAP, false>(mp, p, grid, st, cg);
       default: break;
     }
   }
@@ -641,11 +746,12 @@ void dispatch_epi(int epi, const Maps& mp, const GemmParams& p, int grid, cudaSt
 }
 
 template <int BN>
-void dispatch_major(bool amn, bool bmn, int epi, const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
-  if (!amn && !bmn) return dispatch_epi<BN, false, false>(epi, mp, p, grid, st);
-  if (!amn && bmn) return dispatch_epi<BN, false, true>(epi, mp, p, grid, st);
-  if (amn && !bmn) return dispatch_epi<BN, true, false>(epi, mp, p, grid, st);
-  return dispatch_epi<BN, true, true>(epi, mp, p, grid, st);
+void dispatch_major(bool amn, bool bmn, int epi, const Maps& mp, const GemmParams& p, int grid, cudaStream_t st,
+                    int cg) {
+  if (!amn && !bmn) return dispatch_epi<BN, false, false>(epi, mp, p, grid, st, cg);
+  if (!amn && bmn) return dispatch_epi<BN, false, true>(epi, mp, p, grid, st, cg);
+  if (amn && !bmn) return dispatch_epi<BN, true, false>(epi, mp, p, grid, st, cg);
+  return dispatch_epi<BN, true, true>(epi, mp, p, grid, st, cg);
 }
 
 CUtensorMap bf16_map(const void* base, int64_t inner, int64_t outer, int64_t batch, int64_t ld, int64_t bs, int box_outer) {
@@ -679,14 +785,16 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
   TORCH_CHECK(BN == 128 || BN == 256, "block_n must be 128 or 256");
   Maps mp;
   mp.a = a_mn ? bf16_map(a.data_ptr(), M, K, batch, lda, bsa, 64) : bf16_map(a.data_ptr(), K, M, batch, lda, bsa, BM);
-  mp.b = b_mn ? bf16_map(b.data_ptr(), N, K, batch, ldb, bsb, 64) : bf16_map(b.data_ptr(), K, N, batch, ldb, bsb, BN);
+  const int cg = pair_mode(BN, M);  // a CTA pair loads half of B's tile columns each
+  mp.b = b_mn ? bf16_map(b.data_ptr(), N, K, batch, ldb, bsb, 64)
+              : bf16_map(b.data_ptr(), K, N, batch, ldb, bsb, BN / cg);
   mp.c = out_map(c, M, N, batch, ldc, bsc);
   GemmParams p{};
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
   p.batch = (int)batch;
-  p.m_tiles = (int)((M + BM - 1) / BM);
+  p.m_tiles = (int)((M + BM * cg - 1) / (BM * cg));
   p.n_tiles = (int)((N + BN - 1) / BN);
   p.k_blocks = (int)((K + BK - 1) / BK);
   int splits = (int)std::max<int64_t>(1, k_splits);
@@ -695,7 +803,7 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
     // units fill the persistent grid's waves best (least idle fraction in the last wave), preferring
     // fewer splits (less reduce-add traffic) on ties
     const int tiles = p.m_tiles * p.n_tiles * p.batch;
-    const int sms = num_sms();
+    const int sms = num_sms() / cg;  // persistent slots: SMs, or SM pairs
     splits = 1;
     double best = 1e9;
     const int max_s = std::max(1, std::min(64, p.k_blocks / 16));
@@ -728,12 +836,12 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
   p.beta = (float)beta;
   p.status = status_ptr(a.device().index());
   const int total = p.m_tiles * p.n_tiles * p.batch * p.k_splits;
-  const int grid = std::min(total, num_sms());
+  const int grid = persistent_grid(total, cg);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (BN == 256)
-    dispatch_major<256>(a_mn, b_mn, (int)epi, mp, p, grid, st);
+    dispatch_major<256>(a_mn, b_mn, (int)epi, mp, p, grid, st, cg);
   else
-    dispatch_major<128>(a_mn, b_mn, (int)epi, mp, p, grid, st);
+    dispatch_major<128>(a_mn, b_mn, (int)epi, mp, p, grid, st, cg);
 }
 
 // The lm_head GEMM fused with the softcapped cross-entropy statistics (EPI_SOFTCAP_CE, see CeHead):
@@ -756,7 +864,8 @@ void gemm_softcap_ce(const torch::Tensor& x, const torch::Tensor& w, torch::Tens
   c10::cuda::CUDAGuard guard(x.device());
   Maps mp;
   mp.a = bf16_map(x.data_ptr(), K, M, 1, x.stride(0), 0, BM);
-  mp.b = bf16_map(w.data_ptr(), K, N, 1, w.stride(0), 0, 256);
+  const int cg = pair_mode(256, M);
+  mp.b = bf16_map(w.data_ptr(), K, N, 1, w.stride(0), 0, 256 / cg);
   mp.c = out_map(g, M, N, 1, g.stride(0), 0);
   mp.x = mp.c;
   GemmParams p{};
@@ -764,7 +873,7 @@ void gemm_softcap_ce(const torch::Tensor& x, const torch::Tensor& w, torch::Tens
   p.N = (int)N;
   p.K = (int)K;
   p.batch = 1;
-  p.m_tiles = (int)((M + BM - 1) / BM);
+  p.m_tiles = (int)((M + BM * cg - 1) / (BM * cg));
   p.n_tiles = (int)n_tiles;
   p.k_blocks = (int)((K + BK - 1) / BK);
   p.k_splits = 1;
@@ -778,8 +887,8 @@ void gemm_softcap_ce(const torch::Tensor& x, const torch::Tensor& w, torch::Tens
   p.ce.zt = zt.data_ptr<float>();
   p.ce.store = store ? 1 : 0;
   const int total = p.m_tiles * p.n_tiles;
-  launch_t<256, false, false, EPI_SOFTCAP_CE, false>(mp, p, std::min(total, num_sms()),
-                                                      at::cuda::getCurrentCUDAStream());
+  launch_t<256, false, false, EPI_SOFTCAP_CE, false>(mp, p, persistent_grid(total, cg),
+                                                      at::cuda::getCurrentCUDAStream(), cg);
 }
 
 // out[M, (H+2KV)*128] = x[M, K] @ w[K, N] with the QKV epilogue (RoPE + QK-norm on q/k heads, the
@@ -805,12 +914,13 @@ void gemm_qkv_rope(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor
   mp.b = bf16_map(w.data_ptr(), N, K, 1, w.stride(0), 0, 64);
   mp.c = out_map(out, M, N, 1, out.stride(0), 0);
   mp.x = mp.c;
+  const int cg = pair_mode(256, M);
   GemmParams p{};
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
   p.batch = 1;
-  p.m_tiles = (int)((M + BM - 1) / BM);
+  p.m_tiles = (int)((M + BM * cg - 1) / (BM * cg));
   p.n_tiles = (int)(N / 256);
   p.k_blocks = (int)((K + BK - 1) / BK);
   p.k_splits = 1;
@@ -843,7 +953,11 @@ void gemm_qkv_rope(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor
     r.V = (int)ve->size(0);
   }
   const int total = p.m_tiles * p.n_tiles;
-  launch_t<256, false, true, EPI_QKV_ROPE, false>(mp, p, std::min(total, num_sms()), at::cuda::getCurrentCUDAStream());
+  launch_t<256, false, true, EPI_QKV_ROPE, false>(mp, p, persistent_grid(total, cg), at::cuda::getCurrentCUDAStream(),
+                                                  cg);
 }
+
+void gemm_set_pair(bool on) { g_pair = on; }
+bool gemm_pair() { return g_pair; }
 
 }  // namespace br

@@ -1,8 +1,17 @@
-"""tcgen05 GEMM vs an fp32 PyTorch matmul of the same bf16 operands."""
+"""tcgen05 GEMM vs an fp32 PyTorch matmul of the same bf16 operands, with 256-column tiles run by CTA
+pairs (cta_group::2, the default) and by single CTAs."""
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(params=[True, False], ids=["pair", "single"])
+def pair(request, cuda):
+    from bitresearch_b200.ops._ext import ext
+    ext().gemm_set_pair(request.param)
+    yield request.param
+    ext().gemm_set_pair(True)
 
 
 def _ops():
@@ -23,7 +32,7 @@ def _rand(*shape, dev):
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 512), (300, 520, 200), (1000, 1536, 512), (64, 128, 96)])
 @pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
-def test_gemm_majors_and_tails(cuda, M, N, K, a_t, b_t):
+def test_gemm_majors_and_tails(cuda, pair, M, N, K, a_t, b_t):
     gemm, check_status = _ops()
     torch.manual_seed(0)
     a = _rand(K, M, dev=cuda).t() if a_t else _rand(M, K, dev=cuda)       # logical [M, K]
@@ -36,7 +45,7 @@ def test_gemm_majors_and_tails(cuda, M, N, K, a_t, b_t):
     _close(out, a.float() @ b.float(), K)
 
 
-def test_gemm_epilogues(cuda):
+def test_gemm_epilogues(cuda, pair):
     gemm, check_status = _ops()
     torch.manual_seed(1)
     M, N, K = 384, 512, 256
@@ -57,7 +66,7 @@ def test_gemm_epilogues(cuda):
 
 
 @pytest.mark.parametrize("splits", [1, 4, 0])
-def test_gemm_split_k_weight_grad(cuda, splits):
+def test_gemm_split_k_weight_grad(cuda, pair, splits):
     gemm, check_status = _ops()
     torch.manual_seed(2)
     T, Din, Dout = 8192, 512, 1536
@@ -70,7 +79,7 @@ def test_gemm_split_k_weight_grad(cuda, splits):
     _close(acc, ref, T)
 
 
-def test_gemm_batched(cuda):
+def test_gemm_batched(cuda, pair):
     gemm, check_status = _ops()
     torch.manual_seed(3)
     S, r, c = 6, 512, 256
@@ -84,7 +93,7 @@ def test_gemm_batched(cuda):
 
 
 @pytest.mark.parametrize("with_ve", [False, True])
-def test_qkv_rope_epilogue_matches_gemm_then_rope(cuda, with_ve):
+def test_qkv_rope_epilogue_matches_gemm_then_rope(cuda, pair, with_ve):
     """The fused QKV GEMM epilogue (RoPE + QK-norm on q/k heads, VE add on v heads) against the plain
     GEMM followed by the separate RoPE kernel; M = 3 x 100 leaves a partial last row tile."""
     from bitresearch_b200.ops import gemm
@@ -118,3 +127,37 @@ def test_qkv_rope_epilogue_matches_gemm_then_rope(cuda, with_ve):
     torch.testing.assert_close(rk, rk0, rtol=1e-2, atol=1e-3)
     if with_ve:
         torch.testing.assert_close(gate, gate0, rtol=1e-5, atol=1e-5)
+
+
+def test_pair_and_single_tiles_agree_at_production_shapes(cuda):
+    """The same GEMMs with CTA pairs and with single CTAs: forward K = 512 and K = 2048 shapes, an
+    MN-major weight-gradient GEMM with split-K, and a row count that leaves the last pair half empty."""
+    from bitresearch_b200.ops import gemm
+    from bitresearch_b200.ops._ext import check_status, ext
+    E = ext()
+    torch.manual_seed(5)
+    cases = [((16384 + 128, 512), (512, 1536), gemm.BF16), ((8192, 2048), (2048, 512), gemm.BF16),
+             ((8192, 512), (512, 2048), gemm.RELU2)]
+    try:
+        for (m, k), (k2, n), epi in cases:
+            a, b = _rand(m, k, dev=cuda), _rand(k2, n, dev=cuda)
+            E.gemm_set_pair(True)
+            p = gemm.matmul(a, b, epi=epi)
+            E.gemm_set_pair(False)
+            s1 = gemm.matmul(a, b, epi=epi)
+            torch.cuda.synchronize()
+            assert check_status() == 0
+            torch.testing.assert_close(p.float(), s1.float(), rtol=1e-2, atol=1e-2)
+        x, dy = _rand(8192, 512, dev=cuda), _rand(8192, 2048, dev=cuda)
+        outs = []
+        for on in (True, False):
+            E.gemm_set_pair(on)
+            o = torch.zeros(512, 2048, device=cuda)
+            gemm.matmul(x.t(), dy, out=o, epi=gemm.ATOMIC, k_splits=0)
+            outs.append(o)
+        torch.cuda.synchronize()
+        assert check_status() == 0
+        _close(outs[0], x.float().t() @ dy.float(), 8192)
+        torch.testing.assert_close(outs[0], outs[1], rtol=1e-3, atol=1e-2)
+    finally:
+        E.gemm_set_pair(True)
