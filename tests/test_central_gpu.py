@@ -40,8 +40,9 @@ def test_central_worker_on_engine(cuda):
     assert coord.step == 6 and np.isfinite(coord.losses).all() and coord.losses[-1] < coord.losses[0]
 
 
-def test_central_worker_reference_default_on_eager_path(cuda):
+def test_central_worker_reference_default_on_engine(cuda):
+    """The reference's default model (4 x 64 heads) trains on the sm_100a engine."""
     from bitresearch_b200.config import preset
     coord, out = _run(preset("ref-default"), 2, "reference")
-    assert out["res"]["steps"] == 2 and out["impl"] == "torch"
+    assert out["res"]["steps"] == 2 and out["impl"] == "cuda"
     assert np.isfinite(coord.losses).all()
