@@ -205,6 +205,9 @@ class TrainConfig:
     bos_token_id: int = -1  # data=documents: -1 = vocab_size - 1
     # compute
     impl: str = "cuda"  # "cuda" (sm_100a kernels) or "torch" (eager oracle path)
+    # impl=torch on a GPU: run the eager model under torch.compile with flex attention (a fused
+    # sliding-window kernel), the strongest stock-PyTorch form of the model, for baseline runs
+    torch_compile: bool = False
     dtype: str = "bf16"
     # distributed communication
     comm: str = "p2p"  # "p2p" (in-kernel NVLink), "nccl", "ring" (reference ring algorithm over the PG)

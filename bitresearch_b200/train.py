@@ -132,6 +132,10 @@ class Trainer:
         cfg = self.cfg
         torch.manual_seed(cfg.seed)
         self.model = GPT(cfg.model, init="karpathy", seed=42, device=self.device)
+        self._fwd = self.model.forward_torch
+        if cfg.torch_compile and cfg.impl == "torch" and self.is_cuda:
+            self.model.attn_impl = "flex"
+            self._fwd = torch.compile(self.model.forward_torch)
         self.specs = self.model.specs
         self.metrics.num_params_m = self.model.num_params() / 1e6
         self.flops_per_token = self.model.estimate_flops_per_token()
@@ -224,7 +228,7 @@ class Trainer:
                                                 last_micro=self._micro == self.grad_accum - 1, grad_scale=scale)
         cd = torch.bfloat16 if self.is_cuda and self.cfg.dtype == "bf16" else (
             torch.float16 if self.is_cuda and self.cfg.dtype == "fp16" else None)
-        loss = self.model.forward_torch(x, y, compute_dtype=cd, exact_ce=not self.is_cuda)
+        loss = self._fwd(x, y, compute_dtype=cd, exact_ce=not self.is_cuda)
         (loss * (scale / self.grad_accum)).backward()
         return loss.detach()
 
