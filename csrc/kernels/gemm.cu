@@ -785,7 +785,10 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
   TORCH_CHECK(BN == 128 || BN == 256, "block_n must be 128 or 256");
   Maps mp;
   mp.a = a_mn ? bf16_map(a.data_ptr(), M, K, batch, lda, bsa, 64) : bf16_map(a.data_ptr(), K, M, batch, lda, bsa, BM);
-  const int cg = pair_mode(BN, M);  // a CTA pair loads half of B's tile columns each
+  // a CTA pair loads half of B's tile columns each; epilogues that stream an aux input stay on single
+  // CTAs (their time is the epilogue's, and pairs measured 2-7% slower there)
+  const bool has_aux = aux.has_value() && aux->defined();
+  const int cg = has_aux ? 1 : pair_mode(BN, M);
   mp.b = b_mn ? bf16_map(b.data_ptr(), N, K, batch, ldb, bsb, 64)
               : bf16_map(b.data_ptr(), K, N, batch, ldb, bsb, BN / cg);
   mp.c = out_map(c, M, N, batch, ldc, bsc);
