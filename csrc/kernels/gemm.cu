@@ -95,17 +95,20 @@ constexpr int BK = 64;
 constexpr int CHUNK_BYTES = 32 * 128;  // one epilogue warp's 32 rows x 128 bytes
 constexpr uint64_t kWaitBudgetNs = 2000000000ull;
 
-// AUX: the epilogue reads an auxiliary input. Its loads then run through a 4-buffer ring per
+// AUX: the epilogue reads an auxiliary input. Its loads then run through a 5-buffer ring per
 // epilogue warp, issued up to three chunks (across tile boundaries) ahead of the chunk being
-// processed, so the DRAM latency of the aux tile overlaps the epilogue math; the main loop gives up
-// one stage to make room.
+// processed, so the DRAM latency of the aux tile overlaps the epilogue math. A buffer is reloaded only
+// once the store of the chunk two back has read it: the latest chunk's store stays in flight. The
+// main loop gives up one stage to make room.
 // CG = 2: a CTA pair runs one 256-row tile (cta_group::2); each CTA loads its 128 rows of A and half of
 // B's BN columns, so a stage is 32 KB instead of 48 and the pair reads a third less operand data per
 // output than two single CTAs.
 template <int BN, bool AUX, int CG = 1>
 struct GemmCfg {
-  static constexpr int STAGES = CG == 2 ? (AUX ? 5 : 6) : (AUX ? (BN == 256 ? 3 : 5) : (BN == 256 ? 4 : 6));
-  static constexpr int NBUF = AUX ? 4 : 2;  // staging buffers per epilogue warp
+  static constexpr int STAGES = CG == 2 ? (AUX ? 4 : 6) : (AUX ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6));
+  // staging buffers per epilogue warp; with an aux input the ring holds the aux loads three chunks
+  // ahead plus the latest chunk's store, so a prefetch never waits for the store it follows
+  static constexpr int NBUF = AUX ? 5 : 2;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = (BN / CG) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -426,7 +429,7 @@ __global__ void __launch_bounds__(192, 1)
       decode_unit(p, u, m, n, b, kb0, kb1);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if constexpr (AUX) prefetch(nchunk + NBUF);  // aux of the coming chunks loads during the MMA
+      if constexpr (AUX) prefetch(nchunk + NBUF - 1);  // aux of the coming chunks loads during the MMA
       if (!mbar_wait_warp(&tfull_bar[acc], acc_phase, kWaitBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
@@ -545,7 +548,7 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld32(taddr + c * COLS, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         if constexpr (COLS == 64) tmem_ld32(taddr + c * COLS + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         if constexpr (AUX) {
-          prefetch(nchunk + NBUF);  // keeps up to NBUF - 1 chunks ahead in flight
+          prefetch(nchunk + NBUF - 1);  // keeps NBUF - 2 chunks ahead in flight; waits only for older stores
         } else {
           if (leader) bulk_wait_read1();  // the store that last used this buffer has read it
         }
