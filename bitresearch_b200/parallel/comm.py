@@ -44,6 +44,7 @@ WIRE_CODE = {"fp32": 0, "f32": 0, "bf16": 1, "fp16": 2, "f16": 2}
 WIRE_BYTES = {0: 4, 1: 2, 2: 2}
 ALIGN = 16  # elements; keeps every parameter 64-byte aligned in the flat buffers
 CHUNK = 1 << 16
+COMM_CTAS = 32  # CTAs per bucket kernel of the reduce-scatter
 
 
 def bucket_order(specs, n_layer: int) -> list[list[str]]:
@@ -343,11 +344,14 @@ class P2PGradSync:
                 self._sparse_bucket(b, loss_scale)
                 return
             ep = self.epoch + 1
+            # a small CTA budget: these kernels run beside the backward's compute kernels, and with four
+            # vectors in flight per thread 32 CTAs keep about 1 MB of traffic in flight
             self.E.comm_pack_push(self.tr.flat_grad, self.recv_peers, self.rank, self.slot_elems, self.push_tables[b],
-                                  self.wire, 1.0 / loss_scale, self.bad, 0)
+                                  self.wire, 1.0 / loss_scale, self.bad, COMM_CTAS)
             self.E.comm_signal_all(self.rflag_peers, self.rank, b, ep, self.bad)
             self.E.comm_reduce_local(self.recv.ptr, self.rflags.ptr, self.world, b, ep, self.slot_elems,
-                                     self.own_tables[b], self.red, self.wire, 1.0 / self.world, 0, self.budget)
+                                     self.own_tables[b], self.red, self.wire, 1.0 / self.world, COMM_CTAS,
+                                     self.budget)
             if b == len(self.ranges) - 1:
                 self.E.comm_agree(self.rflags.ptr, self.world, b, ep, self.skip, self.budget)
 
