@@ -1,6 +1,6 @@
 """Per-kernel timings at the d512 depth-8 production shapes, against library baselines.
 
-  python benchmarks/kernels.py [--tokens 262144] [--json out.json] [--only tags] [--pair on|off]
+  python benchmarks/kernels.py [--tokens 262144] [--json out.json] [--only tags] [--pair on|off|all]
 
 Each kernel is timed with CUDA events on the launching stream after warm-up (median of R repeats);
 inputs of the large shapes exceed the 126 MB L2. FLOP/s and bytes/s are reported as fractions of the
@@ -53,13 +53,14 @@ def main():
     ap.add_argument("--tokens", type=int, default=262144)
     ap.add_argument("--json", default="")
     ap.add_argument("--only", default="")
-    ap.add_argument("--pair", default="on", choices=["on", "off"],
-                    help="256-column GEMM tiles on CTA pairs (cta_group::2) or on single CTAs")
+    ap.add_argument("--pair", default="on", choices=["on", "off", "all"],
+                    help="256-column GEMM tiles on CTA pairs (cta_group::2): on (GEMMs without an aux input), "
+                         "all, or off (single CTAs)")
     args = ap.parse_args()
     from bitresearch_b200.ops import gemm
     from bitresearch_b200.ops._ext import check_status, ext
     E = ext()
-    E.gemm_set_pair(args.pair == "on")
+    E.gemm_set_pair({"off": 0, "on": 1, "all": 2}[args.pair])
     dev = torch.device("cuda", 0)
     FLOPS, BW, src = peaks()
     M, D, F4, V, T, H = args.tokens, 512, 2048, 8192, 2048, 4
@@ -204,7 +205,7 @@ def main():
         ms = timeit(lambda: E.gemm_softcap_ce(xf, wb, G, tgt, part, zt, 15.0, True))
         report(f"head: gemm_softcap_ce {M}x{D}x{V}", ms, flops=f_head)
         ms_fin = timeit(lambda: E.ce_finalize(part, zt, tgt, V, 15.0, 1.0 / M, nats=nats, loss_sum=ls, rowscale=rs,
-                                              coef=cf, x=xf, xs=xs, dw=dw))
+                                              x=xf, xs=xs, g=G))
         report("head: ce_finalize", ms_fin, nbytes=M * (4 * (V // 256) + 2 * D * 2))
         ms_old = timeit(lambda: (gemm.matmul(xf, wb.t(), out=G, epi=gemm.SOFTCAP, alpha=1 / 15, beta=15.0),
                                  E.softcap_ce(G, tgt, 15.0, 1.0 / M, nats, ls, True)))

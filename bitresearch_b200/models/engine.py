@@ -17,7 +17,7 @@ Per layer (forward):
   GEMM (F32 epi)      x_next = mid + h @ Wmlp_proj
 Head: rms_fwd -> lm_head GEMM whose epilogue computes the softcapped cross-entropy statistics and writes
 G = exp(z - cap) (1 - (z/cap)^2) instead of the logits -> ce_finalize (loss, per-token nats, per-row scale,
-the target column's fp32 gradient, the scaled activations for dW and the target scatter into dW).
+the target column's gradient written into G, the scaled activations for dW).
 Backward mirrors it: dW via ``X^T @ dY`` split-K GEMMs (fp32 vector reductions), dX via ``dY @ W^T``
 GEMMs (the ReLU^2 derivative fused into the mlp_proj dX epilogue), rms/ladder backward kernels,
 attention backward, RoPE/QK-norm/VE backward and the embedding scatter.
@@ -138,7 +138,7 @@ class FusedGPTEngine:
             "rstdf": torch.empty(M, **f32), "xf": torch.empty(M, D, **bf),
             # fused head: G (dlogits up to a per-row scale and the target column), CE statistics
             "G": torch.empty(M, self.V, **bf), "ce_part": torch.empty((self.V + 255) // 256, M, **f32),
-            "zt": torch.empty(M, **f32), "rowscale": torch.empty(M, **f32), "coef": torch.empty(M, **f32),
+            "zt": torch.empty(M, **f32), "rowscale": torch.empty(M, **f32),
             "xs_head": torch.empty(M, D, **bf), "nats": torch.empty(M, **f32),
             "loss": torch.zeros(1, **f32),
             # backward scratch
@@ -193,13 +193,13 @@ class FusedGPTEngine:
     def _head(self, tg: torch.Tensor, b: dict, scale: float, grad: bool):
         """lm_head + softcap 15 + cross-entropy (gpt.ts:296-313) without writing the logits: the GEMM epilogue
         keeps per-row exp-sums and the target logit, ``ce_finalize`` adds ``scale * sum(nats)`` into the loss.
-        With ``grad`` it also prepares the backward: G, the per-row scale, the scaled activations for the
-        weight-gradient GEMM and the target column's contribution to the lm_head gradient."""
+        With ``grad`` it also prepares the backward: G (with the target column's gradient patched in), the
+        per-row scale and the scaled activations for the weight-gradient GEMM."""
         E = self.E
         E.gemm_softcap_ce(b["xf"], self.shadows["lmHead"], b["G"], tg, b["ce_part"], b["zt"], 15.0, grad)
         if grad:
             E.ce_finalize(b["ce_part"], b["zt"], tg, self.V, 15.0, scale, nats=b["nats"], loss_sum=b["loss"],
-                          rowscale=b["rowscale"], coef=b["coef"], x=b["xf"], xs=b["xs_head"], dw=self.grads["lmHead"])
+                          rowscale=b["rowscale"], x=b["xf"], xs=b["xs_head"], g=b["G"])
         else:
             E.ce_finalize(b["ce_part"], b["zt"], tg, self.V, 15.0, scale, nats=b["nats"])
 
@@ -210,13 +210,12 @@ class FusedGPTEngine:
         Dq, Dkv = self.Dq, self.Dkv
         idx = idx.reshape(-1)
         A = gemm.ATOMIC
-        # head: dlogits = rowscale * G + [target] coef, so dlmHead += G^T (rowscale xf) (the target scatter
-        # ran in ce_finalize) and dxf = rowscale (G lmHead) + coef lmHead[target], folded into rms_bwd
+        # head: dlogits = rowscale * G (ce_finalize wrote the target column into G), so
+        # dlmHead += G^T (rowscale xf) and dxf = rowscale (G lmHead), the scale folded into rms_bwd
         gemm.matmul(b["G"].t(), b["xs_head"], out=G["lmHead"], epi=A, k_splits=0)
         gemm.matmul(b["G"], self.shadows["lmHead"], out=b["dmid"], epi=gemm.F32)
         self._ready(0)
-        E.rms_bwd(b["xs"][-1], b["rstdf"], b["dmid"], None, b["dx"], b["dx_b"], b["rowscale"], b["coef"], tg,
-                  P["lmHead"])
+        E.rms_bwd(b["xs"][-1], b["rstdf"], b["dmid"], None, b["dx"], b["dx_b"], b["rowscale"])
         b["dx0"].zero_()
         for i in reversed(range(self.L)):
             # MLP

@@ -13,8 +13,8 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
                  int64_t ldb, int64_t bsb, torch::Tensor& c, int64_t ldc, int64_t bsc, int64_t M, int64_t N,
                  int64_t K, int64_t batch, int64_t epi, c10::optional<torch::Tensor> aux, int64_t ld_aux,
                  int64_t bs_aux, double alpha, double beta, int64_t k_splits, int64_t block_n);
-void gemm_set_pair(bool on);
-bool gemm_pair();
+void gemm_set_pair(int64_t mode);
+int64_t gemm_pair();
 void embed_rms_fwd(const torch::Tensor& idx, const torch::Tensor& wte, torch::Tensor& x0, torch::Tensor& rstd);
 void ladder_rms_fwd(const torch::Tensor& x, const torch::Tensor& x0, const torch::Tensor& lam_r,
                     const torch::Tensor& lam_0, int64_t layer, torch::Tensor& cur, torch::Tensor& xn,
@@ -29,7 +29,8 @@ void gemm_softcap_ce(const torch::Tensor& x, const torch::Tensor& w, torch::Tens
 void ce_finalize(const torch::Tensor& partial, const torch::Tensor& zt, const torch::Tensor& targets, int64_t V,
                  double cap, double scale, c10::optional<torch::Tensor> nats, c10::optional<torch::Tensor> loss_sum,
                  c10::optional<torch::Tensor> rowscale, c10::optional<torch::Tensor> coef,
-                 c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> xs, c10::optional<torch::Tensor> dw);
+                 c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> xs, c10::optional<torch::Tensor> dw,
+                 c10::optional<torch::Tensor> g);
 void ladder_bwd(const torch::Tensor& x, const torch::Tensor& x0, const torch::Tensor& lam_r,
                 const torch::Tensor& lam_0, int64_t layer, const torch::Tensor& rstd, const torch::Tensor& dxn,
                 const torch::Tensor& dres, c10::optional<torch::Tensor> dgate_in, torch::Tensor& dx,
@@ -131,7 +132,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("V"), pybind11::arg("cap"), pybind11::arg("scale"), pybind11::arg("nats") = pybind11::none(),
         pybind11::arg("loss_sum") = pybind11::none(), pybind11::arg("rowscale") = pybind11::none(),
         pybind11::arg("coef") = pybind11::none(), pybind11::arg("x") = pybind11::none(),
-        pybind11::arg("xs") = pybind11::none(), pybind11::arg("dw") = pybind11::none());
+        pybind11::arg("xs") = pybind11::none(), pybind11::arg("dw") = pybind11::none(),
+        pybind11::arg("g") = pybind11::none());
   m.def("ladder_bwd", &br::ladder_bwd, pybind11::arg("x"), pybind11::arg("x0"), pybind11::arg("lam_r"),
         pybind11::arg("lam_0"), pybind11::arg("layer"), pybind11::arg("rstd"), pybind11::arg("dxn"),
         pybind11::arg("dres"), pybind11::arg("dgate_in"), pybind11::arg("dx"), pybind11::arg("dx0_acc"),

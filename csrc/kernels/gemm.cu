@@ -667,11 +667,13 @@ struct Maps {
   CUtensorMap a, b, c, x;
 };
 
-// 256-column GEMMs with more than one 128-row tile run as CTA pairs unless switched off
-// (gemm_set_pair, for A/B measurements).
-bool g_pair = true;
+// Which 256-column GEMMs with more than one 128-row tile run as CTA pairs (gemm_set_pair, for A/B
+// measurements): 0 none, 1 those without an aux input (the default), 2 all.
+int g_pair = 1;
 
-int pair_mode(int BN, int64_t M) { return g_pair && BN == 256 && M > BM ? 2 : 1; }
+int pair_mode(int BN, int64_t M, bool aux = false) {
+  return BN == 256 && M > BM && (g_pair == 2 || (g_pair == 1 && !aux)) ? 2 : 1;
+}
 
 // Persistent grid: one CTA (or one CTA pair) per SM (pair), no more than there are work units.
 int persistent_grid(int64_t units, int cg) {
@@ -788,10 +790,9 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
   TORCH_CHECK(BN == 128 || BN == 256, "block_n must be 128 or 256");
   Maps mp;
   mp.a = a_mn ? bf16_map(a.data_ptr(), M, K, batch, lda, bsa, 64) : bf16_map(a.data_ptr(), K, M, batch, lda, bsa, BM);
-  // a CTA pair loads half of B's tile columns each; epilogues that stream an aux input stay on single
-  // CTAs (their time is the epilogue's, and pairs measured 2-7% slower there)
+  // a CTA pair loads half of B's tile columns each
   const bool has_aux = aux.has_value() && aux->defined();
-  const int cg = has_aux ? 1 : pair_mode(BN, M);
+  const int cg = pair_mode(BN, M, has_aux);
   mp.b = b_mn ? bf16_map(b.data_ptr(), N, K, batch, ldb, bsb, 64)
               : bf16_map(b.data_ptr(), K, N, batch, ldb, bsb, BN / cg);
   mp.c = out_map(c, M, N, batch, ldc, bsc);
@@ -963,7 +964,10 @@ void gemm_qkv_rope(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor
                                                   cg);
 }
 
-void gemm_set_pair(bool on) { g_pair = on; }
-bool gemm_pair() { return g_pair; }
+void gemm_set_pair(int64_t mode) {
+  TORCH_CHECK(mode >= 0 && mode <= 2, "gemm_set_pair: 0 (none), 1 (without aux input) or 2 (all)");
+  g_pair = (int)mode;
+}
+int64_t gemm_pair() { return g_pair; }
 
 }  // namespace br

@@ -111,6 +111,9 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict_
   }
 }
 
+// Two forms for the target column: with `g` (the patch form the engine uses) G[m, t] = cf / rowscale in
+// bf16, so both backward GEMMs include it and no scatter is needed; with `dw` (the exact fp32 form) the
+// gradient is scattered into dW here and added to dx by rms_bwd's head form.
 // Finishes the cross-entropy of the fused lm_head epilogue (EPI_SOFTCAP_CE in gemm.cu), whose GEMM wrote
 // per (256-column tile, row) partial sums of e_j = exp(z_j - cap), the target's softcapped logit z_t and
 // G = e (1 - (z/cap)^2) with G_t = 0. Per row, with S = sum_j e_j:
@@ -130,7 +133,8 @@ __global__ void __launch_bounds__(kFinRows) ce_finalize_kernel(
     const float* __restrict__ partial, int n_tiles, const float* __restrict__ zt, const int* __restrict__ targets,
     int M, int V, float cap, float scale, float* __restrict__ nats, float* __restrict__ loss_sum,
     float* __restrict__ rowscale, float* __restrict__ coef, const __nv_bfloat16* __restrict__ x,
-    __nv_bfloat16* __restrict__ xs, float* __restrict__ dw, int D, int* status) {
+    __nv_bfloat16* __restrict__ xs, float* __restrict__ dw, int D, __nv_bfloat16* __restrict__ g, int64_t ldg,
+    int* status) {
   __shared__ float s_rs[kFinRows], s_cf[kFinRows], s_red[kFinRows / 32];
   __shared__ int s_t[kFinRows];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -152,6 +156,8 @@ __global__ void __launch_bounds__(kFinRows) ce_finalize_kernel(
       const float rs = r / S, cf = r * (pt - 1.f) * (1.f - zc * zc);
       if (rowscale) rowscale[m] = rs;
       if (coef) coef[m] = cf;
+      // patch form: the target column's gradient goes into G itself (scaled so that rowscale * G gives it)
+      if (g && valid && rs > 0.f) g[(int64_t)m * ldg + t] = __float2bfloat16(cf / rs);
       s_rs[threadIdx.x] = rs;
       s_cf[threadIdx.x] = cf;
       s_t[threadIdx.x] = valid ? t : -1;
@@ -202,7 +208,8 @@ __global__ void __launch_bounds__(kFinRows) ce_finalize_kernel(
 void ce_finalize(const torch::Tensor& partial, const torch::Tensor& zt, const torch::Tensor& targets, int64_t V,
                  double cap, double scale, c10::optional<torch::Tensor> nats, c10::optional<torch::Tensor> loss_sum,
                  c10::optional<torch::Tensor> rowscale, c10::optional<torch::Tensor> coef,
-                 c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> xs, c10::optional<torch::Tensor> dw) {
+                 c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> xs, c10::optional<torch::Tensor> dw,
+                 c10::optional<torch::Tensor> g) {
   const int64_t M = targets.numel();
   const int64_t n_tiles = (V + 255) / 256;
   TORCH_CHECK(targets.scalar_type() == at::kInt && targets.is_contiguous(), "ce_finalize: int32 targets");
@@ -233,19 +240,28 @@ void ce_finalize(const torch::Tensor& partial, const torch::Tensor& zt, const to
       dwp = dw->data_ptr<float>();
     }
   }
+  __nv_bfloat16* gp = nullptr;
+  int64_t ldg = 0;
+  if (g.has_value() && g->defined()) {
+    TORCH_CHECK(g->scalar_type() == at::kBFloat16 && g->dim() == 2 && g->size(0) == M && g->size(1) == V &&
+                    g->stride(1) == 1, "ce_finalize: g bf16 [M, V] with contiguous rows");
+    TORCH_CHECK(rowscale.has_value() && rowscale->defined(), "ce_finalize: the patch form needs rowscale");
+    gp = reinterpret_cast<__nv_bfloat16*>(g->data_ptr());
+    ldg = g->stride(0);
+  }
   float* ls = nullptr;
   if (loss_sum.has_value() && loss_sum->defined()) {
     TORCH_CHECK(loss_sum->scalar_type() == at::kFloat, "ce_finalize: loss_sum fp32");
     ls = loss_sum->data_ptr<float>();
   }
-  c10::cuda::CUDAGuard g(targets.device());
+  c10::cuda::CUDAGuard guard(targets.device());
   int dev = targets.device().index(), sms = 0;
   C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int64_t blocks = std::min<int64_t>((M + kFinRows - 1) / kFinRows, (int64_t)sms * 8);
   ce_finalize_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), kFinRows, 0, at::cuda::getCurrentCUDAStream()>>>(
       partial.data_ptr<float>(), (int)n_tiles, zt.data_ptr<float>(), targets.data_ptr<int>(), (int)M, (int)V,
       (float)cap, (float)scale, f32(nats, "nats"), ls, f32(rowscale, "rowscale"), f32(coef, "coef"), xp, xsp, dwp,
-      (int)D, status_ptr(targets.device().index()));
+      (int)D, gp, ldg, status_ptr(targets.device().index()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -143,9 +143,11 @@ __global__ void rms_bwd_kernel(const float* __restrict__ x, const float* __restr
     const float* wrow = nullptr;
     if constexpr (HEAD) {
       rs = hg.rowscale[row];
-      cf = hg.coef[row];
-      const int t = hg.targets[row];
-      if (t >= 0 && t < hg.V) wrow = hg.w + (int64_t)t * D;
+      if (hg.coef) {  // exact fp32 target form; without coef the target column is already inside dy
+        cf = hg.coef[row];
+        const int t = hg.targets[row];
+        if (t >= 0 && t < hg.V) wrow = hg.w + (int64_t)t * D;
+      }
     }
     float s = 0.f;
     for (int c = lane * 4; c < D; c += 128)
@@ -337,14 +339,19 @@ void rms_bwd(const torch::Tensor& x, const torch::Tensor& rstd, const torch::Ten
   HeadGrad hg{};
   const bool head = rowscale.has_value() && rowscale->defined();
   if (head) {
-    TORCH_CHECK(coef.has_value() && targets.has_value() && wtab.has_value(), "rms_bwd: head form needs coef, targets, w");
     check_rows(*rowscale, M, 1, at::kFloat, "rowscale");
-    check_rows(*coef, M, 1, at::kFloat, "coef");
-    check_rows(*targets, M, 1, at::kInt, "targets");
-    TORCH_CHECK(wtab->scalar_type() == at::kFloat && wtab->is_contiguous() && wtab->dim() == 2 && wtab->size(1) == D,
-                "rms_bwd: w fp32 [V, D]");
-    hg = HeadGrad{rowscale->data_ptr<float>(), coef->data_ptr<float>(), targets->data_ptr<int>(),
-                  wtab->data_ptr<float>(), (int)wtab->size(0)};
+    hg.rowscale = rowscale->data_ptr<float>();
+    if (coef.has_value() && coef->defined()) {
+      TORCH_CHECK(targets.has_value() && wtab.has_value(), "rms_bwd: the exact target form needs targets and w");
+      check_rows(*coef, M, 1, at::kFloat, "coef");
+      check_rows(*targets, M, 1, at::kInt, "targets");
+      TORCH_CHECK(wtab->scalar_type() == at::kFloat && wtab->is_contiguous() && wtab->dim() == 2 &&
+                      wtab->size(1) == D, "rms_bwd: w fp32 [V, D]");
+      hg.coef = coef->data_ptr<float>();
+      hg.targets = targets->data_ptr<int>();
+      hg.w = wtab->data_ptr<float>();
+      hg.V = (int)wtab->size(0);
+    }
   }
   const float* xp = x.data_ptr<float>();
   const float* rp = rstd.data_ptr<float>();

@@ -6,12 +6,13 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=[True, False], ids=["pair", "single"])
+@pytest.fixture(params=[2, 0], ids=["pair", "single"])
 def pair(request, cuda):
+    """2: every 256-column GEMM with more than one row tile on CTA pairs (aux epilogues included); 0: none."""
     from bitresearch_b200.ops._ext import ext
     ext().gemm_set_pair(request.param)
     yield request.param
-    ext().gemm_set_pair(True)
+    ext().gemm_set_pair(1)
 
 
 def _ops():
@@ -141,16 +142,16 @@ def test_pair_and_single_tiles_agree_at_production_shapes(cuda):
     try:
         for (m, k), (k2, n), epi in cases:
             a, b = _rand(m, k, dev=cuda), _rand(k2, n, dev=cuda)
-            E.gemm_set_pair(True)
+            E.gemm_set_pair(2)
             p = gemm.matmul(a, b, epi=epi)
-            E.gemm_set_pair(False)
+            E.gemm_set_pair(0)
             s1 = gemm.matmul(a, b, epi=epi)
             torch.cuda.synchronize()
             assert check_status() == 0
             torch.testing.assert_close(p.float(), s1.float(), rtol=1e-2, atol=1e-2)
         x, dy = _rand(8192, 512, dev=cuda), _rand(8192, 2048, dev=cuda)
         outs = []
-        for on in (True, False):
+        for on in (2, 0):
             E.gemm_set_pair(on)
             o = torch.zeros(512, 2048, device=cuda)
             gemm.matmul(x.t(), dy, out=o, epi=gemm.ATOMIC, k_splits=0)
@@ -160,4 +161,4 @@ def test_pair_and_single_tiles_agree_at_production_shapes(cuda):
         _close(outs[0], x.float().t() @ dy.float(), 8192)
         torch.testing.assert_close(outs[0], outs[1], rtol=1e-3, atol=1e-2)
     finally:
-        E.gemm_set_pair(True)
+        E.gemm_set_pair(1)

@@ -15,8 +15,11 @@ def _assert(a, b, tol, what):
     assert err <= tol * scale, (what, err, scale)
 
 
+@pytest.mark.parametrize("form", ["patch", "scatter"])
 @pytest.mark.parametrize("V", [1000, 8192, 65536])
-def test_fused_head_matches_fp32_reference(cuda, V):
+def test_fused_head_matches_fp32_reference(cuda, V, form):
+    """form "patch" (the engine's): ce_finalize writes the target column's gradient into G; "scatter": it
+    scatters it into dW in fp32 and rms_bwd adds it to dx."""
     from bitresearch_b200.ops import gemm
     from bitresearch_b200.ops._ext import check_status, ext
     E = ext()
@@ -44,12 +47,19 @@ def test_fused_head_matches_fp32_reference(cuda, V):
     loss = torch.zeros(1, device=cuda)
     dw = torch.zeros(V, D, device=cuda)
     E.gemm_softcap_ce(xf, wb, G, tgt, part, zt, CAP, True)
-    E.ce_finalize(part, zt, tgt, V, CAP, scale, nats=nats, loss_sum=loss, rowscale=rs, coef=cf, x=xf, xs=xs, dw=dw)
+    if form == "patch":
+        E.ce_finalize(part, zt, tgt, V, CAP, scale, nats=nats, loss_sum=loss, rowscale=rs, x=xf, xs=xs, g=G)
+    else:
+        E.ce_finalize(part, zt, tgt, V, CAP, scale, nats=nats, loss_sum=loss, rowscale=rs, coef=cf, x=xf, xs=xs,
+                      dw=dw)
     gemm.matmul(G.t(), xs, out=dw, epi=gemm.ATOMIC, k_splits=0)
     raw = torch.empty(M, D, device=cuda)
     gemm.matmul(G, wb, out=raw, epi=gemm.F32)
     dh = torch.empty(M, D, device=cuda)
-    E.rms_bwd(h, rstd, raw, None, dh, None, rs, cf, tgt, w)
+    if form == "patch":
+        E.rms_bwd(h, rstd, raw, None, dh, None, rs)
+    else:
+        E.rms_bwd(h, rstd, raw, None, dh, None, rs, cf, tgt, w)
     # evaluation form: statistics only, no G written
     nats_eval = torch.empty(M, device=cuda)
     G2 = torch.full((M, V), 7.0, dtype=torch.bfloat16, device=cuda)
