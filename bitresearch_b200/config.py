@@ -214,6 +214,10 @@ class TrainConfig:
     wire_dtype: str = "bf16"  # bf16 | fp16 | fp32
     bucket_mb: float = 32.0
     overlap: bool = True
+    # p2p path with the fused engine: the sharded optimizer runs per forward group on the comm stream,
+    # interleaved with the parameter exchange (false: one optimizer call on the compute stream after the
+    # backward, then the exchange)
+    overlap_optimizer: bool = True
     sparsify: SparsifyConfig = field(default_factory=SparsifyConfig)
     comm_timeout_s: float = 10.0  # elastic ring: 0 = the membership's dynamic timeout max(10, 3 rtt + 5) s
     # ring path only: re-form the ring without a lost rank (store heartbeats + a new gloo group)

@@ -272,15 +272,17 @@ class FusedGPTEngine:
         self._grad_scale = grad_scale
         assert idx.shape[1] == self.T
         b = self._buffers(B)
-        if not accumulate:
-            if self.flat_grad is not None:
-                self.flat_grad.zero_()
-            else:
-                for g in self.grads.values():
-                    g.zero_()
         tg = targets.reshape(-1).to(torch.int32).contiguous()
         with traced(self.timer, "forward"):
             self._forward(idx, b, B)
+            # zeroed after the forward: it waited for every parameter group of the last exchange, and with
+            # it for the last reduce-scatter kernels that read the previous step's gradients
+            if not accumulate:
+                if self.flat_grad is not None:
+                    self.flat_grad.zero_()
+                else:
+                    for g in self.grads.values():
+                        g.zero_()
             b["loss"].zero_()
             self._head(tg, b, loss_scale / (B * self.T), grad=True)
         with traced(self.timer, "backward"):  # includes the bucket hooks that launch the gradient reduce

@@ -241,6 +241,9 @@ class P2PGradSync:
                     off, numel, _ = self.layout[n]
                     rows += [(o, ln) for o, ln, _ in chunk_ranges(off, numel)]
             self.push_chunks.append(torch.tensor(sorted(rows), dtype=torch.int64, device=dev).view(-1, 2))
+        # the parameters this rank owns, per forward group: with the fused engine the optimizer steps them
+        # group by group on the comm stream, each group's push following its update
+        self.owned_by_group = [[n for n in grp if n in self.owned_names] for grp in self.fgroups]
         G = len(self.fgroups)
         self.push_flags = SymmetricBuffer(G * self.world * 8)
         self.group_flag_peers = [torch.tensor([p + 8 * g * self.world for p in self.push_flags.peer_ptrs],
@@ -356,7 +359,9 @@ class P2PGradSync:
                 self.E.comm_agree(self.rflags.ptr, self.world, b, ep, self.skip, self.budget)
 
     def begin_step(self) -> None:
-        self.bad.zero_()
+        # on the comm stream: the previous step's last bucket kernels there may still read the flag
+        with torch.cuda.stream(self.comm_stream):
+            self.bad.zero_()
         if self.sparse:
             # the reference counts the step before checking the dense warm-up (gradient-sparsifier.ts:87-91)
             self.sp_step += 1
@@ -370,13 +375,32 @@ class P2PGradSync:
 
         With ``device_skip`` the skip decision is the device word ``agree`` wrote; the host learns it (and
         any status code) from a pinned copy one step later (``poll``), so this returns True before the
-        outcome is known. Otherwise (fp16 loss scaling, top-k) the ranks agree on the host first."""
+        outcome is known. Otherwise (fp16 loss scaling, top-k) the ranks agree on the host first.
+
+        With the fused engine and ``device_skip`` everything after the backward runs on the comm stream and
+        the compute stream never waits for it: per forward group, the optimizer steps the parameters this
+        rank owns in that group and the exchange pushes them, so the next forward's first layers start
+        while the later groups are still being updated. The engine zeroes the gradient buffer only after
+        its forward has waited for every group, i.e. after the last bucket kernels of this step read it."""
         timer = self.tr.timer
+        epoch = self.epoch + 1
+        s = self.comm_stream
+        self.poll()
+        if self.device_skip and self.tr.engine is not None and self.cfg.overlap_optimizer:
+            with torch.cuda.stream(s), traced(timer, "sync.optimizer_exchange"):
+                for g in range(len(self.fgroups)):
+                    if self.owned_by_group[g]:
+                        opt.step({n: self.red_views[n] for n in self.owned_by_group[g]}, skip=self.skip)
+                    self._exchange_group(g, epoch)
+                self.E.status_snapshot(self.snap, self.skip)
+                self.snap_event.record(s)
+            self.snap_pending, self.snap_step = True, step_idx
+            self.tr.engine.param_ready = self.param_ready
+            self.epoch = epoch
+            return True
         cur = torch.cuda.current_stream()
         with traced(timer, "sync.comm_tail"):  # the compute stream waits for the last bucket's reduce
-            cur.wait_stream(self.comm_stream)
-        epoch = self.epoch + 1
-        self.poll()
+            cur.wait_stream(s)
         if self.device_skip:
             ok = True
             with traced(timer, "sync.optimizer"):
@@ -396,27 +420,30 @@ class P2PGradSync:
             if ok:
                 with traced(timer, "sync.optimizer"):
                     opt.step({n: self.red_views[n] for n in self.owned_names})
-        # The parameter exchange runs on the comm stream, overlapped with the next forward: per forward group,
-        # push the (possibly unchanged) owned parameters into every peer's buffer with posted NVLink stores,
-        # flag each peer, wait for the other owners' flags of the group and refresh its bf16 shadows locally,
-        # then record the group's event; the engine's forward waits for group g's event just before its
-        # first kernel that reads group g. Every rank's reduce of the last bucket waited for all ranks'
-        # last packs, so no peer still reads the values being overwritten; pushes only touch a peer's
-        # non-owned regions.
         self.opt_done.record()
-        s = self.comm_stream
         s.wait_event(self.opt_done)
         with torch.cuda.stream(s), traced(timer, "sync.param_exchange"):
             for g in range(len(self.fgroups)):
-                self.E.comm_push(self.params_flat, self.param_buf.peers_dev, self.rank, self.push_chunks[g], 0)
-                self.E.comm_signal_peers(self.group_flag_peers[g], self.rank, epoch)
-                self.E.comm_shadow_refresh(self.params_flat, self.push_flags.ptr + 8 * g * self.world, self.world,
-                                           self.rank, epoch, self.gather_segs[g], 0, self.budget)
-                self.group_events[g].record(s)
+                self._exchange_group(g, epoch)
         if self.tr.engine is not None:
             self.tr.engine.param_ready = self.param_ready
         self.epoch = epoch
         return ok
+
+    def _exchange_group(self, g: int, epoch: int) -> None:
+        """On the comm stream: push the (possibly unchanged) parameters this rank owns in forward group ``g``
+        into every peer's buffer with posted NVLink stores, flag each peer, wait for the other owners'
+        flags of the group, refresh the group's bf16 shadows locally and record the group's event; the
+        engine's forward waits for that event just before its first kernel that reads group ``g``. Every
+        rank's reduce of the last bucket waited for all ranks' last packs, so no peer still reads the
+        values being overwritten; pushes only touch a peer's non-owned regions."""
+        # COMM_CTAS blocks each: these kernels run beside the forward's, and a refresh block that waits for
+        # a flag holds its SM meanwhile
+        self.E.comm_push(self.params_flat, self.param_buf.peers_dev, self.rank, self.push_chunks[g], COMM_CTAS)
+        self.E.comm_signal_peers(self.group_flag_peers[g], self.rank, epoch)
+        self.E.comm_shadow_refresh(self.params_flat, self.push_flags.ptr + 8 * g * self.world, self.world,
+                                   self.rank, epoch, self.gather_segs[g], COMM_CTAS, self.budget)
+        self.group_events[g].record(self.comm_stream)
 
     def param_ready(self, g: int) -> None:
         """Makes the current stream wait until forward group ``g`` of the last exchange has arrived."""
@@ -446,6 +473,7 @@ class P2PGradSync:
     def grad_norm(self) -> float:
         """L2 norm of the step's mean gradient: each rank sums the squares of the reduced gradients it
         owns, one scalar all-reduce adds them up (a collective: every rank calls it on the same steps)."""
+        torch.cuda.current_stream().wait_stream(self.comm_stream)  # the reduces may still run there
         sq = torch.zeros((), device=self.red.device)
         for n in self.owned_names:
             sq = sq + self.red_views[n].float().square().sum()
