@@ -352,6 +352,14 @@ __device__ __forceinline__ float tanh_approx(float x) {
   return y;
 }
 
+// The hardware's approximate square root (one MUFU instruction, no special-case branch); for values that
+// are rounded to bf16 afterwards its error is far below the rounding step.
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float y;
+  asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);

@@ -174,7 +174,7 @@ __device__ __forceinline__ float epi_op(float acc, float aux, const GemmParams& 
     v = fmaxf(v, 0.f);
     v = v * v;
   } else if constexpr (EPI == EPI_RELU2_BWD) {
-    v *= 2.f * sqrtf(fmaxf(aux, 0.f));
+    v *= 2.f * sqrt_approx(fmaxf(aux, 0.f));
   } else if constexpr (EPI == EPI_SOFTCAP) {
     v = p.beta * tanh_approx(v);
   }
