@@ -4,12 +4,13 @@
 //   B: logical [N, K], either K-major (stored [N, K]) or MN-major (stored [K, N]).
 //   bf16 operands, fp32 accumulation in TMEM, 128 x BN x 64 tiles (BN = 128 or 256).
 //
-// Roles (192 threads, one CTA per SM, grid = min(work units, SMs)):
+// Roles (192 threads, or 320 with eight epilogue warps; one CTA per SM, grid = min(work units, SMs)):
 //   warp 0  one elected lane issues TMA loads (128-byte swizzle, no multicast) into a
 //           STAGES-deep ring of shared-memory stages guarded by full/empty mbarriers;
 //   warp 1  allocates TMEM (two BN-column fp32 accumulators) and one elected lane issues
 //           tcgen05.mma (M=128, N=BN, K=16) and tcgen05.commit;
-//   warps 2-5  epilogue. Warp w owns TMEM lanes / tile rows 32*(w%4) .. +31. Per chunk of 128 bytes
+//   warps 2-5 (2-9)  epilogue. Warp w owns TMEM lanes / tile rows 32*(w%4) .. +31 (with eight warps
+//           the two warps of a lane quadrant take one half of the tile's chunks each). Per chunk of 128 bytes
 //           of output row (64 bf16 or 32 fp32 columns) it reads the accumulator with tcgen05.ld,
 //           applies the fused epilogue, writes the 32 x 128 B chunk into a double-buffered, 128-byte
 //           swizzled staging tile in shared memory and issues one TMA store (or TMA reduce-add for
@@ -103,21 +104,27 @@ constexpr uint64_t kWaitBudgetNs = 2000000000ull;
 // CG = 2: a CTA pair runs one 256-row tile (cta_group::2); each CTA loads its 128 rows of A and half of
 // B's BN columns, so a stage is 32 KB instead of 48 and the pair reads a third less operand data per
 // output than two single CTAs.
+// EW: epilogue warps. A CTA pair with an aux input runs eight, two per TMEM lane quadrant, each taking
+// half of a tile's chunks: with one warp per SM sub-partition the aux epilogues were issue-bound (every
+// TMEM load, aux wait and store of the chain exposed), and the pair's smaller stages leave room for the
+// second set of staging buffers.
 template <int BN, bool AUX, int CG = 1>
 struct GemmCfg {
-  static constexpr int STAGES = CG == 2 ? (AUX ? 4 : 6) : (AUX ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6));
-  // staging buffers per epilogue warp; with an aux input the ring holds the aux loads three chunks
+  static constexpr int EW = (AUX && CG == 2) ? 8 : 4;
+  static constexpr int THREADS = 64 + 32 * EW;
+  static constexpr int STAGES = CG == 2 ? (AUX ? 3 : 6) : (AUX ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6));
+  // staging buffers per epilogue warp; with an aux input the ring holds the aux loads NBUF - 2 chunks
   // ahead plus the latest chunk's store, so a prefetch never waits for the store it follows
-  static constexpr int NBUF = AUX ? 5 : 2;
+  static constexpr int NBUF = AUX ? (EW == 8 ? 4 : 5) : 2;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = (BN / CG) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int EPI_BYTES = 4 * NBUF * CHUNK_BYTES;
+  static constexpr int EPI_BYTES = EW * NBUF * CHUNK_BYTES;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024 /*align*/;
   static_assert(SMEM <= 232448, "shared memory per CTA");
-  static_assert((2 * STAGES + 5 + 4 * NBUF) * 8 + 8 <= BAR_BYTES, "barrier region");
+  static_assert((2 * STAGES + 5 + EW * NBUF) * 8 + 8 <= BAR_BYTES, "barrier region");
 };
 
 constexpr bool epi_f32(int e) { return e == EPI_F32 || e == EPI_ATOMIC_F32; }
@@ -182,7 +189,7 @@ __device__ __forceinline__ float epi_op(float acc, float aux, const GemmParams& 
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI, bool AUX, int CG>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GemmCfg<BN, AUX, CG>::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, GemmParams p) {
   static_assert(!AUX || epi_reads_aux(EPI), "aux ring for an epilogue without aux");
@@ -190,6 +197,8 @@ __global__ void __launch_bounds__(192, 1)
   using Cfg = GemmCfg<BN, AUX, CG>;
   constexpr int NBUF = Cfg::NBUF;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int EW = Cfg::EW;
+  static_assert(EW == 4 || (EPI != EPI_QKV_ROPE && EPI != EPI_SOFTCAP_CE), "per-row epilogues use 4 warps");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -201,8 +210,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tfull_bar = bars + 2 * STAGES;
   uint64_t* tempty_bar = bars + 2 * STAGES + 2;
   uint64_t* drain_bar = bars + 2 * STAGES + 4;
-  uint64_t* aux_bar = bars + 2 * STAGES + 5;  // [4][NBUF]: per epilogue warp, one per staging buffer
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5 + 4 * NBUF);
+  uint64_t* aux_bar = bars + 2 * STAGES + 5;  // [EW][NBUF]: per epilogue warp, one per staging buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5 + EW * NBUF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -225,10 +234,10 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128 * CG);  // every epilogue thread of the pair releases the leader's
+      mbar_init(&tempty_bar[a], 32 * EW * CG);  // every epilogue thread of the pair releases the leader's
     }
     mbar_init(drain_bar, 1);
-    for (int w = 0; w < 4 * NBUF; ++w) mbar_init(&aux_bar[w], 1);
+    for (int w = 0; w < EW * NBUF; ++w) mbar_init(&aux_bar[w], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -374,17 +383,24 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(drain_bar, 0, 100000000ull, nullptr);
     }
   } else {
-    // ---------------------------------------------------------------- epilogue warps 2..5
+    // ---------------------------------------------------------------- epilogue warps 2..EW+1
+    // a warp reads TMEM lanes 32 (warp % 4) .. + 31; with eight warps the two of a quadrant split the
+    // tile's chunks into halves (eh = 0, 1)
+    const int ew = warp - 2;
     const int wq = warp & 3;
+    const int eh = ew >> 2;
     const int lane = lane_id();
     const bool leader = lane == 0;
-    uint8_t* ebuf = sE + wq * NBUF * CHUNK_BYTES;
-    uint64_t* xbar = &aux_bar[wq * NBUF];
+    uint8_t* ebuf = sE + ew * NBUF * CHUNK_BYTES;
+    uint64_t* xbar = &aux_bar[ew * NBUF];
     constexpr int COLS = epi_f32(EPI) ? 32 : 64;  // columns per 128-byte chunk
     constexpr int CPT = BN / COLS;                 // chunks per tile
+    constexpr int CPW = CPT / (EW / 4);            // chunks per tile of one warp
+    static_assert(CPW * (EW / 4) == CPT, "chunks split evenly between a quadrant's warps");
+    const int c_lo = eh * CPW;                     // this warp's first chunk of every tile
     int nchunk = 0;                                // chunks this warp has processed (ring position)
     // aux prefetch cursor (AUX only): next chunk to load, its work unit and chunk within the tile
-    int pchunk = 0, pu = unit0, pc = 0;
+    int pchunk = 0, pu = unit0, pc = c_lo;
     auto prefetch = [&](int upto) {
       while (pchunk < upto && pu < total) {
         if (pchunk >= NBUF) {
@@ -401,8 +417,8 @@ __global__ void __launch_bounds__(192, 1)
           tma_load_3d(&tmX, &xbar[slot], ebuf + slot * CHUNK_BYTES, n * BN + pc * COLS, row_base(m) + wq * 32, b);
         }
         ++pchunk;
-        if (++pc == CPT) {
-          pc = 0;
+        if (++pc == c_lo + CPW) {
+          pc = c_lo;
           pu += ustride;
         }
       }
@@ -540,7 +556,7 @@ __global__ void __launch_bounds__(192, 1)
         ce_t = mrow < p.M ? __ldg(p.ce.targets + mrow) : -1;
       }
 #pragma unroll 1
-      for (int c = 0; c < CPT; ++c, ++nchunk) {
+      for (int c = c_lo; c < c_lo + CPW; ++c, ++nchunk) {
         const int slot = nchunk % NBUF;
         uint8_t* buf = ebuf + slot * CHUNK_BYTES;
         const int col0 = n * BN + c * COLS;
@@ -608,7 +624,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         fence_async_smem();
         __syncwarp();
-        if (c == CPT - 1) {
+        if (c == c_lo + CPW - 1) {
           // accumulator fully read: hand it back to the MMA warp
           tc_fence_before();
           release_acc(acc);
@@ -691,10 +707,10 @@ void launch_cg(const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
     attr = true;
   }
   if constexpr (CG == 1) {
-    k<<<grid, 192, Cfg::SMEM, st>>>(mp.a, mp.b, mp.c, mp.x, p);
+    k<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(mp.a, mp.b, mp.c, mp.x, p);
   } else {
     cudaLaunchConfig_t cfg = {};
-    cfg.blockDim = dim3(192);
+    cfg.blockDim = dim3(Cfg::THREADS);
     cfg.dynamicSmemBytes = Cfg::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
