@@ -123,6 +123,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"],
                     help="gradient/parameter exchange for N > 1: in-kernel NVLink (p2p) or NCCL")
+    ap.add_argument("--gemm-pair", type=int, default=None, choices=[0, 1, 2],
+                    help="256-column GEMMs on CTA pairs: 0 none, 1 without an aux input (default), 2 all")
     ap.add_argument("overrides", nargs="*")
     args = ap.parse_args()
     rank, world, local = _rank_world()
@@ -153,6 +155,9 @@ def main():
     if args.impl == "ours":
         cfg.impl = "cuda"
         cfg.comm = args.comm
+        if args.gemm_pair is not None:
+            from bitresearch_b200.ops._ext import ext
+            ext().gemm_set_pair(args.gemm_pair)
         tr = Trainer(cfg, device=device, log=lambda m: None)
         tr.initialize()
         accum = tr.grad_accum
