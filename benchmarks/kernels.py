@@ -195,7 +195,7 @@ def main():
         wb = w.to(torch.bfloat16)
         tgt = torch.randint(0, V, (M,), device=dev, dtype=torch.int32)
         G = torch.empty(M, V, **bf)
-        part = torch.empty((V + 255) // 256, M, device=dev)
+        part = torch.empty(2 * ((V + 255) // 256), M, device=dev)
         zt, rs, cf = (torch.empty(M, device=dev) for _ in range(3))
         nats = torch.empty(M, device=dev)
         ls = torch.zeros(1, device=dev)

@@ -137,7 +137,7 @@ class FusedGPTEngine:
             "h": [torch.empty(M, self.F, **bf) for _ in range(L)],
             "rstdf": torch.empty(M, **f32), "xf": torch.empty(M, D, **bf),
             # fused head: G (dlogits up to a per-row scale and the target column), CE statistics
-            "G": torch.empty(M, self.V, **bf), "ce_part": torch.empty((self.V + 255) // 256, M, **f32),
+            "G": torch.empty(M, self.V, **bf), "ce_part": torch.empty(2 * ((self.V + 255) // 256), M, **f32),
             "zt": torch.empty(M, **f32), "rowscale": torch.empty(M, **f32),
             "xs_head": torch.empty(M, D, **bf), "nats": torch.empty(M, **f32),
             "loss": torch.zeros(1, **f32),

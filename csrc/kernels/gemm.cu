@@ -75,7 +75,7 @@ struct QkvRope {
 // target column's exact fp32 gradient; the logits themselves are never written.
 struct CeHead {
   const int* targets;  // [M] (rows whose target is outside [0, N) are masked)
-  float* partial;      // [n_tiles][M]
+  float* partial;      // [2 n_tiles][M]: per 256-column tile, the sums over its two halves
   float* zt;           // [M]
   int store;           // 0: statistics only (evaluation)
 };
@@ -104,15 +104,18 @@ constexpr uint64_t kWaitBudgetNs = 2000000000ull;
 // CG = 2: a CTA pair runs one 256-row tile (cta_group::2); each CTA loads its 128 rows of A and half of
 // B's BN columns, so a stage is 32 KB instead of 48 and the pair reads a third less operand data per
 // output than two single CTAs.
-// EW: epilogue warps. A CTA pair with an aux input runs eight, two per TMEM lane quadrant, each taking
-// half of a tile's chunks: with one warp per SM sub-partition the aux epilogues were issue-bound (every
-// TMEM load, aux wait and store of the chain exposed), and the pair's smaller stages leave room for the
-// second set of staging buffers.
-template <int BN, bool AUX, int CG = 1>
+// EW: epilogue warps. A CTA pair with an aux input, or computing the cross-entropy statistics, runs
+// eight, two per TMEM lane quadrant, each taking half of a tile's chunks: with one warp per SM
+// sub-partition those epilogues were issue-bound (every TMEM load, aux wait, MUFU op and store of the
+// chain exposed), and the pair's smaller stages leave room for the second set of staging buffers.
+constexpr int epi_warps(int epi, bool aux, int cg) { return cg == 2 && (aux || epi == EPI_SOFTCAP_CE) ? 8 : 4; }
+
+template <int BN, bool AUX, int CG = 1, int EW_ = 4>
 struct GemmCfg {
-  static constexpr int EW = (AUX && CG == 2) ? 8 : 4;
+  static constexpr int EW = EW_;
   static constexpr int THREADS = 64 + 32 * EW;
-  static constexpr int STAGES = CG == 2 ? (AUX ? 3 : 6) : (AUX ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6));
+  static constexpr int STAGES =
+      CG == 2 ? (AUX ? 3 : (EW == 8 ? 5 : 6)) : (AUX ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6));
   // staging buffers per epilogue warp; with an aux input the ring holds the aux loads NBUF - 2 chunks
   // ahead plus the latest chunk's store, so a prefetch never waits for the store it follows
   static constexpr int NBUF = AUX ? (EW == 8 ? 4 : 5) : 2;
@@ -189,16 +192,16 @@ __device__ __forceinline__ float epi_op(float acc, float aux, const GemmParams& 
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI, bool AUX, int CG>
-__global__ void __launch_bounds__(GemmCfg<BN, AUX, CG>::THREADS, 1)
+__global__ void __launch_bounds__(GemmCfg<BN, AUX, CG, epi_warps(EPI, AUX, CG)>::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, GemmParams p) {
   static_assert(!AUX || epi_reads_aux(EPI), "aux ring for an epilogue without aux");
   static_assert(CG == 1 || (CG == 2 && BN == 256), "CTA pairs run 256-column tiles");
-  using Cfg = GemmCfg<BN, AUX, CG>;
+  using Cfg = GemmCfg<BN, AUX, CG, epi_warps(EPI, AUX, CG)>;
   constexpr int NBUF = Cfg::NBUF;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int EW = Cfg::EW;
-  static_assert(EW == 4 || (EPI != EPI_QKV_ROPE && EPI != EPI_SOFTCAP_CE), "per-row epilogues use 4 warps");
+  static_assert(EW == 4 || EPI != EPI_QKV_ROPE, "the QKV epilogue uses 4 warps");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -638,10 +641,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, AUX, CG>::THREADS, 1)
         }
       }
       if constexpr (EPI == EPI_SOFTCAP_CE) {
+        // two partial rows per 256-column tile, one per half of its chunks (with four epilogue warps
+        // the second holds 0), so the layout does not depend on the launch form
         const int mrow = row0 + lane;
         if (ok && mrow < p.M) {
-          p.ce.partial[(int64_t)n * p.M + mrow] = ce_sum;
-          if (ce_t >= n * BN && ce_t < n * BN + BN) p.ce.zt[mrow] = ce_zt;
+          const int cbeg = n * BN + c_lo * COLS;
+          p.ce.partial[(int64_t)(2 * n + eh) * p.M + mrow] = ce_sum;
+          if constexpr (EW == 4) p.ce.partial[(int64_t)(2 * n + 1) * p.M + mrow] = 0.f;
+          if (ce_t >= cbeg && ce_t < cbeg + CPW * COLS) p.ce.zt[mrow] = ce_zt;
         }
       }
     }
@@ -704,7 +711,7 @@ int persistent_grid(int64_t units, int cg) {
 template <int BN, bool AMN, bool BMN, int EPI, bool AUX, int CG>
 void launch_cg(const Maps& mp, const GemmParams& p, int grid, cudaStream_t st) {
   auto k = gemm_kernel<BN, AMN, BMN, EPI, AUX, CG>;
-  using Cfg = GemmCfg<BN, AUX, CG>;
+  using Cfg = GemmCfg<BN, AUX, CG, epi_warps(EPI, AUX, CG)>;
   static bool attr = false;
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
@@ -873,7 +880,7 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
 
 // The lm_head GEMM fused with the softcapped cross-entropy statistics (EPI_SOFTCAP_CE, see CeHead):
 // x [M, K] bf16 rows, w [N, K] bf16 rows (the [vocab, dim] table), g [M, N] bf16 (written when store),
-// targets int32 [M], partial fp32 [ceil(N/256), M], zt fp32 [M].
+// targets int32 [M], partial fp32 [2 ceil(N/256), M], zt fp32 [M].
 void gemm_softcap_ce(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& g, const torch::Tensor& targets,
                      torch::Tensor& partial, torch::Tensor& zt, double cap, bool store) {
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && g.scalar_type() == at::kBFloat16,
@@ -884,8 +891,8 @@ void gemm_softcap_ce(const torch::Tensor& x, const torch::Tensor& w, torch::Tens
   TORCH_CHECK(targets.scalar_type() == at::kInt && targets.is_contiguous() && targets.numel() == M,
               "gemm_softcap_ce: int32 targets [M]");
   const int64_t n_tiles = (N + 255) / 256;
-  TORCH_CHECK(partial.scalar_type() == at::kFloat && partial.is_contiguous() && partial.numel() >= n_tiles * M,
-              "gemm_softcap_ce: partial fp32 [ceil(N/256), M]");
+  TORCH_CHECK(partial.scalar_type() == at::kFloat && partial.is_contiguous() && partial.numel() >= 2 * n_tiles * M,
+              "gemm_softcap_ce: partial fp32 [2 ceil(N/256), M]");
   TORCH_CHECK(zt.scalar_type() == at::kFloat && zt.numel() >= M, "gemm_softcap_ce: zt fp32 [M]");
   TORCH_CHECK(cap > 0, "gemm_softcap_ce: cap > 0");
   c10::cuda::CUDAGuard guard(x.device());

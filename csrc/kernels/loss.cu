@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict_
 // bf16, so both backward GEMMs include it and no scatter is needed; with `dw` (the exact fp32 form) the
 // gradient is scattered into dW here and added to dx by rms_bwd's head form.
 // Finishes the cross-entropy of the fused lm_head epilogue (EPI_SOFTCAP_CE in gemm.cu), whose GEMM wrote
-// per (256-column tile, row) partial sums of e_j = exp(z_j - cap), the target's softcapped logit z_t and
+// per (256-column tile half, row) partial sums of e_j = exp(z_j - cap), the target's softcapped logit z_t and
 // G = e (1 - (z/cap)^2) with G_t = 0. Per row, with S = sum_j e_j:
 //   lse = cap + log S, p_t = exp(z_t - lse), nats = -log(p_t + 1e-10)      (the reference's eps form)
 //   dz_j = r (p_j - [j == t]) c'_j, r = scale p_t / (p_t + 1e-10), c' = 1 - (z/cap)^2
@@ -211,10 +211,10 @@ void ce_finalize(const torch::Tensor& partial, const torch::Tensor& zt, const to
                  c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> xs, c10::optional<torch::Tensor> dw,
                  c10::optional<torch::Tensor> g) {
   const int64_t M = targets.numel();
-  const int64_t n_tiles = (V + 255) / 256;
+  const int64_t n_tiles = 2 * ((V + 255) / 256);  // two partial rows per 256-column tile
   TORCH_CHECK(targets.scalar_type() == at::kInt && targets.is_contiguous(), "ce_finalize: int32 targets");
   TORCH_CHECK(partial.scalar_type() == at::kFloat && partial.is_contiguous() && partial.numel() >= n_tiles * M,
-              "ce_finalize: partial fp32 [ceil(V/256), M]");
+              "ce_finalize: partial fp32 [2 ceil(V/256), M]");
   TORCH_CHECK(zt.scalar_type() == at::kFloat && zt.numel() >= M, "ce_finalize: zt fp32 [M]");
   auto f32 = [&](const c10::optional<torch::Tensor>& t, const char* name) -> float* {
     if (!t.has_value() || !t->defined()) return nullptr;

@@ -15,9 +15,19 @@ def _assert(a, b, tol, what):
     assert err <= tol * scale, (what, err, scale)
 
 
+@pytest.fixture(params=[1, 0], ids=["pairs", "single"])
+def pair(request, cuda):
+    """1: the default CTA-pair policy (the head GEMM on pairs with eight epilogue warps); 0: single CTAs
+    with four."""
+    from bitresearch_b200.ops._ext import ext
+    ext().gemm_set_pair(request.param)
+    yield request.param
+    ext().gemm_set_pair(1)
+
+
 @pytest.mark.parametrize("form", ["patch", "scatter"])
 @pytest.mark.parametrize("V", [1000, 8192, 65536])
-def test_fused_head_matches_fp32_reference(cuda, V, form):
+def test_fused_head_matches_fp32_reference(cuda, V, form, pair):
     """form "patch" (the engine's): ce_finalize writes the target column's gradient into G; "scatter": it
     scatters it into dW in fp32 and rms_bwd adds it to dx."""
     from bitresearch_b200.ops import gemm
@@ -38,7 +48,7 @@ def test_fused_head_matches_fp32_reference(cuda, V, form):
     E.rms_fwd(h, xf, rstd)
     nt = (V + 255) // 256
     G = torch.empty(M, V, dtype=torch.bfloat16, device=cuda)
-    part = torch.empty(nt, M, device=cuda)
+    part = torch.empty(2 * nt, M, device=cuda)
     zt = torch.empty(M, device=cuda)
     rs = torch.empty(M, device=cuda)
     cf = torch.empty(M, device=cuda)

@@ -51,7 +51,7 @@ def test_cross_entropy_masks_and_reports_a_target_outside_the_vocabulary(cuda):
     tgt[5] = V + 3
     tgt[6] = -1
     G = torch.empty(M, V, dtype=torch.bfloat16, device=cuda)
-    part = torch.empty((V + 255) // 256, M, device=cuda)
+    part = torch.empty(2 * ((V + 255) // 256), M, device=cuda)
     zt = torch.empty(M, device=cuda)
     rs, cf = torch.empty(M, device=cuda), torch.empty(M, device=cuda)
     nats = torch.empty(M, device=cuda)
