@@ -79,14 +79,14 @@ class P2PBench:
 
     def setup(self, n: int, chunk: int = 1 << 15):
         """Ownership of an n-element bucket: rank r owns [r*n/N, (r+1)*n/N)."""
-        from bitresearch_b200.parallel.comm import chunk_ranges
+        from bitresearch_b200.parallel.comm import chunk_ranges, interleave_by_owner
         W, r = self.world, self.rank
         per = n // W
         self.n, self.per = n, per
         rows = [(o, ln) for o, ln, _ in chunk_ranges(r * per, per, size=chunk)]
         self.chunks = torch.tensor(rows, dtype=torch.int64, device="cuda").view(-1, 2)
         push = [(o * per + s, ln, o, s) for o in range(W) for _, ln, s in chunk_ranges(o * per, per, size=chunk)]
-        self.push_tab = torch.tensor(push, dtype=torch.int64, device="cuda").view(-1, 4)
+        self.push_tab = torch.tensor(interleave_by_owner(push, r, W), dtype=torch.int64, device="cuda").view(-1, 4)
         self.own_tab = torch.tensor([t for t in push if t[2] == r], dtype=torch.int64, device="cuda").view(-1, 4)
         segs = []
         for o in range(W):

@@ -117,6 +117,25 @@ def assign_owners(specs, world: int) -> dict[str, int]:
     return owner
 
 
+def interleave_by_owner(rows, rank: int, world: int, owner_col: int = 2):
+    """Orders push rows round-robin over their destination owners, starting with owner rank + 1: the
+    blocks of a push kernel take rows in order, so at any moment each rank writes to every peer and
+    every rank receives from all of them (in table order, all ranks would write to the first owner at
+    once and leave the other links idle). Rows keep their order within an owner; this rank's own rows
+    (local stores) come last in each round."""
+    by_owner: dict[int, list] = {}
+    for row in rows:
+        by_owner.setdefault(int(row[owner_col]), []).append(row)
+    order = [(rank + 1 + k) % world for k in range(world)]
+    queues = [by_owner.get(o, []) for o in order]
+    out = []
+    for i in range(max((len(q) for q in queues), default=0)):
+        for q in queues:
+            if i < len(q):
+                out.append(q[i])
+    return out
+
+
 def chunk_ranges(off: int, numel: int, start_in_param: int = 0, size: int = CHUNK):
     out = []
     s = 0
@@ -201,6 +220,7 @@ class P2PGradSync:
                     rows.append(row)
                     if self.owner[n] == self.rank:
                         mine.append(row)
+            rows = interleave_by_owner(rows, self.rank, self.world)
             self.push_tables.append(torch.tensor(rows, dtype=torch.int64, device=dev).view(-1, 4))
             self.own_tables.append(torch.tensor(mine, dtype=torch.int64, device=dev).view(-1, 4))
         # device skip word (the optimizer kernels read it) and its pinned host copy, read one step late

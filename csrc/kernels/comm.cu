@@ -301,8 +301,9 @@ __global__ void __launch_bounds__(256) push_kernel(const float* __restrict__ src
         const int64_t j = j0 + u * step;
         if (j < n4) v[u] = *reinterpret_cast<const float4*>(s + j);
       }
-      for (int p = 0; p < npeers; ++p) {
-        if (p == me) continue;
+      // peers in order from me + 1, so the ranks start on different peers
+      for (int k = 1; k < npeers; ++k) {
+        const int p = me + k < npeers ? me + k : me + k - npeers;
         float* d = peers[p] + ch.off;
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -313,8 +314,7 @@ __global__ void __launch_bounds__(256) push_kernel(const float* __restrict__ src
     }
     for (int64_t j = n4 + threadIdx.x; j < ch.len; j += blockDim.x) {
       const float x = s[j];
-      for (int p = 0; p < npeers; ++p)
-        if (p != me) peers[p][ch.off + j] = x;
+      for (int k = 1; k < npeers; ++k) peers[me + k < npeers ? me + k : me + k - npeers][ch.off + j] = x;
     }
   }
 }

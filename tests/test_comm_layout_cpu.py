@@ -5,7 +5,8 @@ import pytest
 
 from bitresearch_b200.config import preset
 from bitresearch_b200.models.gpt import GPT
-from bitresearch_b200.parallel.comm import ALIGN, assign_owners, bucket_order, chunk_ranges, flat_layout
+from bitresearch_b200.parallel.comm import (ALIGN, assign_owners, bucket_order, chunk_ranges, flat_layout,
+                                             interleave_by_owner)
 
 
 def _specs(name="d512", **model):
@@ -65,3 +66,19 @@ def test_chunk_ranges_cover_exactly():
         assert all(0 < ln <= 65536 for _, ln, _ in ch)
         assert all(a[0] + a[1] == b[0] and a[2] + a[1] == b[2] for a, b in zip(ch, ch[1:]))
         assert ch[0][2] == 7
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_push_rows_interleave_owners_from_the_next_rank(world):
+    """Every row kept once, order within an owner kept, each round visits the owners from rank + 1 on
+    (this rank's own rows last), so the ranks start on different peers."""
+    rows = [(10 * o + i, 1, o, i) for o in range(world) for i in range(3 + o)]  # uneven shares
+    for rank in range(world):
+        out = interleave_by_owner(rows, rank, world)
+        assert sorted(out) == sorted(rows)
+        for o in range(world):
+            assert [r for r in out if r[2] == o] == [r for r in rows if r[2] == o]
+        first = [r[2] for r in out[:world]]
+        assert first == [(rank + 1 + k) % world for k in range(world)]
+    starts = {interleave_by_owner(rows, rank, world)[0][2] for rank in range(world)}
+    assert len(starts) == world
