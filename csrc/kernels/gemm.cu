@@ -581,6 +581,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, AUX, CG, epi_warps(EPI, AUX, CG)>:
           }
         }
         uint8_t* myrow = buf;  // row `lane` of this warp's 32-row chunk
+        // EPI_SOFTCAP_CE: a chunk inside [0, N) holding no lane's target column (most of them) skips the
+        // per-element bounds and target selects
+        bool ce_plain = false;
+        if constexpr (EPI == EPI_SOFTCAP_CE)
+          ce_plain = col0 + COLS <= p.N && !__any_sync(0xffffffffu, ce_t >= col0 && ce_t < col0 + COLS);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {  // eight 16-byte chunks per 128-byte row
           uint4* slotp = reinterpret_cast<uint4*>(myrow + swz_off(lane, q));
@@ -588,6 +593,22 @@ __global__ void __launch_bounds__(GemmCfg<BN, AUX, CG, epi_warps(EPI, AUX, CG)>:
             // z = cap tanh(acc/cap); e = exp(z - cap) = 2^((th - 1) cap log2(e)); G = e (1 - th^2)
             const float k2 = p.beta * 1.4426950408889634f;
             uint32_t os[4];
+            if (ce_plain) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float g[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const float th = tanh_approx(__uint_as_float(r[8 * q + 2 * j + h]) * p.alpha);
+                  const float e = exp2f(fmaf(th, k2, -k2));
+                  ce_sum += e;
+                  g[h] = e * fmaf(-th, th, 1.f);
+                }
+                os[j] = pack_bf16(g[0], g[1]);
+              }
+              *slotp = make_uint4(os[0], os[1], os[2], os[3]);
+              continue;
+            }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               float g[2];
