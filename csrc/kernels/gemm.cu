@@ -177,14 +177,16 @@ __device__ __forceinline__ int swz_off(int r, int c) { return r * 128 + ((c ^ (r
 // Epilogue math on 8 values (one 16-byte bf16 chunk or two fp32 chunks), aux values already unpacked.
 template <int EPI>
 __device__ __forceinline__ float epi_op(float acc, float aux, const GemmParams& p) {
+  if constexpr (EPI == EPI_RELU2_BWD) {
+    // aux = h = relu(u)^2 >= 0, so 2 relu(u) = 2 sqrt(h); (2 alpha) is loop-invariant
+    return (acc * (2.f * p.alpha)) * sqrt_approx(aux);
+  }
   float v = acc * p.alpha;
   if constexpr (EPI == EPI_BF16 || EPI == EPI_F32) {
     v += p.beta * aux;
   } else if constexpr (EPI == EPI_RELU2) {
     v = fmaxf(v, 0.f);
     v = v * v;
-  } else if constexpr (EPI == EPI_RELU2_BWD) {
-    v *= 2.f * sqrt_approx(fmaxf(aux, 0.f));
   } else if constexpr (EPI == EPI_SOFTCAP) {
     v = p.beta * tanh_approx(v);
   }
