@@ -108,9 +108,7 @@ constexpr uint64_t kWaitBudgetNs = 2000000000ull;
 // eight, two per TMEM lane quadrant, each taking half of a tile's chunks: with one warp per SM
 // sub-partition those epilogues were issue-bound (every TMEM load, aux wait, MUFU op and store of the
 // chain exposed), and the pair's smaller stages leave room for the second set of staging buffers.
-constexpr int epi_warps(int epi, bool aux, int cg) {
-  return cg == 2 && (aux || epi == EPI_SOFTCAP_CE || epi == EPI_QKV_ROPE) ? 8 : 4;
-}
+constexpr int epi_warps(int epi, bool aux, int cg) { return cg == 2 && (aux || epi == EPI_SOFTCAP_CE) ? 8 : 4; }
 
 template <int BN, bool AUX, int CG = 1, int EW_ = 4>
 struct GemmCfg {
@@ -205,6 +203,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, AUX, CG, epi_warps(EPI, AUX, CG)>:
   constexpr int NBUF = Cfg::NBUF;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int EW = Cfg::EW;
+  static_assert(EW == 4 || EPI != EPI_QKV_ROPE, "the QKV epilogue uses 4 warps");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -460,139 +459,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, AUX, CG, epi_warps(EPI, AUX, CG)>:
       tc_fence_after();
       const int row0 = row_base(m) + wq * 32;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * BN;
-      if constexpr (EPI == EPI_QKV_ROPE && EW == 8) {
-        // eight warps: the warp of half eh takes head 2n + eh of the tile. A q/k head takes two passes over
-        // 16-column blocks (RoPE pairs columns j and 64 + j): the first sums the squares of the rotated
-        // values, the second rotates again, applies the QK-norm and writes bf16 into the two staging
-        // tiles, so a thread holds 32 accumulator values instead of the whole head (the same arithmetic,
-        // in the same order, as the four-warp form below). A v head gets the value-embedding add.
-        const QkvRope& rp = p.rope;
-        const int mrow = row0 + lane;
-        const bool valid = mrow < p.M;
-        const int64_t msafe = valid ? mrow : 0;
-        const int nqk = rp.H + rp.KV;
-        const int head = n * 2 + eh;
-        const uint32_t hbase = taddr + eh * 128;
-        uint8_t* b0 = ebuf;                // columns 0..63 of the head
-        uint8_t* b1 = ebuf + CHUNK_BYTES;  // columns 64..127
-        if (leader) bulk_wait_read_n(0);   // this warp's stores of its previous tile have read both tiles
-        __syncwarp();
-// 16 values y[0..15] as bf16 at columns 16 jb .. 16 jb + 15 of this lane's row of a staging tile
-#define BR_QKV_PUT16(buf, jb, y)                                                                               \
-  do {                                                                                                         \
-    *reinterpret_cast<uint4*>((buf) + swz_off(lane, 2 * (jb))) =                                               \
-        make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7])); \
-    *reinterpret_cast<uint4*>((buf) + swz_off(lane, 2 * (jb) + 1)) = make_uint4(                               \
-        pack_bf16(y[8], y[9]), pack_bf16(y[10], y[11]), pack_bf16(y[12], y[13]), pack_bf16(y[14], y[15]));     \
-  } while (0)
-        if (head < nqk) {
-          const float4* cr = reinterpret_cast<const float4*>(rp.cosT + (msafe % rp.T) * 64);
-          const float4* sr = reinterpret_cast<const float4*>(rp.sinT + (msafe % rp.T) * 64);
-          // pass 1: sum of squares of the rotated values
-          float ss = 0.f;
-#pragma unroll 1
-          for (int jb = 0; jb < 4; ++jb) {
-            uint32_t u1[16], u2[16];
-            tmem_ld16(hbase + 16 * jb, u1);
-            tmem_ld16(hbase + 64 + 16 * jb, u2);
-            tmem_ld_wait();
-#pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) {
-              const float4 c4 = __ldg(cr + 4 * jb + k4), s4 = __ldg(sr + 4 * jb + k4);
-              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float x1 = __uint_as_float(u1[4 * k4 + k]), x2 = __uint_as_float(u2[4 * k4 + k]);
-                const float y1 = x1 * cc[k] + x2 * sn[k], y2 = x2 * cc[k] - x1 * sn[k];
-                ss = fmaf(y1, y1, fmaf(y2, y2, ss));
-              }
-            }
-          }
-          const float rn = rsqrtf(ss * (1.f / 128.f) + 1e-5f);
-          // pass 2: rotate again, normalise, bf16 into the staging tiles
-#pragma unroll 1
-          for (int jb = 0; jb < 4; ++jb) {
-            uint32_t u1[16], u2[16];
-            tmem_ld16(hbase + 16 * jb, u1);
-            tmem_ld16(hbase + 64 + 16 * jb, u2);
-            tmem_ld_wait();
-            float y1[16], y2[16];
-#pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) {
-              const float4 c4 = __ldg(cr + 4 * jb + k4), s4 = __ldg(sr + 4 * jb + k4);
-              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const int i = 4 * k4 + k;
-                const float x1 = __uint_as_float(u1[i]), x2 = __uint_as_float(u2[i]);
-                y1[i] = (x1 * cc[k] + x2 * sn[k]) * rn;
-                y2[i] = (x2 * cc[k] - x1 * sn[k]) * rn;
-              }
-            }
-            BR_QKV_PUT16(b0, jb, y1);
-            BR_QKV_PUT16(b1, jb, y2);
-          }
-          if (valid) {
-            if (head < rp.H) rp.rq[(int64_t)mrow * rp.H + head] = rn;
-            else rp.rk[(int64_t)mrow * rp.KV + (head - rp.H)] = rn;
-          }
-        } else {
-          const int kvh = head - nqk;
-          const bool use_ve =
-              rp.ve != nullptr && index_ok(__ldg(rp.idx + msafe), rp.V, valid ? p.status : nullptr);
-          float g = 0.f;
-          const float4* e = nullptr;
-          if (use_ve) {
-            const float4* cz = reinterpret_cast<const float4*>(rp.cur + msafe * rp.ld_cur);
-            float z = 0.f;
-#pragma unroll
-            for (int c4 = 0; c4 < 8; ++c4) {
-              const float4 cv = __ldg(cz + c4);
-              z = fmaf(cv.x, __ldg(rp.wg + (4 * c4 + 0) * rp.KV + kvh), z);
-              z = fmaf(cv.y, __ldg(rp.wg + (4 * c4 + 1) * rp.KV + kvh), z);
-              z = fmaf(cv.z, __ldg(rp.wg + (4 * c4 + 2) * rp.KV + kvh), z);
-              z = fmaf(cv.w, __ldg(rp.wg + (4 * c4 + 3) * rp.KV + kvh), z);
-            }
-            g = 2.f / (1.f + __expf(-z));
-            e = reinterpret_cast<const float4*>(rp.ve + (int64_t)__ldg(rp.idx + msafe) * (rp.KV * 128) + kvh * 128);
-            if (valid) rp.gate[(int64_t)mrow * rp.KV + kvh] = g;
-          }
-#pragma unroll 1
-          for (int jb = 0; jb < 8; ++jb) {
-            uint32_t u[16];
-            tmem_ld16(hbase + 16 * jb, u);
-            tmem_ld_wait();
-            float y[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) y[i] = __uint_as_float(u[i]);
-            if (use_ve) {
-#pragma unroll
-              for (int d4 = 0; d4 < 4; ++d4) {
-                const float4 ev = __ldg(e + 4 * jb + d4);
-                y[4 * d4 + 0] = fmaf(ev.x, g, y[4 * d4 + 0]);
-                y[4 * d4 + 1] = fmaf(ev.y, g, y[4 * d4 + 1]);
-                y[4 * d4 + 2] = fmaf(ev.z, g, y[4 * d4 + 2]);
-                y[4 * d4 + 3] = fmaf(ev.w, g, y[4 * d4 + 3]);
-              }
-            }
-            if (jb < 4)
-              BR_QKV_PUT16(b0, jb, y);
-            else
-              BR_QKV_PUT16(b1, jb - 4, y);
-          }
-        }
-        tc_fence_before();
-        release_acc(acc);  // this warp's accumulator columns are read
-        fence_async_smem();
-        __syncwarp();
-        if (leader) {
-          tma_store_3d(&tmC, b0, n * BN + eh * 128, row0, b);
-          tma_store_3d(&tmC, b1, n * BN + eh * 128 + 64, row0, b);
-          bulk_commit();
-        }
-#undef BR_QKV_PUT16
-        continue;
-      } else if constexpr (EPI == EPI_QKV_ROPE) {
+      if constexpr (EPI == EPI_QKV_ROPE) {
         // two heads per tile; thread = row. Each head: 128 accumulator columns -> RoPE + QK-norm
         // (q, k heads) or the value-embedding add (v heads) -> two 64-column bf16 chunks.
         const QkvRope& rp = p.rope;
