@@ -971,10 +971,7 @@ void gemm_qkv_rope(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor
   mp.b = bf16_map(w.data_ptr(), N, K, 1, w.stride(0), 0, 64);
   mp.c = out_map(out, M, N, 1, out.stride(0), 0);
   mp.x = mp.c;
-  // single CTAs unless every GEMM is put on pairs: the RoPE + QK-norm epilogue (a whole 128-wide head per
-  // thread) is the tile's critical path, and pairs only shorten the main loop (measured at M = 2^18,
-  // K = 512: 0.493 ms on single CTAs; an eight-warp pair form with a two-pass epilogue took 0.744)
-  const int cg = g_pair == 2 ? pair_mode(256, M) : 1;
+  const int cg = pair_mode(256, M);
   GemmParams p{};
   p.M = (int)M;
   p.N = (int)N;
