@@ -1,6 +1,6 @@
 """Per-kernel timings at the d512 depth-8 production shapes, against library baselines.
 
-  python benchmarks/kernels.py [--tokens 262144] [--json out.json] [--only tags] [--pair on|off|all]
+  python benchmarks/kernels.py [--tokens 262144] [--json out.json] [--only tags|=tag] [--pair on|off|all]
 
 Each kernel is timed with CUDA events on the launching stream after warm-up (median of R repeats);
 inputs of the large shapes exceed the 126 MB L2. FLOP/s and bytes/s are reported as fractions of the
@@ -85,8 +85,8 @@ def main():
     bf = dict(device=dev, dtype=torch.bfloat16)
     sel = args.only.split(",") if args.only else None
 
-    def want(tag):
-        return sel is None or any(s in tag for s in sel)
+    def want(tag):  # a selector matches tags that contain it; "=tag" matches that tag only
+        return sel is None or any(s[1:] == tag if s.startswith("=") else s in tag for s in sel)
 
     # ------------------------------------------------------------------ GEMMs
     shapes = [  # name, (M, K, N), a transposed?, b transposed?, epilogue
