@@ -124,7 +124,7 @@ def main():
     ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"],
                     help="gradient/parameter exchange for N > 1: in-kernel NVLink (p2p) or NCCL")
     ap.add_argument("--gemm-pair", type=int, default=None, choices=[0, 1, 2],
-                    help="256-column GEMMs on CTA pairs: 0 none, 1 the default policy, 2 all")
+                    help="256-column GEMMs on CTA pairs: 0 none, 1 the default policy (all), 2 all")
     ap.add_argument("overrides", nargs="*")
     args = ap.parse_args()
     rank, world, local = _rank_world()

@@ -54,8 +54,8 @@ def main():
     ap.add_argument("--json", default="")
     ap.add_argument("--only", default="")
     ap.add_argument("--pair", default="on", choices=["on", "off", "all"],
-                    help="256-column GEMM tiles on CTA pairs (cta_group::2): on (the default policy: all but "
-                         "aux-input GEMMs with K > 1024), all, or off (single CTAs)")
+                    help="256-column GEMM tiles on CTA pairs (cta_group::2): on / all (the default policy puts "
+                         "every such GEMM on pairs) or off (single CTAs)")
     args = ap.parse_args()
     from bitresearch_b200.ops import gemm
     from bitresearch_b200.ops._ext import check_status, ext

@@ -115,10 +115,10 @@ struct GemmCfg {
   static constexpr int EW = EW_;
   static constexpr int THREADS = 64 + 32 * EW;
   static constexpr int STAGES =
-      CG == 2 ? (AUX ? 3 : (EW == 8 ? 5 : 6)) : (AUX ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6));
+      CG == 2 ? (AUX ? 4 : (EW == 8 ? 5 : 6)) : (AUX ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6));
   // staging buffers per epilogue warp; with an aux input the ring holds the aux loads NBUF - 2 chunks
   // ahead plus the latest chunk's store, so a prefetch never waits for the store it follows
-  static constexpr int NBUF = AUX ? (EW == 8 ? 4 : 5) : 2;
+  static constexpr int NBUF = AUX ? (EW == 8 ? 3 : 5) : 2;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = (BN / CG) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -714,16 +714,12 @@ struct Maps {
 };
 
 // Which 256-column GEMMs with more than one 128-row tile run as CTA pairs (gemm_set_pair, for A/B
-// measurements): 0 none; 1 (the default) all but those with an aux input and K > 1024, whose main loop
-// wants the single CTA's deeper stages more than the pair's eight epilogue warps (measured at
-// M = 2^18: ReLU^2 backward, K = 512, 0.706 -> 0.625 ms on pairs; residual projection, K = 512,
-// 0.25 -> 0.25; MLP projection with residual, K = 2048, 0.52 -> 0.53); 2 all.
+// measurements): 0 none; 1 (the default) and 2 all of them. Measured at M = 2^18 against single CTAs:
+// ReLU^2 backward (aux, K = 512) 0.612 -> 0.579 ms, MLP projection with residual (aux, K = 2048)
+// 0.519 -> 0.493, residual projection (aux, K = 512) 0.245 -> 0.241.
 int g_pair = 1;
 
-int pair_mode(int BN, int64_t M, bool aux = false, int64_t K = 0) {
-  if (BN != 256 || M <= BM || g_pair == 0) return 1;
-  return (g_pair == 2 || !aux || K <= 1024) ? 2 : 1;
-}
+int pair_mode(int BN, int64_t M) { return BN == 256 && M > BM && g_pair != 0 ? 2 : 1; }
 
 // Persistent grid: one CTA (or one CTA pair) per SM (pair), no more than there are work units.
 int persistent_grid(int64_t units, int cg) {
@@ -841,8 +837,7 @@ void gemm_launch(const torch::Tensor& a, bool a_mn, int64_t lda, int64_t bsa, co
   Maps mp;
   mp.a = a_mn ? bf16_map(a.data_ptr(), M, K, batch, lda, bsa, 64) : bf16_map(a.data_ptr(), K, M, batch, lda, bsa, BM);
   // a CTA pair loads half of B's tile columns each
-  const bool has_aux = aux.has_value() && aux->defined();
-  const int cg = pair_mode(BN, M, has_aux, K);
+  const int cg = pair_mode(BN, M);
   mp.b = b_mn ? bf16_map(b.data_ptr(), N, K, batch, ldb, bsb, 64)
               : bf16_map(b.data_ptr(), K, N, batch, ldb, bsb, BN / cg);
   mp.c = out_map(c, M, N, batch, ldc, bsc);
@@ -1015,7 +1010,7 @@ void gemm_qkv_rope(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor
 }
 
 void gemm_set_pair(int64_t mode) {
-  TORCH_CHECK(mode >= 0 && mode <= 2, "gemm_set_pair: 0 (none), 1 (default policy) or 2 (all)");
+  TORCH_CHECK(mode >= 0 && mode <= 2, "gemm_set_pair: 0 (none), 1 (the default policy: all) or 2 (all)");
   g_pair = (int)mode;
 }
 int64_t gemm_pair() { return g_pair; }
