@@ -43,7 +43,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint64_t kBudgetNs = 2000000000ull;
 
 struct FwdParams {
-  int T, H, KV, Dq, Dkv, window;
+  int B, T, H, KV, Dq, Dkv, window;
   float scale_log2;
   __nv_bfloat16* out;
   int64_t ldo;
@@ -81,6 +81,55 @@ __device__ __forceinline__ Band band_of(int q0, int T, int w) {
   return b;
 }
 
+// Persistent, dynamically scheduled: grid = min(work items, SMs). A CTA's producer takes work items (a
+// pair of 128-query tiles, a head, a batch row) from a device counter and hands each to the MMA and
+// softmax warps through a two-slot ring in shared memory, so TMEM, barriers and the K/V rings are set up
+// once per SM, the next item's Q load and first score MMAs overlap the current item's output epilogue,
+// and items of uneven cost (the causal band holds 2 to 18 key tiles per item) balance across SMs as
+// they would under the hardware's CTA scheduling. Ring positions and barrier phases run on across
+// items. q_empty lets the producer reload the Q tiles once the item's last score MMA has completed;
+// o_empty[x] holds query tile x's first PV MMA of an item until the softmax warps have read the previous
+// item's O. The last CTA to finish resets the counter for the next launch (launches of this kernel on
+// one device must not overlap: they share the counter).
+__device__ int g_fwd_sched[2];  // [0] next work item, [1] CTAs finished
+
+struct FwdItem {
+  int h, b, kvh, q0, u_lo, nu;
+  Band bA, bB;
+  bool same_start;
+  // Last user of key tile t among the two query tiles, in MMA issue order: when both tiles start at
+  // the same key tile, B's MMAs on t come after A's; when B starts one tile later, A's come last.
+  __device__ bool last_is_b(int t) const { return same_start ? bB.uses(t) : !bA.uses(t); }
+};
+
+__device__ __forceinline__ FwdItem fwd_item(int item, const FwdParams& p) {
+  const int n_qp = (p.T + 2 * BQ - 1) / (2 * BQ);
+  FwdItem I;
+  const int qp = item % n_qp;
+  I.h = (item / n_qp) % p.H;
+  I.b = item / (n_qp * p.H);
+  I.kvh = I.h / (p.H / p.KV);
+  I.q0 = qp * 2 * BQ;
+  I.bA = band_of(I.q0, p.T, p.window);
+  I.bB = band_of(I.q0 + BQ, p.T, p.window);
+  // key tiles of the item: bA.lo .. last tile of B (or of A when B is past T)
+  I.u_lo = I.bA.lo;
+  const int u_hi = I.bB.n > 0 ? I.bB.lo + I.bB.n - 1 : I.bA.lo + I.bA.n - 1;
+  I.nu = u_hi - I.u_lo + 1;
+  I.same_start = I.bB.n > 0 && I.bB.lo == I.bA.lo;
+  return I;
+}
+
+// Called once by thread 0 of every CTA on its way out: the last one resets the scheduler.
+__device__ __forceinline__ void fwd_sched_exit() {
+  __threadfence();
+  if (atomicAdd(&g_fwd_sched[1], 1) == (int)gridDim.x - 1) {
+    g_fwd_sched[0] = 0;
+    g_fwd_sched[1] = 0;
+    __threadfence();
+  }
+}
+
 __global__ void __launch_bounds__(320, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -95,27 +144,25 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* p_full = bars + 13;  // [2] per query tile
   uint64_t* o_done = bars + 15;  // [2] per query tile
   uint64_t* drain = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* q_empty = bars + 18;
+  uint64_t* o_empty = bars + 19;     // [2] per query tile
+  uint64_t* item_full = bars + 21;   // [2] item ring slots
+  uint64_t* item_empty = bars + 23;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 25);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* item_ring = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [2]
+  static_assert(25 * 8 + 16 <= 256, "forward barrier region");
 
-  const int qp = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int kvh = h / (p.H / p.KV);
-  const int q0 = qp * 2 * BQ;
-  const int w = p.window;
-  const Band bA = band_of(q0, p.T, w), bB = band_of(q0 + BQ, p.T, w);
-  // key tiles of the CTA: bA.lo .. last tile of B (or of A when B is past T)
-  const int u_lo = bA.lo;
-  const int u_hi = bB.n > 0 ? bB.lo + bB.n - 1 : bA.lo + bA.n - 1;
-  const int nu = u_hi - u_lo + 1;
-  // Last user of key tile t among the two query tiles, in MMA issue order: when both tiles start at
-  // the same key tile, B's MMAs on t come after A's; when B starts one tile later, A's come last.
-  const bool same_start = bB.n > 0 && bB.lo == bA.lo;
-  auto last_is_b = [&](int t) -> bool { return same_start ? bB.uses(t) : !bA.uses(t); };
+  const int n_items = ((p.T + 2 * BQ - 1) / (2 * BQ)) * p.H * p.B;
   const int warp = warp_id();
-  if (device_failed(p.status)) return;
+  if (device_failed(p.status)) {
+    if (threadIdx.x == 0) fwd_sched_exit();
+    return;
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < F2_KST; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -128,6 +175,9 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&s_full[x], 1);
       mbar_init(&p_full[x], 128);
       mbar_init(&o_done[x], 1);
+      mbar_init(&o_empty[x], 128);
+      mbar_init(&item_full[x], 1);
+      mbar_init(&item_empty[x], 9);  // the MMA thread and one lane of each softmax warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -146,42 +196,65 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 0) {
     if (elect_one()) {
       tma_prefetch_desc(&tm);
-      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
-      for (int x = 0; x < 2; ++x) {
-        tma_load_3d(&tm, q_full, smem + F2_Q + x * TILE_BYTES, h * HD, q0 + x * BQ, b);
-        tma_load_3d(&tm, q_full, smem + F2_Q + x * TILE_BYTES + ATOM_BYTES, h * HD + 64, q0 + x * BQ, b);
-      }
-      // K runs up to two tiles ahead of V (B's next scores need K[t+1] while A still reads V[t]),
-      // so the two rings are filled in one interleaved order: K0, K1, V0, K2, V1, K3, V2, ...
-      int ik = 0, iv = 0;
+      int ik = 0, iv = 0;  // K and V tiles loaded so far (ring positions)
       bool ok = true;
-      while (ok && (ik < nu || iv < nu)) {
-        const bool do_k = ik < nu && (ik < iv + 2);
-        if (do_k) {
-          const int st = ik % F2_KST;
-          if (!mbar_wait(&k_empty[st], ((ik / F2_KST) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
-            ok = false;
-            break;
-          }
-          const int k0 = (u_lo + ik) * BKV;
-          uint8_t* ks = smem + F2_K + st * TILE_BYTES;
-          mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
-          tma_load_3d(&tm, &k_full[st], ks, p.Dq + kvh * HD, k0, b);
-          tma_load_3d(&tm, &k_full[st], ks + ATOM_BYTES, p.Dq + kvh * HD + 64, k0, b);
-          ++ik;
-        } else {
-          const int st = iv % F2_VST;
-          if (!mbar_wait(&v_empty[st], ((iv / F2_VST) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
-            ok = false;
-            break;
-          }
-          const int k0 = (u_lo + iv) * BKV;
-          uint8_t* vs = smem + F2_V + st * TILE_BYTES;
-          mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
-          tma_load_3d(&tm, &v_full[st], vs, p.Dq + p.Dkv + kvh * HD, k0, b);
-          tma_load_3d(&tm, &v_full[st], vs + ATOM_BYTES, p.Dq + p.Dkv + kvh * HD + 64, k0, b);
-          ++iv;
+      for (int n = 0;; ++n) {
+        // take the next work item and publish it (or the end, -1) to the MMA and softmax warps
+        const int slot = n & 1;
+        if (n >= 2 && !mbar_wait(&item_empty[slot], ((n - 2) >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+          ok = false;
+          break;
         }
+        int item = atomicAdd(&g_fwd_sched[0], 1);
+        if (item >= n_items) item = -1;
+        item_ring[slot] = item;
+        mbar_arrive(&item_full[slot]);
+        if (item < 0) break;
+        const FwdItem I = fwd_item(item, p);
+        // the previous item's score MMAs have read the Q tiles
+        if (n > 0 && !mbar_wait(q_empty, (n - 1) & 1, kBudgetNs, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+        for (int x = 0; x < 2; ++x) {
+          tma_load_3d(&tm, q_full, smem + F2_Q + x * TILE_BYTES, I.h * HD, I.q0 + x * BQ, I.b);
+          tma_load_3d(&tm, q_full, smem + F2_Q + x * TILE_BYTES + ATOM_BYTES, I.h * HD + 64, I.q0 + x * BQ, I.b);
+        }
+        // K runs up to two tiles ahead of V (B's next scores need K[t+1] while A still reads V[t]),
+        // so the two rings are filled in one interleaved order: K0, K1, V0, K2, V1, K3, V2, ...
+        int lk = 0, lv = 0;
+        while (ok && (lk < I.nu || lv < I.nu)) {
+          const bool do_k = lk < I.nu && (lk < lv + 2);
+          if (do_k) {
+            const int st = ik % F2_KST;
+            if (!mbar_wait(&k_empty[st], ((ik / F2_KST) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            const int k0 = (I.u_lo + lk) * BKV;
+            uint8_t* ks = smem + F2_K + st * TILE_BYTES;
+            mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+            tma_load_3d(&tm, &k_full[st], ks, p.Dq + I.kvh * HD, k0, I.b);
+            tma_load_3d(&tm, &k_full[st], ks + ATOM_BYTES, p.Dq + I.kvh * HD + 64, k0, I.b);
+            ++ik;
+            ++lk;
+          } else {
+            const int st = iv % F2_VST;
+            if (!mbar_wait(&v_empty[st], ((iv / F2_VST) & 1) ^ 1, kBudgetNs, abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            const int k0 = (I.u_lo + lv) * BKV;
+            uint8_t* vs = smem + F2_V + st * TILE_BYTES;
+            mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+            tma_load_3d(&tm, &v_full[st], vs, p.Dq + p.Dkv + I.kvh * HD, k0, I.b);
+            tma_load_3d(&tm, &v_full[st], vs + ATOM_BYTES, p.Dq + p.Dkv + I.kvh * HD + 64, k0, I.b);
+            ++iv;
+            ++lv;
+          }
+        }
+        if (!ok) break;
       }
       if (!ok) fail(kErrTimeoutProducer);
     }
@@ -189,51 +262,78 @@ __global__ void __launch_bounds__(320, 1)
     if (elect_one()) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, false, false);
       constexpr uint32_t idesc_o = umma_idesc_bf16(128, 128, false, true);
-      bool ok = mbar_wait(q_full, 0, kBudgetNs, abort_flag, p.status);
-      // S_X(j) = Q_X K_t^T for key tile t = lo_X + j
-      auto issue_s = [&](int x, int j) -> bool {
-        const Band& bx = x ? bB : bA;
-        const int t = bx.lo + j, i = t - u_lo, st = i % F2_KST;
-        if (!mbar_wait(&k_full[st], (i / F2_KST) & 1, kBudgetNs, abort_flag, p.status)) return false;
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(smem + F2_Q + x * TILE_BYTES);
-        const uint32_t k_addr = smem_u32(smem + F2_K + st * TILE_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
-          umma_bf16_ss(tmem + x * 256, umma_desc_sw128(q_addr + off, 16, 1024),
-                       umma_desc_sw128(k_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+      int kbase = 0, vbase = 0;            // ring positions of the item's first K and V tiles
+      int pc[2] = {0, 0}, oc[2] = {0, 0};  // per query tile: P blocks consumed, items whose O is complete
+      bool ok = true;
+      for (int n = 0; ok; ++n) {
+        const int slot = n & 1;
+        if (!mbar_wait(&item_full[slot], (n >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+          ok = false;
+          break;
         }
-        umma_commit(&s_full[x]);
-        if (last_is_b(t) == (x == 1)) umma_commit(&k_empty[st]);
-        return true;
-      };
-      // O_X += P_X V_t, P from TMEM
-      auto issue_pv = [&](int x, int j) -> bool {
-        const Band& bx = x ? bB : bA;
-        const int t = bx.lo + j, i = t - u_lo, st = i % F2_VST;
-        if (!mbar_wait(&p_full[x], j & 1, kBudgetNs, abort_flag, p.status) ||
-            !mbar_wait(&v_full[st], (i / F2_VST) & 1, kBudgetNs, abort_flag, p.status))
-          return false;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(smem + F2_V + st * TILE_BYTES);
+        const int item = item_ring[slot];
+        mbar_arrive(&item_empty[slot]);
+        if (item < 0) break;
+        const FwdItem I = fwd_item(item, p);
+        const int n_s = I.bA.n + I.bB.n;
+        int s_issued = 0;
+        ok = mbar_wait(q_full, n & 1, kBudgetNs, abort_flag, p.status);
+        // S_X(j) = Q_X K_t^T for key tile t = lo_X + j
+        auto issue_s = [&](int x, int j) -> bool {
+          const Band& bx = x ? I.bB : I.bA;
+          const int t = bx.lo + j, g = kbase + (t - I.u_lo), st = g % F2_KST;
+          if (!mbar_wait(&k_full[st], (g / F2_KST) & 1, kBudgetNs, abort_flag, p.status)) return false;
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(smem + F2_Q + x * TILE_BYTES);
+          const uint32_t k_addr = smem_u32(smem + F2_K + st * TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk)
-          umma_bf16_ts(tmem + x * 256 + 128, tmem + x * 256 + kk * 8,
-                       umma_desc_sw128(v_addr + kk * 2048, ATOM_BYTES, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-        if (last_is_b(t) == (x == 1)) umma_commit(&v_empty[st]);
-        if (j == (x ? bB.n : bA.n) - 1) umma_commit(&o_done[x]);
-        return true;
-      };
-      if (ok && bA.n > 0) ok = issue_s(0, 0);
-      if (ok && bB.n > 0) ok = issue_s(1, 0);
-      for (int j = 0; ok && (j < bA.n || j < bB.n); ++j) {
-        for (int x = 0; x < 2 && ok; ++x) {
-          const int n = x ? bB.n : bA.n;
-          if (j >= n) continue;
-          ok = issue_pv(x, j);
-          if (ok && j + 1 < n) ok = issue_s(x, j + 1);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
+            umma_bf16_ss(tmem + x * 256, umma_desc_sw128(q_addr + off, 16, 1024),
+                         umma_desc_sw128(k_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[x]);
+          if (I.last_is_b(t) == (x == 1)) umma_commit(&k_empty[st]);
+          if (++s_issued == n_s) umma_commit(q_empty);  // the item's last score MMA: Q may be reloaded
+          return true;
+        };
+        // O_X += P_X V_t, P from TMEM
+        auto issue_pv = [&](int x, int j) -> bool {
+          const Band& bx = x ? I.bB : I.bA;
+          const int t = bx.lo + j, g = vbase + (t - I.u_lo), st = g % F2_VST;
+          // the first PV of an item overwrites O: the softmax warps have read the previous item's
+          if (j == 0 && oc[x] > 0 && !mbar_wait(&o_empty[x], (oc[x] - 1) & 1, kBudgetNs, abort_flag, p.status))
+            return false;
+          if (!mbar_wait(&p_full[x], pc[x] & 1, kBudgetNs, abort_flag, p.status) ||
+              !mbar_wait(&v_full[st], (g / F2_VST) & 1, kBudgetNs, abort_flag, p.status))
+            return false;
+          ++pc[x];
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(smem + F2_V + st * TILE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk)
+            umma_bf16_ts(tmem + x * 256 + 128, tmem + x * 256 + kk * 8,
+                         umma_desc_sw128(v_addr + kk * 2048, ATOM_BYTES, 1024), idesc_o,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+          if (I.last_is_b(t) == (x == 1)) umma_commit(&v_empty[st]);
+          if (j == bx.n - 1) {
+            umma_commit(&o_done[x]);
+            ++oc[x];
+          }
+          return true;
+        };
+        if (ok && I.bA.n > 0) ok = issue_s(0, 0);
+        if (ok && I.bB.n > 0) ok = issue_s(1, 0);
+        for (int j = 0; ok && (j < I.bA.n || j < I.bB.n); ++j) {
+          for (int x = 0; x < 2 && ok; ++x) {
+            const int nx = x ? I.bB.n : I.bA.n;
+            if (j >= nx) continue;
+            ok = issue_pv(x, j);
+            if (ok && j + 1 < nx) ok = issue_s(x, j + 1);
+          }
         }
+        kbase += I.nu;
+        vbase += I.nu;
       }
       if (!ok) fail(kErrTimeoutMma);
       umma_commit(drain);
@@ -242,103 +342,128 @@ __global__ void __launch_bounds__(320, 1)
   } else {
     // softmax warps: query tile x = (warp - 2) / 4, row r of the tile (TMEM lane group = warp % 4)
     const int x = (warp - 2) >> 2;
-    const Band bx = x ? bB : bA;
     const int wq = warp & 3;
     const int lane = lane_id();
     const int r = wq * 32 + lane;
-    const int qt = q0 + x * BQ;
-    const int qi = qt + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16) + x * 256;
-    float m_ref = -INFINITY, l = 0.f;
+    int sc = 0, oc = 0;  // score blocks consumed and items finished by this query tile
     bool ok = true;
-    for (int j = 0; j < bx.n; ++j) {
-      if (!mbar_wait_warp(&s_full[x], j & 1, kBudgetNs, abort_flag, p.status)) {
+    for (int n = 0; ok; ++n) {
+      const int slot = n & 1;
+      if (!mbar_wait_warp(&item_full[slot], (n >> 1) & 1, kBudgetNs, abort_flag, p.status)) {
+        fail(kErrTimeoutEpilogue);
+        ok = false;
+        break;
+      }
+      const int item = item_ring[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[slot]);
+      if (item < 0) break;
+      Band bx;
+      int qt;
+      {
+        const FwdItem I = fwd_item(item, p);
+        bx = x ? I.bB : I.bA;
+        qt = I.q0 + x * BQ;
+      }
+      const int qi = qt + r;
+      const int w = p.window;
+      float m_ref = -INFINITY, l = 0.f;
+      for (int j = 0; j < bx.n; ++j, ++sc) {
+        if (!mbar_wait_warp(&s_full[x], sc & 1, kBudgetNs, abort_flag, p.status)) {
+          fail(kErrTimeoutEpilogue);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int k0 = (bx.lo + j) * BKV;
+        // interior tiles (every key visible to every row of the tile) skip the per-element mask
+        const bool interior = (k0 + BKV - 1 <= qt) && (k0 > qt + BQ - 1 - w) && (k0 + BKV <= p.T);
+        uint32_t sr[4][32];  // raw S row (masked entries set to -inf)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + c * 32, sr[c]);
+        tmem_ld_wait();
+        // row max of the raw scores (scale > 0, so it is the max of the scaled ones too); query qi sees
+        // key k0 + 32c + i for i in [qi - w + 1 - k0 - 32c, qi + 1 - k0 - 32c) below T - k0 - 32c
+        float mx = -INFINITY;
+        if (interior) {
+#pragma unroll
+          for (int i = 0; i < BKV; ++i) mx = fmaxf(mx, __uint_as_float(sr[i >> 5][i & 31]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int kc = k0 + 32 * c;
+            const uint32_t vis = qi < p.T ? range_mask32(qi - w + 1 - kc, min(qi + 1 - kc, p.T - kc)) : 0u;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float v = ((vis >> i) & 1u) ? __uint_as_float(sr[c][i]) : -INFINITY;
+              sr[c][i] = __float_as_uint(v);
+              mx = fmaxf(mx, v);
+            }
+          }
+        }
+        mx *= p.scale_log2;
+        // The rescale decision is per row, but tcgen05.ld/st are warp-collective: the warp rescales
+        // together whenever any of its rows needs it, rows that do not use alpha = 1. PV_X(j-1) is
+        // complete here (it was issued before S_X(j)).
+        float alpha = 1.f;
+        bool mine = false;
+        if (j == 0) {
+          m_ref = mx;
+        } else if (mx > m_ref + 8.f) {
+          mine = true;
+          alpha = m_ref == -INFINITY ? 0.f : exp2f(m_ref - mx);
+          l *= alpha;
+          m_ref = mx;
+        }
+        if (__any_sync(0xffffffffu, mine)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t v[32];
+            tmem_ld32(lane_base + 128 + c * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+            tmem_st32(lane_base + 128 + c * 32, v);
+          }
+        }
+        // P = exp2(s * scale_log2 - m_ref) -> bf16 pairs into TMEM columns [0, 64) of this tile (masked
+        // entries are -inf -> 0); the scale-and-subtract and the row sum run on f32x2 pairs
+        const float mref = m_ref == -INFINITY ? 0.f : m_ref;
+        const uint64_t sc2 = f32x2(p.scale_log2, p.scale_log2), nm2 = f32x2(-mref, -mref);
+        uint64_t l2 = f32x2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 64; i += 2) {
+            const int e = c * 64 + i;
+            const float2 t = f32x2_split(fma_f32x2(
+                f32x2(__uint_as_float(sr[e >> 5][e & 31]), __uint_as_float(sr[e >> 5][(e + 1) & 31])), sc2, nm2));
+            const float p0 = exp2f(t.x), p1 = exp2f(t.y);
+            l2 = add_f32x2(l2, f32x2(p0, p1));
+            pk[i / 2] = pack_bf16(p0, p1);
+          }
+          tmem_st32(lane_base + c * 32, pk);
+        }
+        {
+          const float2 ls = f32x2_split(l2);
+          l += ls.x + ls.y;
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[x]);
+      }
+      if (bx.n == 0 || !ok) continue;
+      if (!mbar_wait_warp(&o_done[x], oc & 1, kBudgetNs, abort_flag, p.status)) {
         fail(kErrTimeoutEpilogue);
         ok = false;
         break;
       }
       tc_fence_after();
-      const int k0 = (bx.lo + j) * BKV;
-      // interior tiles (every key visible to every row of the tile) skip the per-element mask
-      const bool interior = (k0 + BKV - 1 <= qt) && (k0 > qt + BQ - 1 - w) && (k0 + BKV <= p.T);
-      uint32_t sr[4][32];  // raw S row (masked entries set to -inf)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + c * 32, sr[c]);
-      tmem_ld_wait();
-      // row max of the raw scores (scale > 0, so it is the max of the scaled ones too); query qi sees
-      // key k0 + 32c + i for i in [qi - w + 1 - k0 - 32c, qi + 1 - k0 - 32c) below T - k0 - 32c
-      float mx = -INFINITY;
-      if (interior) {
-#pragma unroll
-        for (int i = 0; i < BKV; ++i) mx = fmaxf(mx, __uint_as_float(sr[i >> 5][i & 31]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int kc = k0 + 32 * c;
-          const uint32_t vis = qi < p.T ? range_mask32(qi - w + 1 - kc, min(qi + 1 - kc, p.T - kc)) : 0u;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float v = ((vis >> i) & 1u) ? __uint_as_float(sr[c][i]) : -INFINITY;
-            sr[c][i] = __float_as_uint(v);
-            mx = fmaxf(mx, v);
-          }
-        }
-      }
-      mx *= p.scale_log2;
-      // The rescale decision is per row, but tcgen05.ld/st are warp-collective: the warp rescales
-      // together whenever any of its rows needs it, rows that do not use alpha = 1. PV_X(j-1) is
-      // complete here (it was issued before S_X(j)).
-      float alpha = 1.f;
-      bool mine = false;
-      if (j == 0) {
-        m_ref = mx;
-      } else if (mx > m_ref + 8.f) {
-        mine = true;
-        alpha = m_ref == -INFINITY ? 0.f : exp2f(m_ref - mx);
-        l *= alpha;
-        m_ref = mx;
-      }
-      if (__any_sync(0xffffffffu, mine)) {
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(lane_base + 128 + c * 32, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-          tmem_st32(lane_base + 128 + c * 32, v);
-        }
-      }
-      // P = exp2(s * scale_log2 - m_ref) -> bf16 pairs into TMEM columns [0, 64) of this tile (masked
-      // entries are -inf -> 0); the scale-and-subtract and the row sum run on f32x2 pairs
-      const float mref = m_ref == -INFINITY ? 0.f : m_ref;
-      const uint64_t sc2 = f32x2(p.scale_log2, p.scale_log2), nm2 = f32x2(-mref, -mref);
-      uint64_t l2 = f32x2(0.f, 0.f);
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 64; i += 2) {
-          const int e = c * 64 + i;
-          const float2 t = f32x2_split(
-              fma_f32x2(f32x2(__uint_as_float(sr[e >> 5][e & 31]), __uint_as_float(sr[e >> 5][(e + 1) & 31])), sc2, nm2));
-          const float p0 = exp2f(t.x), p1 = exp2f(t.y);
-          l2 = add_f32x2(l2, f32x2(p0, p1));
-          pk[i / 2] = pack_bf16(p0, p1);
-        }
-        tmem_st32(lane_base + c * 32, pk);
-      }
-      {
-        const float2 ls = f32x2_split(l2);
-        l += ls.x + ls.y;
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&p_full[x]);
-    }
-    if (bx.n > 0 && ok && mbar_wait_warp(&o_done[x], 0, kBudgetNs, abort_flag, p.status)) {
-      tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int hb = item / ((p.T + 2 * BQ - 1) / (2 * BQ));  // b * H + h
+      const int h = hb % p.H, b = hb / p.H;
       __nv_bfloat16* orow = p.out + ((int64_t)b * p.T + qi) * p.ldo + h * HD;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
@@ -357,13 +482,16 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       }
-      if (qi < p.T) p.lse[((int64_t)b * p.H + h) * p.T + qi] = m_ref + __log2f(l);  // log2 units
-    } else if (bx.n > 0 && ok) {
-      fail(kErrTimeoutEpilogue);
+      if (qi < p.T) p.lse[(int64_t)hb * p.T + qi] = m_ref + __log2f(l);  // log2 units, [B, H, T]
+      // O is read: the next item's first PV MMA of this tile may overwrite it
+      tc_fence_before();
+      mbar_arrive(&o_empty[x]);
+      ++oc;
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) fwd_sched_exit();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -937,6 +1065,7 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse,
   CUtensorMap tm = tma_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.data_ptr(), W, T, B, qkv.stride(0),
                               qkv.stride(0) * T, 64, 128);
   FwdParams p;
+  p.B = (int)B;
   p.T = (int)T;
   p.H = (int)H;
   p.KV = (int)KV;
@@ -953,8 +1082,12 @@ void attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse,
     C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
     attr = true;
   }
-  dim3 grid((unsigned)((T + 2 * BQ - 1) / (2 * BQ)), (unsigned)H, (unsigned)B);
-  attn_fwd_tc_kernel<<<grid, 320, FWD_SMEM, at::cuda::getCurrentCUDAStream()>>>(tm, p);
+  // persistent: one CTA per SM (shared memory allows no more), no more CTAs than work items
+  int sms = 0;
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, qkv.device().index()));
+  const int64_t items = ((T + 2 * BQ - 1) / (2 * BQ)) * H * B;
+  attn_fwd_tc_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(items, sms)), 320, FWD_SMEM,
+                       at::cuda::getCurrentCUDAStream()>>>(tm, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
