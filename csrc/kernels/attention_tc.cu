@@ -1,7 +1,8 @@
 // tcgen05/TMEM flash attention for sm_100a (head_dim 128, causal + sliding window).
 //
-// Forward: one CTA per (two 128-query tiles A and B, head, batch); 320 threads:
-//   warp 0      TMA: both Q tiles once, then K tiles into a 3-stage ring and V tiles into a 2-stage
+// Forward: persistent, one CTA per SM, 320 threads; a work item is (two 128-query tiles A and B, head,
+// batch), taken from a device counter by warp 0 and handed to the other warps (see the kernel):
+//   warp 0      TMA: the item's two Q tiles, then K tiles into a 3-stage ring and V tiles into a 2-stage
 //               ring (128-byte swizzle, 3-D tensor maps over the fused [B, T, Dq+2Dkv] projection
 //               buffer, zero fill past T; no multicast);
 //   warp 1      TMEM allocation and the single MMA-issuing lane. Per query tile X:
